@@ -1,0 +1,395 @@
+"""Benchmark of the fused NCA step: cell-updates/s of a 64-step fwd+bwd rollout training iteration of K texture NCAs.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    torchrun --nproc-per-node N bench.py --gpus N ...     (one rank per GPU)
+
+Workload (per GPU): K = 32 texture NCAs (12 channels, 96 hidden), batch 2 per NCA drawn
+from a pool of 64 seeded U[-0.1, 0.1] states per NCA, 128 x 128 circular grid, update rate 0.5, TF32 MMA; one step
+of this benchmark is one training iteration: 64 forward steps, the synthetic L2 + 10 x overflow loss, 64 backward
+steps, per-NCA per-tensor gradient normalisation + Adam (lr 1e-3, halved at 256 / 512), pool write-back. With N GPUs
+each rank owns 32 NCAs (weak scaling, K = 32 N in total); rank 0 broadcasts the rollout length and seed over NCCL and
+the per-NCA losses are all-gathered, as the reference's group loop would log them. Inputs: 64 saved states of 50 MB
+per iteration (3.2 GB) exceed the 126 MB L2, so no flush is needed between iterations.
+
+value: K B H W steps x iterations / (max over ranks of the CUDA-event time of the timed iterations).
+e2e:   the same metric through the public operator API (ultranca_b200.nca_ops.step under autograd, the call
+       train.py makes), with the batch copied host -> device from pinned memory and the losses copied back every
+       iteration inside the timed region.
+--impl reference: the reference's eager PyTorch step (the CPU restatement in oracle/, fp32, all host threads) on a
+       bounded sample of the same workload; it prints its own JSON line and no GPU is used.
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+K_PER_GPU, B, C, HID, H, W, STEPS, POOL, RATE = 32, 2, 12, 96, 128, 128, 64, 64, 0.5
+METRIC = 'cell-updates/s fwd+bwd, 64-step rollout'
+UNIT = 'cell-updates/s'
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument('--gpus', type=int, default=1)
+    ap.add_argument('--steps', type=int, default=10)
+    ap.add_argument('--warmup', type=int, default=3)
+    ap.add_argument('--impl', default='ours', choices=['ours', 'reference'])
+    ap.add_argument('--no-e2e', action='store_true')
+    ap.add_argument('--no-cpu', action='store_true')
+    return ap.parse_args()
+
+
+# ------------------------------------------------------------------------------------------------ clocks
+class ClockSampler:
+    """nvidia-smi samples (every 200 ms) of this rank's GPU during the timed region."""
+    FIELDS = ('index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,'
+              'clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,'
+              'clocks_event_reasons.sw_power_cap')
+
+    def __init__(self, gpu_index):
+        self.gpu, self.lines, self.proc = gpu_index, [], None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(['nvidia-smi', f'--query-gpu={self.FIELDS}', '--format=csv,noheader,nounits',
+                                          '-i', str(self.gpu), '-lms', '200'], stdout=subprocess.PIPE,
+                                         stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            self.thread.join(timeout=5)
+
+    def summary(self):
+        rows = [[f.strip() for f in l.split(',')] for l in self.lines if l.count(',') >= 8]
+        if not rows:
+            return {'sm_mhz': None, 'sm_max_mhz': None, 'reasons': ['nvidia-smi unavailable']}
+        sm = [float(r[1]) for r in rows if r[1].replace('.', '').isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace('.', '').isdigit()]
+        names = ('hw_slowdown', 'hw_thermal_slowdown', 'sw_thermal_slowdown', 'sw_power_cap')
+        reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v.lower() == 'active'})
+        return {'sm_mhz': statistics.median(sm) if sm else None, 'sm_max_mhz': max(mx) if mx else None,
+                'reasons': reasons, 'samples': len(rows)}
+
+
+# ------------------------------------------------------------------------------------------------ CPU arms
+def cpu_sample(steps, threads):
+    """The reference's eager fp32 step (CPU restatement, oracle/) with autograd over a `steps`-step rollout of one
+    texture NCA (B = 2, 128 x 128) + synthetic loss backward. Returns (cell-updates, seconds)."""
+    from oracle import nca_oracle as O
+    torch.set_num_threads(threads)
+    x, w1, b1, w2, target = O.make_config_inputs(1, B, C, HID, H, W, seed=0)
+    w1, b1, w2 = (t.requires_grad_() for t in (w1, b1, w2))
+    masks = [O.mask_for(1, B, H, W, O.step_seed(7, i), RATE) for i in range(steps)]
+    t0 = time.perf_counter()
+    cur = x
+    for i in range(steps):
+        cur = O.reference_step(cur, w1, b1, w2, masks[i])
+    obj, _ = O.synthetic_loss(cur, target)
+    obj.backward()
+    dt = time.perf_counter() - t0
+    return B * H * W * steps, dt
+
+
+def cpu_baseline(max_seconds=20.0):
+    threads = os.cpu_count() or 1
+    cells, dt = cpu_sample(4, threads)  # warm-up and size the sample
+    steps = max(4, min(STEPS, int(max_seconds / max(dt / 4, 1e-3))))
+    cells, dt = cpu_sample(steps, threads)
+    return {'value': cells / dt, 'unit': UNIT, 'cores': threads, 'kind': 'port',
+            'sample': f'1 texture NCA x B={B} x {H}x{W}, {steps}-step fwd+bwd rollout + synthetic loss, eager fp32 '
+                      f'reference_step (oracle/nca_oracle.py) on {threads} host threads, {dt:.1f} s'}
+
+
+def run_reference(args):
+    rank = int(os.environ.get('RANK', '0'))
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    steps_per_sample = 8
+    for _ in range(max(args.warmup, 0)):
+        cpu_sample(steps_per_sample, threads)
+    total_cells, total_t = 0, 0.0
+    for _ in range(args.steps):
+        cells, dt = cpu_sample(steps_per_sample, threads)
+        total_cells += cells
+        total_t += dt
+    v = total_cells / total_t
+    line = {'metric': METRIC, 'value': v, 'unit': UNIT, 'n_gpus': args.gpus, 'steps': args.steps,
+            'warmup': args.warmup, 'ms_per_step': 1000 * total_t / args.steps, 'higher_is_better': True,
+            'scaling': 'weak', 'vs_baseline': None, 'dtype': 'fp32', 'data': 'synthetic', 'impl': 'reference',
+            'config': config(args.gpus, 'the reference eager PyTorch step on the host CPU'),
+            'cpu_baseline': {'value': v, 'unit': UNIT, 'cores': threads, 'kind': 'port',
+                             'sample': f'per step: 1 texture NCA x B={B} x {H}x{W}, {steps_per_sample}-step fwd+bwd '
+                                       f'rollout + synthetic loss, eager fp32 (oracle/nca_oracle.py reference_step)'},
+            'e2e': {'value': v, 'unit': UNIT, 'h2d_bytes_per_step': 0, 'd2h_bytes_per_step': 0}}
+    print(json.dumps(line), flush=True)
+
+
+def config(n, note=None):
+    c = {'workload': f'texture NCA training iteration: K={K_PER_GPU * n} NCAs ({K_PER_GPU} per GPU), B={B}, '
+                     f'{H}x{W}, {C} ch / {HID} hidden, {STEPS}-step rollout fwd+bwd, p={RATE}, synthetic L2+overflow '
+                     f'loss, grad-norm + Adam (BASELINE config 1)',
+         'K': K_PER_GPU * n, 'B': B, 'H': H, 'W': W, 'steps_per_rollout': STEPS, 'update_rate': RATE,
+         'parallelism': f'K-sharded x{n}', 'l2': 'inputs larger than L2 (64 saved states of 50 MB per iteration)'}
+    if note:
+        c['note'] = note
+    return c
+
+
+# ------------------------------------------------------------------------------------------------ GPU arm
+def main():
+    args = parse()
+    if args.impl == 'reference':
+        run_reference(args)
+        return
+    from oracle import nca_oracle as O  # seeded synthetic inputs only (same generator as the tests)
+    from ultranca_b200 import nca_ops, training
+    from ultranca_b200._lib import check, lib, ptr
+
+    world = int(os.environ.get('WORLD_SIZE', '1'))
+    rank = int(os.environ.get('RANK', '0'))
+    local = int(os.environ.get('LOCAL_RANK', '0'))
+    torch.cuda.set_device(local)
+    dev = torch.device('cuda', local)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group('nccl', timeout=datetime.timedelta(seconds=120), device_id=dev)
+
+    K = K_PER_GPU
+    k0 = rank * K  # this rank's first NCA
+    # seeded inputs of this shard (NCA k's weights / targets / pool depend on k only)
+    g = torch.Generator().manual_seed(1000 + rank)
+    _, w1, b1, w2, target = O.make_config_inputs(K, 1, C, HID, H, W, seed=1000 + rank)
+    pool = ((torch.rand(K, POOL, C, H, W, generator=g) * 2 - 1) * 0.1).to(dev)
+    w1, b1, w2, target = (t.to(dev).contiguous() for t in (w1, b1, w2, target))
+    trainer = training.RolloutTrainer(w1, b1, w2, B, H, W, STEPS, RATE, growing=False, fp32=False,
+                                      image_offset=k0 * B)
+    ks = torch.arange(K, device=dev)[:, None]
+    stream = torch.cuda.current_stream(dev)
+    # rank 0 draws (rollout length, seed) per iteration and broadcasts them (the only cross-rank traffic)
+    ctl = torch.zeros(2, dtype=torch.int64, device=dev)
+    seed_gen = torch.Generator().manual_seed(0)
+    losses_all = torch.zeros(world * K, device=dev)
+
+    # Control for iteration i + 1 is broadcast on a side stream while iteration i runs, so reading it on the host
+    # never waits for the step kernels (single GPU: drawn on the host, nothing to broadcast).
+    side = torch.cuda.Stream(dev)
+    ctl_host = torch.zeros(2, dtype=torch.int64).pin_memory()
+    ctl_ready = torch.cuda.Event()
+
+    def prefetch_control():
+        with torch.cuda.stream(side):
+            if rank == 0:
+                ctl.copy_(torch.tensor([STEPS, int(torch.randint(0, 2 ** 62, (1,), generator=seed_gen).item())]),
+                          non_blocking=False)
+            if dist is not None:
+                dist.broadcast(ctl, 0)
+            ctl_host.copy_(ctl, non_blocking=True)
+            ctl_ready.record(side)
+
+    def take_control():
+        ctl_ready.synchronize()
+        steps, seed = int(ctl_host[0]), int(ctl_host[1])
+        assert steps == STEPS
+        prefetch_control()
+        return seed
+
+    stage_times = {'fwd': [], 'bwd_main': []}
+
+    def iteration(i, profile=False):
+        seed = take_control()
+        idx = torch.rand(K, POOL, device=dev).argsort(1)[:, :B]
+        x0 = pool[ks, idx]
+        if i % 16 == 0:
+            x0[:, 0] = 0.0  # the zero seed of a texture NCA replaces the first sample (train.py:131-132)
+        if profile:
+            loss = profiled_iteration(x0, seed)
+        else:
+            loss, xT = trainer.iteration(x0, target, seed)
+        pool[ks, idx] = trainer.states[STEPS]
+        if dist is not None:
+            dist.all_gather_into_tensor(losses_all, trainer.loss)
+        return trainer.loss
+
+    def profiled_iteration(x0, seed):
+        """trainer.iteration with CUDA events around every forward launch and every backward main-kernel launch."""
+        t = trainer
+        st = ctypes_stream()
+        t.states[0].copy_(x0)
+        evs = []
+        for s in range(STEPS):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            check(lib.nca_forward(ptr(t.states[s]), ptr(w1), ptr(b1), ptr(w2), ptr(t.states[s + 1]), None, None, t.N, C,
+                                  H, W, K, HID, B, nca_ops.step_seed(seed, s), RATE, 0, 0, t.image_offset, st))
+            e1.record(stream)
+            evs.append(('fwd', e0, e1))
+        training.synthetic_loss(t.states[STEPS], target, 10.0, t.gy[0], t.loss, t.loss_work)
+        cur = t.gy[0]
+        for n, s in enumerate(reversed(range(STEPS))):
+            nxt = t.gy[1] if cur is t.gy[0] else t.gy[0]
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            common = (ptr(t.states[s]), ptr(cur), None, ptr(w1), ptr(b1), ptr(w2), ptr(nxt), ptr(t.grads[0]),
+                      ptr(t.grads[1]), ptr(t.grads[2]), ptr(t.dp), t.dp_floats, ptr(t.partial), t.partial_floats, t.N, C,
+                      H, W, K, HID, B, nca_ops.step_seed(seed, s), RATE, 0, 0, t.image_offset, int(n > 0))
+            e0.record(stream)
+            check(lib.nca_backward_stages(*common, 1, st))
+            e1.record(stream)
+            check(lib.nca_backward_stages(*common, 6, st))
+            evs.append(('bwd_main', e0, e1))
+            cur = nxt
+        t.opt.step(t.grads)
+        pending.append(evs)
+        return t.loss
+
+    import ctypes
+
+    def ctypes_stream():
+        return ctypes.c_void_p(stream.cuda_stream)
+
+    pending = []
+    prefetch_control()
+
+    # warm-up
+    for i in range(args.warmup):
+        iteration(i)
+    torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        start.record(stream)
+        for i in range(args.steps):
+            iteration(args.warmup + i, profile=True)
+        end.record(stream)
+        torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize()
+    ms = start.elapsed_time(end)
+    for evs in pending:
+        for name, e0, e1 in evs:
+            stage_times[name].append(e0.elapsed_time(e1))
+    if dist is not None:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    cells_per_iter = world * K * B * H * W * STEPS
+    value = cells_per_iter * args.steps / (ms / 1000.0)
+    launches_per_iter = STEPS * 1 + 2 + STEPS * 3 + 2
+    # roofline of the dominant kernel (the larger total of the forward kernel and the backward main kernel)
+    tot = {k: sum(v) for k, v in stage_times.items()}
+    dom = max(tot, key=tot.get)
+    avg_ms = statistics.mean(stage_times[dom])
+    alg_bytes = K * B * H * W * 96  # fwd: read x + write y; bwd main: read x + read gy (48 B each per cell)
+    peaks = {}
+    try:
+        peaks = json.load(open(os.path.join(ROOT, 'MEASURED_PEAKS.json')))
+    except (OSError, ValueError):
+        pass
+    peak = peaks.get('hbm_gbs', 6650.0)
+    achieved = alg_bytes / (avg_ms / 1000.0) / 1e9
+    traffic = None
+    try:
+        tr = json.load(open(os.path.join(ROOT, 'profiles', 'traffic.json')))
+        traffic = tr.get({'fwd': 'fwd_kernel', 'bwd_main': 'bwd_kernel'}[dom])
+    except (OSError, ValueError):
+        pass
+    roofline = {'bound': 'hbm', 'achieved': achieved, 'peak': peak, 'unit': 'GB/s', 'frac': achieved / peak,
+                'traffic': traffic, 'kernel': {'fwd': 'fwd_kernel<12,96,TC>', 'bwd_main': 'bwd_kernel<12,96,TC>'}[dom],
+                'algorithmic_bytes_per_launch': alg_bytes, 'avg_launch_ms': avg_ms,
+                'peak_source': 'MEASURED_PEAKS.json hbm_gbs (of measured)' if 'hbm_gbs' in peaks else 'fallback',
+                'stage_ms_per_iteration': {k: v / args.steps for k, v in tot.items()}}
+
+    # e2e through the public operator API with host buffers
+    e2e = None
+    if not args.no_e2e:
+        e2e = run_e2e(args, dev, rank, world, dist, K, w1, b1, w2, target, nca_ops, training)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        cpu = cpu_baseline()
+
+    if rank == 0:
+        line = {'metric': METRIC, 'value': value, 'unit': UNIT, 'n_gpus': world, 'steps': args.steps,
+                'warmup': args.warmup, 'ms_per_step': ms / args.steps, 'higher_is_better': True, 'scaling': 'weak',
+                'vs_baseline': None, 'dtype': 'tf32', 'data': 'synthetic', 'config': config(world),
+                'roofline': roofline, 'cpu_baseline': cpu, 'e2e': e2e, 'clocks': clocks.summary(),
+                'gpu_launches': launches_per_iter * args.steps}
+        print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def run_e2e(args, dev, rank, world, dist, K, w1, b1, w2, target, nca_ops, training):
+    """The training iteration as train.py runs it on the drop-in operator: nca_ops.step per step under autograd,
+    backward through _Step, the fused optimiser; batch H2D from pinned host memory, losses D2H, every iteration."""
+    g = torch.Generator().manual_seed(77 + rank)
+    host = ((torch.rand(K, B, C, H, W, generator=g) * 2 - 1) * 0.1).pin_memory()
+    ws = [t.clone().requires_grad_() for t in (w1, b1, w2)]
+    opt = training.FusedAdam(ws)
+    loss_host = torch.empty(K).pin_memory()
+    stream = torch.cuda.current_stream(dev)
+
+    def it(i):
+        x = host.to(dev, non_blocking=True)
+        for s in range(STEPS):
+            x = nca_ops.step(x, *ws, RATE, seed=1000 * i + s, image_offset=rank * K * B)
+        loss, gy = training.synthetic_loss(x.detach(), target)
+        x.backward(gy)
+        opt.step([w.grad for w in ws])
+        for w in ws:
+            w.grad = None
+        loss_host.copy_(loss, non_blocking=True)
+
+    for i in range(args.warmup):
+        it(i)
+    torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for i in range(args.steps):
+        it(args.warmup + i)
+    end.record(stream)
+    torch.cuda.synchronize()
+    ms = start.elapsed_time(end)
+    if dist is not None:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    return {'value': world * K * B * H * W * STEPS * args.steps / (ms / 1000.0), 'unit': UNIT,
+            'h2d_bytes_per_step': host.numel() * 4, 'd2h_bytes_per_step': K * 4,
+            'path': 'ultranca_b200.nca_ops.step under autograd (train.py call pattern) + fused Adam',
+            'ms_per_step': ms / args.steps}
+
+
+if __name__ == '__main__':
+    main()

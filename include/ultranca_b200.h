@@ -1,0 +1,131 @@
+/*
+ * UltraNCA-B200: C-ABI of the fused batched NCA step for NVIDIA B200 (sm_100a).
+ *
+ * K NCAs with B images each are stacked as N = K B images of C x H x W fp32 state (image n belongs to NCA n / B);
+ * weights w1 (K, hidden, 4C), b1 (K, hidden), w2 (K, C, hidden), all C-contiguous device memory.
+ * Supported (C, hidden): (12, 96) texture and (16, 128) growing NCAs, as in the reference.
+ *
+ * Conventions (the reference's nanobind layer, ncaops/nca_cuda.cu, raises RuntimeError; this layer returns codes):
+ *   - every function returns NCA_OK (0) or an NCA_ERR_* code, with the message in nca_last_error() (thread-local);
+ *   - work is enqueued asynchronously on `stream` (a cudaStream_t; NULL = the legacy default stream);
+ *   - no function allocates device memory; workspaces are sized by nca_backward_workspace();
+ *   - `fp32` = 0 runs the MLP on TF32 tensor cores (tcgen05), 1 in fp32 (the reference's FP32 accuracy mode);
+ *   - `image_offset` is the global index of image 0 (a shard of a multi-GPU job passes its first image, so that the
+ *     Philox update mask equals the single-GPU mask); 0 for a single-GPU call.
+ */
+#ifndef ULTRANCA_B200_H
+#define ULTRANCA_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define NCA_ABI_VERSION 1
+
+enum {
+    NCA_OK = 0,
+    NCA_ERR_ARGUMENT = 1,    /* null pointer or invalid scalar */
+    NCA_ERR_SHAPE = 2,       /* shape / size mismatch (reference: std::runtime_error from validate_array_shape) */
+    NCA_ERR_UNSUPPORTED = 3, /* no kernel for this (channels, hidden) */
+    NCA_ERR_CUDA = 4,        /* a CUDA runtime error (launch or API) */
+    NCA_ERR_INTERNAL = 5
+};
+
+/* Message of the last failed call on this thread (empty if none). */
+const char *nca_last_error(void);
+
+/* NCA_ABI_VERSION of the loaded library. */
+int nca_version(void);
+
+/* One NCA step x -> y.
+ * Replaces nca_cuda.forward (ncaops/nca_cuda.cu:147-155, bound at :335-340).
+ * x, y: (N, C, H, W); growing: alpha (N, H, W) fp32 workspace and alive (N, H, W) uint8 output (the alive mask the
+ * backward needs); both may be NULL when growing = 0. update_rate >= 1: every cell updates. */
+int nca_forward(const float *x, const float *w1, const float *b1, const float *w2, float *y, float *alpha, uint8_t *alive,
+                int64_t N, int64_t C, int64_t H, int64_t W, int64_t K, int64_t hidden, uint32_t batch_per_nca,
+                uint64_t seed, float update_rate, int fp32, int growing, int64_t image_offset, void *stream);
+
+/* `steps` forward steps from x into y without gradients; step i uses seed nca_step_seed(seed, i); x is not modified;
+ * steps = 0 copies x. tmp: workspace like x when steps > 1 (ping-pong). Growing: alpha (N, H, W), alive (N, H, W).
+ * Replaces nca_cuda.rollout (ncaops/nca_cuda.cu:166-188, bound at :341-344). */
+int nca_rollout(const float *x, const float *w1, const float *b1, const float *w2, float *y, float *tmp, float *alpha,
+                uint8_t *alive, int64_t N, int64_t C, int64_t H, int64_t W, int64_t K, int64_t hidden, uint32_t steps,
+                uint32_t batch_per_nca, uint64_t seed, float update_rate, int fp32, int growing, int64_t image_offset,
+                void *stream);
+
+/* splitmix64 seed of rollout step i (ncaops/nca_cuda.cu:157-164). */
+uint64_t nca_step_seed(uint64_t seed, uint64_t i);
+
+/* Workspace sizes of nca_backward for this shape on the current device: dp_floats (the dp scratch, fp32 elements),
+ * partial_floats (weight-gradient partials, fp32 elements) and chunk (images per backward launch: always N).
+ * Replaces nca_cuda.backward_workspace (ncaops/nca_cuda.cu:235-254, bound at :345-346), whose tuple was
+ * (packed bytes per NCA, partial floats per image, images per chunk). */
+int nca_backward_workspace(int64_t C, int64_t hidden, int fp32, int64_t N, int64_t H, int64_t W, int64_t K,
+                           float update_rate, int growing, int64_t *dp_floats, int64_t *partial_floats, int64_t *chunk);
+
+/* Gradients of one step (same seed, update_rate and, growing, alive mask as its forward): gx (N, C, H, W),
+ * dw1 (K, hidden, 4C), db1 (K, hidden), dw2 (K, C, hidden); weight gradients are reduced in a fixed order (bitwise
+ * deterministic). accumulate = 1 adds them to dw1 / db1 / dw2 instead of overwriting (a rollout's backward can then
+ * sum its steps without extra launches). dp, partial: workspaces of at least the sizes nca_backward_workspace gives.
+ * Replaces nca_cuda.backward (ncaops/nca_cuda.cu:256-323, bound at :347-350). */
+int nca_backward(const float *x, const float *gy, const uint8_t *alive, const float *w1, const float *b1, const float *w2,
+                 float *gx, float *dw1, float *db1, float *dw2, float *dp, int64_t dp_floats, float *partial,
+                 int64_t partial_floats, int64_t N, int64_t C, int64_t H, int64_t W, int64_t K, int64_t hidden,
+                 uint32_t batch_per_nca, uint64_t seed, float update_rate, int fp32, int growing, int64_t image_offset,
+                 int accumulate, void *stream);
+
+/* The three stages of nca_backward, separately: NCA_STAGE_MAIN (recompute p, h; dh, dp into the dp scratch; per-CTA
+ * weight-gradient partials), NCA_STAGE_ADJOINT (gx from dp and gy), NCA_STAGE_REDUCE (fixed-order sum of the partials
+ * into dw1 / db1 / dw2). Issued in this order on one stream, any subset equals the matching part of nca_backward, so a
+ * caller can time or interleave the stages. No reference counterpart: the reference launches them only together,
+ * inside nca_cuda.backward (ncaops/nca_cuda.cu:285-322). */
+#define NCA_STAGE_MAIN 1
+#define NCA_STAGE_ADJOINT 2
+#define NCA_STAGE_REDUCE 4
+int nca_backward_stages(const float *x, const float *gy, const uint8_t *alive, const float *w1, const float *b1,
+                        const float *w2, float *gx, float *dw1, float *db1, float *dw2, float *dp, int64_t dp_floats,
+                        float *partial, int64_t partial_floats, int64_t N, int64_t C, int64_t H, int64_t W, int64_t K,
+                        int64_t hidden, uint32_t batch_per_nca, uint64_t seed, float update_rate, int fp32, int growing,
+                        int64_t image_offset, int accumulate, int stages, void *stream);
+
+/* mask (n, h, w) = the {0, 1} update mask the kernels use for `seed` (Philox4x32-10; image index image_offset + i).
+ * Replaces nca_cuda.update_mask (ncaops/nca_cuda.cu:325-331, bound at :351-352). */
+int nca_update_mask(float *mask, int64_t n, int64_t h, int64_t w, uint64_t seed, float update_rate, int64_t image_offset,
+                    void *stream);
+
+/* Synthetic loss of the benchmark configurations, per NCA k:
+ *   loss[k] = mean over (B, 3, H, W) of (x[k, :, :3] - target[k])^2 + overflow_weight * sum over (B, C, H, W) of
+ *             |x - clamp(x, -1, 1)|,
+ * and gy = d(sum_k loss[k]) / dx (N, C, H, W). target (K, 3, H, W); work: K * 128 floats of scratch.
+ * Replaces the task loss the reference's training loop calls (train.py:67-72 / :97-99, Texture / Growing.loss);
+ * deterministic (fixed-order reductions). */
+int nca_synthetic_loss(const float *x, const float *target, float *gy, float *loss, float *work, int64_t K, int64_t B,
+                       int64_t C, int64_t H, int64_t W, float overflow_weight, void *stream);
+
+/* Per-NCA, per-tensor gradient normalisation followed by Adam with a MultiStepLR schedule, for the three weight
+ * tensors at once, in one launch (train.py:120-122 and :136-141: g /= ||g_k||_2 + 1e-8; torch.optim.Adam; lr x gamma
+ * at each milestone). param_i / grad_i / m_i / v_i: K x numel_i fp32 (i = 0, 1, 2 for w1, b1, w2). iteration: device
+ * int64, the 0-based iteration index (step = iteration + 1 for the bias corrections); the call increments it.
+ * milestones: up to 8 iteration indices (host array), n_milestones of them. */
+int nca_adam_step(float *param0, float *param1, float *param2, const float *grad0, const float *grad1, const float *grad2,
+                  float *m0, float *m1, float *m2, float *v0, float *v1, float *v2, int64_t K, int64_t numel0,
+                  int64_t numel1, int64_t numel2, int64_t *iteration, float lr, float beta1, float beta2, float eps,
+                  float gamma, const int64_t *milestones, int n_milestones, void *stream);
+
+/* Reads (and, reset = 1, clears) the device error word of the current device: 0, or 1 when a kernel gave up waiting
+ * for its tensor-core work (a bounded wait ran out; the kernel returned instead of hanging). Synchronous. */
+int nca_device_error(int *code, int reset);
+
+/* Tensor-core layout self-test: D = A B^T on tcgen05 for one of the operand forms the step kernels use
+ * (mode 0: A, B K-major; 1: A, B MN-major; 2: A K-major, B MN-major (B rows = 16); 3: A from Tensor Memory;
+ * 4: A K-major, B MN-major (B rows = 96)). A is (128, K) and B is (N, K) row-major fp32 (rounded to TF32 inside); D is
+ * (128, N). Shapes per mode: 0: K 56, N 96; 1: K 128, N 64; 2: K 16, N 96; 3: K 96, N 16; 4: K 96, N 48. */
+int nca_umma_selftest(int mode, const float *A, const float *B, float *D, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* ULTRANCA_B200_H */

@@ -1,0 +1,267 @@
+"""GPU parity of the sm_100a kernels against the CPU oracle (oracle/nca_oracle.py) and the reference's golden outputs,
+following the reference's own test plan (ncaops/testing/test_nca.py:57-163): forward over several shapes including
+partial tiles, gradients, bitwise determinism and chunk invariance, rollout == repeated steps, the dying grid, the
+exact alive predicate, the mask statistic; plus the tensor-core layout self-test, the bit-exact Philox mask, the
+sharding offset, the synthetic loss and the fused optimiser.
+
+Tolerances (relative error ||a - b|| / ||b||, test_nca.py:35-36):
+  fp32 mode vs fp32 oracle            forward 1e-5, gradients 1e-5   (the reference's FP32 bounds, test_nca.py:17)
+  TF32 mode vs TF32-emulating oracle  forward 1e-3, gradients 1e-3   (the parity bar: 1e-3 relative for TF32)
+  TF32 mode vs fp32 oracle            forward 1e-2, gradients 3e-2   (the reference's TF32 bounds, test_nca.py:17)
+"""
+import ctypes
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import nca_oracle as O
+
+pytestmark = pytest.mark.gpu
+DEV = 'cuda'
+GOLD = os.path.join(os.path.dirname(os.path.abspath(__file__)), 'golden')
+SIZES = ((12, 96), (16, 128))
+FWD_SHAPES = ((3, 2, 128, 128), (2, 3, 37, 50), (1, 1, 8, 16), (3, 2, 80, 80), (17, 2, 129, 65), (1, 1, 6, 200))
+BWD_SHAPES = ((3, 2, 64, 64), (2, 3, 37, 50), (1, 1, 5, 140))
+
+
+@pytest.fixture(scope='module')
+def ops():
+    from ultranca_b200 import nca_ops
+    torch.backends.cuda.matmul.allow_tf32 = False
+    torch.backends.cudnn.allow_tf32 = False
+    return nca_ops
+
+
+def gpu(*ts):
+    return [t.to(DEV) for t in ts]
+
+
+def device_error_clear():
+    from ultranca_b200._lib import lib
+    code = ctypes.c_int()
+    assert lib.nca_device_error(ctypes.byref(code), 1) == 0
+    return code.value == 0
+
+
+# ------------------------------------------------------------------------------------------------ tensor cores
+@pytest.mark.parametrize('mode', range(5))
+def test_umma_layout_selftest(mode):
+    from ultranca_b200._lib import check, lib
+    K, N = {0: (56, 96), 1: (128, 64), 2: (16, 96), 3: (96, 16), 4: (96, 48)}[mode]
+    g = torch.Generator().manual_seed(mode)
+    A = torch.randn(128, K, generator=g)
+    B = torch.randn(N, K, generator=g)
+    D = torch.empty(128, N, device=DEV)
+    Ad, Bd = gpu(A, B)
+    check(lib.nca_umma_selftest(mode, ctypes.c_void_p(Ad.data_ptr()), ctypes.c_void_p(Bd.data_ptr()),
+                                ctypes.c_void_p(D.data_ptr()), None))
+    torch.cuda.synchronize()
+    assert device_error_clear()
+    ref = (O.tf32_round(A).double() @ O.tf32_round(B).double().T).float()
+    assert O.rel(D.cpu(), ref) < 1e-5
+
+
+# ------------------------------------------------------------------------------------------------ mask
+@pytest.mark.parametrize('n,h,w,seed,rate,off', [(4, 128, 128, 7, 0.5, 0), (3, 37, 50, 1234, 0.5, 0),
+                                                 (2, 9, 13, 2 ** 62 - 1, 0.3, 5), (1, 8, 16, 99, 1.0, 0),
+                                                 (2, 5, 7, 1, 0.0, 1)])
+def test_update_mask_bit_exact(ops, n, h, w, seed, rate, off):
+    m = ops.update_mask(n, h, w, seed, rate, image_offset=off)
+    assert torch.equal(m.cpu(), O.update_mask(n, h, w, seed, rate, off))
+
+
+def test_mask_statistic(ops):
+    m = ops.update_mask(4, 128, 128, 7, 0.5)  # test_nca.py:160-161
+    assert sorted(m.unique().tolist()) == [0.0, 1.0] and abs(m.mean().item() - 0.5) < 0.01
+
+
+# ------------------------------------------------------------------------------------------------ forward
+@pytest.mark.parametrize('C,HID', SIZES)
+@pytest.mark.parametrize('rate', [0.5, 1.0])
+@pytest.mark.parametrize('growing', [False, True])
+def test_forward_parity(ops, C, HID, rate, growing):
+    worst = {True: 0.0, False: 0.0}
+    worst_vs32 = 0.0
+    flips = 0
+    for K, B, H, W in FWD_SHAPES:
+        x, w1, b1, w2 = O.make(K, B, C, HID, H, W, seed=H * W, growing=growing)
+        mask = O.mask_for(K, B, H, W, 1234, rate)
+        xd, w1d, b1d, w2d = gpu(x, w1, b1, w2)
+        for fp32 in (True, False):
+            out = ops.step(xd, w1d, b1d, w2d, rate, growing, fp32=fp32, seed=1234).cpu()
+            ref = O.reference_step(x, w1, b1, w2, mask, growing, tf32=not fp32)
+            if growing:
+                raw = ops.step(xd, w1d, b1d, w2d, rate, False, fp32=fp32, seed=1234).cpu()
+                out_alive = O.alive(x) & O.alive(raw)
+                assert torch.equal(out, raw * out_alive), 'growing step must apply the exact alive mask'
+                ref_raw = O.reference_step(x, w1, b1, w2, mask, False, tf32=not fp32)
+                ref_alive = O.alive(x) & O.alive(ref_raw)
+                flip = (out_alive != ref_alive)
+                flips += int(flip.sum())
+                err = max(O.rel(raw, ref_raw), O.rel(out.masked_fill(flip, 0), ref.masked_fill(flip, 0)))
+            else:
+                err = O.rel(out, ref)
+            worst[fp32] = max(worst[fp32], err)
+            if not fp32:
+                ref32 = O.reference_step(x, w1, b1, w2, mask, growing, tf32=False)
+                worst_vs32 = max(worst_vs32, O.rel(out, ref32) if not growing else O.rel(raw, O.reference_step(
+                    x, w1, b1, w2, mask, False)))
+    assert device_error_clear()
+    assert worst[True] < 1e-5, worst
+    assert worst[False] < 1e-3, worst
+    assert worst_vs32 < 1e-2, worst_vs32
+    assert flips <= 32
+
+
+def test_forward_matches_reference_golden(ops):
+    z = np.load(os.path.join(GOLD, 'reference_step.npz'))
+    for case in ('tex_8x16_r05', 'tex_9x13_r10', 'tex_5x37_r05', 'grow_12x10_r05', 'grow_11x14_r10'):
+        g = {k.split('/')[1]: torch.from_numpy(z[k]) for k in z.files if k.startswith(case + '/')}
+        xd, w1d, b1d, w2d = gpu(g['x'], g['w1'], g['b1'], g['w2'])
+        y = ops.step(xd, w1d, b1d, w2d, float(g['rate']), bool(g['growing']), fp32=True, seed=int(g['seed'])).cpu()
+        assert O.rel(y, g['y']) < 1e-5, case
+
+
+# ------------------------------------------------------------------------------------------------ backward
+def grads_gpu(ops, x, w1, b1, w2, R, rate, growing, fp32, seed):
+    params = [t.clone().requires_grad_() for t in gpu(x, w1, b1, w2)]
+    out = ops.step(*params, rate, growing, fp32=fp32, seed=seed)
+    return [g.cpu() for g in torch.autograd.grad((out * R.to(DEV)).sum(), params)], out.detach()
+
+
+@pytest.mark.parametrize('C,HID', SIZES)
+@pytest.mark.parametrize('rate', [0.5, 1.0])
+@pytest.mark.parametrize('growing', [False, True])
+def test_backward_parity(ops, C, HID, rate, growing):
+    for K, B, H, W in BWD_SHAPES:
+        x, w1, b1, w2 = O.make(K, B, C, HID, H, W, seed=7 + H, growing=growing)
+        R = torch.randn(x.shape, generator=torch.Generator().manual_seed(3))
+        mask = O.mask_for(K, B, H, W, 99, rate)
+        ref32 = O.step_grads(x, w1, b1, w2, mask, R, growing)
+        for fp32 in (True, False):
+            got, _ = grads_gpu(ops, x, w1, b1, w2, R, rate, growing, fp32, 99)
+            # the backward uses the alive mask of its own forward (kernel alive, exact predicate checked above)
+            alive_mask = None
+            if growing:
+                y, alive = ops._forward(*gpu(x, w1, b1, w2), rate, 99, fp32, True)
+                alive_mask = alive.cpu().view(K, B, 1, H, W)
+            ref = O.step_backward(x, w1, b1, w2, mask, R, growing, tf32=not fp32, alive_mask=alive_mask)
+            for a, b, name in zip(got, ref, ('gx', 'dw1', 'db1', 'dw2')):
+                e = O.rel(a, b)
+                assert e < (1e-5 if fp32 else 1e-3), (name, fp32, (K, B, H, W), e)
+            if not fp32:
+                for a, b, name in zip(got, ref32, ('gx', 'dw1', 'db1', 'dw2')):
+                    assert O.rel(a, b) < 3e-2, (name, 'vs fp32', (K, B, H, W))
+    assert device_error_clear()
+
+
+def test_backward_matches_reference_golden(ops):
+    z = np.load(os.path.join(GOLD, 'reference_step.npz'))
+    for case in ('tex_8x16_r05', 'tex_5x37_r05', 'grow_12x10_r05', 'grow_11x14_r10'):
+        g = {k.split('/')[1]: torch.from_numpy(z[k]) for k in z.files if k.startswith(case + '/')}
+        got, _ = grads_gpu(ops, g['x'], g['w1'], g['b1'], g['w2'], g['R'], float(g['rate']), bool(g['growing']), True,
+                           int(g['seed']))
+        for a, name in zip(got, ('gx', 'dw1', 'db1', 'dw2')):
+            assert O.rel(a, g[name]) < 1e-5, (case, name)
+
+
+@pytest.mark.parametrize('growing', [False, True])
+def test_backward_deterministic_and_chunk_invariant(ops, growing):
+    """test_nca.py:57-81,120-122: TF32 gradients are bitwise equal across repeats and CHUNK settings."""
+    for K, B in ((32, 1), (16, 2), (5, 1)):
+        for C, HID in SIZES:
+            x, w1, b1, w2 = O.make(K, B, C, HID, 64, 64, growing=growing)
+            R = torch.randn(x.shape, generator=torch.Generator().manual_seed(1))
+            for fp32 in (False, True):
+                ops.CHUNK = K * B
+                ref, _ = grads_gpu(ops, x, w1, b1, w2, R, 0.5, growing, fp32, 99)
+                for chunk in (2, K * B // 2, K * B - 1, None):
+                    ops.CHUNK = chunk
+                    got, _ = grads_gpu(ops, x, w1, b1, w2, R, 0.5, growing, fp32, 99)
+                    assert all(torch.equal(a, b) for a, b in zip(ref, got)), (K, B, C, fp32, chunk)
+    ops.CHUNK = None
+
+
+# ------------------------------------------------------------------------------------------------ rollout
+@pytest.mark.parametrize('C,HID', SIZES)
+@pytest.mark.parametrize('growing', [False, True])
+def test_rollout_equals_repeated_steps(ops, C, HID, growing):
+    """test_nca.py:128-149: rollout(steps) == repeated step() with step_seed, bitwise; x is not modified."""
+    x, w1, b1, w2 = gpu(*O.make(2, 2, C, HID, 37, 50, growing=growing))
+    original = x.clone()
+    for fp32 in (False, True):
+        for rate in (0.0, 0.5, 1.0):
+            ref = x
+            for steps in range(8):
+                if steps:
+                    ref = ops.step(ref, w1, b1, w2, rate, growing, fp32, seed=O.step_seed(99, steps - 1))
+                assert torch.equal(ops.rollout(x, w1, b1, w2, rate, steps, growing, fp32, seed=99), ref)
+    assert torch.equal(x, original)
+
+
+@pytest.mark.parametrize('C,HID', SIZES)
+def test_dying_grid(ops, C, HID):
+    """test_nca.py:151-158: the dense living grid dies; both ping-pong buffers must end cleared."""
+    x = torch.ones(1, 1, C, 8, 16, device=DEV)
+    x[:, :, 3] = 0.2
+    w1 = torch.zeros(1, HID, 4 * C, device=DEV)
+    b1 = torch.ones(1, HID, device=DEV)
+    w2 = torch.full((1, C, HID), 0.01, device=DEV)
+    w2[:, 3] = -0.025 / HID
+    for fp32 in (False, True):
+        y = ops.rollout(x, w1, b1, w2, 1., 7, True, fp32, seed=99)
+        assert torch.equal(y, torch.zeros_like(y))
+
+
+def test_rollout_matches_reference_golden(ops):
+    z = np.load(os.path.join(GOLD, 'reference_step.npz'))
+    for case in ('roll_tex', 'roll_grow'):
+        g = {k.split('/')[1]: torch.from_numpy(z[k]) for k in z.files if k.startswith(case + '/')}
+        xd, w1d, b1d, w2d = gpu(g['x'], g['w1'], g['b1'], g['w2'])
+        for steps in range(1, 5):
+            y = ops.rollout(xd, w1d, b1d, w2d, float(g['rate']), steps, bool(g['growing']), True, seed=int(g['seed']))
+            assert O.rel(y.cpu(), g['ys'][steps - 1]) < 1e-5, (case, steps)
+
+
+# ------------------------------------------------------------------------------------------------ sharding offset
+def test_image_offset_reproduces_single_gpu_shard(ops):
+    """A shard holding NCAs [1, 3) with image_offset = 1 * B computes exactly those NCAs of the full step."""
+    x, w1, b1, w2 = gpu(*O.make(4, 2, 12, 96, 32, 32))
+    full = ops.step(x, w1, b1, w2, 0.5, seed=5)
+    part = ops.step(x[1:3], w1[1:3], b1[1:3], w2[1:3], 0.5, seed=5, image_offset=2)
+    assert torch.equal(full[1:3], part)
+    R = torch.randn(x.shape, device=DEV)
+    ps = [t.clone().requires_grad_() for t in (x, w1, b1, w2)]
+    gf = torch.autograd.grad((ops.step(*ps, 0.5, seed=5) * R).sum(), ps)
+    qs = [t[1:3].clone().requires_grad_() for t in (x, w1, b1, w2)]
+    gp = torch.autograd.grad((ops.step(*qs, 0.5, seed=5, image_offset=2) * R[1:3]).sum(), qs)
+    assert torch.equal(gf[0][1:3], gp[0])
+    for a, b in zip(gf[1:], gp[1:]):
+        assert O.rel(b.cpu(), a[1:3].cpu()) < 1e-5
+
+
+# ------------------------------------------------------------------------------------------------ loss + optimiser
+def test_synthetic_loss(ops):
+    from ultranca_b200 import training
+    x, w1, b1, w2, target = O.make_config_inputs(3, 2, 12, 96, 40, 24)
+    x = x * 30
+    obj_ref, per_ref = O.synthetic_loss(x, target)
+    xr = x.clone().requires_grad_()
+    (g_ref,) = torch.autograd.grad(O.synthetic_loss(xr, target)[0], xr)
+    loss, gy = training.synthetic_loss(x.to(DEV), target.to(DEV))
+    assert O.rel(loss.cpu(), per_ref) < 1e-5
+    assert O.rel(gy.cpu(), g_ref) < 1e-6
+
+
+def test_fused_adam_matches_torch(ops):
+    from ultranca_b200 import training
+    z = np.load(os.path.join(GOLD, 'reference_step.npz'))
+    g = {k.split('/')[1]: torch.from_numpy(z[k]) for k in z.files if k.startswith('adam/')}
+    params = gpu(g['w1'], g['b1'], g['w2'])
+    opt = training.FusedAdam(params, lr=float(g['lr']), milestones=g['milestones'].tolist(), gamma=float(g['gamma']))
+    for i in range(g['g_w1'].shape[0]):
+        opt.step(gpu(g['g_w1'][i], g['g_b1'][i], g['g_w2'][i]))
+        for p, name in zip(params, ('w1_after', 'b1_after', 'w2_after')):
+            assert O.rel(p.cpu(), g[name][i]) < 1e-6, (i, name)

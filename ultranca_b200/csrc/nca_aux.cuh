@@ -1,0 +1,250 @@
+// Auxiliary kernels around the step: update mask, synthetic loss + its gradient, fused per-NCA gradient normalisation
+// + Adam + MultiStepLR, and the tcgen05 operand-layout self-test.
+#pragma once
+#include "nca_common.cuh"
+#include "umma.cuh"
+
+namespace unca {
+
+// mask (n, h, w) of {0, 1} (ncaops/nca_step.cuh:237-245, grid-stride).
+__global__ void mask_kernel(float *__restrict__ mask, int64_t N, int H, int W, uint64_t seed, float rate, int64_t n_offset)
+{
+    const int64_t total = N * H * W;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+        const int X = (int)(i % W), Y = (int)((i / W) % H);
+        const int64_t n = i / ((int64_t)H * W);
+        mask[i] = update_mask_at(seed, rate, n + n_offset, H, W, Y, X);
+    }
+}
+
+// ---------------------------------------------------------------- synthetic loss
+// Block (chunk, k) sums a fixed slice of NCA k's elements (fixed order: strided per thread, then a tree), writes
+// gy for the slice; loss_final sums the chunks of each NCA in order.
+constexpr int LOSS_CHUNKS = 64;
+
+__global__ void __launch_bounds__(256) loss_kernel(const float *__restrict__ x, const float *__restrict__ target,
+                                                   float *__restrict__ gy, float *__restrict__ work, int B, int C, int H,
+                                                   int W, float overflow_weight)
+{
+    const int k = blockIdx.y, chunk = blockIdx.x;
+    const int64_t plane = (int64_t)H * W, per = (int64_t)B * C * plane;
+    const int64_t lo = per * chunk / LOSS_CHUNKS, hi = per * (chunk + 1) / LOSS_CHUNKS;
+    const float inv = 1.f / (float)((int64_t)B * 3 * plane);
+    const float *xk = x + (int64_t)k * per;
+    float *gk = gy + (int64_t)k * per;
+    float l2 = 0.f, of = 0.f;
+    for (int64_t i = lo + threadIdx.x; i < hi; i += blockDim.x) {
+        const int64_t pix = i % plane, c = (i / plane) % C;
+        const float v = xk[i];
+        float g = 0.f;
+        if (c < 3) {
+            const float d = v - target[((int64_t)k * 3 + c) * plane + pix];
+            l2 = fmaf(d, d, l2);
+            g = 2.f * d * inv;
+        }
+        const float o = fabsf(v - fminf(fmaxf(v, -1.f), 1.f));
+        of += o;
+        if (o > 0.f)
+            g += overflow_weight * (v > 0.f ? 1.f : -1.f);
+        gk[i] = g;
+    }
+    __shared__ float s1[256], s2[256];
+    s1[threadIdx.x] = l2;
+    s2[threadIdx.x] = of;
+    __syncthreads();
+    for (int w = 128; w > 0; w >>= 1) {
+        if (threadIdx.x < w) {
+            s1[threadIdx.x] += s1[threadIdx.x + w];
+            s2[threadIdx.x] += s2[threadIdx.x + w];
+        }
+        __syncthreads();
+    }
+    if (threadIdx.x == 0) {
+        work[((int64_t)k * LOSS_CHUNKS + chunk) * 2] = s1[0];
+        work[((int64_t)k * LOSS_CHUNKS + chunk) * 2 + 1] = s2[0];
+    }
+}
+
+__global__ void loss_final_kernel(const float *__restrict__ work, float *__restrict__ loss, int K, int64_t l2_count,
+                                  float overflow_weight)
+{
+    const int k = blockIdx.x * blockDim.x + threadIdx.x;
+    if (k >= K)
+        return;
+    float a = 0.f, b = 0.f;
+    for (int c = 0; c < LOSS_CHUNKS; ++c) {
+        a += work[((int64_t)k * LOSS_CHUNKS + c) * 2];
+        b += work[((int64_t)k * LOSS_CHUNKS + c) * 2 + 1];
+    }
+    loss[k] = a / (float)l2_count + overflow_weight * b;
+}
+
+// ---------------------------------------------------------------- gradient normalisation + Adam
+struct AdamTensor {
+    float *p, *m, *v;
+    const float *g;
+    int64_t numel;  // per NCA
+};
+
+struct AdamArgs {
+    AdamTensor t[3];
+    const int64_t *iteration;
+    float lr, beta1, beta2, eps, gamma;
+    int64_t milestones[8];
+    int n_milestones;
+};
+
+// Block (k, tensor): ||g_k|| in a fixed order, then g / (||g_k|| + 1e-8) through torch.optim.Adam's update
+// (exp_avg.lerp_(g, 1 - beta1); exp_avg_sq = beta2 v + (1 - beta2) g^2; p -= lr / bc1 * m / (sqrt(v) / sqrt(bc2) + eps)).
+__global__ void __launch_bounds__(256) adam_kernel(AdamArgs a)
+{
+    const int k = blockIdx.x;
+    const AdamTensor &T = a.t[blockIdx.y];
+    const int64_t base = (int64_t)k * T.numel;
+    float ss = 0.f;
+    for (int64_t i = threadIdx.x; i < T.numel; i += blockDim.x) {
+        const float g = T.g[base + i];
+        ss = fmaf(g, g, ss);
+    }
+    __shared__ float red[256];
+    red[threadIdx.x] = ss;
+    __syncthreads();
+    for (int w = 128; w > 0; w >>= 1) {
+        if (threadIdx.x < w)
+            red[threadIdx.x] += red[threadIdx.x + w];
+        __syncthreads();
+    }
+    const float norm_eps = sqrtf(red[0]) + 1e-8f;  // train.py:139: p.grad /= ||p.grad_k|| + 1e-8
+    const int64_t it = *a.iteration;
+    int decays = 0;
+    for (int i = 0; i < a.n_milestones; ++i)
+        decays += a.milestones[i] <= it;
+    const double lr = (double)a.lr * pow((double)a.gamma, (double)decays);
+    const double step = (double)(it + 1);
+    const double bc1 = 1.0 - pow((double)a.beta1, step), bc2 = 1.0 - pow((double)a.beta2, step);
+    const float step_size = (float)(lr / bc1), bc2_sqrt = (float)sqrt(bc2);
+    const float w1 = 1.f - a.beta1, w2 = 1.f - a.beta2;
+    for (int64_t i = threadIdx.x; i < T.numel; i += blockDim.x) {
+        const float g = T.g[base + i] / norm_eps;
+        float m = T.m[base + i], v = T.v[base + i];
+        m = m + w1 * (g - m);
+        v = v * a.beta2 + w2 * g * g;
+        T.m[base + i] = m;
+        T.v[base + i] = v;
+        const float denom = sqrtf(v) / bc2_sqrt + a.eps;
+        T.p[base + i] -= step_size * m / denom;
+    }
+}
+
+__global__ void increment_kernel(int64_t *iteration) { *iteration += 1; }
+
+// ---------------------------------------------------------------- tcgen05 layout self-test
+struct SelftestShape {
+    int K, N, a_rows_are_k, b_rows_are_k, b_plane_rows;
+};
+
+__host__ __device__ inline SelftestShape selftest_shape(int mode)
+{
+    switch (mode) {
+    case 0: return {56, 96, 0, 0, 96};
+    case 1: return {128, 64, 1, 1, 128};
+    case 2: return {16, 96, 0, 1, 16};
+    case 3: return {96, 16, 0, 0, 16};
+    default: return {96, 48, 0, 1, 96};
+    }
+}
+
+// A (128 x K) and B (N x K) row-major in global memory; D (128 x N). Operands are staged chunk-planar exactly as the
+// step kernels stage theirs: K-major tiles with rows = M (N), MN-major tiles with rows = K.
+__global__ void __launch_bounds__(128, 1) umma_selftest_kernel(int mode, const float *__restrict__ A,
+                                                               const float *__restrict__ B, float *__restrict__ D)
+{
+    extern __shared__ __align__(128) float sm[];
+    const SelftestShape sh = selftest_shape(mode);
+    float *As = sm, *Bs = sm + 128 * 128;
+    uint64_t *bar = reinterpret_cast<uint64_t *>(Bs + 128 * 128);
+    uint32_t *slot = reinterpret_cast<uint32_t *>(bar + 1);
+    const int tid = threadIdx.x, warp = tid / 32;
+    // A: K-major -> rows m (128), planes over k; MN-major -> rows k, planes over m
+    for (int e = tid; e < 128 * sh.K; e += 128) {
+        const int m = e / sh.K, k = e % sh.K;
+        const float v = tf32_rna(A[e]);
+        if (sh.a_rows_are_k)
+            As[(m / 4) * sh.K * 4 + k * 4 + (m % 4)] = v;
+        else
+            As[(k / 4) * 128 * 4 + m * 4 + (k % 4)] = v;
+    }
+    for (int e = tid; e < sh.N * sh.K; e += 128) {
+        const int n = e / sh.K, k = e % sh.K;
+        const float v = tf32_rna(B[e]);
+        if (sh.b_rows_are_k)
+            Bs[(n / 4) * sh.b_plane_rows * 4 + k * 4 + (n % 4)] = v;
+        else
+            Bs[(k / 4) * sh.b_plane_rows * 4 + n * 4 + (k % 4)] = v;
+    }
+    if (tid == 0) {
+        umma::mbar_init(bar, 1);
+        umma::fence_mbar_init();
+    }
+    if (warp == 0) {
+        umma::tmem_alloc(slot, 256);
+        umma::tmem_relinquish();
+    }
+    umma::fence_proxy_async();
+    umma::fence_before_sync();
+    __syncthreads();
+    umma::fence_after_sync();
+    const uint32_t tmem = *slot;
+    int dcol = 0;
+    if (mode == 3) {  // A into TMEM columns [0, K): thread = lane = row m
+        dcol = 128;
+        for (int c0 = 0; c0 < sh.K; c0 += 16) {
+            float v[16];
+#pragma unroll
+            for (int e = 0; e < 16; ++e)
+                v[e] = tf32_rna(A[tid * sh.K + c0 + e]);
+            umma::tmem_st16(umma::tmem_addr(tmem, warp, c0), v);
+        }
+        umma::tmem_wait_st();
+        umma::fence_before_sync();
+        __syncthreads();
+        umma::fence_after_sync();
+    }
+    if (tid == 0) {
+        const uint32_t aa = umma::smem_u32(As), ba = umma::smem_u32(Bs);
+        const int ksteps = sh.K / 8;
+        for (int ks = 0; ks < ksteps; ++ks) {
+            const uint64_t adesc = sh.a_rows_are_k ? umma::smem_desc(aa + ks * 128, 128, sh.K * 16)
+                                                   : umma::smem_desc(aa + ks * 2 * 128 * 16, 128 * 16, 128);
+            const uint64_t bdesc = sh.b_rows_are_k ? umma::smem_desc(ba + ks * 128, 128, sh.b_plane_rows * 16)
+                                                   : umma::smem_desc(ba + ks * 2 * sh.b_plane_rows * 16, sh.b_plane_rows * 16, 128);
+            const uint32_t idesc = umma::idesc_tf32(128, sh.N, sh.a_rows_are_k, sh.b_rows_are_k);
+            if (mode == 3)
+                umma::mma_ts(tmem + dcol, tmem + ks * 8, bdesc, idesc, ks > 0);
+            else
+                umma::mma_ss(tmem + dcol, adesc, bdesc, idesc, ks > 0);
+        }
+        umma::commit(bar);
+    }
+    const bool ok = umma::mbar_wait(bar, 0);
+    umma::fence_after_sync();
+    if (__syncthreads_and(ok)) {
+        for (int c0 = 0; c0 < sh.N; c0 += 16) {
+            float v[16];
+            umma::tmem_ld16(umma::tmem_addr(tmem, warp, dcol + c0), v);
+            umma::tmem_wait_ld();
+#pragma unroll
+            for (int e = 0; e < 16; ++e)
+                D[tid * sh.N + c0 + e] = v[e];
+        }
+    } else if (tid == 0) {
+        set_device_error(1);
+    }
+    umma::fence_before_sync();
+    __syncthreads();
+    umma::fence_after_sync();
+    if (warp == 0)
+        umma::tmem_dealloc(tmem, 256);
+}
+
+}  // namespace unca

@@ -1,0 +1,498 @@
+// C-ABI of the fused NCA step (the drop-in boundary under ultranca_b200/nca_ops.py). Every entry point takes plain
+// device pointers and sizes, launches asynchronously on the caller's stream and returns 0, or a nonzero status with the
+// message in nca_last_error(). Nothing here allocates device memory: the caller passes every buffer.
+//
+// Mirrors the reference's nanobind module (ncaops/nca_cuda.cu:333-353): forward, rollout, backward_workspace, backward,
+// update_mask, with the same argument meaning and error behaviour (shape / size mismatch and unsupported sizes are
+// errors, ncaops/nca_cuda.cu:35-52,75,128-145,262-284; launch errors are checked after every launch, :23-33).
+// Per-device state (SM count, kernel attributes, occupancy) is cached per device, not process-wide.
+#include <cuda_runtime.h>
+#include <algorithm>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <mutex>
+#include <stdexcept>
+#include <utility>
+#include <string>
+
+#include "nca_kernels.cuh"
+#include "nca_aux.cuh"
+#include "../../include/ultranca_b200.h"
+
+namespace unca {
+namespace {
+
+thread_local std::string g_last_error;
+
+struct Error : std::runtime_error {
+    int code;
+    Error(int c, const std::string &m) : std::runtime_error(m), code(c) {}
+};
+
+[[noreturn]] void fail(int code, const char *fmt, ...)
+{
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    throw Error(code, buf);
+}
+
+#define CUDA_OK(call)                                                                                         \
+    do {                                                                                                      \
+        cudaError_t e_ = (call);                                                                              \
+        if (e_ != cudaSuccess)                                                                                \
+            fail(NCA_ERR_CUDA, "CUDA error at %s:%d - %s", __FILE__, __LINE__, cudaGetErrorString(e_));      \
+    } while (0)
+
+template <class F>
+int guarded(F &&f)
+{
+    try {
+        f();
+        return NCA_OK;
+    } catch (const Error &e) {
+        g_last_error = e.what();
+        return e.code;
+    } catch (const std::exception &e) {
+        g_last_error = e.what();
+        return NCA_ERR_INTERNAL;
+    }
+}
+
+// ---------------------------------------------------------------- per-device cache
+constexpr int MAX_DEV = 64;
+struct DeviceInfo {
+    bool init = false;
+    int sms = 0;
+    int smem_optin = 0;
+};
+DeviceInfo g_dev[MAX_DEV];
+std::mutex g_mutex;
+
+int current_device()
+{
+    int d = 0;
+    CUDA_OK(cudaGetDevice(&d));
+    if (d < 0 || d >= MAX_DEV)
+        fail(NCA_ERR_CUDA, "device index %d out of range", d);
+    return d;
+}
+
+const DeviceInfo &device_info()
+{
+    const int d = current_device();
+    std::lock_guard<std::mutex> lk(g_mutex);
+    DeviceInfo &di = g_dev[d];
+    if (!di.init) {
+        CUDA_OK(cudaDeviceGetAttribute(&di.sms, cudaDevAttrMultiProcessorCount, d));
+        CUDA_OK(cudaDeviceGetAttribute(&di.smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, d));
+        di.init = true;
+    }
+    return di;
+}
+
+// Resident CTAs per SM of `kernel` with `smem` bytes, capped by the Tensor Memory columns each CTA allocates.
+// The dynamic shared memory attribute is set once per (kernel, device).
+std::map<std::pair<const void *, int>, int> g_occupancy;
+
+template <class K>
+int ctas_per_sm(K kernel, size_t smem, int tmem_cols)
+{
+    const int d = current_device();
+    std::lock_guard<std::mutex> lk(g_mutex);
+    const auto key = std::make_pair(reinterpret_cast<const void *>(kernel), d);
+    auto it = g_occupancy.find(key);
+    if (it != g_occupancy.end())
+        return it->second;
+    CUDA_OK(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    int b = 0;
+    CUDA_OK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, kernel, 128, smem));
+    if (tmem_cols > 0)
+        b = std::min(b, 512 / tmem_cols);
+    b = std::max(b, 1);
+    g_occupancy[key] = b;
+    return b;
+}
+
+// Sets the dynamic shared memory limit of `kernel` once per device.
+template <class K>
+void set_smem_once(K kernel, size_t smem)
+{
+    const int d = current_device();
+    std::lock_guard<std::mutex> lk(g_mutex);
+    const auto key = std::make_pair(reinterpret_cast<const void *>(kernel), -1 - d);
+    if (g_occupancy.count(key))
+        return;
+    CUDA_OK(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    g_occupancy[key] = 1;
+}
+
+// ---------------------------------------------------------------- dispatch
+template <int C_, int HID_, bool FP32_, bool GROW_>
+struct Inst {
+    static constexpr int C = C_, HID = HID_;
+    static constexpr bool FP32 = FP32_, GROW = GROW_;
+};
+
+template <class F>
+void dispatch(int64_t C, int64_t HID, bool fp32, bool growing, F &&f)
+{
+    auto go = [&](auto fp, auto gr) {
+        constexpr bool FP = decltype(fp)::value, GR = decltype(gr)::value;
+        if (C == 12 && HID == 96)
+            return f(Inst<12, 96, FP, GR>{});
+        if (C == 16 && HID == 128)
+            return f(Inst<16, 128, FP, GR>{});
+        fail(NCA_ERR_UNSUPPORTED, "no kernel instantiated for channels=%lld, hidden=%lld", (long long)C, (long long)HID);
+    };
+    if (fp32) {
+        if (growing)
+            go(std::true_type{}, std::true_type{});
+        else
+            go(std::true_type{}, std::false_type{});
+    } else {
+        if (growing)
+            go(std::false_type{}, std::true_type{});
+        else
+            go(std::false_type{}, std::false_type{});
+    }
+}
+
+void check_ptr(const void *p, const char *name)
+{
+    if (!p)
+        fail(NCA_ERR_ARGUMENT, "%s must not be null", name);
+}
+
+struct Shape {
+    int64_t N, C, H, W, K, HID, B;
+};
+
+void validate(const Shape &s, bool growing)
+{
+    if (s.N <= 0 || s.C <= 0 || s.H <= 0 || s.W <= 0 || s.K <= 0 || s.HID <= 0 || s.B <= 0)
+        fail(NCA_ERR_SHAPE, "sizes must be positive (N=%lld C=%lld H=%lld W=%lld K=%lld hidden=%lld B=%lld)",
+             (long long)s.N, (long long)s.C, (long long)s.H, (long long)s.W, (long long)s.K, (long long)s.HID, (long long)s.B);
+    if (s.N != s.K * s.B)
+        fail(NCA_ERR_SHAPE, "x.shape[0] must equal (number of NCAs) * batch_per_nca (%lld != %lld * %lld)", (long long)s.N,
+             (long long)s.K, (long long)s.B);
+    if (growing && s.C < 4)
+        fail(NCA_ERR_SHAPE, "a growing NCA needs at least 4 channels (alpha = channel 3)");
+    if (s.H >= (1 << 24) || s.W >= (1 << 24) || s.N >= (1 << 30))
+        fail(NCA_ERR_SHAPE, "grid too large");
+}
+
+// Persistent grid size of a step kernel (tiles T): the resident CTA slots of the device, at most one CTA per tile.
+int grid_for(int64_t T, int per_sm)
+{
+    const int slots = device_info().sms * per_sm;
+    return (int)std::max<int64_t>(1, std::min<int64_t>(T, slots));
+}
+
+template <class I>
+int fwd_ctas_per_sm()
+{
+    using D = Dims<I::C, I::HID>;
+    auto kernel = I::FP32 ? fwd_kernel<I::C, I::HID, false, I::GROW> : fwd_kernel<I::C, I::HID, true, I::GROW>;
+    return ctas_per_sm(kernel, D::fwd_smem(), I::FP32 ? 0 : D::FWD_TMEM);
+}
+
+template <class I>
+int bwd_ctas_per_sm()
+{
+    using D = Dims<I::C, I::HID>;
+    if (I::FP32)
+        return ctas_per_sm(bwd_kernel<I::C, I::HID, false, I::GROW>, D::bwd_smem_cc(), 0);
+    return ctas_per_sm(bwd_kernel<I::C, I::HID, true, I::GROW>, D::bwd_smem_tc(), D::BWD_TMEM);
+}
+
+void launch_forward(const float *x, const float *w1, const float *b1, const float *w2, float *y, float *alpha,
+                    uint8_t *alive, const Shape &s, uint64_t seed, float rate, bool fp32, bool growing, int64_t n_offset,
+                    cudaStream_t stream)
+{
+    dispatch(s.C, s.HID, fp32, growing, [&](auto I) {
+        using II = decltype(I);
+        using D = Dims<II::C, II::HID>;
+        StepArgs a{};
+        a.x = x; a.w1 = w1; a.b1 = b1; a.w2 = w2; a.y = y; a.alpha = alpha;
+        a.N = (int)s.N; a.B = (int)s.B; a.H = (int)s.H; a.W = (int)s.W;
+        a.seed = seed; a.rate = rate; a.n_offset = n_offset;
+        const TileGeom g = make_geom((int)s.H, (int)s.W);
+        const int G = grid_for(s.N * g.tiles_per_image, fwd_ctas_per_sm<II>());
+        if (II::FP32)
+            fwd_kernel<II::C, II::HID, false, II::GROW><<<G, 128, D::fwd_smem(), stream>>>(a);
+        else
+            fwd_kernel<II::C, II::HID, true, II::GROW><<<G, 128, D::fwd_smem(), stream>>>(a);
+        CUDA_OK(cudaGetLastError());
+        if (II::GROW) {
+            const int64_t total = s.N * s.H * s.W;
+            alive_kernel<II::C><<<(unsigned)((total + 255) / 256), 256, 0, stream>>>(x, alpha, y, alive, (int)s.H, (int)s.W, total);
+            CUDA_OK(cudaGetLastError());
+        }
+    });
+}
+
+// Workspaces of backward(): dp floats, partial floats (both exact), grid size.
+struct BwdWork {
+    int64_t dp_floats, partial_floats;
+    int grid;
+};
+
+BwdWork backward_work(const Shape &s, bool fp32, bool growing)
+{
+    BwdWork w{};
+    dispatch(s.C, s.HID, fp32, growing, [&](auto I) {
+        using II = decltype(I);
+        using D = Dims<II::C, II::HID>;
+        const TileGeom g = make_geom((int)s.H, (int)s.W);
+        w.grid = grid_for(s.N * g.tiles_per_image, bwd_ctas_per_sm<II>());
+        w.dp_floats = s.N * D::PIN * s.H * s.W;
+        w.partial_floats = (int64_t)(w.grid + s.K - 1) * D::PART;
+    });
+    return w;
+}
+
+}  // namespace
+}  // namespace unca
+
+using namespace unca;
+
+extern "C" {
+
+const char *nca_last_error(void) { return g_last_error.c_str(); }
+
+int nca_version(void) { return NCA_ABI_VERSION; }
+
+int nca_forward(const float *x, const float *w1, const float *b1, const float *w2, float *y, float *alpha, uint8_t *alive,
+                int64_t N, int64_t C, int64_t H, int64_t W, int64_t K, int64_t hidden, uint32_t batch_per_nca,
+                uint64_t seed, float update_rate, int fp32, int growing, int64_t image_offset, void *stream)
+{
+    return guarded([&] {
+        const Shape s{N, C, H, W, K, hidden, (int64_t)batch_per_nca};
+        validate(s, growing);
+        check_ptr(x, "x"); check_ptr(w1, "w1"); check_ptr(b1, "b1"); check_ptr(w2, "w2"); check_ptr(y, "y");
+        if (growing) {
+            check_ptr(alpha, "alpha");
+            check_ptr(alive, "alive");
+        }
+        launch_forward(x, w1, b1, w2, y, alpha, alive, s, seed, update_rate, fp32, growing, image_offset,
+                       static_cast<cudaStream_t>(stream));
+    });
+}
+
+int nca_rollout(const float *x, const float *w1, const float *b1, const float *w2, float *y, float *tmp, float *alpha,
+                uint8_t *alive, int64_t N, int64_t C, int64_t H, int64_t W, int64_t K, int64_t hidden, uint32_t steps,
+                uint32_t batch_per_nca, uint64_t seed, float update_rate, int fp32, int growing, int64_t image_offset,
+                void *stream)
+{
+    return guarded([&] {
+        const Shape s{N, C, H, W, K, hidden, (int64_t)batch_per_nca};
+        validate(s, growing);
+        check_ptr(x, "x"); check_ptr(w1, "w1"); check_ptr(b1, "b1"); check_ptr(w2, "w2"); check_ptr(y, "y");
+        if (steps > 1)
+            check_ptr(tmp, "tmp");
+        if (growing) {
+            check_ptr(alpha, "alpha");
+            check_ptr(alive, "alive");
+        }
+        const auto st = static_cast<cudaStream_t>(stream);
+        if (steps == 0)
+            CUDA_OK(cudaMemcpyAsync(y, x, (size_t)(N * C * H * W) * sizeof(float), cudaMemcpyDeviceToDevice, st));
+        const float *src = x;
+        for (uint32_t i = 0; i < steps; ++i) {  // ping-pong so that the result ends in y (x is not modified)
+            float *dst = (steps - i) % 2 ? y : tmp;
+            launch_forward(src, w1, b1, w2, dst, alpha, alive, s, nca_step_seed(seed, i), update_rate, fp32, growing,
+                           image_offset, st);
+            src = dst;
+        }
+    });
+}
+
+uint64_t nca_step_seed(uint64_t seed, uint64_t i)
+{
+    uint64_t z = seed + (i + 1) * 0x9E3779B97F4A7C15ull;  // splitmix64, ncaops/nca_cuda.cu:157-164
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    return z ^ (z >> 31);
+}
+
+int nca_backward_workspace(int64_t C, int64_t hidden, int fp32, int64_t N, int64_t H, int64_t W, int64_t K,
+                           float update_rate, int growing, int64_t *dp_floats, int64_t *partial_floats, int64_t *chunk)
+{
+    (void)update_rate;
+    return guarded([&] {
+        const Shape s{N, C, H, W, K, hidden, K > 0 ? N / K : 0};
+        validate(s, growing);
+        const BwdWork w = backward_work(s, fp32, growing);
+        if (dp_floats)
+            *dp_floats = w.dp_floats;
+        if (partial_floats)
+            *partial_floats = w.partial_floats;
+        if (chunk)
+            *chunk = N;  // one launch over all images (B200: the reference also picks one launch, nca_cuda.cu:211-212)
+    });
+}
+
+int nca_backward_stages(const float *x, const float *gy, const uint8_t *alive, const float *w1, const float *b1,
+                        const float *w2, float *gx, float *dw1, float *db1, float *dw2, float *dp, int64_t dp_floats,
+                        float *partial, int64_t partial_floats, int64_t N, int64_t C, int64_t H, int64_t W, int64_t K,
+                        int64_t hidden, uint32_t batch_per_nca, uint64_t seed, float update_rate, int fp32, int growing,
+                        int64_t image_offset, int accumulate, int stages, void *stream)
+{
+    return guarded([&] {
+        const Shape s{N, C, H, W, K, hidden, (int64_t)batch_per_nca};
+        validate(s, growing);
+        if (stages <= 0 || stages > 7)
+            fail(NCA_ERR_ARGUMENT, "stages must be a nonzero mask of NCA_STAGE_* bits");
+        check_ptr(x, "x"); check_ptr(gy, "gy"); check_ptr(w1, "w1"); check_ptr(b1, "b1"); check_ptr(w2, "w2");
+        check_ptr(gx, "gx"); check_ptr(dw1, "dw1"); check_ptr(db1, "db1"); check_ptr(dw2, "dw2"); check_ptr(dp, "dp");
+        check_ptr(partial, "partial");
+        if (growing)
+            check_ptr(alive, "alive");
+        const BwdWork w = backward_work(s, fp32, growing);
+        if (dp_floats < w.dp_floats)
+            fail(NCA_ERR_SHAPE, "dp workspace too small: %lld floats, need %lld", (long long)dp_floats, (long long)w.dp_floats);
+        if (partial_floats < w.partial_floats)
+            fail(NCA_ERR_SHAPE, "partial workspace too small: %lld floats, need %lld", (long long)partial_floats,
+                 (long long)w.partial_floats);
+        const auto st = static_cast<cudaStream_t>(stream);
+        dispatch(C, hidden, fp32, growing, [&](auto I) {
+            using II = decltype(I);
+            using D = Dims<II::C, II::HID>;
+            StepArgs a{};
+            a.x = x; a.w1 = w1; a.b1 = b1; a.w2 = w2; a.gy = gy; a.alive = alive; a.dp = dp; a.partial = partial;
+            a.N = (int)N; a.B = (int)batch_per_nca; a.H = (int)H; a.W = (int)W;
+            a.seed = seed; a.rate = update_rate; a.n_offset = image_offset;
+            const TileGeom g = make_geom((int)H, (int)W);
+            if (stages & NCA_STAGE_MAIN) {
+                if (II::FP32)
+                    bwd_kernel<II::C, II::HID, false, II::GROW><<<w.grid, 128, D::bwd_smem_cc(), st>>>(a);
+                else
+                    bwd_kernel<II::C, II::HID, true, II::GROW><<<w.grid, 128, D::bwd_smem_tc(), st>>>(a);
+                CUDA_OK(cudaGetLastError());
+            }
+            if (stages & NCA_STAGE_ADJOINT) {
+                const size_t adj_smem = (size_t)D::PIN * (ADJ_TH + 2) * (ADJ_TW + 2) * sizeof(float);
+                set_smem_once(adjoint_kernel<II::C, II::GROW>, adj_smem);
+                const dim3 agrid((unsigned)(((W + ADJ_TW - 1) / ADJ_TW) * ((H + ADJ_TH - 1) / ADJ_TH)), (unsigned)N);
+                adjoint_kernel<II::C, II::GROW><<<agrid, ADJ_TW * ADJ_TH, adj_smem, st>>>(dp, gy, alive, gx, (int)H, (int)W);
+                CUDA_OK(cudaGetLastError());
+            }
+            if (stages & NCA_STAGE_REDUCE) {
+                const int64_t T = N * g.tiles_per_image;
+                reduce_kernel<II::C, II::HID><<<dim3((D::PART + 255) / 256, (unsigned)K), 256, 0, st>>>(
+                    partial, T, w.grid, (int64_t)batch_per_nca * g.tiles_per_image, dw1, db1, dw2, accumulate);
+                CUDA_OK(cudaGetLastError());
+            }
+        });
+    });
+}
+
+int nca_backward(const float *x, const float *gy, const uint8_t *alive, const float *w1, const float *b1, const float *w2,
+                 float *gx, float *dw1, float *db1, float *dw2, float *dp, int64_t dp_floats, float *partial,
+                 int64_t partial_floats, int64_t N, int64_t C, int64_t H, int64_t W, int64_t K, int64_t hidden,
+                 uint32_t batch_per_nca, uint64_t seed, float update_rate, int fp32, int growing, int64_t image_offset,
+                 int accumulate, void *stream)
+{
+    return nca_backward_stages(x, gy, alive, w1, b1, w2, gx, dw1, db1, dw2, dp, dp_floats, partial, partial_floats, N, C,
+                               H, W, K, hidden, batch_per_nca, seed, update_rate, fp32, growing, image_offset, accumulate,
+                               NCA_STAGE_MAIN | NCA_STAGE_ADJOINT | NCA_STAGE_REDUCE, stream);
+}
+
+int nca_device_error(int *code, int reset)
+{
+    return guarded([&] {
+        int v = 0;
+        CUDA_OK(cudaMemcpyFromSymbol(&v, g_device_error, sizeof(int)));
+        if (code)
+            *code = v;
+        if (reset) {
+            const int z = 0;
+            CUDA_OK(cudaMemcpyToSymbol(g_device_error, &z, sizeof(int)));
+        }
+    });
+}
+
+int nca_update_mask(float *mask, int64_t n, int64_t h, int64_t w, uint64_t seed, float update_rate, int64_t image_offset,
+                    void *stream)
+{
+    return guarded([&] {
+        check_ptr(mask, "mask");
+        if (n <= 0 || h <= 0 || w <= 0)
+            fail(NCA_ERR_SHAPE, "mask sizes must be positive");
+        const int64_t total = n * h * w;
+        const unsigned blocks = (unsigned)std::min<int64_t>((total + 255) / 256, 65535);
+        mask_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(mask, n, (int)h, (int)w, seed, update_rate,
+                                                                            image_offset);
+        CUDA_OK(cudaGetLastError());
+    });
+}
+
+int nca_synthetic_loss(const float *x, const float *target, float *gy, float *loss, float *work, int64_t K, int64_t B,
+                       int64_t C, int64_t H, int64_t W, float overflow_weight, void *stream)
+{
+    return guarded([&] {
+        check_ptr(x, "x"); check_ptr(target, "target"); check_ptr(gy, "gy"); check_ptr(loss, "loss"); check_ptr(work, "work");
+        if (K <= 0 || B <= 0 || C < 3 || H <= 0 || W <= 0)
+            fail(NCA_ERR_SHAPE, "loss sizes must be positive with at least 3 channels");
+        const auto st = static_cast<cudaStream_t>(stream);
+        loss_kernel<<<dim3(LOSS_CHUNKS, (unsigned)K), 256, 0, st>>>(x, target, gy, work, (int)B, (int)C, (int)H, (int)W,
+                                                                   overflow_weight);
+        CUDA_OK(cudaGetLastError());
+        loss_final_kernel<<<(unsigned)((K + 127) / 128), 128, 0, st>>>(work, loss, (int)K, B * 3 * H * W, overflow_weight);
+        CUDA_OK(cudaGetLastError());
+    });
+}
+
+int nca_adam_step(float *param0, float *param1, float *param2, const float *grad0, const float *grad1, const float *grad2,
+                  float *m0, float *m1, float *m2, float *v0, float *v1, float *v2, int64_t K, int64_t numel0,
+                  int64_t numel1, int64_t numel2, int64_t *iteration, float lr, float beta1, float beta2, float eps,
+                  float gamma, const int64_t *milestones, int n_milestones, void *stream)
+{
+    return guarded([&] {
+        float *p[3] = {param0, param1, param2}, *m[3] = {m0, m1, m2}, *v[3] = {v0, v1, v2};
+        const float *g[3] = {grad0, grad1, grad2};
+        const int64_t ne[3] = {numel0, numel1, numel2};
+        if (K <= 0)
+            fail(NCA_ERR_SHAPE, "K must be positive");
+        if (n_milestones < 0 || n_milestones > 8 || (n_milestones > 0 && !milestones))
+            fail(NCA_ERR_ARGUMENT, "at most 8 milestones");
+        check_ptr(iteration, "iteration");
+        AdamArgs a{};
+        for (int i = 0; i < 3; ++i) {
+            check_ptr(p[i], "param"); check_ptr(g[i], "grad"); check_ptr(m[i], "m"); check_ptr(v[i], "v");
+            if (ne[i] <= 0)
+                fail(NCA_ERR_SHAPE, "numel must be positive");
+            a.t[i] = AdamTensor{p[i], m[i], v[i], g[i], ne[i]};
+        }
+        a.iteration = iteration;
+        a.lr = lr; a.beta1 = beta1; a.beta2 = beta2; a.eps = eps; a.gamma = gamma;
+        a.n_milestones = n_milestones;
+        for (int i = 0; i < n_milestones; ++i)
+            a.milestones[i] = milestones[i];
+        const auto st = static_cast<cudaStream_t>(stream);
+        adam_kernel<<<dim3((unsigned)K, 3), 256, 0, st>>>(a);
+        CUDA_OK(cudaGetLastError());
+        increment_kernel<<<1, 1, 0, st>>>(iteration);
+        CUDA_OK(cudaGetLastError());
+    });
+}
+
+int nca_umma_selftest(int mode, const float *A, const float *B, float *D, void *stream)
+{
+    return guarded([&] {
+        if (mode < 0 || mode > 4)
+            fail(NCA_ERR_ARGUMENT, "self-test mode must be 0..4");
+        check_ptr(A, "A"); check_ptr(B, "B"); check_ptr(D, "D");
+        const size_t smem = 2 * 128 * 128 * sizeof(float) + 16;
+        set_smem_once(umma_selftest_kernel, smem);
+        umma_selftest_kernel<<<1, 128, smem, static_cast<cudaStream_t>(stream)>>>(mode, A, B, D);
+        CUDA_OK(cudaGetLastError());
+    });
+}
+
+}  // extern "C"

@@ -1,0 +1,113 @@
+// Shared device helpers of the UltraNCA-B200 kernels: update-mask RNG, TF32 rounding, tile geometry, error word.
+//
+// Semantics restated from the UltraNCA reference (paths relative to that repository):
+//   - Philox4x32-10 update mask: ncaops/nca_step.cuh:187-212 (key = seed, counter = (n H + Y) ceil(W/4) + X/4, word X%4,
+//     m = floor(U + rate) != 0 with U = (word >> 8) 2^-24), the published algorithm of Salmon et al. (SC'11);
+//   - TF32 operand rounding, round to nearest, ties away: ncaops/nca_step.cuh:115-120 (cvt.rna.tf32.f32);
+//   - perception filters [identity, sobel_x, sobel_x^T, laplacian], circular padding, feature 4c + f:
+//     ncaops/nca_step.cuh:81-87,311-321 and ncaops/testing/test_nca.py:11-12,29.
+#pragma once
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace unca {
+
+// ---------------------------------------------------------------- error word
+// Device-side failures (a bounded wait that ran out) set this word instead of trapping; the host reads it with
+// nca_device_error(). Codes: 1 = MMA completion wait timed out. (The library is one translation unit.)
+__device__ int g_device_error = 0;
+
+__device__ __forceinline__ void set_device_error(int code) { atomicCAS(&g_device_error, 0, code); }
+
+// ---------------------------------------------------------------- Philox mask
+__device__ __forceinline__ uint4 philox4x32_10(uint64_t seed, uint64_t counter)
+{
+    uint32_t c0 = (uint32_t)counter, c1 = (uint32_t)(counter >> 32), c2 = 0u, c3 = 0u;
+    uint32_t k0 = (uint32_t)seed, k1 = (uint32_t)(seed >> 32);
+#pragma unroll
+    for (int r = 0; r < 10; ++r) {
+        const uint32_t lo0 = 0xD2511F53u * c0, hi0 = __umulhi(0xD2511F53u, c0);
+        const uint32_t lo1 = 0xCD9E8D57u * c2, hi1 = __umulhi(0xCD9E8D57u, c2);
+        const uint32_t n0 = hi1 ^ c1 ^ k0, n2 = hi0 ^ c3 ^ k1;
+        c0 = n0; c1 = lo1; c2 = n2; c3 = lo0;
+        k0 += 0x9E3779B9u; k1 += 0xBB67AE85u;
+    }
+    return make_uint4(c0, c1, c2, c3);
+}
+
+// m(n, Y, X) in {0, 1}; n is the GLOBAL image index (a shard adds its image offset).
+__device__ __forceinline__ float update_mask_at(uint64_t seed, float rate, int64_t n, int H, int W, int Y, int X)
+{
+    const uint64_t quads = (uint64_t)((W + 3) / 4);
+    const uint64_t counter = ((uint64_t)n * (uint64_t)H + (uint64_t)Y) * quads + (uint64_t)(X / 4);
+    const uint4 w = philox4x32_10(seed, counter);
+    const int e = X & 3;
+    const uint32_t word = e == 0 ? w.x : e == 1 ? w.y : e == 2 ? w.z : w.w;
+    const float u = __fmul_rn((float)(word >> 8), 1.0f / 16777216.0f);
+    return floorf(__fadd_rn(u, rate)) != 0.f ? 1.f : 0.f;
+}
+
+// ---------------------------------------------------------------- TF32
+__device__ __forceinline__ float tf32_rna(float v)
+{
+    uint32_t r;
+    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(v));
+    return __uint_as_float(r);
+}
+
+// ---------------------------------------------------------------- perception
+// The four filters of one channel from its 3x3 neighbourhood v (rows dy = -1..1, columns dx = -1..1), summed in the
+// reference's grouping (ncaops/nca_step.cuh:317-320).
+__device__ __forceinline__ float4 perceive3x3(const float (&v)[3][3])
+{
+    float4 p;
+    p.x = v[1][1];
+    p.y = __fadd_rn(__fadd_rn(__fsub_rn(v[0][2], v[0][0]), __fmul_rn(2.f, __fsub_rn(v[1][2], v[1][0]))), __fsub_rn(v[2][2], v[2][0]));
+    p.z = __fadd_rn(__fadd_rn(__fsub_rn(v[2][0], v[0][0]), __fmul_rn(2.f, __fsub_rn(v[2][1], v[0][1]))), __fsub_rn(v[2][2], v[0][2]));
+    const float corners = __fadd_rn(__fadd_rn(__fadd_rn(v[0][0], v[0][2]), v[2][0]), v[2][2]);
+    const float edges = __fadd_rn(__fadd_rn(__fadd_rn(v[0][1], v[1][0]), v[1][2]), v[2][1]);
+    p.w = __fsub_rn(__fadd_rn(corners, __fmul_rn(2.f, edges)), __fmul_rn(12.f, v[1][1]));
+    return p;
+}
+
+// Filter tap f at (i, j) (row dy = i - 1, column dx = j - 1), cross-correlation.
+__host__ __device__ __forceinline__ constexpr float filter_tap(int f, int i, int j)
+{
+    return f == 0 ? (i == 1 && j == 1 ? 1.f : 0.f)
+         : f == 1 ? (float)((j - 1) * (i == 1 ? 2 : 1))
+         : f == 2 ? (float)((i - 1) * (j == 1 ? 2 : 1))
+                  : (i == 1 && j == 1 ? -12.f : (i == 1 || j == 1) ? 2.f : 1.f);
+}
+
+__device__ __forceinline__ int wrap_index(int i, int n)
+{
+    i %= n;
+    return i < 0 ? i + n : i;
+}
+
+// ---------------------------------------------------------------- tile geometry
+// A tile is R rows x S columns (R S <= 128) of one image: S = min(W, 128) columns, R = 128 / W rows when W <= 128
+// (else one row of a 128-column strip). Tile pixel i (0..127) is (i / S, i % S); tiles of an image are strips-fastest.
+struct TileGeom {
+    int H, W, S, R, strips, tiles_per_image;
+};
+
+__host__ __device__ inline TileGeom make_geom(int H, int W)
+{
+    TileGeom g;
+    g.H = H; g.W = W;
+    g.S = W <= 128 ? W : 128;
+    g.R = W <= 128 ? 128 / W : 1;
+    g.strips = (W + g.S - 1) / g.S;
+    g.tiles_per_image = g.strips * ((H + g.R - 1) / g.R);
+    return g;
+}
+
+// The contiguous tile range [*a, *b) of persistent CTA c out of G over T tiles.
+__host__ __device__ inline void cta_range(int64_t T, int G, int c, int64_t *a, int64_t *b)
+{
+    *a = T * c / G;  // T * G stays far below 2^63 for any grid that fits in device memory
+    *b = T * (c + 1) / G;
+}
+
+}  // namespace unca

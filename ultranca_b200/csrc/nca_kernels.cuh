@@ -1,0 +1,729 @@
+// Kernels of the fused batched NCA step for sm_100a.
+//
+// One step for N = K B images (image n belongs to NCA n / B), state x (N, C, H, W):
+//   p = [id, sobel_x, sobel_x^T, laplacian](x) (circular 3x3, feature 4c + f), h = relu(W1 p + b1), u = W2 h,
+//   y = x + u m (m = Philox update mask), growing: y *= a, a = (maxpool3(x_alpha) > .1) & (maxpool3(y_alpha) > .1).
+// Reference semantics: ncaops/nca_step.cuh:1-19 (header comment), :343-691 (forward), :693-727 (alive),
+// :729-1162 (backward), :1164-1193 (reduce), :1195-1263 (adjoint); oracle math ncaops/testing/test_nca.py:21-32.
+//
+// Design (B200-first, not the reference's warp-MMA design):
+//   * persistent CTAs of 128 threads; CTA c owns the contiguous tile range [T c / G, T (c+1) / G) over all images, so
+//     weights are staged once per NCA segment and weight gradients accumulate in Tensor Memory across the segment;
+//   * a tile is 128 pixels (R rows x S columns); thread i owns tile pixel i and TMEM lane i;
+//   * the MLP is three tcgen05.mma kind::tf32 contractions per tile in the forward (p -> h, h -> u with A = relu(h) read
+//     back from TMEM) and five in the backward (h, dh, dp and the two weight-gradient contractions whose K dimension is
+//     the tile's pixels, with MN-major operands so the same shared-memory tile feeds both orientations);
+//   * the bias is folded into the first contraction as two TF32 columns (b1_hi + b1_lo = b1 to 2^-22 relative);
+//   * weight gradients are reduced across CTAs in a fixed order (partial slot = CTA + NCA): bitwise deterministic;
+//   * fp32 mode (the reference's 3xTF32 accuracy mode) runs the same tile loop with the MLP on CUDA cores in fp32.
+#pragma once
+#include "nca_common.cuh"
+#include "umma.cuh"
+
+namespace unca {
+
+template <int C_, int HID_>
+struct Dims {
+    static constexpr int C = C_, HID = HID_;
+    static constexpr int PIN = 4 * C;                    // perception features
+    static constexpr int KP = PIN + 8;                   // + bias-hi, bias-lo and six zero columns
+    static constexpr int CP = 16;                        // channels padded to the MMA N / K granule
+    static constexpr int NP = ((KP + 15) / 16) * 16;     // N of the dW1' contraction
+    static constexpr int TILE = 128;
+    static constexpr int PLANE = TILE * 4;               // floats of one chunk plane of a 128-row operand
+    static constexpr int XS_FLOATS = C * 390;            // (R + 2)(S + 2) <= 390 for R S <= 128
+    static constexpr int HT = TILE + 1;                  // padded pixel stride of the fp32-mode transposed buffers
+    // TMEM columns
+    static constexpr int FWD_TMEM = (HID + 16) <= 128 ? 128 : 256;
+    static constexpr int ACC1 = HID;                                   // dW1' accumulator (lanes = hidden units)
+    static constexpr int ACC2 = ((HID + NP + 31) / 32) * 32;           // dW2^T accumulator
+    static constexpr int BWD_TMEM = 256;
+    static_assert(ACC2 + 16 <= BWD_TMEM, "backward TMEM budget");
+    static_assert(HID % 16 == 0 && HID <= 128 && C <= 16 && C % 4 == 0, "supported NCA sizes");
+    // shared memory (floats)
+    static constexpr int W1S = HID * KP, W2S = CP * HID, P = TILE * KP, G = TILE * CP, RHDH = TILE * HID;
+    static constexpr size_t fwd_smem() { return (size_t)(W1S + W2S + P + XS_FLOATS) * 4 + 16; }
+    static constexpr size_t bwd_smem_tc() { return (size_t)(W1S + W2S + RHDH + P + G) * 4 + 16; }
+    static constexpr size_t bwd_smem_cc() { return (size_t)(W1S + W2S + P + G + 2 * HID * HT) * 4 + 16; }
+    static constexpr int PART = HID * PIN + HID + C * HID;  // weight-gradient partial: dW1, db1, dW2
+};
+
+struct StepArgs {
+    const float *x, *w1, *b1, *w2;
+    float *y, *alpha;              // forward outputs (alpha: growing only)
+    const float *gy;               // backward
+    const uint8_t *alive;          // backward, growing
+    float *dp, *partial;           // backward workspaces
+    int N, B, H, W;
+    uint64_t seed;
+    float rate;
+    int64_t n_offset;              // global index of image 0 (Philox counter)
+};
+
+// Stage one NCA's weights: W1' (HID x KP, chunk-planar: plane f/4, row j) with the bias columns, W2 (16 x HID,
+// chunk-planar: plane j/4, row c). TF32 mode rounds (b1 split into hi + lo); fp32 mode keeps fp32 and b1 in column PIN.
+template <class D, bool TC>
+__device__ __forceinline__ void stage_weights(float *W1s, float *W2s, const float *w1, const float *b1, const float *w2)
+{
+    for (int e = threadIdx.x; e < D::HID * D::KP; e += blockDim.x) {
+        const int j = e / D::KP, f = e % D::KP;
+        float v = 0.f;
+        if (f < D::PIN)
+            v = TC ? tf32_rna(w1[j * D::PIN + f]) : w1[j * D::PIN + f];
+        else if (f == D::PIN)
+            v = TC ? tf32_rna(b1[j]) : b1[j];
+        else if (f == D::PIN + 1 && TC)
+            v = tf32_rna(b1[j] - tf32_rna(b1[j]));
+        W1s[(f / 4) * D::HID * 4 + j * 4 + (f % 4)] = v;
+    }
+    for (int e = threadIdx.x; e < D::CP * D::HID; e += blockDim.x) {
+        const int c = e / D::HID, j = e % D::HID;
+        const float v = c < D::C ? (TC ? tf32_rna(w2[c * D::HID + j]) : w2[c * D::HID + j]) : 0.f;
+        W2s[(j / 4) * D::CP * 4 + c * 4 + (j % 4)] = v;
+    }
+}
+
+// State of image n around the tile at (y0, x0), with a one-pixel circular halo: XS[c][r][s], r < R+2, s < S+2.
+template <class D>
+__device__ __forceinline__ void load_halo(float *XS, const float *x, int n, const TileGeom &g, int y0, int x0)
+{
+    const int RR = g.R + 2, SS = g.S + 2, per = RR * SS;
+    const float *xn = x + (size_t)n * D::C * g.H * g.W;
+    for (int e = threadIdx.x; e < D::C * per; e += blockDim.x) {
+        const int c = e / per, rem = e - c * per, r = rem / SS, s = rem - r * SS;
+        const int Y = wrap_index(y0 - 1 + r, g.H), X = wrap_index(x0 - 1 + s, g.W);
+        XS[e] = __ldg(xn + ((size_t)c * g.H + Y) * g.W + X);
+    }
+}
+
+// Perception of tile pixel i into P (chunk-planar, plane c = the four filters of channel c, then the bias plane
+// {1, 1, 0, 0} and a zero plane). Invalid pixels get an all-zero row.
+template <class D, bool TC>
+__device__ __forceinline__ void perceive_tile(float *P, const float *XS, const TileGeom &g, int i, bool valid)
+{
+    const int r = i / g.S, s = i - r * g.S, SS = g.S + 2, per = (g.R + 2) * SS;
+#pragma unroll 4
+    for (int c = 0; c < D::C; ++c) {
+        float4 p = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (valid) {
+            float v[3][3];
+            const float *b = XS + c * per + r * SS + s;
+#pragma unroll
+            for (int dy = 0; dy < 3; ++dy)
+#pragma unroll
+                for (int dx = 0; dx < 3; ++dx)
+                    v[dy][dx] = b[dy * SS + dx];
+            p = perceive3x3(v);
+            if (TC)
+                p = make_float4(tf32_rna(p.x), tf32_rna(p.y), tf32_rna(p.z), tf32_rna(p.w));
+        }
+        *reinterpret_cast<float4 *>(P + c * D::PLANE + i * 4) = p;
+    }
+    *reinterpret_cast<float4 *>(P + (D::PIN / 4) * D::PLANE + i * 4) = valid ? make_float4(1.f, 1.f, 0.f, 0.f) : make_float4(0.f, 0.f, 0.f, 0.f);
+    *reinterpret_cast<float4 *>(P + (D::PIN / 4 + 1) * D::PLANE + i * 4) = make_float4(0.f, 0.f, 0.f, 0.f);
+}
+
+struct TileCoord {
+    int n, k, y0, x0;
+};
+
+__device__ __forceinline__ TileCoord tile_coord(int64_t t, const TileGeom &g, int B)
+{
+    TileCoord tc;
+    tc.n = (int)(t / g.tiles_per_image);
+    const int ti = (int)(t - (int64_t)tc.n * g.tiles_per_image);
+    tc.k = tc.n / B;
+    tc.y0 = (ti / g.strips) * g.R;
+    tc.x0 = (ti % g.strips) * g.S;
+    return tc;
+}
+
+// ================================================================ forward
+// One CTA per SM slot, tiles [T c / G, T (c+1) / G). Writes y (growing: the unmasked y and its alpha plane, the alive
+// kernel then masks it).
+template <int C, int HID, bool TC, bool GROWING>
+__global__ void __launch_bounds__(128, 1) fwd_kernel(StepArgs a)
+{
+    using D = Dims<C, HID>;
+    extern __shared__ __align__(128) float smem[];
+    float *W1s = smem, *W2s = W1s + D::W1S, *P = W2s + D::W2S, *XS = P + D::P;
+    uint64_t *bar = reinterpret_cast<uint64_t *>(XS + D::XS_FLOATS);
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bar + 1);
+
+    const int tid = threadIdx.x, warp = tid / 32;
+    const TileGeom g = make_geom(a.H, a.W);
+    const int64_t T = (int64_t)a.N * g.tiles_per_image;
+    int64_t t0, t1;
+    cta_range(T, gridDim.x, blockIdx.x, &t0, &t1);
+    const bool stoch = a.rate < 1.f;
+    const size_t plane = (size_t)a.H * a.W;
+
+    uint32_t tmem = 0;
+    if constexpr (TC) {
+        if (tid == 0) {
+            umma::mbar_init(bar, 1);
+            umma::fence_mbar_init();
+        }
+        if (warp == 0) {
+            umma::tmem_alloc(tmem_slot, D::FWD_TMEM);
+            umma::tmem_relinquish();
+        }
+        umma::fence_before_sync();
+        __syncthreads();
+        umma::fence_after_sync();
+        tmem = *tmem_slot;
+    }
+    uint32_t phase = 0;
+    int cur_k = -1;
+    bool failed = false;
+    for (int64_t t = t0; t < t1 && !failed; ++t) {
+        const TileCoord tc = tile_coord(t, g, a.B);
+        if (tc.k != cur_k) {
+            stage_weights<D, TC>(W1s, W2s, a.w1 + (size_t)tc.k * HID * D::PIN, a.b1 + (size_t)tc.k * HID,
+                                 a.w2 + (size_t)tc.k * C * HID);
+            cur_k = tc.k;
+        }
+        load_halo<D>(XS, a.x, tc.n, g, tc.y0, tc.x0);
+        __syncthreads();
+        const int r = tid / g.S, s = tid - r * g.S;
+        const bool valid = tid < g.R * g.S && tc.y0 + r < a.H && tc.x0 + s < a.W;
+        perceive_tile<D, TC>(P, XS, g, tid, valid);
+        float u[16];
+        if constexpr (TC) {
+            umma::fence_proxy_async();
+            __syncthreads();
+            if (tid == 0) {
+                umma::fence_after_sync();
+                const uint32_t pa = umma::smem_u32(P), wa = umma::smem_u32(W1s);
+#pragma unroll
+                for (int ks = 0; ks < D::KP / 8; ++ks)
+                    umma::mma_ss(tmem, umma::smem_desc(pa + ks * 2 * D::PLANE * 4, D::PLANE * 4, 128),
+                                 umma::smem_desc(wa + ks * 2 * HID * 16, HID * 16, 128), umma::idesc_tf32(128, HID, false, false),
+                                 ks > 0);
+                umma::commit(bar);
+            }
+            bool ok = umma::mbar_wait(bar, phase);
+            phase ^= 1;
+            if (!__syncthreads_and(ok)) {
+                failed = true;
+                break;
+            }
+            umma::fence_after_sync();
+            // relu(h) back into the same TMEM columns (TF32-rounded): the A operand of h -> u
+#pragma unroll
+            for (int cc = 0; cc < HID / 16; ++cc) {
+                float v[16];
+                const uint32_t ad = umma::tmem_addr(tmem, warp, cc * 16);
+                umma::tmem_ld16(ad, v);
+                umma::tmem_wait_ld();
+#pragma unroll
+                for (int e = 0; e < 16; ++e)
+                    v[e] = tf32_rna(fmaxf(v[e], 0.f));
+                umma::tmem_st16(ad, v);
+            }
+            umma::tmem_wait_st();
+            umma::fence_before_sync();
+            __syncthreads();
+            if (tid == 0) {
+                umma::fence_after_sync();
+                const uint32_t w2a = umma::smem_u32(W2s);
+#pragma unroll
+                for (int ks = 0; ks < HID / 8; ++ks)
+                    umma::mma_ts(tmem + HID, tmem + ks * 8, umma::smem_desc(w2a + ks * 2 * D::CP * 16, D::CP * 16, 128),
+                                 umma::idesc_tf32(128, 16, false, false), ks > 0);
+                umma::commit(bar);
+            }
+            ok = umma::mbar_wait(bar, phase);
+            phase ^= 1;
+            if (!__syncthreads_and(ok)) {
+                failed = true;
+                break;
+            }
+            umma::fence_after_sync();
+            umma::tmem_ld16(umma::tmem_addr(tmem, warp, HID), u);
+            umma::tmem_wait_ld();
+        } else {
+#pragma unroll
+            for (int c = 0; c < 16; ++c)
+                u[c] = 0.f;
+            if (valid) {
+                float p[D::PIN];
+#pragma unroll
+                for (int f = 0; f < D::PIN; ++f)
+                    p[f] = P[(f / 4) * D::PLANE + tid * 4 + (f % 4)];
+                for (int j = 0; j < HID; ++j) {
+                    const float *wrow = W1s + j * 4;
+                    float h = wrow[(D::PIN / 4) * HID * 4];
+#pragma unroll
+                    for (int f = 0; f < D::PIN; ++f)
+                        h = fmaf(wrow[(f / 4) * HID * 4 + (f % 4)], p[f], h);
+                    h = fmaxf(h, 0.f);
+                    const float *w2c = W2s + (j / 4) * D::CP * 4 + (j % 4);
+#pragma unroll
+                    for (int c = 0; c < C; ++c)
+                        u[c] = fmaf(w2c[c * 4], h, u[c]);
+                }
+            }
+        }
+        if (valid) {
+            const int Y = tc.y0 + r, X = tc.x0 + s;
+            const float m = stoch ? update_mask_at(a.seed, a.rate, tc.n + a.n_offset, a.H, a.W, Y, X) : 1.f;
+            const int SS = g.S + 2, per = (g.R + 2) * SS;
+            float *yn = a.y + (size_t)tc.n * C * plane + (size_t)Y * a.W + X;
+#pragma unroll
+            for (int c = 0; c < C; ++c) {
+                const float xc = XS[c * per + (r + 1) * SS + s + 1];
+                const float v = m != 0.f ? xc + u[c] : xc;
+                yn[(size_t)c * plane] = v;
+                if (GROWING && c == 3)
+                    a.alpha[(size_t)tc.n * plane + (size_t)Y * a.W + X] = v;
+            }
+        }
+        if constexpr (TC)
+            umma::fence_before_sync();
+        __syncthreads();  // XS, P and TMEM are reused by the next tile
+    }
+    if constexpr (TC) {
+        __syncthreads();
+        umma::fence_after_sync();
+        if (warp == 0)
+            umma::tmem_dealloc(tmem, D::FWD_TMEM);
+        if (failed && tid == 0)
+            set_device_error(1);
+    }
+}
+
+// Growing NCA alive mask (ncaops/nca_step.cuh:693-727): a = (maxpool3(x_alpha) > 0.1) & (maxpool3(alpha) > 0.1), zero
+// padding; y *= a (zeroing the whole cell); alive = a. One thread per pixel.
+template <int C>
+__global__ void alive_kernel(const float *__restrict__ x, const float *__restrict__ alpha, float *__restrict__ y,
+                             uint8_t *__restrict__ alive, int H, int W, int64_t total)
+{
+    const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+    if (i >= total)
+        return;
+    const int64_t plane = (int64_t)H * W, n = i / plane, pix = i - n * plane;
+    const int Y = (int)(pix / W), X = (int)(pix - (int64_t)Y * W);
+    const float *xa = x + (n * C + 3) * plane, *ya = alpha + n * plane;
+    float mx = 0.f, my = 0.f;
+#pragma unroll
+    for (int dy = -1; dy <= 1; ++dy)
+#pragma unroll
+        for (int dx = -1; dx <= 1; ++dx) {
+            const int yy = Y + dy, xx = X + dx;
+            if (yy >= 0 && yy < H && xx >= 0 && xx < W) {
+                mx = fmaxf(mx, xa[(int64_t)yy * W + xx]);
+                my = fmaxf(my, ya[(int64_t)yy * W + xx]);
+            }
+        }
+    const bool live = mx > 0.1f && my > 0.1f;
+    alive[i] = live;
+    if (!live)
+#pragma unroll
+        for (int c = 0; c < C; ++c)
+            y[(n * C + c) * plane + pix] = 0.f;
+}
+
+// ================================================================ backward
+// Per tile: recompute p and h, gm = gy m (a); dh = (gm W2) [h > 0]; dp = dh W1 -> dp scratch (N, 4C, H, W);
+// dW1' += dh^T p' (column PIN of p' is 1: db1), dW2^T += relu(h)^T gm, accumulated per NCA segment (TMEM in TF32 mode,
+// registers of threads j < HID in fp32 mode) and written to partial slot (CTA + NCA).
+template <class D>
+__device__ __forceinline__ void write_partial_row(float *out, int j, const float *dw1_row, float db1, const float *dw2_col)
+{
+    for (int f = 0; f < D::PIN; ++f)
+        out[j * D::PIN + f] = dw1_row[f];
+    out[D::HID * D::PIN + j] = db1;
+    for (int c = 0; c < D::C; ++c)
+        out[D::HID * (D::PIN + 1) + c * D::HID + j] = dw2_col[c];
+}
+
+template <int C, int HID, bool TC, bool GROWING>
+__global__ void __launch_bounds__(128, 1) bwd_kernel(StepArgs a)
+{
+    using D = Dims<C, HID>;
+    extern __shared__ __align__(128) float smem[];
+    float *W1s = smem, *W2s = W1s + D::W1S;
+    // TF32: RHDH (relu(h), then dh), P, G; the halo tile XS aliases RHDH. fp32: P, G, RHt, DHt (transposed, padded).
+    float *RHDH = W2s + D::W2S, *P = TC ? RHDH + D::RHDH : W2s + D::W2S, *G = P + D::P;
+    float *RHt = G + D::G, *DHt = RHt + D::HID * D::HT;
+    float *XS = TC ? RHDH : RHt;
+    uint64_t *bar = reinterpret_cast<uint64_t *>(TC ? G + D::G : DHt + D::HID * D::HT);
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bar + 1);
+
+    const int tid = threadIdx.x, warp = tid / 32;
+    const TileGeom g = make_geom(a.H, a.W);
+    const int64_t T = (int64_t)a.N * g.tiles_per_image;
+    int64_t t0, t1;
+    cta_range(T, gridDim.x, blockIdx.x, &t0, &t1);
+    const bool stoch = a.rate < 1.f;
+    const size_t plane = (size_t)a.H * a.W;
+
+    uint32_t tmem = 0;
+    if constexpr (TC) {
+        if (tid == 0) {
+            umma::mbar_init(bar, 1);
+            umma::fence_mbar_init();
+        }
+        if (warp == 0) {
+            umma::tmem_alloc(tmem_slot, D::BWD_TMEM);
+            umma::tmem_relinquish();
+        }
+        umma::fence_before_sync();
+        __syncthreads();
+        umma::fence_after_sync();
+        tmem = *tmem_slot;
+    }
+    // fp32-mode accumulators (thread j < HID owns hidden unit j)
+    float acc1[TC ? 1 : D::PIN], accb = 0.f, acc2[TC ? 1 : C];
+    if constexpr (!TC) {
+#pragma unroll
+        for (int f = 0; f < D::PIN; ++f)
+            acc1[f] = 0.f;
+#pragma unroll
+        for (int c = 0; c < C; ++c)
+            acc2[c] = 0.f;
+    }
+    uint32_t phase = 0;
+    int cur_k = -1;
+    bool started = false, failed = false;
+
+    auto flush = [&](int k) {  // this CTA's weight gradients of NCA k -> partial slot (blockIdx.x + k)
+        float *out = a.partial + (size_t)(blockIdx.x + k) * D::PART;
+        if constexpr (TC) {
+            float row[((D::PIN + 1 + 15) / 16) * 16], col[16];
+#pragma unroll
+            for (int cc = 0; cc < (D::PIN + 1 + 15) / 16; ++cc) {
+                float v[16];
+                umma::tmem_ld16(umma::tmem_addr(tmem, warp, D::ACC1 + cc * 16), v);
+                umma::tmem_wait_ld();
+#pragma unroll
+                for (int e = 0; e < 16; ++e)
+                    row[cc * 16 + e] = v[e];
+            }
+            umma::tmem_ld16(umma::tmem_addr(tmem, warp, D::ACC2), col);
+            umma::tmem_wait_ld();
+            if (tid < HID)
+                write_partial_row<D>(out, tid, row, row[D::PIN], col);
+            umma::fence_before_sync();
+        } else {
+            if (tid < HID)
+                write_partial_row<D>(out, tid, acc1, accb, acc2);
+#pragma unroll
+            for (int f = 0; f < D::PIN; ++f)
+                acc1[f] = 0.f;
+#pragma unroll
+            for (int c = 0; c < C; ++c)
+                acc2[c] = 0.f;
+            accb = 0.f;
+        }
+    };
+
+    for (int64_t t = t0; t < t1 && !failed; ++t) {
+        const TileCoord tc = tile_coord(t, g, a.B);
+        if (tc.k != cur_k) {
+            if (cur_k >= 0)
+                flush(cur_k);
+            __syncthreads();
+            stage_weights<D, TC>(W1s, W2s, a.w1 + (size_t)tc.k * HID * D::PIN, a.b1 + (size_t)tc.k * HID,
+                                 a.w2 + (size_t)tc.k * C * HID);
+            cur_k = tc.k;
+            started = false;
+        }
+        load_halo<D>(XS, a.x, tc.n, g, tc.y0, tc.x0);
+        const int r = tid / g.S, s = tid - r * g.S;
+        const bool valid = tid < g.R * g.S && tc.y0 + r < a.H && tc.x0 + s < a.W;
+        const int Y = tc.y0 + r, X = tc.x0 + s;
+        // gm = gy m (a): chunk-planar G, 16 channels
+        {
+            float gm[16];
+#pragma unroll
+            for (int c = 0; c < 16; ++c)
+                gm[c] = 0.f;
+            if (valid) {
+                float m = stoch ? update_mask_at(a.seed, a.rate, tc.n + a.n_offset, a.H, a.W, Y, X) : 1.f;
+                if (GROWING && !a.alive[(size_t)tc.n * plane + (size_t)Y * a.W + X])
+                    m = 0.f;
+                if (m != 0.f) {
+                    const float *gyn = a.gy + (size_t)tc.n * C * plane + (size_t)Y * a.W + X;
+#pragma unroll
+                    for (int c = 0; c < C; ++c)
+                        gm[c] = TC ? tf32_rna(gyn[(size_t)c * plane]) : gyn[(size_t)c * plane];
+                }
+            }
+#pragma unroll
+            for (int q = 0; q < 4; ++q)
+                *reinterpret_cast<float4 *>(G + q * D::PLANE + tid * 4) = make_float4(gm[4 * q], gm[4 * q + 1], gm[4 * q + 2], gm[4 * q + 3]);
+        }
+        __syncthreads();
+        perceive_tile<D, TC>(P, XS, g, tid, valid);
+        float *dpn = a.dp + (size_t)tc.n * D::PIN * plane + (size_t)Y * a.W + X;
+        if constexpr (TC) {
+            umma::fence_proxy_async();
+            __syncthreads();  // P, G complete; XS (aliasing RHDH) no longer read
+            const uint32_t pa = umma::smem_u32(P), ga = umma::smem_u32(G), wa = umma::smem_u32(W1s),
+                           w2a = umma::smem_u32(W2s), ra = umma::smem_u32(RHDH);
+            if (tid == 0) {
+                umma::fence_after_sync();
+#pragma unroll
+                for (int ks = 0; ks < D::KP / 8; ++ks)  // H = P W1'^T
+                    umma::mma_ss(tmem, umma::smem_desc(pa + ks * 2 * D::PLANE * 4, D::PLANE * 4, 128),
+                                 umma::smem_desc(wa + ks * 2 * HID * 16, HID * 16, 128), umma::idesc_tf32(128, HID, false, false),
+                                 ks > 0);
+                umma::commit(bar);
+            }
+            bool ok = umma::mbar_wait(bar, phase);
+            phase ^= 1;
+            if (!__syncthreads_and(ok)) {
+                failed = true;
+                break;
+            }
+            umma::fence_after_sync();
+            uint32_t pos[HID / 32];  // bit e of word w: h > 0 for hidden unit 32 w + e
+#pragma unroll
+            for (int w = 0; w < HID / 32; ++w)
+                pos[w] = 0u;
+#pragma unroll
+            for (int cc = 0; cc < HID / 16; ++cc) {
+                float v[16];
+                umma::tmem_ld16(umma::tmem_addr(tmem, warp, cc * 16), v);
+                umma::tmem_wait_ld();
+#pragma unroll
+                for (int e = 0; e < 16; ++e) {
+                    if (v[e] > 0.f)
+                        pos[(cc * 16 + e) / 32] |= 1u << ((cc * 16 + e) % 32);
+                    v[e] = tf32_rna(fmaxf(v[e], 0.f));
+                }
+#pragma unroll
+                for (int q = 0; q < 4; ++q)
+                    *reinterpret_cast<float4 *>(RHDH + (cc * 4 + q) * D::PLANE + tid * 4) =
+                        make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+            }
+            umma::fence_proxy_async();
+            umma::fence_before_sync();
+            __syncthreads();
+            if (tid == 0) {
+                umma::fence_after_sync();
+#pragma unroll
+                for (int ks = 0; ks < 16; ++ks)  // dW2^T += relu(h)^T gm (K = pixels; both operands MN-major)
+                    umma::mma_ss(tmem + D::ACC2, umma::smem_desc(ra + ks * 128, 128, D::PLANE * 4),
+                                 umma::smem_desc(ga + ks * 128, 128, D::PLANE * 4), umma::idesc_tf32(128, 16, true, true),
+                                 started || ks > 0);
+#pragma unroll
+                for (int ks = 0; ks < 2; ++ks)  // DHP = gm W2 (B = W2 MN-major: rows are channels)
+                    umma::mma_ss(tmem, umma::smem_desc(ga + ks * 2 * D::PLANE * 4, D::PLANE * 4, 128),
+                                 umma::smem_desc(w2a + ks * 128, 128, D::CP * 16), umma::idesc_tf32(128, HID, false, true),
+                                 ks > 0);
+                umma::commit(bar);
+            }
+            ok = umma::mbar_wait(bar, phase);
+            phase ^= 1;
+            if (!__syncthreads_and(ok)) {
+                failed = true;
+                break;
+            }
+            umma::fence_after_sync();
+#pragma unroll
+            for (int cc = 0; cc < HID / 16; ++cc) {
+                float v[16];
+                umma::tmem_ld16(umma::tmem_addr(tmem, warp, cc * 16), v);
+                umma::tmem_wait_ld();
+#pragma unroll
+                for (int e = 0; e < 16; ++e)
+                    v[e] = (pos[(cc * 16 + e) / 32] >> ((cc * 16 + e) % 32)) & 1u ? tf32_rna(v[e]) : 0.f;
+#pragma unroll
+                for (int q = 0; q < 4; ++q)
+                    *reinterpret_cast<float4 *>(RHDH + (cc * 4 + q) * D::PLANE + tid * 4) =
+                        make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+            }
+            umma::fence_proxy_async();
+            umma::fence_before_sync();
+            __syncthreads();
+            if (tid == 0) {
+                umma::fence_after_sync();
+#pragma unroll
+                for (int ks = 0; ks < 16; ++ks)  // dW1' += dh^T p' (K = pixels; MN-major)
+                    umma::mma_ss(tmem + D::ACC1, umma::smem_desc(ra + ks * 128, 128, D::PLANE * 4),
+                                 umma::smem_desc(pa + ks * 128, 128, D::PLANE * 4), umma::idesc_tf32(128, D::NP, true, true),
+                                 started || ks > 0);
+#pragma unroll
+                for (int ks = 0; ks < HID / 8; ++ks)  // DP = dh W1 (A K-major over hidden; B = W1' MN-major)
+                    umma::mma_ss(tmem, umma::smem_desc(ra + ks * 2 * D::PLANE * 4, D::PLANE * 4, 128),
+                                 umma::smem_desc(wa + ks * 128, 128, HID * 16), umma::idesc_tf32(128, D::PIN, false, true),
+                                 ks > 0);
+                umma::commit(bar);
+            }
+            started = true;
+            ok = umma::mbar_wait(bar, phase);
+            phase ^= 1;
+            if (!__syncthreads_and(ok)) {
+                failed = true;
+                break;
+            }
+            umma::fence_after_sync();
+#pragma unroll
+            for (int cc = 0; cc < D::PIN / 16; ++cc) {
+                float v[16];
+                umma::tmem_ld16(umma::tmem_addr(tmem, warp, cc * 16), v);
+                umma::tmem_wait_ld();
+                if (valid)
+#pragma unroll
+                    for (int e = 0; e < 16; ++e)
+                        dpn[(size_t)(cc * 16 + e) * plane] = v[e];
+            }
+            umma::fence_before_sync();
+        } else {
+            __syncthreads();
+            // per pixel: h, dh = (W2^T gm) [h > 0], dp = W1^T dh; relu(h) and dh into the transposed buffers
+            float p[D::PIN], gm[C], dpv[D::PIN];
+#pragma unroll
+            for (int f = 0; f < D::PIN; ++f) {
+                p[f] = P[(f / 4) * D::PLANE + tid * 4 + (f % 4)];
+                dpv[f] = 0.f;
+            }
+#pragma unroll
+            for (int c = 0; c < C; ++c)
+                gm[c] = G[(c / 4) * D::PLANE + tid * 4 + (c % 4)];
+            for (int j = 0; j < HID; ++j) {
+                const float *wrow = W1s + j * 4;
+                float h = wrow[(D::PIN / 4) * HID * 4];
+#pragma unroll
+                for (int f = 0; f < D::PIN; ++f)
+                    h = fmaf(wrow[(f / 4) * HID * 4 + (f % 4)], p[f], h);
+                const float *w2c = W2s + (j / 4) * D::CP * 4 + (j % 4);
+                float dh = 0.f;
+#pragma unroll
+                for (int c = 0; c < C; ++c)
+                    dh = fmaf(w2c[c * 4], gm[c], dh);
+                dh = h > 0.f ? dh : 0.f;
+                RHt[j * D::HT + tid] = valid ? fmaxf(h, 0.f) : 0.f;
+                DHt[j * D::HT + tid] = dh;
+#pragma unroll
+                for (int f = 0; f < D::PIN; ++f)
+                    dpv[f] = fmaf(wrow[(f / 4) * HID * 4 + (f % 4)], dh, dpv[f]);
+            }
+            if (valid)
+#pragma unroll
+                for (int f = 0; f < D::PIN; ++f)
+                    dpn[(size_t)f * plane] = dpv[f];
+            __syncthreads();
+            if (tid < HID)  // weight gradients of hidden unit j = tid over the tile's pixels, fixed order
+                for (int q = 0; q < D::TILE; ++q) {
+                    const float dh = DHt[tid * D::HT + q], rh = RHt[tid * D::HT + q];
+#pragma unroll
+                    for (int f = 0; f < D::PIN; ++f)
+                        acc1[f] = fmaf(dh, P[(f / 4) * D::PLANE + q * 4 + (f % 4)], acc1[f]);
+                    accb += dh;
+#pragma unroll
+                    for (int c = 0; c < C; ++c)
+                        acc2[c] = fmaf(G[(c / 4) * D::PLANE + q * 4 + (c % 4)], rh, acc2[c]);
+                }
+        }
+        __syncthreads();  // shared buffers and TMEM are reused by the next tile
+    }
+    if (cur_k >= 0 && !failed)
+        flush(cur_k);
+    if constexpr (TC) {
+        umma::fence_before_sync();
+        __syncthreads();
+        umma::fence_after_sync();
+        if (warp == 0)
+            umma::tmem_dealloc(tmem, D::BWD_TMEM);
+        if (failed && tid == 0)
+            set_device_error(1);
+    }
+}
+
+// gx = gy a + sum_f P_f^T dp_f: the transpose of the circular perception (ncaops/nca_step.cuh:1195-1263), fp32, fixed
+// tap order. Block: 32 x 8 output pixels of one image, all channels; dp halo staged in shared memory.
+constexpr int ADJ_TW = 32, ADJ_TH = 8;
+template <int C, bool GROWING>
+__global__ void __launch_bounds__(256) adjoint_kernel(const float *__restrict__ dp, const float *__restrict__ gy,
+                                                      const uint8_t *__restrict__ alive, float *__restrict__ gx, int H, int W)
+{
+    constexpr int PIN = 4 * C, HW_ = ADJ_TW + 2, HH_ = ADJ_TH + 2;
+    extern __shared__ __align__(16) float sdp[];  // [PIN][HH_][HW_]
+    const int tiles_x = (W + ADJ_TW - 1) / ADJ_TW;
+    const int x0 = (blockIdx.x % tiles_x) * ADJ_TW, y0 = (blockIdx.x / tiles_x) * ADJ_TH;
+    const int64_t n = blockIdx.y, plane = (int64_t)H * W;
+    const float *dpn = dp + n * PIN * plane;
+    for (int e = threadIdx.x; e < PIN * HH_ * HW_; e += blockDim.x) {
+        const int f = e / (HH_ * HW_), rem = e - f * HH_ * HW_, r = rem / HW_, s = rem - r * HW_;
+        const int Y = wrap_index(y0 - 1 + r, H), X = wrap_index(x0 - 1 + s, W);
+        sdp[e] = dpn[(int64_t)f * plane + (int64_t)Y * W + X];
+    }
+    __syncthreads();
+    const int r = threadIdx.x / ADJ_TW, s = threadIdx.x % ADJ_TW, Y = y0 + r, X = x0 + s;
+    if (Y >= H || X >= W)
+        return;
+    const int64_t pix = (int64_t)Y * W + X;
+    const bool live = !GROWING || alive[n * plane + pix];
+#pragma unroll 1
+    for (int c = 0; c < C; ++c) {
+        float acc = 0.f;
+#pragma unroll
+        for (int f = 0; f < 4; ++f)
+#pragma unroll
+            for (int i = 0; i < 3; ++i)
+#pragma unroll
+                for (int j = 0; j < 3; ++j) {
+                    // output (Y, X) receives tap (i, j) of the pixel (Y - (i - 1), X - (j - 1))
+                    const float k = filter_tap(f, i, j);
+                    if (k != 0.f)
+                        acc = fmaf(k, sdp[((4 * c + f) * HH_ + (r + 1 - (i - 1))) * HW_ + (s + 1 - (j - 1))], acc);
+                }
+        const int64_t o = (n * C + c) * plane + pix;
+        gx[o] = (live ? gy[o] : 0.f) + acc;
+    }
+}
+
+// Fixed-order sum of the partial slots (c + k) of the CTAs c whose tile ranges overlap NCA k -> dw1, db1, dw2
+// (accumulate: added to the outputs). ncaops/nca_step.cuh:1164-1193 sums per-block partials the same way.
+template <int C, int HID>
+__global__ void reduce_kernel(const float *__restrict__ partial, int64_t T, int G, int64_t tiles_per_nca,
+                              float *__restrict__ dw1, float *__restrict__ db1, float *__restrict__ dw2, int accumulate)
+{
+    using D = Dims<C, HID>;
+    const int k = blockIdx.y, e = blockIdx.x * blockDim.x + threadIdx.x;
+    __shared__ int range[2];
+    if (threadIdx.x == 0) {
+        const int64_t lo = (int64_t)k * tiles_per_nca, hi = lo + tiles_per_nca;
+        int c0 = (int)(lo * G / T) - 1;
+        c0 = c0 < 0 ? 0 : c0;
+        int64_t a, b;
+        cta_range(T, G, c0, &a, &b);
+        while (b <= lo) {
+            ++c0;
+            cta_range(T, G, c0, &a, &b);
+        }
+        int c1 = c0;
+        while (c1 + 1 < G) {
+            cta_range(T, G, c1 + 1, &a, &b);
+            if (a >= hi)
+                break;
+            ++c1;
+        }
+        range[0] = c0;
+        range[1] = c1;
+    }
+    __syncthreads();
+    if (e >= D::PART)
+        return;
+    float s = 0.f;
+    for (int c = range[0]; c <= range[1]; ++c) {
+        int64_t a, b;
+        cta_range(T, G, c, &a, &b);
+        if (b > a)
+            s += partial[(size_t)(c + k) * D::PART + e];
+    }
+    float *dst;
+    if (e < HID * D::PIN)
+        dst = dw1 + (size_t)k * HID * D::PIN + e;
+    else if (e < HID * (D::PIN + 1))
+        dst = db1 + (size_t)k * HID + (e - HID * D::PIN);
+    else
+        dst = dw2 + (size_t)k * C * HID + (e - HID * (D::PIN + 1));
+    *dst = accumulate ? *dst + s : s;
+}
+
+}  // namespace unca
