@@ -118,11 +118,13 @@ int nca_adam_step(float *param0, float *param1, float *param2, const float *grad
  * for its tensor-core work (a bounded wait ran out; the kernel returned instead of hanging). Synchronous. */
 int nca_device_error(int *code, int reset);
 
-/* Tensor-core layout self-test: D = A B^T on tcgen05 for one of the operand forms the step kernels use
- * (mode 0: A, B K-major; 1: A, B MN-major; 2: A K-major, B MN-major (B rows = 16); 3: A from Tensor Memory;
- * 4: A K-major, B MN-major (B rows = 96)). A is (128, K) and B is (N, K) row-major fp32 (rounded to TF32 inside); D is
- * (128, N). Shapes per mode: 0: K 56, N 96; 1: K 128, N 64; 2: K 16, N 96; 3: K 96, N 16; 4: K 96, N 48. */
-int nca_umma_selftest(int mode, const float *A, const float *B, float *D, void *stream);
+/* Tensor-core layout self-test: D (128 x N) = A (128 x K) B (N x K)^T on tcgen05 (kind::tf32) with the operands
+ * staged in one of the forms the step kernels use: form 0: A and B K-major without swizzle; 1: A in Tensor Memory,
+ * B K-major; 2: A and B MN-major with the 128-byte / 32-byte-atom swizzle; 3: form 2 with the two descriptor strides
+ * exchanged (a diagnostic that must NOT match). A, B, D row-major fp32 device memory (A, B rounded to TF32 inside);
+ * N in 16..128 (multiple of 16), K in 8..128 (multiple of 8). No reference counterpart (the reference has no
+ * tcgen05 path). */
+int nca_umma_selftest(int form, int N, int K, const float *A, const float *B, float *D, void *stream);
 
 #ifdef __cplusplus
 }

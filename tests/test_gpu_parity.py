@@ -46,21 +46,35 @@ def device_error_clear():
 
 
 # ------------------------------------------------------------------------------------------------ tensor cores
-@pytest.mark.parametrize('mode', range(5))
-def test_umma_layout_selftest(mode):
+UMMA_CASES = [(0, 96, 56), (1, 16, 96), (1, 96, 56), (1, 96, 16), (1, 48, 96), (1, 128, 72), (2, 64, 128),
+              (2, 16, 128), (2, 96, 128), (2, 128, 128)]
+
+
+def umma_selftest(form, N, K, seed=0):
     from ultranca_b200._lib import check, lib
-    K, N = {0: (56, 96), 1: (128, 64), 2: (16, 96), 3: (96, 16), 4: (96, 48)}[mode]
-    g = torch.Generator().manual_seed(mode)
+    g = torch.Generator().manual_seed(seed + 100 * form + N + K)
     A = torch.randn(128, K, generator=g)
     B = torch.randn(N, K, generator=g)
     D = torch.empty(128, N, device=DEV)
     Ad, Bd = gpu(A, B)
-    check(lib.nca_umma_selftest(mode, ctypes.c_void_p(Ad.data_ptr()), ctypes.c_void_p(Bd.data_ptr()),
+    check(lib.nca_umma_selftest(form, N, K, ctypes.c_void_p(Ad.data_ptr()), ctypes.c_void_p(Bd.data_ptr()),
                                 ctypes.c_void_p(D.data_ptr()), None))
     torch.cuda.synchronize()
-    assert device_error_clear()
     ref = (O.tf32_round(A).double() @ O.tf32_round(B).double().T).float()
-    assert O.rel(D.cpu(), ref) < 1e-5
+    return O.rel(D.cpu(), ref)
+
+
+@pytest.mark.parametrize('form,N,K', UMMA_CASES)
+def test_umma_layout_selftest(form, N, K):
+    """Every tcgen05 operand form the step kernels use computes A B^T exactly (up to fp32 accumulation order)."""
+    assert umma_selftest(form, N, K) < 1e-5
+    assert device_error_clear()
+
+
+def test_umma_swapped_strides_are_detected():
+    """The self-test can tell the two stride conventions of the swizzled MN-major descriptor apart."""
+    assert umma_selftest(3, 64, 128) > 1e-2
+    assert device_error_clear()
 
 
 # ------------------------------------------------------------------------------------------------ mask

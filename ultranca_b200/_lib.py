@@ -43,7 +43,7 @@ SIGNATURES = {
                               c_f32p, c_i64, c_i64, c_i64, c_i64, c_vp, c_float, c_float, c_float, c_float, c_float,
                               ctypes.POINTER(c_i64), c_int, c_vp]),
     'nca_device_error': (c_int, [ctypes.POINTER(c_int), c_int]),
-    'nca_umma_selftest': (c_int, [c_int, c_f32p, c_f32p, c_f32p, c_vp]),
+    'nca_umma_selftest': (c_int, [c_int, c_int, c_int, c_f32p, c_f32p, c_f32p, c_vp]),
 }
 
 

@@ -139,55 +139,45 @@ __global__ void __launch_bounds__(256) adam_kernel(AdamArgs a)
 __global__ void increment_kernel(int64_t *iteration) { *iteration += 1; }
 
 // ---------------------------------------------------------------- tcgen05 layout self-test
-struct SelftestShape {
-    int K, N, a_rows_are_k, b_rows_are_k, b_plane_rows;
-};
-
-__host__ __device__ inline SelftestShape selftest_shape(int mode)
-{
-    switch (mode) {
-    case 0: return {56, 96, 0, 0, 96};
-    case 1: return {128, 64, 1, 1, 128};
-    case 2: return {16, 96, 0, 1, 16};
-    case 3: return {96, 16, 0, 0, 16};
-    default: return {96, 48, 0, 1, 96};
-    }
-}
-
-// A (128 x K) and B (N x K) row-major in global memory; D (128 x N). Operands are staged chunk-planar exactly as the
-// step kernels stage theirs: K-major tiles with rows = M (N), MN-major tiles with rows = K.
-__global__ void __launch_bounds__(128, 1) umma_selftest_kernel(int mode, const float *__restrict__ A,
+// D (128 x N) = A (128 x K) B (N x K)^T from row-major fp32 in global memory (rounded to TF32), with the operands
+// staged in one of the forms the step kernels use:
+//   form 0: A, B K-major, no swizzle (chunk-planar);           form 1: A in TMEM (lane = row), B K-major;
+//   form 2: A, B MN-major SW128_32B (rows = K);                 form 3: form 2 with LBO / SBO exchanged (diagnostic).
+__global__ void __launch_bounds__(128, 1) umma_selftest_kernel(int form, int N, int K, const float *__restrict__ A,
                                                                const float *__restrict__ B, float *__restrict__ D)
 {
-    extern __shared__ __align__(128) float sm[];
-    const SelftestShape sh = selftest_shape(mode);
-    float *As = sm, *Bs = sm + 128 * 128;
+    extern __shared__ __align__(128) unsigned char raw[];
+    unsigned char *base = raw + ((1024 - (umma::smem_u32(raw) & 1023)) & 1023);
+    float *As = reinterpret_cast<float *>(base), *Bs = As + 128 * 128;
     uint64_t *bar = reinterpret_cast<uint64_t *>(Bs + 128 * 128);
     uint32_t *slot = reinterpret_cast<uint32_t *>(bar + 1);
     const int tid = threadIdx.x, warp = tid / 32;
-    // A: K-major -> rows m (128), planes over k; MN-major -> rows k, planes over m
-    for (int e = tid; e < 128 * sh.K; e += 128) {
-        const int m = e / sh.K, k = e % sh.K;
+    const bool mn = form >= 2;
+    for (int e = tid; e < 128 * 128; e += 128)
+        As[e] = Bs[e] = 0.f;
+    __syncthreads();
+    for (int e = tid; e < 128 * K; e += 128) {
+        const int m = e / K, k = e % K;
         const float v = tf32_rna(A[e]);
-        if (sh.a_rows_are_k)
-            As[(m / 4) * sh.K * 4 + k * 4 + (m % 4)] = v;
+        if (mn)
+            As[umma::sw32_offset(m, k, K) / 4] = v;
         else
             As[(k / 4) * 128 * 4 + m * 4 + (k % 4)] = v;
     }
-    for (int e = tid; e < sh.N * sh.K; e += 128) {
-        const int n = e / sh.K, k = e % sh.K;
+    for (int e = tid; e < N * K; e += 128) {
+        const int n = e / K, k = e % K;
         const float v = tf32_rna(B[e]);
-        if (sh.b_rows_are_k)
-            Bs[(n / 4) * sh.b_plane_rows * 4 + k * 4 + (n % 4)] = v;
+        if (mn)
+            Bs[umma::sw32_offset(n, k, K) / 4] = v;
         else
-            Bs[(k / 4) * sh.b_plane_rows * 4 + n * 4 + (k % 4)] = v;
+            Bs[(k / 4) * N * 4 + n * 4 + (k % 4)] = v;
     }
     if (tid == 0) {
         umma::mbar_init(bar, 1);
         umma::fence_mbar_init();
     }
     if (warp == 0) {
-        umma::tmem_alloc(slot, 256);
+        umma::tmem_alloc(slot, 512);
         umma::tmem_relinquish();
     }
     umma::fence_proxy_async();
@@ -195,14 +185,13 @@ __global__ void __launch_bounds__(128, 1) umma_selftest_kernel(int mode, const f
     __syncthreads();
     umma::fence_after_sync();
     const uint32_t tmem = *slot;
-    int dcol = 0;
-    if (mode == 3) {  // A into TMEM columns [0, K): thread = lane = row m
-        dcol = 128;
-        for (int c0 = 0; c0 < sh.K; c0 += 16) {
+    const int dcol = 256;
+    if (form == 1) {  // A into TMEM columns [0, K): thread = lane = row m
+        for (int c0 = 0; c0 < K; c0 += 16) {
             float v[16];
 #pragma unroll
             for (int e = 0; e < 16; ++e)
-                v[e] = tf32_rna(A[tid * sh.K + c0 + e]);
+                v[e] = c0 + e < K ? tf32_rna(A[tid * K + c0 + e]) : 0.f;
             umma::tmem_st16(umma::tmem_addr(tmem, warp, c0), v);
         }
         umma::tmem_wait_st();
@@ -212,14 +201,18 @@ __global__ void __launch_bounds__(128, 1) umma_selftest_kernel(int mode, const f
     }
     if (tid == 0) {
         const uint32_t aa = umma::smem_u32(As), ba = umma::smem_u32(Bs);
-        const int ksteps = sh.K / 8;
-        for (int ks = 0; ks < ksteps; ++ks) {
-            const uint64_t adesc = sh.a_rows_are_k ? umma::smem_desc(aa + ks * 128, 128, sh.K * 16)
-                                                   : umma::smem_desc(aa + ks * 2 * 128 * 16, 128 * 16, 128);
-            const uint64_t bdesc = sh.b_rows_are_k ? umma::smem_desc(ba + ks * 128, 128, sh.b_plane_rows * 16)
-                                                   : umma::smem_desc(ba + ks * 2 * sh.b_plane_rows * 16, sh.b_plane_rows * 16, 128);
-            const uint32_t idesc = umma::idesc_tf32(128, sh.N, sh.a_rows_are_k, sh.b_rows_are_k);
-            if (mode == 3)
+        const uint32_t idesc = umma::idesc_tf32(128, N, mn, mn);
+        for (int ks = 0; ks < K / 8; ++ks) {
+            uint64_t adesc, bdesc;
+            if (mn) {
+                const uint32_t lbo = form == 2 ? K * 128 : 512, sbo = form == 2 ? 512 : K * 128;
+                adesc = umma::smem_desc(aa + ks * 1024, lbo, sbo, umma::LAYOUT_SW128_32B);
+                bdesc = umma::smem_desc(ba + ks * 1024, lbo, sbo, umma::LAYOUT_SW128_32B);
+            } else {
+                adesc = umma::smem_desc(aa + ks * 2 * 128 * 16, 128 * 16, 128);
+                bdesc = umma::smem_desc(ba + ks * 2 * N * 16, N * 16, 128);
+            }
+            if (form == 1)
                 umma::mma_ts(tmem + dcol, tmem + ks * 8, bdesc, idesc, ks > 0);
             else
                 umma::mma_ss(tmem + dcol, adesc, bdesc, idesc, ks > 0);
@@ -229,13 +222,14 @@ __global__ void __launch_bounds__(128, 1) umma_selftest_kernel(int mode, const f
     const bool ok = umma::mbar_wait(bar, 0);
     umma::fence_after_sync();
     if (__syncthreads_and(ok)) {
-        for (int c0 = 0; c0 < sh.N; c0 += 16) {
+        for (int c0 = 0; c0 < N; c0 += 16) {
             float v[16];
             umma::tmem_ld16(umma::tmem_addr(tmem, warp, dcol + c0), v);
             umma::tmem_wait_ld();
 #pragma unroll
             for (int e = 0; e < 16; ++e)
-                D[tid * sh.N + c0 + e] = v[e];
+                if (c0 + e < N)
+                    D[tid * N + c0 + e] = v[e];
         }
     } else if (tid == 0) {
         set_device_error(1);
@@ -244,7 +238,7 @@ __global__ void __launch_bounds__(128, 1) umma_selftest_kernel(int mode, const f
     __syncthreads();
     umma::fence_after_sync();
     if (warp == 0)
-        umma::tmem_dealloc(tmem, 256);
+        umma::tmem_dealloc(tmem, 512);
 }
 
 }  // namespace unca

@@ -206,8 +206,8 @@ int bwd_ctas_per_sm()
 {
     using D = Dims<I::C, I::HID>;
     if (I::FP32)
-        return ctas_per_sm(bwd_kernel<I::C, I::HID, false, I::GROW>, D::bwd_smem_cc(), 0);
-    return ctas_per_sm(bwd_kernel<I::C, I::HID, true, I::GROW>, D::bwd_smem_tc(), D::BWD_TMEM);
+        return ctas_per_sm(bwd_kernel_cc<I::C, I::HID, I::GROW>, D::bwd_smem_cc(), 0);
+    return ctas_per_sm(bwd_kernel_tc<I::C, I::HID, I::GROW>, D::bwd_smem_tc(), D::BWD_TMEM);
 }
 
 void launch_forward(const float *x, const float *w1, const float *b1, const float *w2, float *y, float *alpha,
@@ -370,9 +370,9 @@ int nca_backward_stages(const float *x, const float *gy, const uint8_t *alive, c
             const TileGeom g = make_geom((int)H, (int)W);
             if (stages & NCA_STAGE_MAIN) {
                 if (II::FP32)
-                    bwd_kernel<II::C, II::HID, false, II::GROW><<<w.grid, 128, D::bwd_smem_cc(), st>>>(a);
+                    bwd_kernel_cc<II::C, II::HID, II::GROW><<<w.grid, 128, D::bwd_smem_cc(), st>>>(a);
                 else
-                    bwd_kernel<II::C, II::HID, true, II::GROW><<<w.grid, 128, D::bwd_smem_tc(), st>>>(a);
+                    bwd_kernel_tc<II::C, II::HID, II::GROW><<<w.grid, 128, D::bwd_smem_tc(), st>>>(a);
                 CUDA_OK(cudaGetLastError());
             }
             if (stages & NCA_STAGE_ADJOINT) {
@@ -482,15 +482,17 @@ int nca_adam_step(float *param0, float *param1, float *param2, const float *grad
     });
 }
 
-int nca_umma_selftest(int mode, const float *A, const float *B, float *D, void *stream)
+int nca_umma_selftest(int form, int N, int K, const float *A, const float *B, float *D, void *stream)
 {
     return guarded([&] {
-        if (mode < 0 || mode > 4)
-            fail(NCA_ERR_ARGUMENT, "self-test mode must be 0..4");
+        if (form < 0 || form > 3)
+            fail(NCA_ERR_ARGUMENT, "self-test form must be 0..3");
+        if (N < 16 || N > 128 || N % 16 || K < 8 || K > 128 || K % 8)
+            fail(NCA_ERR_ARGUMENT, "self-test sizes: N in 16..128 (multiple of 16), K in 8..128 (multiple of 8)");
         check_ptr(A, "A"); check_ptr(B, "B"); check_ptr(D, "D");
-        const size_t smem = 2 * 128 * 128 * sizeof(float) + 16;
+        const size_t smem = 2 * 128 * 128 * sizeof(float) + 1024 + 16;
         set_smem_once(umma_selftest_kernel, smem);
-        umma_selftest_kernel<<<1, 128, smem, static_cast<cudaStream_t>(stream)>>>(mode, A, B, D);
+        umma_selftest_kernel<<<1, 128, smem, static_cast<cudaStream_t>(stream)>>>(form, N, K, A, B, D);
         CUDA_OK(cudaGetLastError());
     });
 }

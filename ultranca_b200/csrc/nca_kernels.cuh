@@ -35,15 +35,20 @@ struct Dims {
     static constexpr int HT = TILE + 1;                  // padded pixel stride of the fp32-mode transposed buffers
     // TMEM columns
     static constexpr int FWD_TMEM = (HID + 16) <= 128 ? 128 : 256;
-    static constexpr int ACC1 = HID;                                   // dW1' accumulator (lanes = hidden units)
-    static constexpr int ACC2 = ((HID + NP + 31) / 32) * 32;           // dW2^T accumulator
-    static constexpr int BWD_TMEM = 256;
-    static_assert(ACC2 + 16 <= BWD_TMEM, "backward TMEM budget");
-    static_assert(HID % 16 == 0 && HID <= 128 && C <= 16 && C % 4 == 0, "supported NCA sizes");
+    // backward (TF32): H, then dh (A of dp) | dh before the relu mask | p (A of p -> h), then dp | g m (A of dh) |
+    // dW1' accumulator (lanes = hidden units) | dW2^T accumulator
+    static constexpr int T_H = 0, T_DHP = 128, T_P = 256, T_G = 352, T_ACC1 = 384, T_ACC2 = 480, BWD_TMEM = 512;
+    static constexpr int NPW = ((KP + 31) / 32) * 32;            // N of the dW1' contraction (whole 32-wide blocks)
+    static_assert(T_ACC1 + NPW <= T_ACC2 && ((KP + 15) / 16) * 16 <= T_G - T_P, "backward TMEM budget");
+    static_assert(HID % 32 == 0 && HID <= 128 && C <= 16 && C % 4 == 0, "supported NCA sizes");
     // shared memory (floats)
     static constexpr int W1S = HID * KP, W2S = CP * HID, P = TILE * KP, G = TILE * CP, RHDH = TILE * HID;
+    static constexpr int W1T = PIN * HID, W2T = HID * CP;          // backward B operands (K-major, transposed)
+    static constexpr int PSW = TILE * NPW, GSW = TILE * 32;         // backward swizzled MN-major operands
     static constexpr size_t fwd_smem() { return (size_t)(W1S + W2S + P + XS_FLOATS) * 4 + 16; }
-    static constexpr size_t bwd_smem_tc() { return (size_t)(W1S + W2S + RHDH + P + G) * 4 + 16; }
+    // TF32 backward: [W1S | W1T | W2T | pad to 1 KB] [RHDH (XS aliases it) | PSW | GSW] + barrier
+    static constexpr int BWD_W = ((W1S + W1T + W2T) * 4 + 1023) / 1024 * 1024;
+    static constexpr size_t bwd_smem_tc() { return 1024 + (size_t)BWD_W + (size_t)(RHDH + PSW + GSW) * 4 + 16; }
     static constexpr size_t bwd_smem_cc() { return (size_t)(W1S + W2S + P + G + 2 * HID * HT) * 4 + 16; }
     static constexpr int PART = HID * PIN + HID + C * HID;  // weight-gradient partial: dW1, db1, dW2
 };
@@ -83,17 +88,35 @@ __device__ __forceinline__ void stage_weights(float *W1s, float *W2s, const floa
     }
 }
 
-// State of image n around the tile at (y0, x0), with a one-pixel circular halo: XS[c][r][s], r < R+2, s < S+2.
-template <class D>
-__device__ __forceinline__ void load_halo(float *XS, const float *x, int n, const TileGeom &g, int y0, int x0)
+__device__ __forceinline__ void cp_async4(float *dst, const float *src)
 {
-    const int RR = g.R + 2, SS = g.S + 2, per = RR * SS;
-    const float *xn = x + (size_t)n * D::C * g.H * g.W;
-    for (int e = threadIdx.x; e < D::C * per; e += blockDim.x) {
-        const int c = e / per, rem = e - c * per, r = rem / SS, s = rem - r * SS;
-        const int Y = wrap_index(y0 - 1 + r, g.H), X = wrap_index(x0 - 1 + s, g.W);
-        XS[e] = __ldg(xn + ((size_t)c * g.H + Y) * g.W + X);
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(umma::smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
+// State of image n around the tile at (y0, x0), with a one-pixel circular halo: XS[c][r][s], r < R+2, s < S+2, copied
+// asynchronously (cp.async; the caller waits with cp_async_wait_all + a barrier). Thread t copies the halo positions
+// t, t + 128, t + 256, t + 384 of every channel; index arithmetic is done once per tile, not per element.
+template <class D>
+__device__ __forceinline__ void load_halo_async(float *XS, const float *x, int n, const TileGeom &g, int y0, int x0)
+{
+    const int SS = g.S + 2, per = (g.R + 2) * SS;
+    const size_t plane = (size_t)g.H * g.W;
+    const float *xn = x + (size_t)n * D::C * plane;
+    int goff[4], soff[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int e = threadIdx.x + 128 * i;
+        const int r = e / SS, s = e - r * SS;
+        soff[i] = e < per ? e : -1;
+        goff[i] = wrap_index(y0 - 1 + r, g.H) * g.W + wrap_index(x0 - 1 + s, g.W);
     }
+#pragma unroll 4
+    for (int c = 0; c < D::C; ++c)
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+            if (soff[i] >= 0)
+                cp_async4(XS + c * per + soff[i], xn + c * plane + goff[i]);
 }
 
 // Perception of tile pixel i into P (chunk-planar, plane c = the four filters of channel c, then the bias plane
@@ -183,7 +206,8 @@ __global__ void __launch_bounds__(128, 1) fwd_kernel(StepArgs a)
                                  a.w2 + (size_t)tc.k * C * HID);
             cur_k = tc.k;
         }
-        load_halo<D>(XS, a.x, tc.n, g, tc.y0, tc.x0);
+        load_halo_async<D>(XS, a.x, tc.n, g, tc.y0, tc.x0);
+        cp_async_wait_all();
         __syncthreads();
         const int r = tid / g.S, s = tid - r * g.S;
         const bool valid = tid < g.R * g.S && tc.y0 + r < a.H && tc.x0 + s < a.W;
@@ -338,17 +362,186 @@ __device__ __forceinline__ void write_partial_row(float *out, int j, const float
         out[D::HID * (D::PIN + 1) + c * D::HID + j] = dw2_col[c];
 }
 
-template <int C, int HID, bool TC, bool GROWING>
-__global__ void __launch_bounds__(128, 1) bwd_kernel(StepArgs a)
+// Per tile pixel: gm = gy m (a) (growing: a = the alive mask of the forward), 16 channels, fp32.
+template <int C, bool GROWING>
+__device__ __forceinline__ void load_gm(float (&gm)[16], const StepArgs &a, const TileCoord &tc, int Y, int X,
+                                        bool valid, bool stoch)
+{
+#pragma unroll
+    for (int c = 0; c < 16; ++c)
+        gm[c] = 0.f;
+    if (!valid)
+        return;
+    const size_t plane = (size_t)a.H * a.W;
+    float m = stoch ? update_mask_at(a.seed, a.rate, tc.n + a.n_offset, a.H, a.W, Y, X) : 1.f;
+    if (GROWING && !a.alive[(size_t)tc.n * plane + (size_t)Y * a.W + X])
+        m = 0.f;
+    if (m == 0.f)
+        return;
+    const float *gyn = a.gy + (size_t)tc.n * C * plane + (size_t)Y * a.W + X;
+#pragma unroll
+    for (int c = 0; c < C; ++c)
+        gm[c] = __ldg(gyn + (size_t)c * plane);
+}
+
+// fp32 mode: the MLP on CUDA cores in fp32, weight gradients accumulated by threads j < HID in registers.
+template <int C, int HID, bool GROWING>
+__global__ void __launch_bounds__(128, 1) bwd_kernel_cc(StepArgs a)
 {
     using D = Dims<C, HID>;
     extern __shared__ __align__(128) float smem[];
-    float *W1s = smem, *W2s = W1s + D::W1S;
-    // TF32: RHDH (relu(h), then dh), P, G; the halo tile XS aliases RHDH. fp32: P, G, RHt, DHt (transposed, padded).
-    float *RHDH = W2s + D::W2S, *P = TC ? RHDH + D::RHDH : W2s + D::W2S, *G = P + D::P;
+    float *W1s = smem, *W2s = W1s + D::W1S, *P = W2s + D::W2S, *G = P + D::P;
     float *RHt = G + D::G, *DHt = RHt + D::HID * D::HT;
-    float *XS = TC ? RHDH : RHt;
-    uint64_t *bar = reinterpret_cast<uint64_t *>(TC ? G + D::G : DHt + D::HID * D::HT);
+    float *XS = RHt;  // the halo tile is dead before RHt is written
+
+    const int tid = threadIdx.x;
+    const TileGeom g = make_geom(a.H, a.W);
+    const int64_t T = (int64_t)a.N * g.tiles_per_image;
+    int64_t t0, t1;
+    cta_range(T, gridDim.x, blockIdx.x, &t0, &t1);
+    const bool stoch = a.rate < 1.f;
+    const size_t plane = (size_t)a.H * a.W;
+    float acc1[D::PIN], accb = 0.f, acc2[C];
+#pragma unroll
+    for (int f = 0; f < D::PIN; ++f)
+        acc1[f] = 0.f;
+#pragma unroll
+    for (int c = 0; c < C; ++c)
+        acc2[c] = 0.f;
+    int cur_k = -1;
+    auto flush = [&](int k) {
+        if (tid < HID)
+            write_partial_row<D>(a.partial + (size_t)(blockIdx.x + k) * D::PART, tid, acc1, accb, acc2);
+#pragma unroll
+        for (int f = 0; f < D::PIN; ++f)
+            acc1[f] = 0.f;
+#pragma unroll
+        for (int c = 0; c < C; ++c)
+            acc2[c] = 0.f;
+        accb = 0.f;
+    };
+    for (int64_t t = t0; t < t1; ++t) {
+        const TileCoord tc = tile_coord(t, g, a.B);
+        if (tc.k != cur_k) {
+            if (cur_k >= 0)
+                flush(cur_k);
+            __syncthreads();
+            stage_weights<D, false>(W1s, W2s, a.w1 + (size_t)tc.k * HID * D::PIN, a.b1 + (size_t)tc.k * HID,
+                                    a.w2 + (size_t)tc.k * C * HID);
+            cur_k = tc.k;
+        }
+        load_halo_async<D>(XS, a.x, tc.n, g, tc.y0, tc.x0);
+        const int r = tid / g.S, s = tid - r * g.S;
+        const bool valid = tid < g.R * g.S && tc.y0 + r < a.H && tc.x0 + s < a.W;
+        const int Y = tc.y0 + r, X = tc.x0 + s;
+        float gm[16];
+        load_gm<C, GROWING>(gm, a, tc, Y, X, valid, stoch);
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+            *reinterpret_cast<float4 *>(G + q * D::PLANE + tid * 4) = make_float4(gm[4 * q], gm[4 * q + 1], gm[4 * q + 2], gm[4 * q + 3]);
+        cp_async_wait_all();
+        __syncthreads();
+        perceive_tile<D, false>(P, XS, g, tid, valid);
+        __syncthreads();
+        float p[D::PIN], dpv[D::PIN];
+#pragma unroll
+        for (int f = 0; f < D::PIN; ++f) {
+            p[f] = P[(f / 4) * D::PLANE + tid * 4 + (f % 4)];
+            dpv[f] = 0.f;
+        }
+        for (int j = 0; j < HID; ++j) {
+            const float *wrow = W1s + j * 4;
+            float h = wrow[(D::PIN / 4) * HID * 4];
+#pragma unroll
+            for (int f = 0; f < D::PIN; ++f)
+                h = fmaf(wrow[(f / 4) * HID * 4 + (f % 4)], p[f], h);
+            const float *w2c = W2s + (j / 4) * D::CP * 4 + (j % 4);
+            float dh = 0.f;
+#pragma unroll
+            for (int c = 0; c < C; ++c)
+                dh = fmaf(w2c[c * 4], gm[c], dh);
+            dh = h > 0.f ? dh : 0.f;
+            RHt[j * D::HT + tid] = valid ? fmaxf(h, 0.f) : 0.f;
+            DHt[j * D::HT + tid] = dh;
+#pragma unroll
+            for (int f = 0; f < D::PIN; ++f)
+                dpv[f] = fmaf(wrow[(f / 4) * HID * 4 + (f % 4)], dh, dpv[f]);
+        }
+        if (valid) {
+            float *dpn = a.dp + (size_t)tc.n * D::PIN * plane + (size_t)Y * a.W + X;
+#pragma unroll
+            for (int f = 0; f < D::PIN; ++f)
+                dpn[(size_t)f * plane] = dpv[f];
+        }
+        __syncthreads();
+        if (tid < HID)  // weight gradients of hidden unit j = tid over the tile's pixels, fixed order
+            for (int q = 0; q < D::TILE; ++q) {
+                const float dh = DHt[tid * D::HT + q], rh = RHt[tid * D::HT + q];
+#pragma unroll
+                for (int f = 0; f < D::PIN; ++f)
+                    acc1[f] = fmaf(dh, P[(f / 4) * D::PLANE + q * 4 + (f % 4)], acc1[f]);
+                accb += dh;
+#pragma unroll
+                for (int c = 0; c < C; ++c)
+                    acc2[c] = fmaf(G[(c / 4) * D::PLANE + q * 4 + (c % 4)], rh, acc2[c]);
+            }
+        __syncthreads();
+    }
+    if (cur_k >= 0)
+        flush(cur_k);
+}
+
+// Stage one NCA's backward weights: W1' (HID x KP, K-major: B of p -> h), W1^T (PIN x HID, K-major: B of dh -> dp),
+// W2^T (HID x 16, K-major: B of gm -> dh), all TF32, chunk-planar without swizzle.
+template <class D>
+__device__ __forceinline__ void stage_bwd_weights(float *W1s, float *W1T, float *W2T, const float *w1, const float *b1,
+                                                  const float *w2)
+{
+    float *unused = nullptr;
+    (void)unused;
+    for (int e = threadIdx.x; e < D::HID * D::KP; e += blockDim.x) {
+        const int j = e / D::KP, f = e % D::KP;
+        float v = 0.f;
+        if (f < D::PIN)
+            v = tf32_rna(w1[j * D::PIN + f]);
+        else if (f == D::PIN)
+            v = tf32_rna(b1[j]);
+        else if (f == D::PIN + 1)
+            v = tf32_rna(b1[j] - tf32_rna(b1[j]));
+        W1s[(f / 4) * D::HID * 4 + j * 4 + (f % 4)] = v;
+        if (f < D::PIN)
+            W1T[(j / 4) * D::PIN * 4 + f * 4 + (j % 4)] = v;
+    }
+    for (int e = threadIdx.x; e < D::HID * D::CP; e += blockDim.x) {
+        const int j = e / D::CP, c = e % D::CP;
+        W2T[(c / 4) * D::HID * 4 + j * 4 + (c % 4)] = c < D::C ? tf32_rna(w2[c * D::HID + j]) : 0.f;
+    }
+}
+
+// Eight consecutive values v[0..7] of MN index mn0 (mn0 % 8 == 0) at K row k of a swizzled MN-major tile.
+__device__ __forceinline__ void st_sw32x8(float *tile, int mn0, int k, int krows, const float *v)
+{
+    float *dst = tile + umma::sw32_offset(mn0, k, krows) / 4;
+    *reinterpret_cast<float4 *>(dst) = make_float4(v[0], v[1], v[2], v[3]);
+    *reinterpret_cast<float4 *>(dst + 4) = make_float4(v[4], v[5], v[6], v[7]);
+}
+
+// TF32 mode. Per tile (thread = pixel = TMEM lane):
+//   1. halo tile (cp.async) and gm; p' and gm into TMEM (A operands) and into swizzled MN-major smem (weight grads);
+//   2. H = p' W1'^T and DHP = gm W2 (A from TMEM);
+//   3. relu(h) -> smem (swizzled), dh = DHP [h > 0] -> TMEM (A of dp);
+//   4. dW2^T += relu(h)^T gm and DP = dh W1 (A from TMEM);
+//   5. dh -> smem (swizzled, over relu(h)); dW1' += dh^T p' while dp is stored to the dp scratch.
+template <int C, int HID, bool GROWING>
+__global__ void __launch_bounds__(128, 1) bwd_kernel_tc(StepArgs a)
+{
+    using D = Dims<C, HID>;
+    extern __shared__ __align__(128) unsigned char smem_raw[];
+    unsigned char *base = smem_raw + ((1024 - (umma::smem_u32(smem_raw) & 1023)) & 1023);
+    float *W1s = reinterpret_cast<float *>(base), *W1T = W1s + D::W1S, *W2T = W1T + D::W1T;
+    float *RHDH = reinterpret_cast<float *>(base + D::BWD_W), *PSW = RHDH + D::RHDH, *GSW = PSW + D::PSW;
+    float *XS = RHDH;
+    uint64_t *bar = reinterpret_cast<uint64_t *>(GSW + D::GSW);
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bar + 1);
 
     const int tid = threadIdx.x, warp = tid / 32;
@@ -359,279 +552,217 @@ __global__ void __launch_bounds__(128, 1) bwd_kernel(StepArgs a)
     const bool stoch = a.rate < 1.f;
     const size_t plane = (size_t)a.H * a.W;
 
-    uint32_t tmem = 0;
-    if constexpr (TC) {
-        if (tid == 0) {
-            umma::mbar_init(bar, 1);
-            umma::fence_mbar_init();
-        }
-        if (warp == 0) {
-            umma::tmem_alloc(tmem_slot, D::BWD_TMEM);
-            umma::tmem_relinquish();
-        }
-        umma::fence_before_sync();
-        __syncthreads();
-        umma::fence_after_sync();
-        tmem = *tmem_slot;
+    // the swizzled gm tile holds 16 channels in a 32-wide block: zero it once (its other 16 lanes are never written)
+    for (int e = tid; e < D::GSW; e += 128)
+        GSW[e] = 0.f;
+    if (tid == 0) {
+        umma::mbar_init(bar, 1);
+        umma::fence_mbar_init();
     }
-    // fp32-mode accumulators (thread j < HID owns hidden unit j)
-    float acc1[TC ? 1 : D::PIN], accb = 0.f, acc2[TC ? 1 : C];
-    if constexpr (!TC) {
-#pragma unroll
-        for (int f = 0; f < D::PIN; ++f)
-            acc1[f] = 0.f;
-#pragma unroll
-        for (int c = 0; c < C; ++c)
-            acc2[c] = 0.f;
+    if (warp == 0) {
+        umma::tmem_alloc(tmem_slot, D::BWD_TMEM);
+        umma::tmem_relinquish();
     }
+    umma::fence_before_sync();
+    __syncthreads();
+    umma::fence_after_sync();
+    const uint32_t tmem = *tmem_slot;
+    const uint32_t lane_base = umma::tmem_addr(tmem, warp, 0);
+    const uint32_t sW1 = umma::smem_u32(W1s), sW1T = umma::smem_u32(W1T), sW2T = umma::smem_u32(W2T);
+    const uint32_t sRH = umma::smem_u32(RHDH), sP = umma::smem_u32(PSW), sG = umma::smem_u32(GSW);
+
     uint32_t phase = 0;
     int cur_k = -1;
     bool started = false, failed = false;
-
+    auto wait_mma = [&]() {
+        const bool ok = umma::mbar_wait(bar, phase);
+        phase ^= 1;
+        if (!__syncthreads_and(ok))
+            failed = true;
+        umma::fence_after_sync();
+        return !failed;
+    };
     auto flush = [&](int k) {  // this CTA's weight gradients of NCA k -> partial slot (blockIdx.x + k)
-        float *out = a.partial + (size_t)(blockIdx.x + k) * D::PART;
-        if constexpr (TC) {
-            float row[((D::PIN + 1 + 15) / 16) * 16], col[16];
+        float row[((D::PIN + 1 + 15) / 16) * 16], col[16];
 #pragma unroll
-            for (int cc = 0; cc < (D::PIN + 1 + 15) / 16; ++cc) {
-                float v[16];
-                umma::tmem_ld16(umma::tmem_addr(tmem, warp, D::ACC1 + cc * 16), v);
-                umma::tmem_wait_ld();
-#pragma unroll
-                for (int e = 0; e < 16; ++e)
-                    row[cc * 16 + e] = v[e];
-            }
-            umma::tmem_ld16(umma::tmem_addr(tmem, warp, D::ACC2), col);
+        for (int cc = 0; cc < (D::PIN + 1 + 15) / 16; ++cc) {
+            float v[16];
+            umma::tmem_ld16(lane_base + D::T_ACC1 + cc * 16, v);
             umma::tmem_wait_ld();
-            if (tid < HID)
-                write_partial_row<D>(out, tid, row, row[D::PIN], col);
-            umma::fence_before_sync();
-        } else {
-            if (tid < HID)
-                write_partial_row<D>(out, tid, acc1, accb, acc2);
 #pragma unroll
-            for (int f = 0; f < D::PIN; ++f)
-                acc1[f] = 0.f;
-#pragma unroll
-            for (int c = 0; c < C; ++c)
-                acc2[c] = 0.f;
-            accb = 0.f;
+            for (int e = 0; e < 16; ++e)
+                row[cc * 16 + e] = v[e];
         }
+        umma::tmem_ld16(lane_base + D::T_ACC2, col);
+        umma::tmem_wait_ld();
+        if (tid < HID)
+            write_partial_row<D>(a.partial + (size_t)(blockIdx.x + k) * D::PART, tid, row, row[D::PIN], col);
+        umma::fence_before_sync();
     };
 
-    for (int64_t t = t0; t < t1 && !failed; ++t) {
+    for (int64_t t = t0; t < t1; ++t) {
         const TileCoord tc = tile_coord(t, g, a.B);
         if (tc.k != cur_k) {
             if (cur_k >= 0)
                 flush(cur_k);
             __syncthreads();
-            stage_weights<D, TC>(W1s, W2s, a.w1 + (size_t)tc.k * HID * D::PIN, a.b1 + (size_t)tc.k * HID,
+            stage_bwd_weights<D>(W1s, W1T, W2T, a.w1 + (size_t)tc.k * HID * D::PIN, a.b1 + (size_t)tc.k * HID,
                                  a.w2 + (size_t)tc.k * C * HID);
             cur_k = tc.k;
             started = false;
         }
-        load_halo<D>(XS, a.x, tc.n, g, tc.y0, tc.x0);
+        // ---- 1. inputs
+        load_halo_async<D>(XS, a.x, tc.n, g, tc.y0, tc.x0);
         const int r = tid / g.S, s = tid - r * g.S;
         const bool valid = tid < g.R * g.S && tc.y0 + r < a.H && tc.x0 + s < a.W;
         const int Y = tc.y0 + r, X = tc.x0 + s;
-        // gm = gy m (a): chunk-planar G, 16 channels
-        {
-            float gm[16];
+        float gm[16];
+        load_gm<C, GROWING>(gm, a, tc, Y, X, valid, stoch);
 #pragma unroll
-            for (int c = 0; c < 16; ++c)
-                gm[c] = 0.f;
-            if (valid) {
-                float m = stoch ? update_mask_at(a.seed, a.rate, tc.n + a.n_offset, a.H, a.W, Y, X) : 1.f;
-                if (GROWING && !a.alive[(size_t)tc.n * plane + (size_t)Y * a.W + X])
-                    m = 0.f;
-                if (m != 0.f) {
-                    const float *gyn = a.gy + (size_t)tc.n * C * plane + (size_t)Y * a.W + X;
-#pragma unroll
-                    for (int c = 0; c < C; ++c)
-                        gm[c] = TC ? tf32_rna(gyn[(size_t)c * plane]) : gyn[(size_t)c * plane];
-                }
-            }
-#pragma unroll
-            for (int q = 0; q < 4; ++q)
-                *reinterpret_cast<float4 *>(G + q * D::PLANE + tid * 4) = make_float4(gm[4 * q], gm[4 * q + 1], gm[4 * q + 2], gm[4 * q + 3]);
-        }
+        for (int c = 0; c < 16; ++c)
+            gm[c] = tf32_rna(gm[c]);
+        umma::tmem_st16(lane_base + D::T_G, gm);
+        st_sw32x8(GSW, 0, tid, 128, gm);
+        st_sw32x8(GSW, 8, tid, 128, gm + 8);
+        cp_async_wait_all();
         __syncthreads();
-        perceive_tile<D, TC>(P, XS, g, tid, valid);
-        float *dpn = a.dp + (size_t)tc.n * D::PIN * plane + (size_t)Y * a.W + X;
-        if constexpr (TC) {
-            umma::fence_proxy_async();
-            __syncthreads();  // P, G complete; XS (aliasing RHDH) no longer read
-            const uint32_t pa = umma::smem_u32(P), ga = umma::smem_u32(G), wa = umma::smem_u32(W1s),
-                           w2a = umma::smem_u32(W2s), ra = umma::smem_u32(RHDH);
-            if (tid == 0) {
-                umma::fence_after_sync();
+        {
+            const int SS = g.S + 2, per = (g.R + 2) * SS;
+            float pv[((D::KP + 15) / 16) * 16];
 #pragma unroll
-                for (int ks = 0; ks < D::KP / 8; ++ks)  // H = P W1'^T
-                    umma::mma_ss(tmem, umma::smem_desc(pa + ks * 2 * D::PLANE * 4, D::PLANE * 4, 128),
-                                 umma::smem_desc(wa + ks * 2 * HID * 16, HID * 16, 128), umma::idesc_tf32(128, HID, false, false),
-                                 ks > 0);
-                umma::commit(bar);
-            }
-            bool ok = umma::mbar_wait(bar, phase);
-            phase ^= 1;
-            if (!__syncthreads_and(ok)) {
-                failed = true;
-                break;
-            }
-            umma::fence_after_sync();
-            uint32_t pos[HID / 32];  // bit e of word w: h > 0 for hidden unit 32 w + e
+            for (int c = 0; c < C; ++c) {
+                float4 p = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (valid) {
+                    float v[3][3];
+                    const float *b = XS + c * per + r * SS + s;
 #pragma unroll
-            for (int w = 0; w < HID / 32; ++w)
-                pos[w] = 0u;
+                    for (int dy = 0; dy < 3; ++dy)
 #pragma unroll
-            for (int cc = 0; cc < HID / 16; ++cc) {
-                float v[16];
-                umma::tmem_ld16(umma::tmem_addr(tmem, warp, cc * 16), v);
-                umma::tmem_wait_ld();
-#pragma unroll
-                for (int e = 0; e < 16; ++e) {
-                    if (v[e] > 0.f)
-                        pos[(cc * 16 + e) / 32] |= 1u << ((cc * 16 + e) % 32);
-                    v[e] = tf32_rna(fmaxf(v[e], 0.f));
+                        for (int dx = 0; dx < 3; ++dx)
+                            v[dy][dx] = b[dy * SS + dx];
+                    p = perceive3x3(v);
                 }
-#pragma unroll
-                for (int q = 0; q < 4; ++q)
-                    *reinterpret_cast<float4 *>(RHDH + (cc * 4 + q) * D::PLANE + tid * 4) =
-                        make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+                pv[4 * c] = tf32_rna(p.x); pv[4 * c + 1] = tf32_rna(p.y);
+                pv[4 * c + 2] = tf32_rna(p.z); pv[4 * c + 3] = tf32_rna(p.w);
             }
-            umma::fence_proxy_async();
-            umma::fence_before_sync();
-            __syncthreads();
-            if (tid == 0) {
-                umma::fence_after_sync();
 #pragma unroll
-                for (int ks = 0; ks < 16; ++ks)  // dW2^T += relu(h)^T gm (K = pixels; both operands MN-major)
-                    umma::mma_ss(tmem + D::ACC2, umma::smem_desc(ra + ks * 128, 128, D::PLANE * 4),
-                                 umma::smem_desc(ga + ks * 128, 128, D::PLANE * 4), umma::idesc_tf32(128, 16, true, true),
-                                 started || ks > 0);
+            for (int f = D::PIN; f < ((D::KP + 15) / 16) * 16; ++f)
+                pv[f] = (valid && f < D::PIN + 2) ? 1.f : 0.f;  // bias-hi and bias-lo features
 #pragma unroll
-                for (int ks = 0; ks < 2; ++ks)  // DHP = gm W2 (B = W2 MN-major: rows are channels)
-                    umma::mma_ss(tmem, umma::smem_desc(ga + ks * 2 * D::PLANE * 4, D::PLANE * 4, 128),
-                                 umma::smem_desc(w2a + ks * 128, 128, D::CP * 16), umma::idesc_tf32(128, HID, false, true),
-                                 ks > 0);
-                umma::commit(bar);
+            for (int cc = 0; cc < ((D::KP + 15) / 16); ++cc)
+                umma::tmem_st16(lane_base + D::T_P + cc * 16, *reinterpret_cast<float(*)[16]>(pv + cc * 16));
+#pragma unroll
+            for (int f8 = 0; f8 < D::NPW / 8; ++f8) {
+                float z[8];
+#pragma unroll
+                for (int e = 0; e < 8; ++e)
+                    z[e] = f8 * 8 + e < ((D::KP + 15) / 16) * 16 ? pv[(f8 * 8 + e) % (((D::KP + 15) / 16) * 16)] : 0.f;
+                st_sw32x8(PSW, f8 * 8, tid, 128, z);
             }
-            ok = umma::mbar_wait(bar, phase);
-            phase ^= 1;
-            if (!__syncthreads_and(ok)) {
-                failed = true;
-                break;
-            }
+        }
+        umma::tmem_wait_st();
+        umma::fence_proxy_async();
+        umma::fence_before_sync();
+        __syncthreads();
+        // ---- 2. H = p' W1'^T, DHP = gm W2 (A from TMEM)
+        if (tid == 0) {
             umma::fence_after_sync();
 #pragma unroll
-            for (int cc = 0; cc < HID / 16; ++cc) {
-                float v[16];
-                umma::tmem_ld16(umma::tmem_addr(tmem, warp, cc * 16), v);
-                umma::tmem_wait_ld();
+            for (int ks = 0; ks < D::KP / 8; ++ks)
+                umma::mma_ts(tmem + D::T_H, tmem + D::T_P + ks * 8, umma::smem_desc(sW1 + ks * 2 * HID * 16, HID * 16, 128),
+                             umma::idesc_tf32(128, HID, false, false), ks > 0);
 #pragma unroll
-                for (int e = 0; e < 16; ++e)
-                    v[e] = (pos[(cc * 16 + e) / 32] >> ((cc * 16 + e) % 32)) & 1u ? tf32_rna(v[e]) : 0.f;
+            for (int ks = 0; ks < 2; ++ks)
+                umma::mma_ts(tmem + D::T_DHP, tmem + D::T_G + ks * 8, umma::smem_desc(sW2T + ks * 2 * HID * 16, HID * 16, 128),
+                             umma::idesc_tf32(128, HID, false, false), ks > 0);
+            umma::commit(bar);
+        }
+        if (!wait_mma())
+            break;
+        // ---- 3. relu(h) -> smem (swizzled MN-major), dh -> TMEM
 #pragma unroll
-                for (int q = 0; q < 4; ++q)
-                    *reinterpret_cast<float4 *>(RHDH + (cc * 4 + q) * D::PLANE + tid * 4) =
-                        make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+        for (int cc = 0; cc < HID / 16; ++cc) {
+            float h[16], d[16];
+            umma::tmem_ld16(lane_base + D::T_H + cc * 16, h);
+            umma::tmem_ld16(lane_base + D::T_DHP + cc * 16, d);
+            umma::tmem_wait_ld();
+#pragma unroll
+            for (int e = 0; e < 16; ++e) {
+                d[e] = h[e] > 0.f ? tf32_rna(d[e]) : 0.f;
+                h[e] = tf32_rna(fmaxf(h[e], 0.f));
             }
-            umma::fence_proxy_async();
-            umma::fence_before_sync();
-            __syncthreads();
-            if (tid == 0) {
-                umma::fence_after_sync();
-#pragma unroll
-                for (int ks = 0; ks < 16; ++ks)  // dW1' += dh^T p' (K = pixels; MN-major)
-                    umma::mma_ss(tmem + D::ACC1, umma::smem_desc(ra + ks * 128, 128, D::PLANE * 4),
-                                 umma::smem_desc(pa + ks * 128, 128, D::PLANE * 4), umma::idesc_tf32(128, D::NP, true, true),
-                                 started || ks > 0);
-#pragma unroll
-                for (int ks = 0; ks < HID / 8; ++ks)  // DP = dh W1 (A K-major over hidden; B = W1' MN-major)
-                    umma::mma_ss(tmem, umma::smem_desc(ra + ks * 2 * D::PLANE * 4, D::PLANE * 4, 128),
-                                 umma::smem_desc(wa + ks * 128, 128, HID * 16), umma::idesc_tf32(128, D::PIN, false, true),
-                                 ks > 0);
-                umma::commit(bar);
-            }
-            started = true;
-            ok = umma::mbar_wait(bar, phase);
-            phase ^= 1;
-            if (!__syncthreads_and(ok)) {
-                failed = true;
-                break;
-            }
+            st_sw32x8(RHDH, cc * 16, tid, 128, h);
+            st_sw32x8(RHDH, cc * 16 + 8, tid, 128, h + 8);
+            umma::tmem_st16(lane_base + D::T_H + cc * 16, d);
+        }
+        umma::tmem_wait_st();
+        umma::fence_proxy_async();
+        umma::fence_before_sync();
+        __syncthreads();
+        // ---- 4. dW2^T += relu(h)^T gm (K = pixels, MN-major), DP = dh W1 (A from TMEM)
+        if (tid == 0) {
             umma::fence_after_sync();
+#pragma unroll
+            for (int ks = 0; ks < 16; ++ks)
+                umma::mma_ss(tmem + D::T_ACC2, umma::smem_desc(sRH + ks * 1024, 128 * 128, 512, umma::LAYOUT_SW128_32B),
+                             umma::smem_desc(sG + ks * 1024, 128 * 128, 512, umma::LAYOUT_SW128_32B),
+                             umma::idesc_tf32(128, 16, true, true), started || ks > 0);
+#pragma unroll
+            for (int ks = 0; ks < HID / 8; ++ks)
+                umma::mma_ts(tmem + D::T_P, tmem + D::T_H + ks * 8, umma::smem_desc(sW1T + ks * 2 * D::PIN * 16, D::PIN * 16, 128),
+                             umma::idesc_tf32(128, D::PIN, false, false), ks > 0);
+            umma::commit(bar);
+        }
+        if (!wait_mma())
+            break;
+        // ---- 5. dh -> smem (swizzled, over relu(h)); dW1' += dh^T p'; dp -> dp scratch
+#pragma unroll
+        for (int cc = 0; cc < HID / 16; ++cc) {
+            float d[16];
+            umma::tmem_ld16(lane_base + D::T_H + cc * 16, d);
+            umma::tmem_wait_ld();
+            st_sw32x8(RHDH, cc * 16, tid, 128, d);
+            st_sw32x8(RHDH, cc * 16 + 8, tid, 128, d + 8);
+        }
+        umma::fence_proxy_async();
+        umma::fence_before_sync();
+        __syncthreads();
+        if (tid == 0) {
+            umma::fence_after_sync();
+#pragma unroll
+            for (int ks = 0; ks < 16; ++ks)
+                umma::mma_ss(tmem + D::T_ACC1, umma::smem_desc(sRH + ks * 1024, 128 * 128, 512, umma::LAYOUT_SW128_32B),
+                             umma::smem_desc(sP + ks * 1024, 128 * 128, 512, umma::LAYOUT_SW128_32B),
+                             umma::idesc_tf32(128, D::NPW, true, true), started || ks > 0);
+            umma::commit(bar);
+        }
+        started = true;
+        {
+            float *dpn = a.dp + (size_t)tc.n * D::PIN * plane + (size_t)Y * a.W + X;
 #pragma unroll
             for (int cc = 0; cc < D::PIN / 16; ++cc) {
                 float v[16];
-                umma::tmem_ld16(umma::tmem_addr(tmem, warp, cc * 16), v);
+                umma::tmem_ld16(lane_base + D::T_P + cc * 16, v);
                 umma::tmem_wait_ld();
                 if (valid)
 #pragma unroll
                     for (int e = 0; e < 16; ++e)
                         dpn[(size_t)(cc * 16 + e) * plane] = v[e];
             }
-            umma::fence_before_sync();
-        } else {
-            __syncthreads();
-            // per pixel: h, dh = (W2^T gm) [h > 0], dp = W1^T dh; relu(h) and dh into the transposed buffers
-            float p[D::PIN], gm[C], dpv[D::PIN];
-#pragma unroll
-            for (int f = 0; f < D::PIN; ++f) {
-                p[f] = P[(f / 4) * D::PLANE + tid * 4 + (f % 4)];
-                dpv[f] = 0.f;
-            }
-#pragma unroll
-            for (int c = 0; c < C; ++c)
-                gm[c] = G[(c / 4) * D::PLANE + tid * 4 + (c % 4)];
-            for (int j = 0; j < HID; ++j) {
-                const float *wrow = W1s + j * 4;
-                float h = wrow[(D::PIN / 4) * HID * 4];
-#pragma unroll
-                for (int f = 0; f < D::PIN; ++f)
-                    h = fmaf(wrow[(f / 4) * HID * 4 + (f % 4)], p[f], h);
-                const float *w2c = W2s + (j / 4) * D::CP * 4 + (j % 4);
-                float dh = 0.f;
-#pragma unroll
-                for (int c = 0; c < C; ++c)
-                    dh = fmaf(w2c[c * 4], gm[c], dh);
-                dh = h > 0.f ? dh : 0.f;
-                RHt[j * D::HT + tid] = valid ? fmaxf(h, 0.f) : 0.f;
-                DHt[j * D::HT + tid] = dh;
-#pragma unroll
-                for (int f = 0; f < D::PIN; ++f)
-                    dpv[f] = fmaf(wrow[(f / 4) * HID * 4 + (f % 4)], dh, dpv[f]);
-            }
-            if (valid)
-#pragma unroll
-                for (int f = 0; f < D::PIN; ++f)
-                    dpn[(size_t)f * plane] = dpv[f];
-            __syncthreads();
-            if (tid < HID)  // weight gradients of hidden unit j = tid over the tile's pixels, fixed order
-                for (int q = 0; q < D::TILE; ++q) {
-                    const float dh = DHt[tid * D::HT + q], rh = RHt[tid * D::HT + q];
-#pragma unroll
-                    for (int f = 0; f < D::PIN; ++f)
-                        acc1[f] = fmaf(dh, P[(f / 4) * D::PLANE + q * 4 + (f % 4)], acc1[f]);
-                    accb += dh;
-#pragma unroll
-                    for (int c = 0; c < C; ++c)
-                        acc2[c] = fmaf(G[(c / 4) * D::PLANE + q * 4 + (c % 4)], rh, acc2[c]);
-                }
         }
-        __syncthreads();  // shared buffers and TMEM are reused by the next tile
+        umma::fence_before_sync();
+        if (!wait_mma())  // dW1' done: RHDH / PSW / TMEM are free for the next tile
+            break;
     }
     if (cur_k >= 0 && !failed)
         flush(cur_k);
-    if constexpr (TC) {
-        umma::fence_before_sync();
-        __syncthreads();
-        umma::fence_after_sync();
-        if (warp == 0)
-            umma::tmem_dealloc(tmem, D::BWD_TMEM);
-        if (failed && tid == 0)
-            set_device_error(1);
-    }
+    umma::fence_before_sync();
+    __syncthreads();
+    umma::fence_after_sync();
+    if (warp == 0)
+        umma::tmem_dealloc(tmem, D::BWD_TMEM);
+    if (failed && tid == 0)
+        set_device_error(1);
 }
 
 // gx = gy a + sum_f P_f^T dp_f: the transpose of the circular perception (ncaops/nca_step.cuh:1195-1263), fp32, fixed

@@ -16,16 +16,27 @@ namespace umma {
 
 __device__ __forceinline__ uint32_t smem_u32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
 
-// Shared-memory matrix descriptor (SWIZZLE_NONE, descriptor version 1 for sm_100).
-__device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_bytes)
+// Shared-memory matrix descriptor, descriptor version 1 (sm_100). layout: 0 = no swizzle, 1 = 128-byte swizzle with
+// 32-byte atoms (the only MN-major layout for TF32).
+__device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_bytes, uint32_t layout = 0)
 {
     uint64_t d = 0;
     d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
     d |= (uint64_t)((lbo_bytes >> 4) & 0x3FFFu) << 16;
     d |= (uint64_t)((sbo_bytes >> 4) & 0x3FFFu) << 32;
-    d |= (uint64_t)1 << 46;  // version
-    return d;                // base offset 0, LBO mode 0, layout type 0 (no swizzle)
+    d |= (uint64_t)1 << 46;              // version
+    d |= (uint64_t)(layout & 7u) << 61;  // layout type (base offset 0: swizzled tiles start 1024-byte aligned)
+    return d;
 }
+
+// MN-major TF32 operand in the 128-byte / 32-byte-atom swizzle ("SW128_32B"): rows are K (128 bytes = 32 elements of
+// M or N each), 4-row groups SBO = 512 bytes apart, 32-element MN blocks LBO = K * 128 bytes apart; inside a row the
+// four 32-byte chunks are permuted by XOR with (row % 4). Byte offset of element (mn, k) of a tile with `krows` rows:
+__host__ __device__ __forceinline__ uint32_t sw32_offset(int mn, int k, int krows)
+{
+    return (uint32_t)((mn >> 5) * krows * 128 + k * 128 + ((((mn & 31) >> 3) ^ (k & 3)) << 5) + ((mn & 7) << 2));
+}
+constexpr uint32_t LAYOUT_SW128_32B = 1;
 
 // Instruction descriptor of kind::tf32: D f32, A/B tf32, dense, no negation; a_mn / b_mn select MN-major operands.
 __host__ __device__ constexpr uint32_t idesc_tf32(int M, int N, bool a_mn, bool b_mn)
