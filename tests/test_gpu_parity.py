@@ -145,13 +145,28 @@ def grads_gpu(ops, x, w1, b1, w2, R, rate, growing, fp32, seed):
     return [g.cpu() for g in torch.autograd.grad((out * R.to(DEV)).sum(), params)], out.detach()
 
 
+def unambiguous(x, w1, b1, R, tf32=True, rel_eps=1e-5):
+    """R with zeros at the pixels where some hidden pre-activation lies within fp32 accumulation noise of 0 (relative
+    rel_eps of the largest |h| of its NCA): there two correct fp32 summation orders may take different sides of the
+    ReLU, so those pixels get no upstream gradient and the comparison does not depend on that choice."""
+    K, B, C, H, W = x.shape
+    r = O.tf32_round if tf32 else (lambda t: t)
+    h = r(w1)[:, None] @ r(O.perceive(x)) + b1[:, None, :, None]          # (K, B, HID, HW)
+    scale = h.abs().amax(dim=(1, 2, 3), keepdim=True)
+    amb = (h.abs() < rel_eps * scale).any(dim=2).reshape(K, B, 1, H, W)
+    return R.masked_fill(amb, 0.0), int(amb.sum())
+
+
 @pytest.mark.parametrize('C,HID', SIZES)
 @pytest.mark.parametrize('rate', [0.5, 1.0])
 @pytest.mark.parametrize('growing', [False, True])
 def test_backward_parity(ops, C, HID, rate, growing):
+    worst = {True: 0.0, False: 0.0}
     for K, B, H, W in BWD_SHAPES:
         x, w1, b1, w2 = O.make(K, B, C, HID, H, W, seed=7 + H, growing=growing)
-        R = torch.randn(x.shape, generator=torch.Generator().manual_seed(3))
+        R0 = torch.randn(x.shape, generator=torch.Generator().manual_seed(3))
+        R, n_amb = unambiguous(x, w1, b1, R0)
+        assert n_amb <= 0.05 * K * B * H * W
         mask = O.mask_for(K, B, H, W, 99, rate)
         ref32 = O.step_grads(x, w1, b1, w2, mask, R, growing)
         for fp32 in (True, False):
@@ -164,10 +179,13 @@ def test_backward_parity(ops, C, HID, rate, growing):
             ref = O.step_backward(x, w1, b1, w2, mask, R, growing, tf32=not fp32, alive_mask=alive_mask)
             for a, b, name in zip(got, ref, ('gx', 'dw1', 'db1', 'dw2')):
                 e = O.rel(a, b)
+                worst[fp32] = max(worst[fp32], e)
                 assert e < (1e-5 if fp32 else 1e-3), (name, fp32, (K, B, H, W), e)
             if not fp32:
                 for a, b, name in zip(got, ref32, ('gx', 'dw1', 'db1', 'dw2')):
                     assert O.rel(a, b) < 3e-2, (name, 'vs fp32', (K, B, H, W))
+    print(f'backward {C}/{HID} rate={rate} growing={growing}: worst rel err fp32 {worst[True]:.2e}, '
+          f'tf32 {worst[False]:.2e}')
     assert device_error_clear()
 
 

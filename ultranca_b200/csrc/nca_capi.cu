@@ -19,6 +19,7 @@
 
 #include "nca_kernels.cuh"
 #include "nca_aux.cuh"
+#include "nca_rows.cuh"
 #include "../../include/ultranca_b200.h"
 
 namespace unca {
@@ -100,7 +101,7 @@ const DeviceInfo &device_info()
 std::map<std::pair<const void *, int>, int> g_occupancy;
 
 template <class K>
-int ctas_per_sm(K kernel, size_t smem, int tmem_cols)
+int ctas_per_sm(K kernel, size_t smem, int tmem_cols, int threads = 128)
 {
     const int d = current_device();
     std::lock_guard<std::mutex> lk(g_mutex);
@@ -109,8 +110,11 @@ int ctas_per_sm(K kernel, size_t smem, int tmem_cols)
     if (it != g_occupancy.end())
         return it->second;
     CUDA_OK(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    // the step kernels keep their working set in shared memory / TMEM: ask for the largest shared-memory carveout, so
+    // that the occupancy query and the launch agree on how many CTAs fit
+    CUDA_OK(cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout, 100));
     int b = 0;
-    CUDA_OK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, kernel, 128, smem));
+    CUDA_OK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, kernel, threads, smem));
     if (tmem_cols > 0)
         b = std::min(b, 512 / tmem_cols);
     b = std::max(b, 1);
@@ -128,6 +132,7 @@ void set_smem_once(K kernel, size_t smem)
     if (g_occupancy.count(key))
         return;
     CUDA_OK(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    CUDA_OK(cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout, 100));
     g_occupancy[key] = 1;
 }
 
@@ -210,17 +215,45 @@ int bwd_ctas_per_sm()
     return ctas_per_sm(bwd_kernel_tc<I::C, I::HID, I::GROW>, D::bwd_smem_tc(), D::BWD_TMEM);
 }
 
+// Row-streaming kernels (the benchmark's hot path): TF32 texture NCAs whose rows are whole 16-byte multiples that
+// fit one 128-lane tile; every other case runs the tile kernels.
+constexpr int FWD_ROWS_PARTS = 2, BWD_ROWS_PARTS = 4;
+bool rows_path(const Shape &s, bool fp32, bool growing)
+{
+    return !fp32 && !growing && s.C == 12 && s.HID == 96 && s.W <= 128 && s.W % 4 == 0;
+}
+bool aligned16(const void *p) { return ((uintptr_t)p & 15) == 0; }
+
+int fwd_rows_grid(const Shape &s)
+{
+    using FR = FwdRows<12, 96, FWD_ROWS_PARTS>;
+    const int per = ctas_per_sm(fwd_rows_kernel<12, 96, FWD_ROWS_PARTS>, FR::smem(), FR::TMEM, FR::THREADS);
+    return grid_for(s.N * s.H, per);
+}
+int bwd_rows_grid(const Shape &s)
+{
+    using BR = BwdRows<12, 96, BWD_ROWS_PARTS>;
+    const int per = ctas_per_sm(bwd_rows_kernel<12, 96, BWD_ROWS_PARTS>, BR::smem(), BR::TMEM, BR::THREADS);
+    return grid_for(s.N * s.H, per);
+}
+
 void launch_forward(const float *x, const float *w1, const float *b1, const float *w2, float *y, float *alpha,
                     uint8_t *alive, const Shape &s, uint64_t seed, float rate, bool fp32, bool growing, int64_t n_offset,
                     cudaStream_t stream)
 {
+    StepArgs a{};
+    a.x = x; a.w1 = w1; a.b1 = b1; a.w2 = w2; a.y = y; a.alpha = alpha;
+    a.N = (int)s.N; a.B = (int)s.B; a.H = (int)s.H; a.W = (int)s.W;
+    a.seed = seed; a.rate = rate; a.n_offset = n_offset;
+    if (rows_path(s, fp32, growing) && aligned16(x)) {
+        using FR = FwdRows<12, 96, FWD_ROWS_PARTS>;
+        fwd_rows_kernel<12, 96, FWD_ROWS_PARTS><<<fwd_rows_grid(s), FR::THREADS, FR::smem(), stream>>>(a);
+        CUDA_OK(cudaGetLastError());
+        return;
+    }
     dispatch(s.C, s.HID, fp32, growing, [&](auto I) {
         using II = decltype(I);
         using D = Dims<II::C, II::HID>;
-        StepArgs a{};
-        a.x = x; a.w1 = w1; a.b1 = b1; a.w2 = w2; a.y = y; a.alpha = alpha;
-        a.N = (int)s.N; a.B = (int)s.B; a.H = (int)s.H; a.W = (int)s.W;
-        a.seed = seed; a.rate = rate; a.n_offset = n_offset;
         const TileGeom g = make_geom((int)s.H, (int)s.W);
         const int G = grid_for(s.N * g.tiles_per_image, fwd_ctas_per_sm<II>());
         if (II::FP32)
@@ -251,7 +284,10 @@ BwdWork backward_work(const Shape &s, bool fp32, bool growing)
         const TileGeom g = make_geom((int)s.H, (int)s.W);
         w.grid = grid_for(s.N * g.tiles_per_image, bwd_ctas_per_sm<II>());
         w.dp_floats = s.N * D::PIN * s.H * s.W;
-        w.partial_floats = (int64_t)(w.grid + s.K - 1) * D::PART;
+        int slots = w.grid;
+        if (rows_path(s, fp32, growing))  // either kernel may run (the row kernel needs 16-byte aligned rows)
+            slots = std::max(slots, bwd_rows_grid(s));
+        w.partial_floats = (int64_t)(slots + s.K - 1) * D::PART;
     });
     return w;
 }
@@ -368,24 +404,38 @@ int nca_backward_stages(const float *x, const float *gy, const uint8_t *alive, c
             a.N = (int)N; a.B = (int)batch_per_nca; a.H = (int)H; a.W = (int)W;
             a.seed = seed; a.rate = update_rate; a.n_offset = image_offset;
             const TileGeom g = make_geom((int)H, (int)W);
-            if (stages & NCA_STAGE_MAIN) {
-                if (II::FP32)
-                    bwd_kernel_cc<II::C, II::HID, II::GROW><<<w.grid, 128, D::bwd_smem_cc(), st>>>(a);
-                else
-                    bwd_kernel_tc<II::C, II::HID, II::GROW><<<w.grid, 128, D::bwd_smem_tc(), st>>>(a);
-                CUDA_OK(cudaGetLastError());
-            }
-            if (stages & NCA_STAGE_ADJOINT) {
-                const size_t adj_smem = (size_t)D::PIN * (ADJ_TH + 2) * (ADJ_TW + 2) * sizeof(float);
-                set_smem_once(adjoint_kernel<II::C, II::GROW>, adj_smem);
-                const dim3 agrid((unsigned)(((W + ADJ_TW - 1) / ADJ_TW) * ((H + ADJ_TH - 1) / ADJ_TH)), (unsigned)N);
-                adjoint_kernel<II::C, II::GROW><<<agrid, ADJ_TW * ADJ_TH, adj_smem, st>>>(dp, gy, alive, gx, (int)H, (int)W);
-                CUDA_OK(cudaGetLastError());
+            const bool rows = rows_path(s, fp32, growing) && aligned16(x) && aligned16(gy) && aligned16(gx);
+            int64_t units = N * g.tiles_per_image, units_per_nca = (int64_t)batch_per_nca * g.tiles_per_image;
+            int grid = w.grid;
+            if (rows) {  // one launch: backward + fused adjoint; the dp scratch is not used
+                using BR = BwdRows<12, 96, BWD_ROWS_PARTS>;
+                grid = bwd_rows_grid(s);
+                units = N * H;
+                units_per_nca = (int64_t)batch_per_nca * H;
+                a.gx = gx;
+                if (stages & NCA_STAGE_MAIN) {
+                    bwd_rows_kernel<12, 96, BWD_ROWS_PARTS><<<grid, BR::THREADS, BR::smem(), st>>>(a);
+                    CUDA_OK(cudaGetLastError());
+                }
+            } else {
+                if (stages & NCA_STAGE_MAIN) {
+                    if (II::FP32)
+                        bwd_kernel_cc<II::C, II::HID, II::GROW><<<w.grid, 128, D::bwd_smem_cc(), st>>>(a);
+                    else
+                        bwd_kernel_tc<II::C, II::HID, II::GROW><<<w.grid, 128, D::bwd_smem_tc(), st>>>(a);
+                    CUDA_OK(cudaGetLastError());
+                }
+                if (stages & NCA_STAGE_ADJOINT) {
+                    const size_t adj_smem = (size_t)D::PIN * (ADJ_TH + 2) * (ADJ_TW + 2) * sizeof(float);
+                    set_smem_once(adjoint_kernel<II::C, II::GROW>, adj_smem);
+                    const dim3 agrid((unsigned)(((W + ADJ_TW - 1) / ADJ_TW) * ((H + ADJ_TH - 1) / ADJ_TH)), (unsigned)N);
+                    adjoint_kernel<II::C, II::GROW><<<agrid, ADJ_TW * ADJ_TH, adj_smem, st>>>(dp, gy, alive, gx, (int)H, (int)W);
+                    CUDA_OK(cudaGetLastError());
+                }
             }
             if (stages & NCA_STAGE_REDUCE) {
-                const int64_t T = N * g.tiles_per_image;
                 reduce_kernel<II::C, II::HID><<<dim3((D::PART + 255) / 256, (unsigned)K), 256, 0, st>>>(
-                    partial, T, w.grid, (int64_t)batch_per_nca * g.tiles_per_image, dw1, db1, dw2, accumulate);
+                    partial, units, grid, units_per_nca, dw1, db1, dw2, accumulate);
                 CUDA_OK(cudaGetLastError());
             }
         });

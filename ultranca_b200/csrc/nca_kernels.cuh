@@ -59,6 +59,7 @@ struct StepArgs {
     const float *gy;               // backward
     const uint8_t *alive;          // backward, growing
     float *dp, *partial;           // backward workspaces
+    float *gx;                     // backward output of the row-streaming kernel (adjoint fused)
     int N, B, H, W;
     uint64_t seed;
     float rate;
