@@ -45,6 +45,7 @@ def parse():
     ap.add_argument('--impl', default='ours', choices=['ours', 'reference'])
     ap.add_argument('--no-e2e', action='store_true')
     ap.add_argument('--no-cpu', action='store_true')
+    ap.add_argument('--no-ref-kernels', action='store_true')
     return ap.parse_args()
 
 
@@ -302,7 +303,9 @@ def main():
         ms = float(t.item())
     cells_per_iter = world * K * B * H * W * STEPS
     value = cells_per_iter * args.steps / (ms / 1000.0)
-    launches_per_iter = STEPS * 1 + 2 + STEPS * 3 + 2
+    rows = nca_ops.launch_info(C, HID, False, K * B, H, W, K)['rows_path']
+    # forward 1 / step; backward: fused kernel + reduce (row path) or main + adjoint + reduce; loss 2; optimiser 2
+    launches_per_iter = STEPS * 1 + 2 + STEPS * (2 if rows else 3) + 2
     # roofline of the dominant kernel (the larger total of the forward kernel and the backward main kernel)
     tot = {k: sum(v) for k, v in stage_times.items()}
     dom = max(tot, key=tot.get)
@@ -335,17 +338,68 @@ def main():
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         cpu = cpu_baseline()
+    ref_b200 = None
+    if rank == 0 and world == 1 and not args.no_ref_kernels:
+        ref_b200 = reference_kernels_b200(args, dev)
 
     if rank == 0:
         line = {'metric': METRIC, 'value': value, 'unit': UNIT, 'n_gpus': world, 'steps': args.steps,
                 'warmup': args.warmup, 'ms_per_step': ms / args.steps, 'higher_is_better': True, 'scaling': 'weak',
                 'vs_baseline': None, 'dtype': 'tf32', 'data': 'synthetic', 'config': config(world),
                 'roofline': roofline, 'cpu_baseline': cpu, 'e2e': e2e, 'clocks': clocks.summary(),
-                'gpu_launches': launches_per_iter * args.steps}
+                'gpu_launches': launches_per_iter * args.steps, 'reference_kernels_b200': ref_b200,
+                'launch': nca_ops.launch_info(C, HID, False, K * B, H, W, K)}
         print(json.dumps(line), flush=True)
     if dist is not None:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def reference_kernels_b200(args, dev):
+    """The reference's own CUDA kernels (ncaops/nca_step.cuh compiled for sm_100a, oracle/_ref) on the same workload
+    and GPU: 64 forward launches (states kept, as the reference's autograd saves x), 64 backward launches (pack,
+    backward, adjoint, reduce) and the per-step weight-gradient accumulation autograd performs. A comparison point,
+    not this repository's product; None when oracle/_ref was not built."""
+    from oracle import nca_oracle as O
+    from oracle import ref_kernels as R
+    if not R.available():
+        return None
+    from ultranca_b200 import nca_ops
+    x0, w1, b1, w2, _ = O.make_config_inputs(K_PER_GPU, B, C, HID, H, W, seed=5)
+    x0, w1, b1, w2 = (t.to(dev).contiguous() for t in (x0, w1, b1, w2))
+    states = torch.empty((STEPS + 1,) + tuple(x0.shape), device=dev)
+    gy = torch.randn_like(x0)
+    bwd = R.Backward(K_PER_GPU, B, C, HID, H, W, RATE)
+    outs = [torch.empty_like(x0), torch.empty_like(w1), torch.empty_like(b1), torch.empty_like(w2)]
+    acc = [torch.zeros_like(w1), torch.zeros_like(b1), torch.zeros_like(w2)]
+
+    def it(i):
+        states[0].copy_(x0)
+        for s in range(STEPS):
+            y, _ = R.forward(states[s], w1, b1, w2, RATE, nca_ops.step_seed(i, s))
+            states[s + 1].copy_(y)
+        g = gy
+        for s in reversed(range(STEPS)):
+            gx, dw1, db1, dw2 = bwd(states[s], g, None, w1, b1, w2, nca_ops.step_seed(i, s), out=outs)
+            for a_, d_ in zip(acc, (dw1, db1, dw2)):
+                a_.add_(d_)
+            g = gx.clone()
+
+    for i in range(args.warmup):
+        it(i)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    n_it = max(1, min(args.steps, 5))
+    e0.record()
+    for i in range(n_it):
+        it(100 + i)
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / n_it
+    return {'value': K_PER_GPU * B * H * W * STEPS / (ms / 1000.0), 'unit': UNIT, 'ms_per_step': ms,
+            'note': 'the reference CUDA kernels (ncaops/nca_step.cuh, mma.sync TF32) compiled for sm_100a and run on '
+                    'this B200 on the same 64-step fwd+bwd rollout (1 GPU, without the optimiser step and without '
+                    'Python/autograd overhead), timed with CUDA events'}
 
 
 def run_e2e(args, dev, rank, world, dist, K, w1, b1, w2, target, nca_ops, training):

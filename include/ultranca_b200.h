@@ -114,6 +114,13 @@ int nca_adam_step(float *param0, float *param1, float *param2, const float *grad
                   int64_t numel1, int64_t numel2, int64_t *iteration, float lr, float beta1, float beta2, float eps,
                   float gamma, const int64_t *milestones, int n_milestones, void *stream);
 
+/* Launch configuration the step kernels use for this shape on the current device, into info[0..11]: row-streaming
+ * path (1) or tile path (0), forward grid, forward threads per CTA, backward grid, backward threads per CTA, SM count,
+ * tile-path forward CTAs per SM, tile-path backward grid, and the occupancy query, registers, dynamic shared memory
+ * limit and carveout of the row-streaming forward kernel. Diagnostic; no reference counterpart. */
+int nca_launch_info(int64_t C, int64_t hidden, int fp32, int growing, int64_t N, int64_t H, int64_t W, int64_t K,
+                    int32_t *info);
+
 /* Reads (and, reset = 1, clears) the device error word of the current device: 0, or 1 when a kernel gave up waiting
  * for its tensor-core work (a bounded wait ran out; the kernel returned instead of hanging). Synchronous. */
 int nca_device_error(int *code, int reset);

@@ -42,6 +42,7 @@ SIGNATURES = {
     'nca_adam_step': (c_int, [c_f32p, c_f32p, c_f32p, c_f32p, c_f32p, c_f32p, c_f32p, c_f32p, c_f32p, c_f32p, c_f32p,
                               c_f32p, c_i64, c_i64, c_i64, c_i64, c_vp, c_float, c_float, c_float, c_float, c_float,
                               ctypes.POINTER(c_i64), c_int, c_vp]),
+    'nca_launch_info': (c_int, [c_i64, c_i64, c_int, c_int, c_i64, c_i64, c_i64, c_i64, ctypes.POINTER(ctypes.c_int32)]),
     'nca_device_error': (c_int, [ctypes.POINTER(c_int), c_int]),
     'nca_umma_selftest': (c_int, [c_int, c_int, c_int, c_f32p, c_f32p, c_f32p, c_vp]),
 }

@@ -96,8 +96,12 @@ const DeviceInfo &device_info()
     return di;
 }
 
-// Resident CTAs per SM of `kernel` with `smem` bytes, capped by the Tensor Memory columns each CTA allocates.
-// The dynamic shared memory attribute is set once per (kernel, device).
+// Resident CTAs per SM of `kernel` launched with `threads` threads and `smem` bytes of dynamic shared memory:
+// min over registers (allocated per warp in units of 8 per thread), shared memory (plus the 1 KB the driver reserves
+// per CTA), warps (64 per SM) and Tensor Memory columns (512 per SM). Computed from the kernel's attributes rather
+// than cudaOccupancyMaxActiveBlocksPerMultiprocessor, which answers 1 for these tcgen05 kernels on this driver where
+// the hardware limits (as Nsight Compute reports them) allow more. The step kernels' CTAs never wait on each other,
+// so an over-estimate would only cost a second wave, never a hang. Cached per (kernel, device).
 std::map<std::pair<const void *, int>, int> g_occupancy;
 
 template <class K>
@@ -110,11 +114,18 @@ int ctas_per_sm(K kernel, size_t smem, int tmem_cols, int threads = 128)
     if (it != g_occupancy.end())
         return it->second;
     CUDA_OK(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    // the step kernels keep their working set in shared memory / TMEM: ask for the largest shared-memory carveout, so
-    // that the occupancy query and the launch agree on how many CTAs fit
     CUDA_OK(cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout, 100));
-    int b = 0;
-    CUDA_OK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, kernel, threads, smem));
+    cudaFuncAttributes fa{};
+    CUDA_OK(cudaFuncGetAttributes(&fa, kernel));
+    int smem_sm = 0, regs_sm = 0, warps_sm = 0;
+    CUDA_OK(cudaDeviceGetAttribute(&smem_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, d));
+    CUDA_OK(cudaDeviceGetAttribute(&regs_sm, cudaDevAttrMaxRegistersPerMultiprocessor, d));
+    CUDA_OK(cudaDeviceGetAttribute(&warps_sm, cudaDevAttrMaxThreadsPerMultiProcessor, d));
+    warps_sm /= 32;
+    const int warps = (threads + 31) / 32;
+    const int regs_warp = ((fa.numRegs + 7) / 8) * 8 * 32;
+    int b = std::min(regs_sm / (regs_warp * warps), warps_sm / warps);
+    b = std::min<int>(b, (int)(smem_sm / (smem + fa.sharedSizeBytes + 1024)));
     if (tmem_cols > 0)
         b = std::min(b, 512 / tmem_cols);
     b = std::max(b, 1);
@@ -451,6 +462,43 @@ int nca_backward(const float *x, const float *gy, const uint8_t *alive, const fl
     return nca_backward_stages(x, gy, alive, w1, b1, w2, gx, dw1, db1, dw2, dp, dp_floats, partial, partial_floats, N, C,
                                H, W, K, hidden, batch_per_nca, seed, update_rate, fp32, growing, image_offset, accumulate,
                                NCA_STAGE_MAIN | NCA_STAGE_ADJOINT | NCA_STAGE_REDUCE, stream);
+}
+
+int nca_launch_info(int64_t C, int64_t hidden, int fp32, int growing, int64_t N, int64_t H, int64_t W, int64_t K,
+                    int32_t *info)
+{
+    return guarded([&] {
+        check_ptr(info, "info");
+        const Shape s{N, C, H, W, K, hidden, K > 0 ? N / K : 0};
+        validate(s, growing);
+        const bool rows = rows_path(s, fp32, growing);
+        const BwdWork w = backward_work(s, fp32, growing);
+        int fwd_grid = 0, fwd_per = 0;
+        dispatch(C, hidden, fp32, growing, [&](auto I) {
+            using II = decltype(I);
+            const TileGeom g = make_geom((int)H, (int)W);
+            fwd_per = fwd_ctas_per_sm<II>();
+            fwd_grid = grid_for(N * g.tiles_per_image, fwd_per);
+        });
+        info[0] = rows ? 1 : 0;
+        info[1] = rows ? fwd_rows_grid(s) : fwd_grid;
+        info[2] = rows ? FwdRows<12, 96, FWD_ROWS_PARTS>::THREADS : 128;
+        info[3] = rows ? bwd_rows_grid(s) : w.grid;
+        info[4] = rows ? BwdRows<12, 96, BWD_ROWS_PARTS>::THREADS : 128;
+        info[5] = device_info().sms;
+        info[6] = fwd_per;
+        info[7] = w.grid;
+        // raw occupancy-query results of the row-streaming forward kernel (diagnostic)
+        using FR = FwdRows<12, 96, FWD_ROWS_PARTS>;
+        int b = -1;
+        CUDA_OK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, fwd_rows_kernel<12, 96, FWD_ROWS_PARTS>, FR::THREADS, FR::smem()));
+        info[8] = b;
+        cudaFuncAttributes fa{};
+        CUDA_OK(cudaFuncGetAttributes(&fa, fwd_rows_kernel<12, 96, FWD_ROWS_PARTS>));
+        info[9] = fa.numRegs;
+        info[10] = fa.maxDynamicSharedSizeBytes;
+        info[11] = fa.preferredShmemCarveout;
+    });
 }
 
 int nca_device_error(int *code, int reset)

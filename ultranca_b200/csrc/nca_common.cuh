@@ -48,11 +48,12 @@ __device__ __forceinline__ float update_mask_at(uint64_t seed, float rate, int64
 }
 
 // ---------------------------------------------------------------- TF32
+// Round to TF32 (10 explicit mantissa bits), to nearest with ties away from zero: the result of cvt.rna.tf32.f32 for
+// every finite input, computed with two integer ALU operations instead of the conversion unit (adding half of the
+// dropped 13-bit unit to the magnitude carries exactly when the dropped bits are >= half; the sign is untouched).
 __device__ __forceinline__ float tf32_rna(float v)
 {
-    uint32_t r;
-    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(v));
-    return __uint_as_float(r);
+    return __uint_as_float((__float_as_uint(v) + 0x1000u) & 0xFFFFE000u);
 }
 
 // ---------------------------------------------------------------- perception

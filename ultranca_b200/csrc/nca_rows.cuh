@@ -38,7 +38,8 @@ __device__ __forceinline__ bool next_segment(int64_t &g, int64_t gend, int H, Ro
     return true;
 }
 
-// Waits for ring entries [*waited, upto] (slot = entry % RING, parity bits in *par); false on timeout.
+// Waits for ring entries [*waited, upto] (slot = entry % RING, parity bits in *par); false on timeout. Called by one
+// thread; the barrier that follows publishes the data to the CTA.
 template <int RING>
 __device__ __forceinline__ bool ring_wait(uint64_t *full, int &waited, int upto, uint32_t &par)
 {
@@ -52,6 +53,29 @@ __device__ __forceinline__ bool ring_wait(uint64_t *full, int &waited, int upto,
     return ok;
 }
 
+// Update mask of one image row (global image index n, row Y, W <= 128) by one warp: lane l draws the Philox block of
+// pixels 4l .. 4l + 3 (one call per 4 pixels, as the counter layout intends) and writes mk[x] in {0, 1}.
+__device__ __forceinline__ void row_mask_warp(float *mk, uint64_t seed, float rate, int64_t n, int H, int W, int Y, int lane)
+{
+    const int quads = (W + 3) / 4;
+    if (rate >= 1.f) {
+        for (int x = lane; x < W; x += 32)
+            mk[x] = 1.f;
+        return;
+    }
+    if (lane < quads) {
+        const uint64_t counter = ((uint64_t)n * (uint64_t)H + (uint64_t)Y) * (uint64_t)quads + (uint64_t)lane;
+        const uint4 w = philox4x32_10(seed, counter);
+        const uint32_t words[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const int x = 4 * lane + e;
+            if (x < W)
+                mk[x] = floorf(__fadd_rn(__fmul_rn((float)(words[e] >> 8), 1.0f / 16777216.0f), rate)) != 0.f ? 1.f : 0.f;
+        }
+    }
+}
+
 // ================================================================ forward
 template <int C, int HID, int NPART>
 struct FwdRows {
@@ -60,7 +84,7 @@ struct FwdRows {
     static constexpr int KPAD = ((D::KP + 15) / 16) * 16;
     static constexpr int T_P = 0, T_H = 128, T_U = T_H + HID, TMEM = 256;
     static_assert(C % NPART == 0 && HPP % 8 == 0 && KPAD <= T_H && T_U + 16 <= TMEM, "forward row-kernel layout");
-    static constexpr size_t smem() { return (size_t)(D::W1S + D::W2S + RING * C * 128) * 4 + 8 * (RING + 1) + 16; }
+    static constexpr size_t smem() { return (size_t)(D::W1S + D::W2S + RING * C * 128 + 2 * 128) * 4 + 8 * (RING + 1) + 16; }
 };
 
 template <int C, int HID, int NPART>
@@ -69,18 +93,18 @@ __global__ void __launch_bounds__(128 * NPART, 4 / NPART) fwd_rows_kernel(StepAr
     using F = FwdRows<C, HID, NPART>;
     using D = typename F::D;
     extern __shared__ __align__(128) float smem[];
-    float *W1s = smem, *W2s = W1s + D::W1S, *XR = W2s + D::W2S;
-    uint64_t *xfull = reinterpret_cast<uint64_t *>(XR + F::RING * C * 128), *mbar = xfull + F::RING;
+    float *W1s = smem, *W2s = W1s + D::W1S, *XR = W2s + D::W2S, *MK = XR + F::RING * C * 128;
+    uint64_t *xfull = reinterpret_cast<uint64_t *>(MK + 2 * 128), *mbar = xfull + F::RING;
     uint32_t *tslot = reinterpret_cast<uint32_t *>(mbar + 1);
 
     const int tid = threadIdx.x, warp = tid / 32, part = tid / 128, x = tid % 128;
+    const int lane32 = tid % 32, mask_warp = F::THREADS / 32 - 1;
     const int H = a.H, W = a.W;
     const bool vx = x < W;
     const int xc = vx ? x : 0, xl = xc == 0 ? W - 1 : xc - 1, xr = xc + 1 >= W ? 0 : xc + 1;
     int64_t g0, g1;
     cta_range((int64_t)a.N * H, gridDim.x, blockIdx.x, &g0, &g1);
     const size_t plane = (size_t)H * W;
-    const bool stoch = a.rate < 1.f;
 
     if (tid == 0) {
         for (int i = 0; i < F::RING; ++i)
@@ -106,13 +130,14 @@ __global__ void __launch_bounds__(128 * NPART, 4 / NPART) fwd_rows_kernel(StepAr
     }
     uint32_t xpar = 0, mphase = 0;
     int cur_k = -1;
-    bool failed = false;
+    bool ok = true;
     int64_t g = g0;
     RowSeg sg;
-    while (!failed && next_segment(g, g1, H, sg)) {
+    while (ok && next_segment(g, g1, H, sg)) {
         const int n = sg.n, k = n / a.B, L = sg.r1 - sg.r0;
+        umma::fence_before_sync();
+        __syncthreads();  // the previous segment's ring, mask and TMEM reads are complete
         if (k != cur_k) {
-            __syncthreads();
             stage_weights<D, true>(W1s, W2s, a.w1 + (size_t)k * HID * D::PIN, a.b1 + (size_t)k * HID,
                                    a.w2 + (size_t)k * C * HID);
             umma::fence_proxy_async();
@@ -125,17 +150,20 @@ __global__ void __launch_bounds__(128 * NPART, 4 / NPART) fwd_rows_kernel(StepAr
             for (int c = 0; c < C; ++c)
                 umma::bulk_g2s(XR + ((size_t)slot * C + c) * W, xn + ((size_t)c * H + Y) * W, (uint32_t)(W * 4), &xfull[slot]);
         };
-        __syncthreads();  // previous segment's ring reads and weight staging are complete
         if (tid == 0)
             for (int e = 0; e < min(L + 2, F::RING); ++e)
                 issue(e);
+        if (warp == mask_warp)
+            row_mask_warp(MK, a.seed, a.rate, n + a.n_offset, H, W, sg.r0, lane32);
         int waited = 0;
-        for (int i = 0; i < L; ++i) {
+        for (int i = 0; i < L && ok; ++i) {
             const int Y = sg.r0 + i;
-            if (!__syncthreads_and(ring_wait<F::RING>(xfull, waited, i + 2, xpar))) {
-                failed = true;
+            if (tid == 0)
+                ok = ring_wait<F::RING>(xfull, waited, i + 2, xpar);
+            ok = __syncthreads_and(ok);  // rows Y-1 .. Y+1 and the mask of row Y are in shared memory
+            if (!ok)
                 break;
-            }
+            umma::fence_after_sync();
             const float *rm = XR + (size_t)(i % F::RING) * C * W, *r0 = XR + (size_t)((i + 1) % F::RING) * C * W,
                         *rp = XR + (size_t)((i + 2) % F::RING) * C * W;
 #pragma unroll
@@ -147,9 +175,14 @@ __global__ void __launch_bounds__(128 * NPART, 4 / NPART) fwd_rows_kernel(StepAr
                 const float pv[4] = {tf32_rna(p.x), tf32_rna(p.y), tf32_rna(p.z), tf32_rna(p.w)};
                 umma::tmem_st4(lane + F::T_P + 4 * c, pv);
             }
+            const float m = MK[(i & 1) * 128 + xc];
+            float xv[F::CPP];
+#pragma unroll
+            for (int cc = 0; cc < F::CPP; ++cc)
+                xv[cc] = r0[(part + NPART * cc) * W + xc];
             umma::tmem_wait_st();
             umma::fence_before_sync();
-            __syncthreads();
+            __syncthreads();  // p' complete; row Y-1 (ring entry i) is no longer read
             if (tid == 0) {
                 umma::fence_after_sync();
 #pragma unroll
@@ -158,10 +191,14 @@ __global__ void __launch_bounds__(128 * NPART, 4 / NPART) fwd_rows_kernel(StepAr
                                  umma::smem_desc(umma::smem_u32(W1s) + ks * 2 * HID * 16, HID * 16, 128),
                                  umma::idesc_tf32(128, HID, false, false), ks > 0);
                 umma::commit(mbar);
+                if (i + 4 < L + 2)
+                    issue(i + 4);
+                ok = umma::mbar_wait(mbar, mphase);
             }
-            const float m = (stoch && vx) ? update_mask_at(a.seed, a.rate, n + a.n_offset, H, W, Y, x) : 1.f;
-            bool ok = umma::mbar_wait(mbar, mphase);
             mphase ^= 1;
+            if (warp == mask_warp && i + 1 < L)
+                row_mask_warp(MK + ((i + 1) & 1) * 128, a.seed, a.rate, n + a.n_offset, H, W, Y + 1, lane32);
+            ok = __syncthreads_and(ok);
             umma::fence_after_sync();
 #pragma unroll
             for (int q = 0; q < F::HPP / 8; ++q) {
@@ -175,11 +212,8 @@ __global__ void __launch_bounds__(128 * NPART, 4 / NPART) fwd_rows_kernel(StepAr
             }
             umma::tmem_wait_st();
             umma::fence_before_sync();
-            if (!__syncthreads_and(ok)) {
-                failed = true;
-                break;
-            }
-            if (tid == 0) {
+            __syncthreads();
+            if (tid == 0 && ok) {
                 umma::fence_after_sync();
 #pragma unroll
                 for (int ks = 0; ks < HID / 8; ++ks)
@@ -187,9 +221,10 @@ __global__ void __launch_bounds__(128 * NPART, 4 / NPART) fwd_rows_kernel(StepAr
                                  umma::smem_desc(umma::smem_u32(W2s) + ks * 2 * D::CP * 16, D::CP * 16, 128),
                                  umma::idesc_tf32(128, 16, false, false), ks > 0);
                 umma::commit(mbar);
+                ok = umma::mbar_wait(mbar, mphase);
             }
-            ok = umma::mbar_wait(mbar, mphase);
             mphase ^= 1;
+            ok = __syncthreads_and(ok);
             umma::fence_after_sync();
             float u[16];
             umma::tmem_ld16(lane + F::T_U, u);
@@ -199,17 +234,10 @@ __global__ void __launch_bounds__(128 * NPART, 4 / NPART) fwd_rows_kernel(StepAr
 #pragma unroll
                 for (int cc = 0; cc < F::CPP; ++cc) {
                     const int c = part + NPART * cc;
-                    const float xv = r0[c * W + x];
-                    yn[(size_t)c * plane] = m != 0.f ? xv + u[c] : xv;
+                    yn[(size_t)c * plane] = m != 0.f ? xv[cc] + u[c] : xv[cc];
                 }
             }
-            umma::fence_before_sync();
-            if (!__syncthreads_and(ok)) {  // TMEM and ring slot i % RING are free
-                failed = true;
-                break;
-            }
-            if (tid == 0 && i + 4 < L + 2)
-                issue(i + 4);
+            umma::fence_before_sync();  // the next row's barriers order these TMEM reads before its MMAs
         }
     }
     umma::fence_before_sync();
@@ -217,7 +245,7 @@ __global__ void __launch_bounds__(128 * NPART, 4 / NPART) fwd_rows_kernel(StepAr
     umma::fence_after_sync();
     if (warp == 0)
         umma::tmem_dealloc(tmem, F::TMEM);
-    if (failed && tid == 0)
+    if (!ok && tid == 0)
         set_device_error(1);
 }
 
@@ -225,17 +253,18 @@ __global__ void __launch_bounds__(128 * NPART, 4 / NPART) fwd_rows_kernel(StepAr
 template <int C, int HID, int NPART>
 struct BwdRows {
     using D = Dims<C, HID>;
-    static constexpr int THREADS = 128 * NPART, CPP = C / NPART, HPP = HID / NPART, XRING = 4, GRING = 3;
+    static constexpr int THREADS = 128 * NPART, CPP = C / NPART, HPP = HID / NPART, XRING = 4, GRING = 4;
     static constexpr int KPAD = ((D::KP + 15) / 16) * 16;
     // TMEM: H (then dh) | DHP | p' (then dp) | gm | dW1' | dW2^T
     static constexpr int T_H = 0, T_DHP = 128, T_P = 256, T_G = 256 + KPAD, T_ACC1 = 384, T_ACC2 = 384 + D::NPW, TMEM = 512;
     static_assert(C % NPART == 0 && HPP % 8 == 0 && T_G + 16 <= T_ACC1 && T_ACC2 + 16 <= TMEM, "backward row-kernel layout");
-    // shared memory, 1024-aligned base: weights | RHDH | PSW | GSW (swizzled) | XR | GR | EX | barriers
+    // shared memory, 1024-aligned base: weights | RHDH | PSW | GSW (swizzled) | XR | GR | EX | MK | barriers
     static constexpr size_t OFF_SW = (size_t)D::BWD_W;
     static constexpr size_t OFF_XR = OFF_SW + (size_t)(D::RHDH + D::PSW + D::GSW) * 4;
     static constexpr size_t OFF_GR = OFF_XR + (size_t)XRING * C * 128 * 4;
     static constexpr size_t OFF_EX = OFF_GR + (size_t)GRING * C * 128 * 4;
-    static constexpr size_t OFF_BAR = OFF_EX + (size_t)C * 128 * 16;
+    static constexpr size_t OFF_MK = OFF_EX + (size_t)C * 128 * 16;
+    static constexpr size_t OFF_BAR = OFF_MK + 2 * 128 * 4;
     static constexpr size_t smem() { return 1024 + OFF_BAR + 8 * (XRING + GRING + 2) + 16; }
 };
 
@@ -250,18 +279,19 @@ __global__ void __launch_bounds__(128 * NPART, 1) bwd_rows_kernel(StepArgs a)
     float *RHDH = reinterpret_cast<float *>(base + F::OFF_SW), *PSW = RHDH + D::RHDH, *GSW = PSW + D::PSW;
     float *XR = reinterpret_cast<float *>(base + F::OFF_XR), *GR = reinterpret_cast<float *>(base + F::OFF_GR);
     float4 *EX = reinterpret_cast<float4 *>(base + F::OFF_EX);
+    float *MK = reinterpret_cast<float *>(base + F::OFF_MK);
     uint64_t *xfull = reinterpret_cast<uint64_t *>(base + F::OFF_BAR), *gfull = xfull + F::XRING;
     uint64_t *mbar = gfull + F::GRING, *wbar = mbar + 1;
     uint32_t *tslot = reinterpret_cast<uint32_t *>(wbar + 1);
 
     const int tid = threadIdx.x, warp = tid / 32, part = tid / 128, x = tid % 128;
+    const int lane32 = tid % 32, mask_warp = F::THREADS / 32 - 1;
     const int H = a.H, W = a.W;
     const bool vx = x < W;
     const int xc = vx ? x : 0, xl = xc == 0 ? W - 1 : xc - 1, xr = xc + 1 >= W ? 0 : xc + 1;
     int64_t g0, g1;
     cta_range((int64_t)a.N * H, gridDim.x, blockIdx.x, &g0, &g1);
     const size_t plane = (size_t)H * W;
-    const bool stoch = a.rate < 1.f;
 
     for (int e = tid; e < D::GSW; e += blockDim.x)
         GSW[e] = 0.f;
@@ -299,10 +329,10 @@ __global__ void __launch_bounds__(128 * NPART, 1) bwd_rows_kernel(StepArgs a)
     const uint32_t sW1 = umma::smem_u32(W1s), sW1T = umma::smem_u32(W1T), sW2T = umma::smem_u32(W2T);
     const uint32_t sRH = umma::smem_u32(RHDH), sP = umma::smem_u32(PSW), sG = umma::smem_u32(GSW);
     uint32_t xpar = 0, gpar = 0, mphase = 0, wphase = 0;
-    bool w_pending = false, started = false, failed = false;
+    bool w_pending = false, started = false, ok = true;
     int cur_k = -1;
 
-    auto flush = [&](int k) {  // this CTA's weight gradients of NCA k -> partial slot (blockIdx.x + k)
+    auto flush = [&](int k) {  // this CTA's weight gradients of NCA k -> partial slot (blockIdx.x + k); part 0 only
         if (part != 0)
             return;
         float row[((D::PIN + 1 + 15) / 16) * 16], col[16];
@@ -320,23 +350,25 @@ __global__ void __launch_bounds__(128 * NPART, 1) bwd_rows_kernel(StepArgs a)
         if (x < HID)
             write_partial_row<D>(a.partial + (size_t)(blockIdx.x + k) * D::PART, x, row, row[D::PIN], col);
     };
-    auto wait_w = [&]() {  // the previous row's dW1' (reads RHDH and PSW) has completed
-        bool ok = true;
-        if (w_pending) {
-            ok = umma::mbar_wait(wbar, wphase);
+    auto wait_w = [&]() {  // by thread 0: the last issued dW1' (reads RHDH and PSW) has completed
+        bool r = true;
+        if (w_pending && tid == 0)
+            r = umma::mbar_wait(wbar, wphase);
+        if (w_pending)
             wphase ^= 1;
-            w_pending = false;
-        }
-        return ok;
+        w_pending = false;
+        return r;
     };
 
     int64_t g = g0;
     RowSeg sg;
-    while (!failed && next_segment(g, g1, H, sg)) {
+    while (ok && next_segment(g, g1, H, sg)) {
         const int n = sg.n, k = n / a.B, L = sg.r1 - sg.r0 + 2;  // sequence: halo, owned rows, halo
-        bool ok = wait_w();
+        ok = __syncthreads_and(wait_w());  // previous segment complete (ring, EX, MK reads; dW1')
+        umma::fence_after_sync();
+        if (!ok)
+            break;
         if (k != cur_k) {
-            umma::fence_after_sync();
             if (cur_k >= 0)
                 flush(cur_k);
             umma::fence_before_sync();
@@ -361,58 +393,55 @@ __global__ void __launch_bounds__(128 * NPART, 1) bwd_rows_kernel(StepArgs a)
             for (int c = 0; c < C; ++c)
                 umma::bulk_g2s(GR + ((size_t)slot * C + c) * W, gyn + ((size_t)c * H + Y) * W, (uint32_t)(W * 4), &gfull[slot]);
         };
-        if (!__syncthreads_and(ok)) {
-            failed = true;
-            break;
-        }
         if (tid == 0) {
             for (int e = 0; e < min(L + 2, F::XRING); ++e)
                 issue_x(e);
-            for (int e = 0; e < min(L, F::GRING - 1); ++e)  // entry i + 2 is issued at the end of iteration i
+            for (int e = 0; e < min(L, 2); ++e)  // entry i + 2 is issued during iteration i
                 issue_g(e);
         }
+        if (warp == mask_warp)
+            row_mask_warp(MK, a.seed, a.rate, n + a.n_offset, H, W, wrap_index(sg.r0 - 1, H), lane32);
         int xwaited = 0, gwaited = 0;
         float accm[F::CPP], acc0[F::CPP], accp[F::CPP];
 #pragma unroll
         for (int cc = 0; cc < F::CPP; ++cc)
             accm[cc] = acc0[cc] = accp[cc] = 0.f;
-        for (int i = 0; i < L; ++i) {
+        for (int i = 0; i < L && ok; ++i) {
             const int Y = wrap_index(sg.r0 - 1 + i, H);
             const bool owned = i >= 1 && i <= L - 2;
-            ok = ring_wait<F::XRING>(xfull, xwaited, i + 2, xpar);
-            ok &= ring_wait<F::GRING>(gfull, gwaited, i, gpar);
-            // ---- front end: p' and gm of row Y (this part's channels)
+            // ---- B1: x rows Y-1 .. Y+1, gy row Y, mask of row Y; the previous dW1' has completed
+            if (tid == 0) {
+                ok = ring_wait<F::XRING>(xfull, xwaited, i + 2, xpar);
+                ok &= ring_wait<F::GRING>(gfull, gwaited, i, gpar);
+            }
+            ok &= wait_w();
+            ok = __syncthreads_and(ok);
+            if (!ok)
+                break;
+            umma::fence_after_sync();
+            if (tid == 0 && i + 2 < L)
+                issue_g(i + 2);  // slot of entry i - 2, last read by the finalize of iteration i - 1
             const float *rm = XR + (size_t)(i % F::XRING) * C * W, *r0 = XR + (size_t)((i + 1) % F::XRING) * C * W,
                         *rp = XR + (size_t)((i + 2) % F::XRING) * C * W, *gr = GR + (size_t)(i % F::GRING) * C * W;
-            const float m = (stoch && vx) ? update_mask_at(a.seed, a.rate, n + a.n_offset, H, W, Y, x) : 1.f;
-            float4 pv[F::CPP];
-            float gmv[F::CPP];
+            const float m = MK[(i & 1) * 128 + xc];
 #pragma unroll
             for (int cc = 0; cc < F::CPP; ++cc) {
                 const int c = part + NPART * cc;
                 const float *bm = rm + c * W, *b0 = r0 + c * W, *bp = rp + c * W;
                 const float v[3][3] = {{bm[xl], bm[xc], bm[xr]}, {b0[xl], b0[xc], b0[xr]}, {bp[xl], bp[xc], bp[xr]}};
                 const float4 p = perceive3x3(v);
-                pv[cc] = make_float4(tf32_rna(p.x), tf32_rna(p.y), tf32_rna(p.z), tf32_rna(p.w));
-                gmv[cc] = (vx && m != 0.f) ? tf32_rna(gr[c * W + xc]) : 0.f;
-            }
-            ok &= wait_w();
-#pragma unroll
-            for (int cc = 0; cc < F::CPP; ++cc) {
-                const int c = part + NPART * cc;
-                const float t4[4] = {pv[cc].x, pv[cc].y, pv[cc].z, pv[cc].w};
+                const float4 pv = make_float4(tf32_rna(p.x), tf32_rna(p.y), tf32_rna(p.z), tf32_rna(p.w));
+                const float gmv = (vx && m != 0.f) ? tf32_rna(gr[c * W + xc]) : 0.f;
+                const float t4[4] = {pv.x, pv.y, pv.z, pv.w};
                 umma::tmem_st4(lane + F::T_P + 4 * c, t4);
-                *reinterpret_cast<float4 *>(PSW + umma::sw32_offset(4 * c, x, 128) / 4) = pv[cc];
-                umma::tmem_st1(lane + F::T_G + c, gmv[cc]);
-                GSW[umma::sw32_offset(c, x, 128) / 4] = gmv[cc];
+                *reinterpret_cast<float4 *>(PSW + umma::sw32_offset(4 * c, x, 128) / 4) = pv;
+                umma::tmem_st1(lane + F::T_G + c, gmv);
+                GSW[umma::sw32_offset(c, x, 128) / 4] = gmv;
             }
             umma::tmem_wait_st();
             umma::fence_proxy_async();
             umma::fence_before_sync();
-            if (!__syncthreads_and(ok)) {
-                failed = true;
-                break;
-            }
+            __syncthreads();  // B2: p', gm ready; x row Y-1 (entry i) no longer read
             // ---- H = p' W1'^T, DHP = gm W2 (A from TMEM)
             if (tid == 0) {
                 umma::fence_after_sync();
@@ -425,9 +454,14 @@ __global__ void __launch_bounds__(128 * NPART, 1) bwd_rows_kernel(StepArgs a)
                     umma::mma_ts(tmem + F::T_DHP, tmem + F::T_G + ks * 8, umma::smem_desc(sW2T + ks * 2 * HID * 16, HID * 16, 128),
                                  umma::idesc_tf32(128, HID, false, false), ks > 0);
                 umma::commit(mbar);
+                if (i + 4 < L + 2)
+                    issue_x(i + 4);
+                ok = umma::mbar_wait(mbar, mphase);
             }
-            ok = umma::mbar_wait(mbar, mphase);
             mphase ^= 1;
+            if (warp == mask_warp && i + 1 < L)
+                row_mask_warp(MK + ((i + 1) & 1) * 128, a.seed, a.rate, n + a.n_offset, H, W, wrap_index(Y + 1, H), lane32);
+            ok = __syncthreads_and(ok);  // B3
             umma::fence_after_sync();
             // ---- relu(h) -> RHDH (swizzled), dh -> TMEM (this part's hidden units)
 #pragma unroll
@@ -449,12 +483,9 @@ __global__ void __launch_bounds__(128 * NPART, 1) bwd_rows_kernel(StepArgs a)
             umma::tmem_wait_st();
             umma::fence_proxy_async();
             umma::fence_before_sync();
-            if (!__syncthreads_and(ok)) {
-                failed = true;
-                break;
-            }
+            __syncthreads();  // B4
             // ---- dW2^T += relu(h)^T gm (owned rows), DP = dh W1 (A from TMEM)
-            if (tid == 0) {
+            if (tid == 0 && ok) {
                 umma::fence_after_sync();
                 if (owned)
 #pragma unroll
@@ -467,11 +498,12 @@ __global__ void __launch_bounds__(128 * NPART, 1) bwd_rows_kernel(StepArgs a)
                     umma::mma_ts(tmem + F::T_P, tmem + F::T_H + ks * 8, umma::smem_desc(sW1T + ks * 2 * D::PIN * 16, D::PIN * 16, 128),
                                  umma::idesc_tf32(128, D::PIN, false, false), ks > 0);
                 umma::commit(mbar);
+                ok = umma::mbar_wait(mbar, mphase);
             }
-            ok = umma::mbar_wait(mbar, mphase);
             mphase ^= 1;
+            ok = __syncthreads_and(ok);  // B5
             umma::fence_after_sync();
-            // ---- dh -> RHDH (swizzled, over relu(h)); dW1' += dh^T p' (owned rows)
+            // ---- dh -> RHDH (swizzled, over relu(h)); dp -> exchange buffer
             if (owned) {
 #pragma unroll
                 for (int q = 0; q < F::HPP / 8; ++q) {
@@ -482,26 +514,19 @@ __global__ void __launch_bounds__(128 * NPART, 1) bwd_rows_kernel(StepArgs a)
                     st_sw32x8(RHDH, j0, x, 128, d);
                 }
             }
-            // ---- adjoint: dp of row Y -> contributions to gx rows Y-1, Y, Y+1; exchange (sx, sy, lap) with x -+ 1
             float dpv[F::CPP][4];
 #pragma unroll
-            for (int cc = 0; cc < F::CPP; ++cc) {
-                const int c = part + NPART * cc;
-                umma::tmem_ld4(lane + F::T_P + 4 * c, dpv[cc]);
-            }
+            for (int cc = 0; cc < F::CPP; ++cc)
+                umma::tmem_ld4(lane + F::T_P + 4 * (part + NPART * cc), dpv[cc]);
             umma::tmem_wait_ld();
 #pragma unroll
-            for (int cc = 0; cc < F::CPP; ++cc) {
-                const int c = part + NPART * cc;
-                EX[c * 128 + x] = vx ? make_float4(dpv[cc][1], dpv[cc][2], dpv[cc][3], 0.f) : make_float4(0.f, 0.f, 0.f, 0.f);
-            }
+            for (int cc = 0; cc < F::CPP; ++cc)
+                EX[(part + NPART * cc) * 128 + x] = vx ? make_float4(dpv[cc][1], dpv[cc][2], dpv[cc][3], 0.f)
+                                                      : make_float4(0.f, 0.f, 0.f, 0.f);
             umma::fence_proxy_async();
             umma::fence_before_sync();
-            if (!__syncthreads_and(ok)) {
-                failed = true;
-                break;
-            }
-            if (tid == 0 && owned) {
+            __syncthreads();  // B6: dh (swizzled) and the exchange buffer are complete
+            if (tid == 0 && owned && ok) {
                 umma::fence_after_sync();
 #pragma unroll
                 for (int ks = 0; ks < 16; ++ks)
@@ -514,38 +539,33 @@ __global__ void __launch_bounds__(128 * NPART, 1) bwd_rows_kernel(StepArgs a)
                 w_pending = true;
                 started = true;
             }
-            const int Yprev = wrap_index(Y - 1, H);
+            // ---- adjoint: dp of row Y -> gx rows Y-1, Y, Y+1; row Y-1 is final when owned
+            const bool fin = i >= 2 && vx;
             const float *gprev = GR + (size_t)((i + F::GRING - 1) % F::GRING) * C * W;
+            float *gxrow = gxn + (size_t)wrap_index(Y - 1, H) * W + x;
 #pragma unroll
             for (int cc = 0; cc < F::CPP; ++cc) {
                 const int c = part + NPART * cc;
                 const float4 el = EX[c * 128 + xl], er = EX[c * 128 + xr];
-                const float rsx = el.x - er.x;                                        // horizontal transpose of sobel_x
-                const float rsy = er.y + 2.f * dpv[cc][2] + el.y;                     // ... of sobel_y (smoothing)
-                const float rlap = el.z + 2.f * dpv[cc][3] + er.z;                    // ... of the laplacian
+                const float rsx = el.x - er.x;                     // horizontal transpose of sobel_x
+                const float rsy = er.y + 2.f * dpv[cc][2] + el.y;  // ... of sobel_y (smoothing)
+                const float rlap = el.z + 2.f * dpv[cc][3] + er.z; // ... of the laplacian
                 accm[cc] += rsx - rsy + rlap;
                 acc0[cc] += 2.f * rsx + 2.f * rlap + dpv[cc][0] - 16.f * dpv[cc][3];
                 accp[cc] += rsx + rsy + rlap;
-                if (i >= 2 && i - 1 <= L - 2 && vx)  // row Y-1 is owned and now final
-                    gxn[((size_t)c * H + Yprev) * W + x] = gprev[c * W + x] + accm[cc];
+                if (fin)
+                    gxrow[(size_t)c * plane] = gprev[c * W + x] + accm[cc];
                 accm[cc] = acc0[cc];
                 acc0[cc] = accp[cc];
                 accp[cc] = 0.f;
             }
-            umma::fence_before_sync();
-            __syncthreads();  // TMEM rows, EX and the ring slots of entries i (x) and i - 1 (gy) are free
-            if (tid == 0) {
-                if (i + 4 < L + 2)
-                    issue_x(i + 4);
-                if (i + 2 < L)
-                    issue_g(i + 2);
-            }
+            umma::fence_before_sync();  // the next row's barriers order these TMEM reads before its writes
         }
     }
-    if (!failed) {
-        failed = !__syncthreads_and(wait_w());
+    if (ok) {
+        ok = __syncthreads_and(wait_w());
         umma::fence_after_sync();
-        if (!failed && cur_k >= 0)
+        if (ok && cur_k >= 0)
             flush(cur_k);
     }
     umma::fence_before_sync();
@@ -553,7 +573,7 @@ __global__ void __launch_bounds__(128 * NPART, 1) bwd_rows_kernel(StepArgs a)
     umma::fence_after_sync();
     if (warp == 0)
         umma::tmem_dealloc(tmem, F::TMEM);
-    if (failed && tid == 0)
+    if (!ok && tid == 0)
         set_device_error(1);
 }
 

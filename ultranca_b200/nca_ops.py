@@ -79,6 +79,16 @@ def backward_workspace(C, hidden, fp32, N, H, W, K, update_rate, growing, device
     return dp.value, part.value, chunk.value
 
 
+def launch_info(C, hidden, fp32, N, H, W, K, growing=False, device=None):
+    """The launch configuration of the step kernels for this shape (diagnostic): dict of path, grids, threads."""
+    info = (ctypes.c_int32 * 12)()
+    with torch.cuda.device(device if device is not None else torch.cuda.current_device()):
+        check(lib.nca_launch_info(C, hidden, int(bool(fp32)), int(bool(growing)), N, H, W, K, info))
+    keys = ('rows_path', 'fwd_grid', 'fwd_threads', 'bwd_grid', 'bwd_threads', 'sms', 'tile_fwd_ctas_per_sm',
+            'tile_bwd_grid', 'rows_fwd_occupancy', 'rows_fwd_regs', 'rows_fwd_max_dyn_smem', 'rows_fwd_carveout')
+    return dict(zip(keys, list(info)))
+
+
 def _backward(x, gy, alive, w1, b1, w2, update_rate, seed, fp32, growing, image_offset=0, grads=None):
     K, B, C, H, W, HID = _shapes(x, w1, b1, w2)
     N = K * B
