@@ -310,7 +310,10 @@ def main():
     tot = {k: sum(v) for k, v in stage_times.items()}
     dom = max(tot, key=tot.get)
     avg_ms = statistics.mean(stage_times[dom])
-    alg_bytes = K * B * H * W * 96  # fwd: read x + write y; bwd main: read x + read gy (48 B each per cell)
+    # algorithmic bytes per cell (fp32, 12 channels): forward reads x and writes y (96 B); the fused backward reads x
+    # and gy and writes gx (144 B); the tile-path backward main kernel reads x and gy (96 B)
+    alg_per_cell = 96 if dom == 'fwd' else (144 if rows else 96)
+    alg_bytes = K * B * H * W * alg_per_cell
     peaks = {}
     try:
         peaks = json.load(open(os.path.join(ROOT, 'MEASURED_PEAKS.json')))
@@ -321,11 +324,14 @@ def main():
     traffic = None
     try:
         tr = json.load(open(os.path.join(ROOT, 'profiles', 'traffic.json')))
-        traffic = tr.get({'fwd': 'fwd_kernel', 'bwd_main': 'bwd_kernel'}[dom])
+        traffic = tr.get({'fwd': 'fwd_rows_kernel' if rows else 'fwd_kernel',
+                          'bwd_main': 'bwd_rows_kernel' if rows else 'bwd_kernel_tc'}[dom])
     except (OSError, ValueError):
         pass
     roofline = {'bound': 'hbm', 'achieved': achieved, 'peak': peak, 'unit': 'GB/s', 'frac': achieved / peak,
-                'traffic': traffic, 'kernel': {'fwd': 'fwd_kernel<12,96,TC>', 'bwd_main': 'bwd_kernel<12,96,TC>'}[dom],
+                'traffic': traffic,
+                'kernel': {'fwd': 'fwd_rows_kernel<12,96,2>' if rows else 'fwd_kernel<12,96,TC>',
+                           'bwd_main': 'bwd_rows_kernel<12,96,4>' if rows else 'bwd_kernel_tc<12,96>'}[dom],
                 'algorithmic_bytes_per_launch': alg_bytes, 'avg_launch_ms': avg_ms,
                 'peak_source': 'MEASURED_PEAKS.json hbm_gbs (of measured)' if 'hbm_gbs' in peaks else 'fallback',
                 'stage_ms_per_iteration': {k: v / args.steps for k, v in tot.items()}}

@@ -91,21 +91,21 @@ class RolloutTrainer:
         self.partial = torch.empty(self.partial_floats, device=dev)
         self.opt = FusedAdam((w1, b1, w2), lr=lr, milestones=milestones, gamma=gamma)
 
-    def forward_steps(self, seed):
+    def forward_steps(self, seed, steps=None):
         s = self.states
         st = _stream(s.device)
-        for i in range(self.steps):
+        for i in range(self.steps if steps is None else steps):
             alive = ptr(self.alive[i]) if self.growing else None
             check(lib.nca_forward(ptr(s[i]), ptr(self.w1), ptr(self.b1), ptr(self.w2), ptr(s[i + 1]),
                                   ptr(self.alpha) if self.growing else None, alive, self.N, self.C, self.H, self.W,
                                   self.K, self.HID, self.B, step_seed(seed, i), self.rate, int(self.fp32),
                                   int(self.growing), self.image_offset, st))
 
-    def backward_steps(self, seed, gy_last):
+    def backward_steps(self, seed, gy_last, steps=None):
         s, g = self.states, self.grads
         st = _stream(s.device)
         cur = gy_last
-        for n, i in enumerate(reversed(range(self.steps))):
+        for n, i in enumerate(reversed(range(self.steps if steps is None else steps))):
             nxt = self.gy[1] if cur is self.gy[0] else self.gy[0]
             alive = ptr(self.alive[i]) if self.growing else None
             check(lib.nca_backward(ptr(s[i]), ptr(cur), alive, ptr(self.w1), ptr(self.b1), ptr(self.w2), ptr(nxt),
@@ -116,12 +116,16 @@ class RolloutTrainer:
             cur = nxt
         return cur
 
-    def iteration(self, x0, target, seed):
-        """x0 (K, B, C, H, W) -> per-NCA loss (K,) (device); updates w1, b1, w2 in place. Returns the final state too."""
+    def iteration(self, x0, target, seed, steps=None):
+        """x0 (K, B, C, H, W) -> (per-NCA loss (K,), final state), both on the device; a rollout of `steps` (default:
+        the buffer length) fwd + bwd steps, then the fused optimiser step updates w1, b1, w2 in place."""
+        n = self.steps if steps is None else int(steps)
+        if not 1 <= n <= self.steps:
+            raise ValueError(f'rollout length {n} outside 1..{self.steps}')
         with torch.cuda.device(self.w1.device):
             self.states[0].copy_(x0)
-            self.forward_steps(seed)
-            synthetic_loss(self.states[self.steps], target, self.overflow_weight, self.gy[0], self.loss, self.loss_work)
-            self.backward_steps(seed, self.gy[0])
+            self.forward_steps(seed, n)
+            synthetic_loss(self.states[n], target, self.overflow_weight, self.gy[0], self.loss, self.loss_work)
+            self.backward_steps(seed, self.gy[0], n)
             self.opt.step(self.grads)
-        return self.loss, self.states[self.steps]
+        return self.loss, self.states[n]
