@@ -90,6 +90,23 @@ int nca_backward_stages(const float *x, const float *gy, const uint8_t *alive, c
                         int64_t hidden, uint32_t batch_per_nca, uint64_t seed, float update_rate, int fp32, int growing,
                         int64_t image_offset, int accumulate, int stages, void *stream);
 
+/* nca_backward for the TF32 texture row kernel (C = 12, hidden = 96, W <= 128 and a multiple of 4; x, gy, gx
+ * 16-byte aligned; growing = 0, fp32 = 0) with its scratch held by the library: the weight-gradient partials live in
+ * a file-scope device array of NCA_STATIC_SCRATCH_FLOATS floats (16 MiB) that every device which loads this library
+ * holds until the process exits. For callers that cannot allocate device memory where they run the backward (a
+ * binding that only holds buffers it was handed, or a loop that must not grow the device footprint after set-up);
+ * the call allocates nothing. Needs (backward grid + K - 1) x 5856 floats: larger K is rejected with NCA_ERR_SHAPE
+ * (about 560 NCAs on 148 SMs); other shapes or modes with NCA_ERR_UNSUPPORTED. The first call on a device looks up
+ * the array's address (cudaGetSymbolAddress, which may load the module): make it before any stream capture on that
+ * device. Every call shares the one array and nothing in it needs to start at zero; calls that overlap on the GPU
+ * (other streams, other host threads) race on it and must be serialised by the caller. Outputs and accumulate as
+ * nca_backward. No counterpart in the reference (its backward always takes caller-allocated workspaces). */
+#define NCA_STATIC_SCRATCH_FLOATS (4 * 1024 * 1024)
+int nca_backward_static_scratch(const float *x, const float *gy, const float *w1, const float *b1, const float *w2,
+                                float *gx, float *dw1, float *db1, float *dw2, int64_t N, int64_t C, int64_t H,
+                                int64_t W, int64_t K, int64_t hidden, uint32_t batch_per_nca, uint64_t seed,
+                                float update_rate, int64_t image_offset, int accumulate, void *stream);
+
 /* mask (n, h, w) = the {0, 1} update mask the kernels use for `seed` (Philox4x32-10; image index image_offset + i).
  * Replaces nca_cuda.update_mask (ncaops/nca_cuda.cu:325-331, bound at :351-352). */
 int nca_update_mask(float *mask, int64_t n, int64_t h, int64_t w, uint64_t seed, float update_rate, int64_t image_offset,

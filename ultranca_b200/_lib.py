@@ -36,6 +36,9 @@ SIGNATURES = {
     'nca_backward_stages': (c_int, [c_f32p, c_f32p, c_u8p, c_f32p, c_f32p, c_f32p, c_f32p, c_f32p, c_f32p, c_f32p,
                                     c_f32p, c_i64, c_f32p, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_u32,
                                     c_u64, c_float, c_int, c_int, c_i64, c_int, c_int, c_vp]),
+    'nca_backward_static_scratch': (c_int, [c_f32p, c_f32p, c_f32p, c_f32p, c_f32p, c_f32p, c_f32p, c_f32p, c_f32p,
+                                            c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_u32, c_u64, c_float, c_i64,
+                                            c_int, c_vp]),
     'nca_update_mask': (c_int, [c_f32p, c_i64, c_i64, c_i64, c_u64, c_float, c_i64, c_vp]),
     'nca_synthetic_loss': (c_int, [c_f32p, c_f32p, c_f32p, c_f32p, c_f32p, c_i64, c_i64, c_i64, c_i64, c_i64, c_float,
                                    c_vp]),

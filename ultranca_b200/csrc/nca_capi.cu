@@ -596,3 +596,79 @@ int nca_umma_selftest(int form, int N, int K, const float *A, const float *B, fl
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------- backward with library-owned scratch
+// nca_backward_static_scratch: the row-streaming backward (bwd_rows_kernel + reduce_kernel) with its only scratch, the
+// per-CTA weight-gradient partials, in the file-scope array below instead of a caller-passed workspace. It is for
+// callers that cannot allocate device memory at the point where they run the backward: a host runtime whose memory
+// is owned by another allocator (a foreign-language binding that only holds the buffers it was given), or code that
+// must not grow the device footprint between set-up and the timed or captured loop. The array is part of the loaded
+// module: every device that loads this library holds NCA_STATIC_SCRATCH_FLOATS floats (16 MiB) until the process
+// exits, whether or not the entry point is ever called.
+namespace unca {
+namespace {
+
+static __device__ __align__(256) float g_static_scratch[NCA_STATIC_SCRATCH_FLOATS];
+
+// Device address of g_static_scratch on the current device, looked up once per device (in host code the array's
+// name stands for the symbol, not for a device address). The lookup may load the module on that device, so the
+// first call on a device must come before any stream capture on it.
+float *static_scratch_ptr()
+{
+    const int d = current_device();
+    static std::map<int, float *> ptrs;
+    std::lock_guard<std::mutex> lk(g_mutex);
+    auto it = ptrs.find(d);
+    if (it != ptrs.end())
+        return it->second;
+    float *p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(reinterpret_cast<void **>(&p), g_static_scratch);
+    if (e != cudaSuccess || p == nullptr)
+        fail(NCA_ERR_CUDA, "cudaGetSymbolAddress of the static scratch failed on device %d: %s", d,
+             cudaGetErrorString(e));
+    ptrs[d] = p;
+    return p;
+}
+
+}  // namespace
+}  // namespace unca
+
+extern "C" int nca_backward_static_scratch(const float *x, const float *gy, const float *w1, const float *b1,
+                                           const float *w2, float *gx, float *dw1, float *db1, float *dw2, int64_t N,
+                                           int64_t C, int64_t H, int64_t W, int64_t K, int64_t hidden,
+                                           uint32_t batch_per_nca, uint64_t seed, float update_rate,
+                                           int64_t image_offset, int accumulate, void *stream)
+{
+    return guarded([&] {
+        const Shape s{N, C, H, W, K, hidden, (int64_t)batch_per_nca};
+        validate(s, false);
+        check_ptr(x, "x"); check_ptr(gy, "gy"); check_ptr(w1, "w1"); check_ptr(b1, "b1"); check_ptr(w2, "w2");
+        check_ptr(gx, "gx"); check_ptr(dw1, "dw1"); check_ptr(db1, "db1"); check_ptr(dw2, "dw2");
+        if (!rows_path(s, false, false))
+            fail(NCA_ERR_UNSUPPORTED, "static-scratch backward: only the TF32 texture row kernel (12 channels, hidden 96, "
+                 "W <= 128 and a multiple of 4); got C=%lld hidden=%lld W=%lld", (long long)C, (long long)hidden,
+                 (long long)W);
+        if (!aligned16(x) || !aligned16(gy) || !aligned16(gx))
+            fail(NCA_ERR_ARGUMENT, "static-scratch backward: x, gy and gx must be 16-byte aligned");
+        using D = Dims<12, 96>;
+        using BR = BwdRows<12, 96, BWD_ROWS_PARTS>;
+        const int grid = bwd_rows_grid(s);
+        const int64_t need = (int64_t)(grid + K - 1) * D::PART;
+        if (need > NCA_STATIC_SCRATCH_FLOATS)
+            fail(NCA_ERR_SHAPE, "static-scratch backward: %lld NCAs over %d CTAs need %lld floats of scratch, the static "
+                 "array holds %lld (use nca_backward with a caller-allocated workspace)", (long long)K, grid,
+                 (long long)need, (long long)NCA_STATIC_SCRATCH_FLOATS);
+        float *partial = static_scratch_ptr();
+        const auto st = static_cast<cudaStream_t>(stream);
+        StepArgs a{};
+        a.x = x; a.w1 = w1; a.b1 = b1; a.w2 = w2; a.gy = gy; a.gx = gx; a.partial = partial;
+        a.N = (int)N; a.B = (int)batch_per_nca; a.H = (int)H; a.W = (int)W;
+        a.seed = seed; a.rate = update_rate; a.n_offset = image_offset;
+        // every partial slot the reduction reads is written by the row kernel of the same call: nothing to clear
+        bwd_rows_kernel<12, 96, BWD_ROWS_PARTS><<<grid, BR::THREADS, BR::smem(), st>>>(a);
+        CUDA_OK(cudaGetLastError());
+        reduce_kernel<12, 96><<<dim3((D::PART + 255) / 256, (unsigned)K), 256, 0, st>>>(
+            partial, N * H, grid, (int64_t)batch_per_nca * H, dw1, db1, dw2, accumulate);
+        CUDA_OK(cudaGetLastError());
+    });
+}
