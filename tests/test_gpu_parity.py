@@ -23,7 +23,7 @@ DEV = 'cuda'
 GOLD = os.path.join(os.path.dirname(os.path.abspath(__file__)), 'golden')
 SIZES = ((12, 96), (16, 128))
 FWD_SHAPES = ((3, 2, 128, 128), (2, 3, 37, 50), (1, 1, 8, 16), (3, 2, 80, 80), (17, 2, 129, 65), (1, 1, 6, 200))
-BWD_SHAPES = ((3, 2, 64, 64), (2, 3, 37, 50), (1, 1, 5, 140))
+BWD_SHAPES = ((3, 2, 64, 64), (2, 3, 37, 50), (1, 1, 5, 140), (2, 2, 23, 100), (1, 3, 4, 8))
 
 
 @pytest.fixture(scope='module')

@@ -496,11 +496,11 @@ __global__ void __launch_bounds__(128, 1) bwd_kernel_cc(StepArgs a)
 // W2^T (HID x 16, K-major: B of gm -> dh), all TF32, chunk-planar without swizzle.
 template <class D>
 __device__ __forceinline__ void stage_bwd_weights(float *W1s, float *W1T, float *W2T, const float *w1, const float *b1,
-                                                  const float *w2)
+                                                  const float *w2, int t0 = threadIdx.x, int nt = blockDim.x,
+                                                  int gm_off = 0)
 {
-    float *unused = nullptr;
-    (void)unused;
-    for (int e = threadIdx.x; e < D::HID * D::KP; e += blockDim.x) {
+    // gm_off: W2T's K index of channel 0 (the row kernel keeps gm at feature PIN + 2 of its tensor-memory operand)
+    for (int e = t0; e < D::HID * D::KP; e += nt) {
         const int j = e / D::KP, f = e % D::KP;
         float v = 0.f;
         if (f < D::PIN)
@@ -513,9 +513,9 @@ __device__ __forceinline__ void stage_bwd_weights(float *W1s, float *W1T, float 
         if (f < D::PIN)
             W1T[(j / 4) * D::PIN * 4 + f * 4 + (j % 4)] = v;
     }
-    for (int e = threadIdx.x; e < D::HID * D::CP; e += blockDim.x) {
-        const int j = e / D::CP, c = e % D::CP;
-        W2T[(c / 4) * D::HID * 4 + j * 4 + (c % 4)] = c < D::C ? tf32_rna(w2[c * D::HID + j]) : 0.f;
+    for (int e = t0; e < D::HID * D::CP; e += nt) {
+        const int j = e / D::CP, kk = e % D::CP, c = kk - gm_off;
+        W2T[(kk / 4) * D::HID * 4 + j * 4 + (kk % 4)] = c >= 0 && c < D::C ? tf32_rna(w2[c * D::HID + j]) : 0.f;
     }
 }
 

@@ -250,62 +250,113 @@ __global__ void __launch_bounds__(128 * NPART, 4 / NPART) fwd_rows_kernel(StepAr
 }
 
 // ================================================================ backward with the fused adjoint
+// Eight consecutive values v[0..7] of MN index mn0 (mn0 % 8 == 0) at K row k of a swizzled MN-major tile, as two
+// 16-byte stores whose order alternates with bit 2 of k: a warp's 32 rows then cover all eight 16-byte bank slots of a
+// 128-byte row four times per instruction (the minimum of 4 wavefronts; one fixed order costs 8).
+__device__ __forceinline__ void st_sw32x8_balanced(float *tile, int mn0, int k, int krows, const float *v)
+{
+    float *dst = tile + umma::sw32_offset(mn0, k, krows) / 4;
+    const int flip = (k >> 2) & 1;
+    const float4 lo = make_float4(v[0], v[1], v[2], v[3]), hi = make_float4(v[4], v[5], v[6], v[7]);
+    *reinterpret_cast<float4 *>(dst + 4 * flip) = flip ? hi : lo;
+    *reinterpret_cast<float4 *>(dst + 4 * (1 - flip)) = flip ? lo : hi;
+}
+
+// Named barrier `id` over `count` threads, and the same with an AND over `pred`.
+__device__ __forceinline__ void bar_sync(int id, int count)
+{
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+__device__ __forceinline__ bool bar_and(int id, int count, bool pred)
+{
+    uint32_t r;
+    asm volatile("{\n\t.reg .pred q, r;\n\tsetp.ne.u32 q, %1, 0;\n\tbar.red.and.pred r, %2, %3, q;\n\t"
+                 "selp.u32 %0, 1, 0, r;\n\t}\n"
+                 : "=r"(r)
+                 : "r"((uint32_t)pred), "r"(id), "r"(count)
+                 : "memory");
+    return r != 0;
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar)
+{
+    asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.shared::cta.b64 st, [%0];\n\t}\n" ::"r"(umma::smem_u32(bar))
+                 : "memory");
+}
+
+// Backward, software-pipelined across rows, with the tensor-core work issued by two dedicated warps.
+// Warps 0 .. 4 NPART - 1 compute (NPART parts of 4 warps: part p owns channels [CPP p, CPP (p+1)) and hidden units
+// [HPP p, HPP (p+1)) of pixel x = its TMEM lane); warp W_MMA issues G1 (h = p' W1^T, dhp = W2^T gm) and DP
+// (dp = dh W1); warp W_PROD issues the bulk copies of x rows (one lane per channel) and draws the update masks two
+// rows ahead; warp W_WG issues the weight-gradient group WG and synchronises only through mbarriers, so that its
+// blocking issue never holds up a barrier. Per row i of the band sequence (halo, owned rows, halo):
+//   B_a [G1(i), WG(i-1), x rows of FE(i+1)]  EA(i): relu(h) -> RH, dh -> DH (swizzled smem) and TMEM H
+//   B_b                                      MMA warp: DP(i) -> TMEM P[i%2]; WG warp: WG(i)
+//                                            compute: FE(i+1): p', gm -> TMEM P[(i+1)%2] and PSW[(i+1)%2]
+//   B_c [DP(i)]                              MMA warp: G1(i+1); producer: x row i+4, mask of row i+3
+//                                            compute: dp(i) -> registers -> adjoint -> gx(Y_{i-1}) final
+// WG is one chain of M = 128 (features of PSW: p' 0..PIN-1, the constant 1 at PIN, gm at GM0..GM0+C-1), N = 2 HID
+// (relu(h) | dh), K = 128 pixels: columns [0, HID) of rows GM0.. hold dW2, columns [HID, 2 HID) of rows 0..PIN hold
+// dW1 and db1 (transposed); the other blocks are not used.
 template <int C, int HID, int NPART>
 struct BwdRows {
     using D = Dims<C, HID>;
-    static constexpr int THREADS = 128 * NPART, CPP = C / NPART, HPP = HID / NPART, XRING = 4, GRING = 4;
-    static constexpr int KPAD = ((D::KP + 15) / 16) * 16;
-    // TMEM: H (then dh) | DHP | p' (then dp) | gm | dW1' | dW2^T
-    static constexpr int T_H = 0, T_DHP = 128, T_P = 256, T_G = 256 + KPAD, T_ACC1 = 384, T_ACC2 = 384 + D::NPW, TMEM = 512;
-    static_assert(C % NPART == 0 && HPP % 8 == 0 && T_G + 16 <= T_ACC1 && T_ACC2 + 16 <= TMEM, "backward row-kernel layout");
-    // shared memory, 1024-aligned base: weights | RHDH | PSW | GSW (swizzled) | XR | GR | EX | MK | barriers
-    static constexpr size_t OFF_SW = (size_t)D::BWD_W;
-    static constexpr size_t OFF_XR = OFF_SW + (size_t)(D::RHDH + D::PSW + D::GSW) * 4;
-    static constexpr size_t OFF_GR = OFF_XR + (size_t)XRING * C * 128 * 4;
-    static constexpr size_t OFF_EX = OFF_GR + (size_t)GRING * C * 128 * 4;
-    static constexpr size_t OFF_MK = OFF_EX + (size_t)C * 128 * 16;
+    static constexpr int CW = 128 * NPART, W_MMA = CW / 32, W_PROD = W_MMA + 1, W_WG = W_MMA + 2;
+    static constexpr int THREADS = CW + 96, GROUP = CW + 64;  // GROUP: the warps on named barrier 1 (all but W_WG)
+    static constexpr int CPP = C / NPART, HPP = HID / NPART, XRING = 3, GM0 = D::PIN + 2;
+    // TMEM: h / dh, dhp, WG accumulator, P[2] (p' 0..PIN-1 then dp; 1, 1 at PIN, PIN+1; gm at GM0..; zeros)
+    static constexpr int T_H = 0, T_DHP = HID, T_ACC = 2 * HID, NACC = 2 * HID, T_P0 = T_ACC + NACC, T_P1 = T_P0 + 64;
+    static constexpr int TMEM = 512;
+    static_assert(C % NPART == 0 && HPP % 8 == 0 && D::KP == 56 && GM0 + C <= 62 && T_P1 + 64 <= TMEM &&
+                  HID % 32 == 0 && NACC <= 256 && D::NPW == 64, "backward row-kernel layout");
+    // shared memory, 1024-aligned base: weights | PSW[2] | RH | DH (swizzled MN-major) | XR | EDGE | MK | barriers
+    // (WG reads 4 MN blocks of PSW[b] for M = 128: for b = 1 the last two are RH, in bounds and unused)
+    static constexpr size_t OFF_PSW = (size_t)D::BWD_W;
+    static constexpr size_t OFF_RH = OFF_PSW + (size_t)2 * D::PSW * 4;
+    static constexpr size_t OFF_XR = OFF_RH + (size_t)2 * D::RHDH * 4;
+    static constexpr size_t OFF_EDGE = OFF_XR + (size_t)XRING * C * 128 * 4;
+    static constexpr int EDGE_SLOTS = 9;  // left / right edge lane of each of the 4 warps of a part, and x = W - 1
+    static constexpr size_t OFF_MK = OFF_EDGE + (size_t)EDGE_SLOTS * C * 16;
     static constexpr size_t OFF_BAR = OFF_MK + 2 * 128 * 4;
-    static constexpr size_t smem() { return 1024 + OFF_BAR + 8 * (XRING + GRING + 2) + 16; }
+    static constexpr int NBAR = XRING + 4;  // x ring, g1, dp, wg (tensor-core completions), wg_go (WG may start)
+    static constexpr size_t smem() { return 1024 + OFF_BAR + 8 * NBAR + 16; }
 };
 
 template <int C, int HID, int NPART>
-__global__ void __launch_bounds__(128 * NPART, 1) bwd_rows_kernel(StepArgs a)
+__global__ void __launch_bounds__(128 * NPART + 96, 1) bwd_rows_kernel(StepArgs a)
 {
     using F = BwdRows<C, HID, NPART>;
     using D = typename F::D;
     extern __shared__ __align__(128) unsigned char smem_raw[];
     unsigned char *base = smem_raw + ((1024 - (umma::smem_u32(smem_raw) & 1023)) & 1023);
     float *W1s = reinterpret_cast<float *>(base), *W1T = W1s + D::W1S, *W2T = W1T + D::W1T;
-    float *RHDH = reinterpret_cast<float *>(base + F::OFF_SW), *PSW = RHDH + D::RHDH, *GSW = PSW + D::PSW;
-    float *XR = reinterpret_cast<float *>(base + F::OFF_XR), *GR = reinterpret_cast<float *>(base + F::OFF_GR);
-    float4 *EX = reinterpret_cast<float4 *>(base + F::OFF_EX);
+    float *PSW = reinterpret_cast<float *>(base + F::OFF_PSW), *RH = reinterpret_cast<float *>(base + F::OFF_RH),
+          *DH = RH + D::RHDH;
+    float *XR = reinterpret_cast<float *>(base + F::OFF_XR);
+    float4 *EDGE = reinterpret_cast<float4 *>(base + F::OFF_EDGE);
     float *MK = reinterpret_cast<float *>(base + F::OFF_MK);
-    uint64_t *xfull = reinterpret_cast<uint64_t *>(base + F::OFF_BAR), *gfull = xfull + F::XRING;
-    uint64_t *mbar = gfull + F::GRING, *wbar = mbar + 1;
-    uint32_t *tslot = reinterpret_cast<uint32_t *>(wbar + 1);
+    uint64_t *xfull = reinterpret_cast<uint64_t *>(base + F::OFF_BAR), *g1bar = xfull + F::XRING, *dpbar = g1bar + 1,
+             *wgbar = dpbar + 1, *wggo = wgbar + 1;
+    uint32_t *tslot = reinterpret_cast<uint32_t *>(wggo + 1);
 
-    const int tid = threadIdx.x, warp = tid / 32, part = tid / 128, x = tid % 128;
-    const int lane32 = tid % 32, mask_warp = F::THREADS / 32 - 1;
+    const int tid = threadIdx.x, warp = tid / 32, lane32 = tid % 32;
+    const bool compute = warp < F::W_MMA, mma = warp == F::W_MMA, prod = warp == F::W_PROD;
+    const int part = compute ? tid / 128 : 0, x = tid % 128, wq = warp & 3;
     const int H = a.H, W = a.W;
-    const bool vx = x < W;
-    const int xc = vx ? x : 0, xl = xc == 0 ? W - 1 : xc - 1, xr = xc + 1 >= W ? 0 : xc + 1;
+    const bool vx = compute && x < W;
+    const int xc = x < W ? x : 0, xl = xc == 0 ? W - 1 : xc - 1, xr = xc + 1 >= W ? 0 : xc + 1;
     int64_t g0, g1;
     cta_range((int64_t)a.N * H, gridDim.x, blockIdx.x, &g0, &g1);
     const size_t plane = (size_t)H * W;
 
-    for (int e = tid; e < D::GSW; e += blockDim.x)
-        GSW[e] = 0.f;
-    for (int e = tid; e < 128 * (D::NPW - D::PIN); e += blockDim.x) {  // p' features past the channels: 1, 1, 0...
-        const int q = e / (D::NPW - D::PIN), f = D::PIN + e % (D::NPW - D::PIN);
-        PSW[umma::sw32_offset(f, q, 128) / 4] = f < D::PIN + 2 ? 1.f : 0.f;
+    // constant PSW features of both buffers: 1 at PIN and PIN + 1, 0 at GM0 + C .. 63
+    for (int e = tid; e < 2 * 128 * 64; e += blockDim.x) {
+        const int b = e / (128 * 64), q = (e / 64) % 128, f = e % 64;
+        if (f >= D::PIN && (f < F::GM0 || f >= F::GM0 + C))
+            PSW[b * D::PSW + umma::sw32_offset(f, q, 128) / 4] = f < F::GM0 ? 1.f : 0.f;
     }
     if (tid == 0) {
-        for (int i = 0; i < F::XRING; ++i)
+        for (int i = 0; i < F::NBAR; ++i)
             umma::mbar_init(&xfull[i], 1);
-        for (int i = 0; i < F::GRING; ++i)
-            umma::mbar_init(&gfull[i], 1);
-        umma::mbar_init(mbar, 1);
-        umma::mbar_init(wbar, 1);
         umma::fence_mbar_init();
     }
     if (warp == 0) {
@@ -316,255 +367,332 @@ __global__ void __launch_bounds__(128 * NPART, 1) bwd_rows_kernel(StepArgs a)
     __syncthreads();
     umma::fence_after_sync();
     const uint32_t tmem = *tslot, lane = umma::tmem_addr(tmem, warp, 0);
-    if (part == 0) {  // constant p' columns and zero gm columns in TMEM (never overwritten)
-        float v[8] = {1.f, 1.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-        umma::tmem_st8(lane + F::T_P + D::PIN, v);
-        const float z[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-        for (int c0 = D::PIN + 8; c0 < F::KPAD; c0 += 8)
-            umma::tmem_st8(lane + F::T_P + c0, z);
-        for (int c = C; c < 16; ++c)
-            umma::tmem_st1(lane + F::T_G + c, 0.f);
+    if (compute && part == 0) {  // constant P columns of both buffers: 1, 1 at PIN, PIN + 1; 0 up to 63
+        const float v[8] = {1.f, 1.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f}, z[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        umma::tmem_st8(lane + F::T_P0 + D::PIN, v);
+        umma::tmem_st8(lane + F::T_P0 + D::PIN + 8, z);
+        umma::tmem_st8(lane + F::T_P1 + D::PIN, v);
+        umma::tmem_st8(lane + F::T_P1 + D::PIN + 8, z);
         umma::tmem_wait_st();
     }
-    const uint32_t sW1 = umma::smem_u32(W1s), sW1T = umma::smem_u32(W1T), sW2T = umma::smem_u32(W2T);
-    const uint32_t sRH = umma::smem_u32(RHDH), sP = umma::smem_u32(PSW), sG = umma::smem_u32(GSW);
-    uint32_t xpar = 0, gpar = 0, mphase = 0, wphase = 0;
-    bool w_pending = false, started = false, ok = true;
-    int cur_k = -1;
+    umma::fence_before_sync();
+    __syncthreads();
+    umma::fence_after_sync();
+    bool ok = true;
 
-    auto flush = [&](int k) {  // this CTA's weight gradients of NCA k -> partial slot (blockIdx.x + k); part 0 only
-        if (part != 0)
-            return;
-        float row[((D::PIN + 1 + 15) / 16) * 16], col[16];
-#pragma unroll
-        for (int cc = 0; cc < (D::PIN + 1 + 15) / 16; ++cc) {
-            float v[16];
-            umma::tmem_ld16(lane + F::T_ACC1 + cc * 16, v);
-            umma::tmem_wait_ld();
-#pragma unroll
-            for (int e = 0; e < 16; ++e)
-                row[cc * 16 + e] = v[e];
-        }
-        umma::tmem_ld16(lane + F::T_ACC2, col);
-        umma::tmem_wait_ld();
-        if (x < HID)
-            write_partial_row<D>(a.partial + (size_t)(blockIdx.x + k) * D::PART, x, row, row[D::PIN], col);
-    };
-    auto wait_w = [&]() {  // by thread 0: the last issued dW1' (reads RHDH and PSW) has completed
-        bool r = true;
-        if (w_pending && tid == 0)
-            r = umma::mbar_wait(wbar, wphase);
-        if (w_pending)
-            wphase ^= 1;
-        w_pending = false;
-        return r;
-    };
-
-    int64_t g = g0;
-    RowSeg sg;
-    while (ok && next_segment(g, g1, H, sg)) {
-        const int n = sg.n, k = n / a.B, L = sg.r1 - sg.r0 + 2;  // sequence: halo, owned rows, halo
-        ok = __syncthreads_and(wait_w());  // previous segment complete (ring, EX, MK reads; dW1')
-        umma::fence_after_sync();
-        if (!ok)
-            break;
-        if (k != cur_k) {
-            if (cur_k >= 0)
-                flush(cur_k);
-            umma::fence_before_sync();
-            __syncthreads();
-            stage_bwd_weights<D>(W1s, W1T, W2T, a.w1 + (size_t)k * HID * D::PIN, a.b1 + (size_t)k * HID,
-                                 a.w2 + (size_t)k * C * HID);
-            umma::fence_proxy_async();
-            cur_k = k;
-            started = false;
-        }
-        const float *xn = a.x + (size_t)n * C * plane, *gyn = a.gy + (size_t)n * C * plane;
-        float *gxn = a.gx + (size_t)n * C * plane;
-        auto issue_x = [&](int e) {  // x row wrap(r0 - 2 + e)
-            const int slot = e % F::XRING, Y = wrap_index(sg.r0 - 2 + e, H);
-            umma::mbar_arrive_expect_tx(&xfull[slot], (uint32_t)(C * W * 4));
-            for (int c = 0; c < C; ++c)
-                umma::bulk_g2s(XR + ((size_t)slot * C + c) * W, xn + ((size_t)c * H + Y) * W, (uint32_t)(W * 4), &xfull[slot]);
-        };
-        auto issue_g = [&](int e) {  // gy row wrap(r0 - 1 + e)
-            const int slot = e % F::GRING, Y = wrap_index(sg.r0 - 1 + e, H);
-            umma::mbar_arrive_expect_tx(&gfull[slot], (uint32_t)(C * W * 4));
-            for (int c = 0; c < C; ++c)
-                umma::bulk_g2s(GR + ((size_t)slot * C + c) * W, gyn + ((size_t)c * H + Y) * W, (uint32_t)(W * 4), &gfull[slot]);
-        };
-        if (tid == 0) {
-            for (int e = 0; e < min(L + 2, F::XRING); ++e)
-                issue_x(e);
-            for (int e = 0; e < min(L, 2); ++e)  // entry i + 2 is issued during iteration i
-                issue_g(e);
-        }
-        if (warp == mask_warp)
-            row_mask_warp(MK, a.seed, a.rate, n + a.n_offset, H, W, wrap_index(sg.r0 - 1, H), lane32);
-        int xwaited = 0, gwaited = 0;
-        float accm[F::CPP], acc0[F::CPP], accp[F::CPP];
-#pragma unroll
-        for (int cc = 0; cc < F::CPP; ++cc)
-            accm[cc] = acc0[cc] = accp[cc] = 0.f;
-        for (int i = 0; i < L && ok; ++i) {
-            const int Y = wrap_index(sg.r0 - 1 + i, H);
-            const bool owned = i >= 1 && i <= L - 2;
-            // ---- B1: x rows Y-1 .. Y+1, gy row Y, mask of row Y; the previous dW1' has completed
-            if (tid == 0) {
-                ok = ring_wait<F::XRING>(xfull, xwaited, i + 2, xpar);
-                ok &= ring_wait<F::GRING>(gfull, gwaited, i, gpar);
-            }
-            ok &= wait_w();
-            ok = __syncthreads_and(ok);
-            if (!ok)
-                break;
-            umma::fence_after_sync();
-            if (tid == 0 && i + 2 < L)
-                issue_g(i + 2);  // slot of entry i - 2, last read by the finalize of iteration i - 1
-            const float *rm = XR + (size_t)(i % F::XRING) * C * W, *r0 = XR + (size_t)((i + 1) % F::XRING) * C * W,
-                        *rp = XR + (size_t)((i + 2) % F::XRING) * C * W, *gr = GR + (size_t)(i % F::GRING) * C * W;
-            const float m = MK[(i & 1) * 128 + xc];
-#pragma unroll
-            for (int cc = 0; cc < F::CPP; ++cc) {
-                const int c = part + NPART * cc;
-                const float *bm = rm + c * W, *b0 = r0 + c * W, *bp = rp + c * W;
-                const float v[3][3] = {{bm[xl], bm[xc], bm[xr]}, {b0[xl], b0[xc], b0[xr]}, {bp[xl], bp[xc], bp[xr]}};
-                const float4 p = perceive3x3(v);
-                const float4 pv = make_float4(tf32_rna(p.x), tf32_rna(p.y), tf32_rna(p.z), tf32_rna(p.w));
-                const float gmv = (vx && m != 0.f) ? tf32_rna(gr[c * W + xc]) : 0.f;
-                const float t4[4] = {pv.x, pv.y, pv.z, pv.w};
-                umma::tmem_st4(lane + F::T_P + 4 * c, t4);
-                *reinterpret_cast<float4 *>(PSW + umma::sw32_offset(4 * c, x, 128) / 4) = pv;
-                umma::tmem_st1(lane + F::T_G + c, gmv);
-                GSW[umma::sw32_offset(c, x, 128) / 4] = gmv;
-            }
-            umma::tmem_wait_st();
-            umma::fence_proxy_async();
-            umma::fence_before_sync();
-            __syncthreads();  // B2: p', gm ready; x row Y-1 (entry i) no longer read
-            // ---- H = p' W1'^T, DHP = gm W2 (A from TMEM)
-            if (tid == 0) {
-                umma::fence_after_sync();
-#pragma unroll
-                for (int ks = 0; ks < D::KP / 8; ++ks)
-                    umma::mma_ts(tmem + F::T_H, tmem + F::T_P + ks * 8, umma::smem_desc(sW1 + ks * 2 * HID * 16, HID * 16, 128),
-                                 umma::idesc_tf32(128, HID, false, false), ks > 0);
-#pragma unroll
-                for (int ks = 0; ks < 2; ++ks)
-                    umma::mma_ts(tmem + F::T_DHP, tmem + F::T_G + ks * 8, umma::smem_desc(sW2T + ks * 2 * HID * 16, HID * 16, 128),
-                                 umma::idesc_tf32(128, HID, false, false), ks > 0);
-                umma::commit(mbar);
-                if (i + 4 < L + 2)
-                    issue_x(i + 4);
-                ok = umma::mbar_wait(mbar, mphase);
-            }
-            mphase ^= 1;
-            if (warp == mask_warp && i + 1 < L)
-                row_mask_warp(MK + ((i + 1) & 1) * 128, a.seed, a.rate, n + a.n_offset, H, W, wrap_index(Y + 1, H), lane32);
-            ok = __syncthreads_and(ok);  // B3
-            umma::fence_after_sync();
-            // ---- relu(h) -> RHDH (swizzled), dh -> TMEM (this part's hidden units)
-#pragma unroll
-            for (int q = 0; q < F::HPP / 8; ++q) {
-                const int j0 = part * F::HPP + q * 8;
-                float h[8], d[8];
-                umma::tmem_ld8(lane + F::T_H + j0, h);
-                umma::tmem_ld8(lane + F::T_DHP + j0, d);
-                umma::tmem_wait_ld();
-#pragma unroll
-                for (int e = 0; e < 8; ++e) {
-                    d[e] = h[e] > 0.f ? tf32_rna(d[e]) : 0.f;
-                    h[e] = tf32_rna(fmaxf(h[e], 0.f));
+    if (warp == F::W_WG) {
+        // ---------------- weight-gradient issuer: one WG group per owned row, in the order of the group's rows
+        if (lane32 == 0) {
+            const uint64_t dA0 = umma::smem_desc(umma::smem_u32(PSW), 128 * 128, 512, umma::LAYOUT_SW128_32B);
+            const uint64_t dA1 = umma::smem_desc(umma::smem_u32(PSW + D::PSW), 128 * 128, 512, umma::LAYOUT_SW128_32B);
+            const uint64_t dB = umma::smem_desc(umma::smem_u32(RH), 128 * 128, 512, umma::LAYOUT_SW128_32B);
+            constexpr uint32_t IWG = umma::idesc_tf32(128, F::NACC, true, true);
+            uint32_t goph = 0;
+            int wk = -1, issued = 0;
+            bool started = false;
+            int64_t g = g0;
+            RowSeg sg;
+            while (ok && next_segment(g, g1, H, sg)) {
+                const int k = sg.n / a.B, L = sg.r1 - sg.r0 + 2;
+                if (k != wk) {
+                    wk = k;
+                    started = false;
                 }
-                if (owned)
-                    st_sw32x8(RHDH, j0, x, 128, h);
-                umma::tmem_st8(lane + F::T_H + j0, d);
-            }
-            umma::tmem_wait_st();
-            umma::fence_proxy_async();
-            umma::fence_before_sync();
-            __syncthreads();  // B4
-            // ---- dW2^T += relu(h)^T gm (owned rows), DP = dh W1 (A from TMEM)
-            if (tid == 0 && ok) {
-                umma::fence_after_sync();
-                if (owned)
+                for (int i = 1; i <= L - 2; ++i) {
+                    ok = umma::mbar_wait(wggo, goph);
+                    goph ^= 1;
+                    if (!ok)
+                        break;
+                    umma::fence_after_sync();
+                    const uint64_t dA = (i & 1) ? dA1 : dA0;
 #pragma unroll
                     for (int ks = 0; ks < 16; ++ks)
-                        umma::mma_ss(tmem + F::T_ACC2, umma::smem_desc(sRH + ks * 1024, 128 * 128, 512, umma::LAYOUT_SW128_32B),
-                                     umma::smem_desc(sG + ks * 1024, 128 * 128, 512, umma::LAYOUT_SW128_32B),
-                                     umma::idesc_tf32(128, 16, true, true), started || ks > 0);
-#pragma unroll
-                for (int ks = 0; ks < HID / 8; ++ks)
-                    umma::mma_ts(tmem + F::T_P, tmem + F::T_H + ks * 8, umma::smem_desc(sW1T + ks * 2 * D::PIN * 16, D::PIN * 16, 128),
-                                 umma::idesc_tf32(128, D::PIN, false, false), ks > 0);
-                umma::commit(mbar);
-                ok = umma::mbar_wait(mbar, mphase);
-            }
-            mphase ^= 1;
-            ok = __syncthreads_and(ok);  // B5
-            umma::fence_after_sync();
-            // ---- dh -> RHDH (swizzled, over relu(h)); dp -> exchange buffer
-            if (owned) {
-#pragma unroll
-                for (int q = 0; q < F::HPP / 8; ++q) {
-                    const int j0 = part * F::HPP + q * 8;
-                    float d[8];
-                    umma::tmem_ld8(lane + F::T_H + j0, d);
-                    umma::tmem_wait_ld();
-                    st_sw32x8(RHDH, j0, x, 128, d);
+                        umma::mma_ss(tmem + F::T_ACC, dA + (uint64_t)(ks * 64), dB + (uint64_t)(ks * 64), IWG,
+                                     started || ks > 0);
+                    umma::commit(wgbar);
+                    started = true;
+                    ++issued;
                 }
             }
-            float dpv[F::CPP][4];
-#pragma unroll
-            for (int cc = 0; cc < F::CPP; ++cc)
-                umma::tmem_ld4(lane + F::T_P + 4 * (part + NPART * cc), dpv[cc]);
-            umma::tmem_wait_ld();
-#pragma unroll
-            for (int cc = 0; cc < F::CPP; ++cc)
-                EX[(part + NPART * cc) * 128 + x] = vx ? make_float4(dpv[cc][1], dpv[cc][2], dpv[cc][3], 0.f)
-                                                      : make_float4(0.f, 0.f, 0.f, 0.f);
-            umma::fence_proxy_async();
-            umma::fence_before_sync();
-            __syncthreads();  // B6: dh (swizzled) and the exchange buffer are complete
-            if (tid == 0 && owned && ok) {
-                umma::fence_after_sync();
-#pragma unroll
-                for (int ks = 0; ks < 16; ++ks)
-                    umma::mma_ss(tmem + F::T_ACC1, umma::smem_desc(sRH + ks * 1024, 128 * 128, 512, umma::LAYOUT_SW128_32B),
-                                 umma::smem_desc(sP + ks * 1024, 128 * 128, 512, umma::LAYOUT_SW128_32B),
-                                 umma::idesc_tf32(128, D::NPW, true, true), started || ks > 0);
-                umma::commit(wbar);
-            }
-            if (owned) {
-                w_pending = true;
-                started = true;
-            }
-            // ---- adjoint: dp of row Y -> gx rows Y-1, Y, Y+1; row Y-1 is final when owned
-            const bool fin = i >= 2 && vx;
-            const float *gprev = GR + (size_t)((i + F::GRING - 1) % F::GRING) * C * W;
-            float *gxrow = gxn + (size_t)wrap_index(Y - 1, H) * W + x;
-#pragma unroll
-            for (int cc = 0; cc < F::CPP; ++cc) {
-                const int c = part + NPART * cc;
-                const float4 el = EX[c * 128 + xl], er = EX[c * 128 + xr];
-                const float rsx = el.x - er.x;                     // horizontal transpose of sobel_x
-                const float rsy = er.y + 2.f * dpv[cc][2] + el.y;  // ... of sobel_y (smoothing)
-                const float rlap = el.z + 2.f * dpv[cc][3] + er.z; // ... of the laplacian
-                accm[cc] += rsx - rsy + rlap;
-                acc0[cc] += 2.f * rsx + 2.f * rlap + dpv[cc][0] - 16.f * dpv[cc][3];
-                accp[cc] += rsx + rsy + rlap;
-                if (fin)
-                    gxrow[(size_t)c * plane] = gprev[c * W + x] + accm[cc];
-                accm[cc] = acc0[cc];
-                acc0[cc] = accp[cc];
-                accp[cc] = 0.f;
-            }
-            umma::fence_before_sync();  // the next row's barriers order these TMEM reads before its writes
+            if (issued > 0 && !umma::mbar_wait(wgbar, (uint32_t)((issued - 1) & 1)))  // own MMAs done before teardown
+                ok = false;
         }
-    }
-    if (ok) {
-        ok = __syncthreads_and(wait_w());
-        umma::fence_after_sync();
+    } else {
+        // ---------------- compute, MMA and producer warps (named barrier 1)
+        const uint64_t dW1 = umma::smem_desc(umma::smem_u32(W1s), HID * 16, 128);
+        const uint64_t dW1T = umma::smem_desc(umma::smem_u32(W1T), D::PIN * 16, 128);
+        const uint64_t dW2T = umma::smem_desc(umma::smem_u32(W2T), HID * 16, 128);
+        constexpr uint32_t I1 = umma::idesc_tf32(128, HID, false, false), IP = umma::idesc_tf32(128, D::PIN, false, false);
+        uint32_t xpar = 0, g1ph = 0, dpph = 0, wgph = 0;
+        int cur_k = -1;
+        auto sync = [&]() {
+            umma::fence_before_sync();
+            bar_sync(1, F::GROUP);
+            umma::fence_after_sync();
+        };
+        auto sync_and = [&](bool p) {
+            umma::fence_before_sync();
+            const bool r = bar_and(1, F::GROUP, p);
+            umma::fence_after_sync();
+            return r;
+        };
+        auto flush = [&](int kk) {  // WG accumulator -> partial slot (blockIdx.x + kk); TMEM lanes 0..63 (warps 0, 1)
+            if (!compute || part != 0 || wq >= 2)
+                return;
+            const int f = x;
+            float *out = a.partial + (size_t)(blockIdx.x + kk) * D::PART;
+#pragma unroll 1
+            for (int cc = 0; cc < F::NACC / 16; ++cc) {
+                float v[16];
+                umma::tmem_ld16(lane + F::T_ACC + cc * 16, v);
+                umma::tmem_wait_ld();
+#pragma unroll
+                for (int e = 0; e < 16; ++e) {
+                    const int j = cc * 16 + e;
+                    if (j < HID) {
+                        if (f >= F::GM0 && f < F::GM0 + C)
+                            out[HID * (D::PIN + 1) + (f - F::GM0) * HID + j] = v[e];  // dw2[c][j]
+                    } else if (f < D::PIN) {
+                        out[(j - HID) * D::PIN + f] = v[e];                          // dw1[j][f]
+                    } else if (f == D::PIN) {
+                        out[HID * D::PIN + (j - HID)] = v[e];                        // db1[j]
+                    }
+                }
+            }
+        };
+        auto g1_issue = [&](int bj) {  // G1: h = [p' 1 1 0..] W1ext^T -> H, dhp = [1 1 gm 0 0] W2T' -> DHP
+            const uint32_t tp = tmem + (bj ? F::T_P1 : F::T_P0);
+#pragma unroll
+            for (int ks = 0; ks < D::KP / 8; ++ks)
+                umma::mma_ts(tmem + F::T_H, tp + ks * 8, dW1 + (uint64_t)(ks * 2 * HID), I1, ks > 0);
+#pragma unroll
+            for (int ks = 0; ks < 2; ++ks)
+                umma::mma_ts(tmem + F::T_DHP, tp + D::PIN + ks * 8, dW2T + (uint64_t)(ks * 2 * HID), I1, ks > 0);
+            umma::commit(g1bar);
+        };
+
+        int64_t g = g0;
+        RowSeg sg;
+        while (ok && next_segment(g, g1, H, sg)) {
+            const int n = sg.n, k = n / a.B, L = sg.r1 - sg.r0 + 2;  // sequence: halo, owned rows, halo
+            const float *xn = a.x + (size_t)n * C * plane, *gyn = a.gy + (size_t)n * C * plane;
+            float *gxn = a.gx + (size_t)n * C * plane;
+            auto rowY = [&](int i) { return wrap_index(sg.r0 - 1 + i, H); };
+            auto issue_x = [&](int e) {  // producer warp: x row wrap(r0 - 2 + e) -> slot e % XRING, one lane per channel
+                const int slot = e % F::XRING, Y = wrap_index(sg.r0 - 2 + e, H);
+                if (lane32 == 0)
+                    umma::mbar_arrive_expect_tx(&xfull[slot], (uint32_t)(C * W * 4));
+                __syncwarp();
+                if (lane32 < C)
+                    umma::bulk_g2s(XR + ((size_t)slot * C + lane32) * W, xn + ((size_t)lane32 * H + Y) * W,
+                                   (uint32_t)(W * 4), &xfull[slot]);
+            };
+            auto mask_row = [&](int j) {  // producer warp: update mask of sequence row j -> MK[j % 2]
+                row_mask_warp(MK + (j & 1) * 128, a.seed, a.rate, n + a.n_offset, H, W, rowY(j), lane32);
+            };
+            int xwaited = 0;
+            // ---- segment prologue (every WG of earlier rows completed at the last row's B_a)
+            if (k != cur_k) {
+                if (cur_k >= 0)
+                    flush(cur_k);
+                sync();
+                stage_bwd_weights<D>(W1s, W1T, W2T, a.w1 + (size_t)k * HID * D::PIN, a.b1 + (size_t)k * HID,
+                                     a.w2 + (size_t)k * C * HID, tid, F::GROUP, F::GM0 - D::PIN);
+                umma::fence_proxy_async();
+                cur_k = k;
+            }
+            float gyA[F::CPP];  // gy of the next front end's row
+            if (prod) {
+                for (int e = 0; e < F::XRING; ++e)
+                    issue_x(e);
+                if (lane32 == 0)
+                    ok = ring_wait<F::XRING>(xfull, xwaited, 2, xpar);
+                mask_row(0);
+                mask_row(1);
+            }
+            auto load_gy = [&](int j) {  // gy(Y_j) of this thread's channels (plain loads, used one row later)
+                const float *src = gyn + (size_t)rowY(j) * W + xc;
+#pragma unroll
+                for (int cc = 0; cc < F::CPP; ++cc)
+                    gyA[cc] = __ldg(src + (size_t)(F::CPP * part + cc) * plane);
+            };
+            // front end of sequence row j into buffer bj: p' and gm -> TMEM P[bj] and PSW[bj]
+            auto front_end = [&](int j, int bj) {
+                const float *rm = XR + (size_t)(j % F::XRING) * C * W, *r0 = XR + (size_t)((j + 1) % F::XRING) * C * W,
+                            *rp = XR + (size_t)((j + 2) % F::XRING) * C * W;
+                const float m = MK[(j & 1) * 128 + xc];
+                float *psw = PSW + bj * D::PSW;
+                const uint32_t tp = lane + (bj ? F::T_P1 : F::T_P0);
+#pragma unroll
+                for (int cc = 0; cc < F::CPP; ++cc) {  // warp-uniform channel: tcgen05.st takes one column per warp
+                    const int c = F::CPP * part + cc;
+                    const float *bm = rm + c * W, *b0 = r0 + c * W, *bp = rp + c * W;
+                    const float v[3][3] = {{bm[xl], bm[xc], bm[xr]}, {b0[xl], b0[xc], b0[xr]}, {bp[xl], bp[xc], bp[xr]}};
+                    const float4 p = perceive3x3(v);
+                    const float t4[4] = {tf32_rna(p.x), tf32_rna(p.y), tf32_rna(p.z), tf32_rna(p.w)};
+                    umma::tmem_st4(tp + 4 * c, t4);
+                    *reinterpret_cast<float4 *>(psw + umma::sw32_offset(4 * c, x, 128) / 4) =
+                        make_float4(t4[0], t4[1], t4[2], t4[3]);
+                    const float gmv = (vx && m != 0.f) ? tf32_rna(gyA[cc]) : 0.f;
+                    umma::tmem_st1(tp + F::GM0 + c, gmv);
+                    psw[umma::sw32_offset(F::GM0 + c, x, 128) / 4] = gmv;
+                }
+                umma::tmem_wait_st();
+                umma::fence_proxy_async();
+            };
+            if (compute)
+                load_gy(0);
+            ok = sync_and(ok);
+            if (!ok)
+                break;
+            if (compute) {
+                front_end(0, 0);
+                if (L > 1)
+                    load_gy(1);
+            }
+            sync();
+            if (mma && lane32 == 0)
+                g1_issue(0);
+            if (prod) {
+                if (F::XRING < L + 2)
+                    issue_x(F::XRING);  // into the slot of entry 0, read only by FE(0)
+                if (L > 2)
+                    mask_row(2);
+            }
+            float accm[F::CPP], acc0[F::CPP], accp[F::CPP];
+#pragma unroll
+            for (int cc = 0; cc < F::CPP; ++cc)
+                accm[cc] = acc0[cc] = accp[cc] = 0.f;
+
+            for (int i = 0; i < L; ++i) {
+                const int b = i & 1, Y = rowY(i);
+                const bool owned = i >= 1 && i <= L - 2, next = i + 1 < L, prev_owned = i >= 2;
+                // ---- B_a: G1(i), WG(i-1) complete; x rows of FE(i+1) present
+                if (mma && lane32 == 0) {
+                    ok = umma::mbar_wait(g1bar, g1ph);
+                    if (prev_owned)
+                        ok &= umma::mbar_wait(wgbar, wgph);
+                }
+                if (prod && lane32 == 0 && next)
+                    ok = ring_wait<F::XRING>(xfull, xwaited, i + 3, xpar);
+                g1ph ^= 1;
+                if (prev_owned)
+                    wgph ^= 1;
+                ok = sync_and(ok);
+                if (!ok)
+                    break;
+                // ---- EA(i): relu(h) -> RH, dh -> DH (owned rows) and TMEM H
+                if (compute) {
+#pragma unroll
+                    for (int q = 0; q < F::HPP / 8; ++q) {
+                        const int j0 = part * F::HPP + q * 8;
+                        float h[8], d[8];
+                        umma::tmem_ld8(lane + F::T_H + j0, h);
+                        umma::tmem_ld8(lane + F::T_DHP + j0, d);
+                        umma::tmem_wait_ld();
+#pragma unroll
+                        for (int e = 0; e < 8; ++e) {
+                            d[e] = h[e] > 0.f ? tf32_rna(d[e]) : 0.f;
+                            h[e] = tf32_rna(fmaxf(h[e], 0.f));
+                        }
+                        if (owned) {
+                            st_sw32x8_balanced(RH, j0, x, 128, h);
+                            st_sw32x8_balanced(DH, j0, x, 128, d);
+                        }
+                        umma::tmem_st8(lane + F::T_H + j0, d);
+                    }
+                    umma::tmem_wait_st();
+                    umma::fence_proxy_async();
+                }
+                sync();  // ---- B_b
+                if (mma && lane32 == 0) {  // DP(i): dp = dh W1 -> P[b] columns 0..PIN-1; then let WG(i) start
+                    const uint32_t tp = tmem + (b ? F::T_P1 : F::T_P0);
+#pragma unroll
+                    for (int ks = 0; ks < HID / 8; ++ks)
+                        umma::mma_ts(tp, tmem + F::T_H + ks * 8, dW1T + (uint64_t)(ks * 2 * D::PIN), IP, ks > 0);
+                    umma::commit(dpbar);
+                    if (owned)
+                        mbar_arrive(wggo);
+                }
+                if (compute && next) {
+                    front_end(i + 1, b ^ 1);
+                    if (i + 2 < L)
+                        load_gy(i + 2);
+                }
+                if (mma && lane32 == 0)
+                    ok = umma::mbar_wait(dpbar, dpph);
+                dpph ^= 1;
+                ok = sync_and(ok);  // ---- B_c
+                if (!ok)
+                    break;
+                if (mma && lane32 == 0 && next)
+                    g1_issue(b ^ 1);
+                if (prod) {
+                    if (i + 4 < L + 2)
+                        issue_x(i + 4);  // slot of entry i + 1, last read by FE(i + 1)
+                    if (i + 3 < L)
+                        mask_row(i + 3);
+                }
+                if (compute) {  // ---- adjoint of dp(i): gx rows Y - 1, Y, Y + 1; gx(Y - 1) final
+                    float dpv[F::CPP][4];
+#pragma unroll
+                    for (int cc = 0; cc < F::CPP; ++cc)
+                        umma::tmem_ld4(lane + (b ? F::T_P1 : F::T_P0) + 4 * (F::CPP * part + cc), dpv[cc]);
+                    umma::tmem_wait_ld();
+#pragma unroll
+                    for (int cc = 0; cc < F::CPP; ++cc) {  // edge lanes publish (sobel_x, sobel_y, laplacian) parts
+                        const int c = F::CPP * part + cc;
+                        const float4 t = make_float4(dpv[cc][1], dpv[cc][2], dpv[cc][3], 0.f);
+                        if (lane32 == 0)
+                            EDGE[wq * C + c] = t;
+                        if (lane32 == 31)
+                            EDGE[(4 + wq) * C + c] = t;
+                        if (x == W - 1)
+                            EDGE[8 * C + c] = t;
+                    }
+                    bar_sync(2 + part, 128);
+                    const bool fin = i >= 2 && vx;
+                    const size_t prow = (size_t)wrap_index(Y - 1, H) * W + xc;
+                    float gprev[F::CPP];  // gy of row Y - 1 (read two rows ago by its front end: an L2 hit)
+#pragma unroll
+                    for (int cc = 0; cc < F::CPP; ++cc)
+                        gprev[cc] = fin ? __ldg(gyn + prow + (size_t)(F::CPP * part + cc) * plane) : 0.f;
+#pragma unroll
+                    for (int cc = 0; cc < F::CPP; ++cc) {
+                        const int c = F::CPP * part + cc;
+                        // neighbours x - 1 and x + 1 (circular in the row): shuffles in the warp, edge slots across warps
+                        float lx = __shfl_up_sync(~0u, dpv[cc][1], 1), ly = __shfl_up_sync(~0u, dpv[cc][2], 1),
+                              lz = __shfl_up_sync(~0u, dpv[cc][3], 1);
+                        float rx = __shfl_down_sync(~0u, dpv[cc][1], 1), ry = __shfl_down_sync(~0u, dpv[cc][2], 1),
+                              rz = __shfl_down_sync(~0u, dpv[cc][3], 1);
+                        if (lane32 == 0 || x == 0) {
+                            const float4 e = x == 0 ? EDGE[8 * C + c] : EDGE[(4 + wq - 1) * C + c];
+                            lx = e.x;
+                            ly = e.y;
+                            lz = e.z;
+                        }
+                        if (lane32 == 31 || x == W - 1) {
+                            const float4 e = x == W - 1 ? EDGE[c] : EDGE[(wq + 1) * C + c];
+                            rx = e.x;
+                            ry = e.y;
+                            rz = e.z;
+                        }
+                        const float rsx = lx - rx;                      // horizontal transpose of sobel_x
+                        const float rsy = ry + 2.f * dpv[cc][2] + ly;   // ... of sobel_y (smoothing)
+                        const float rlap = lz + 2.f * dpv[cc][3] + rz;  // ... of the laplacian
+                        accm[cc] += rsx - rsy + rlap;
+                        acc0[cc] += 2.f * rsx + 2.f * rlap + dpv[cc][0] - 16.f * dpv[cc][3];
+                        accp[cc] += rsx + rsy + rlap;
+                        if (fin)
+                            gxn[prow + (size_t)c * plane] = gprev[cc] + accm[cc];
+                        accm[cc] = acc0[cc];
+                        acc0[cc] = accp[cc];
+                        accp[cc] = 0.f;
+                    }
+                    umma::fence_before_sync();
+                }
+            }
+        }
         if (ok && cur_k >= 0)
             flush(cur_k);
     }
@@ -573,7 +701,7 @@ __global__ void __launch_bounds__(128 * NPART, 1) bwd_rows_kernel(StepArgs a)
     umma::fence_after_sync();
     if (warp == 0)
         umma::tmem_dealloc(tmem, F::TMEM);
-    if (!ok && tid == 0)
+    if (!ok)
         set_device_error(1);
 }
 
