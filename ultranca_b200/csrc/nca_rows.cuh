@@ -55,12 +55,13 @@ __device__ __forceinline__ bool ring_wait(uint64_t *full, int &waited, int upto,
 
 // Update mask of one image row (global image index n, row Y, W <= 128) by one warp: lane l draws the Philox block of
 // pixels 4l .. 4l + 3 (one call per 4 pixels, as the counter layout intends) and writes mk[x] in {0, 1}.
-__device__ __forceinline__ void row_mask_warp(float *mk, uint64_t seed, float rate, int64_t n, int H, int W, int Y, int lane)
+template <class T>
+__device__ __forceinline__ void row_mask_warp(T *mk, uint64_t seed, float rate, int64_t n, int H, int W, int Y, int lane)
 {
     const int quads = (W + 3) / 4;
     if (rate >= 1.f) {
         for (int x = lane; x < W; x += 32)
-            mk[x] = 1.f;
+            mk[x] = T(1);
         return;
     }
     if (lane < quads) {
@@ -71,7 +72,7 @@ __device__ __forceinline__ void row_mask_warp(float *mk, uint64_t seed, float ra
         for (int e = 0; e < 4; ++e) {
             const int x = 4 * lane + e;
             if (x < W)
-                mk[x] = floorf(__fadd_rn(__fmul_rn((float)(words[e] >> 8), 1.0f / 16777216.0f), rate)) != 0.f ? 1.f : 0.f;
+                mk[x] = floorf(__fadd_rn(__fmul_rn((float)(words[e] >> 8), 1.0f / 16777216.0f), rate)) != 0.f ? T(1) : T(0);
         }
     }
 }
@@ -283,17 +284,42 @@ __device__ __forceinline__ void mbar_arrive(uint64_t *bar)
                  : "memory");
 }
 
-// Backward, software-pipelined across rows, with the tensor-core work issued by two dedicated warps.
-// Warps 0 .. 4 NPART - 1 compute (NPART parts of 4 warps: part p owns channels [CPP p, CPP (p+1)) and hidden units
-// [HPP p, HPP (p+1)) of pixel x = its TMEM lane); warp W_MMA issues G1 (h = p' W1^T, dhp = W2^T gm) and DP
+// Bounded mbarrier wait that gives up early once any warp of the CTA has given up (abort != 0), and sets abort when
+// its own 2 s limit runs out: after a failure every warp keeps its loop and barrier sequence (so no named barrier is
+// left short of a participant) while its remaining waits return at once.
+__device__ __forceinline__ bool wait_bar(uint64_t *bar, uint32_t parity, volatile uint32_t *abort)
+{
+    if (*abort)
+        return false;
+    if (umma::mbar_try_wait(bar, parity))
+        return true;
+    uint64_t t0;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+    while (true) {
+        if (umma::mbar_try_wait(bar, parity))
+            return true;
+        if (*abort)
+            return false;
+        uint64_t t;
+        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+        if (t - t0 > 2000000000ull) {
+            *abort = 1;
+            return false;
+        }
+    }
+}
+
+// Backward, software-pipelined across rows, with the warps synchronised by mbarriers only (no CTA-wide barrier per
+// row). Warps 0 .. 4 NPART - 1 compute (NPART parts of 4 warps: part p owns channels [CPP p, CPP (p+1)) and hidden
+// units [HPP p, HPP (p+1)) of pixel x = its TMEM lane); warp W_MMA issues G1 (h = p' W1^T, dhp = W2^T gm) and DP
 // (dp = dh W1); warp W_PROD issues the bulk copies of x rows (one lane per channel) and draws the update masks two
-// rows ahead; warp W_WG issues the weight-gradient group WG and synchronises only through mbarriers, so that its
-// blocking issue never holds up a barrier. Per row i of the band sequence (halo, owned rows, halo):
-//   B_a [G1(i), WG(i-1), x rows of FE(i+1)]  EA(i): relu(h) -> RH, dh -> DH (swizzled smem) and TMEM H
-//   B_b                                      MMA warp: DP(i) -> TMEM P[i%2]; WG warp: WG(i)
-//                                            compute: FE(i+1): p', gm -> TMEM P[(i+1)%2] and PSW[(i+1)%2]
-//   B_c [DP(i)]                              MMA warp: G1(i+1); producer: x row i+4, mask of row i+3
-//                                            compute: dp(i) -> registers -> adjoint -> gx(Y_{i-1}) final
+// rows ahead; warp W_WG issues the weight-gradient group WG. Per row i of the band
+// sequence (halo, owned rows, halo), each compute warp runs
+//   EA(i)   [G1(i), WG(i-1)]   relu(h) -> RH, dh -> DH (owned rows, swizzled smem) and TMEM H   -> ea_done
+//   FE(i+1) [x rows, mask]     p', gm -> TMEM P[(i+1)%2] and PSW[(i+1)%2]                      -> fe_done
+//   ADJ(i)  [DP(i)]            dp(i) -> adjoint (edge lanes exchanged per part) -> gx(Y_{i-1}) final
+// while the MMA warp issues DP(i) after ea_done(i) (then lets WG(i) start) and G1(i+1) after fe_done(i+1) and DP(i),
+// and the producer, after fe_done(j), refills the x slot of row j and draws the mask of row j + 2.
 // WG is one chain of M = 128 (features of PSW: p' 0..PIN-1, the constant 1 at PIN, gm at GM0..GM0+C-1), N = 2 HID
 // (relu(h) | dh), K = 128 pixels: columns [0, HID) of rows GM0.. hold dW2, columns [HID, 2 HID) of rows 0..PIN hold
 // dW1 and db1 (transposed); the other blocks are not used.
@@ -308,17 +334,19 @@ struct BwdRows {
     static constexpr int TMEM = 512;
     static_assert(C % NPART == 0 && HPP % 8 == 0 && D::KP == 56 && GM0 + C <= 62 && T_P1 + 64 <= TMEM &&
                   HID % 32 == 0 && NACC <= 256 && D::NPW == 64, "backward row-kernel layout");
-    // shared memory, 1024-aligned base: weights | PSW[2] | RH | DH (swizzled MN-major) | XR | EDGE | MK | barriers
+    // shared memory, 1024-aligned base: weights | PSW[2] | RH | DH (swizzled MN-major) | XR | EDGE[2] | MK[2] | bars
     // (WG reads 4 MN blocks of PSW[b] for M = 128: for b = 1 the last two are RH, in bounds and unused)
     static constexpr size_t OFF_PSW = (size_t)D::BWD_W;
     static constexpr size_t OFF_RH = OFF_PSW + (size_t)2 * D::PSW * 4;
     static constexpr size_t OFF_XR = OFF_RH + (size_t)2 * D::RHDH * 4;
     static constexpr size_t OFF_EDGE = OFF_XR + (size_t)XRING * C * 128 * 4;
     static constexpr int EDGE_SLOTS = 9;  // left / right edge lane of each of the 4 warps of a part, and x = W - 1
-    static constexpr size_t OFF_MK = OFF_EDGE + (size_t)EDGE_SLOTS * C * 16;
-    static constexpr size_t OFF_BAR = OFF_MK + 2 * 128 * 4;
-    static constexpr int NBAR = XRING + 4;  // x ring, g1, dp, wg (tensor-core completions), wg_go (WG may start)
+    static constexpr size_t OFF_MK = OFF_EDGE + (size_t)2 * EDGE_SLOTS * C * 3 * 4;
+    static constexpr size_t OFF_BAR = OFF_MK + 2 * 128;
+    // x ring, mask buffers, g1, dp, wg (tensor-core completions), wg_go, ea_done, fe_done (one arrival per warp)
+    static constexpr int NBAR = XRING + 8;
     static constexpr size_t smem() { return 1024 + OFF_BAR + 8 * NBAR + 16; }
+    static_assert(OFF_BAR % 8 == 0, "mbarrier alignment");
 };
 
 template <int C, int HID, int NPART>
@@ -332,11 +360,12 @@ __global__ void __launch_bounds__(128 * NPART + 96, 1) bwd_rows_kernel(StepArgs 
     float *PSW = reinterpret_cast<float *>(base + F::OFF_PSW), *RH = reinterpret_cast<float *>(base + F::OFF_RH),
           *DH = RH + D::RHDH;
     float *XR = reinterpret_cast<float *>(base + F::OFF_XR);
-    float4 *EDGE = reinterpret_cast<float4 *>(base + F::OFF_EDGE);
-    float *MK = reinterpret_cast<float *>(base + F::OFF_MK);
+    float *EDGE = reinterpret_cast<float *>(base + F::OFF_EDGE);
+    uint8_t *MK = base + F::OFF_MK;
     uint64_t *xfull = reinterpret_cast<uint64_t *>(base + F::OFF_BAR), *g1bar = xfull + F::XRING, *dpbar = g1bar + 1,
-             *wgbar = dpbar + 1, *wggo = wgbar + 1;
-    uint32_t *tslot = reinterpret_cast<uint32_t *>(wggo + 1);
+             *wgbar = dpbar + 1, *wggo = wgbar + 1, *ea_done = wggo + 1, *fe_done = ea_done + 1, *mkfull = fe_done + 1;
+    uint32_t *tslot = reinterpret_cast<uint32_t *>(mkfull + 2);
+    volatile uint32_t *abort = tslot + 1;
 
     const int tid = threadIdx.x, warp = tid / 32, lane32 = tid % 32;
     const bool compute = warp < F::W_MMA, mma = warp == F::W_MMA, prod = warp == F::W_PROD;
@@ -355,8 +384,17 @@ __global__ void __launch_bounds__(128 * NPART + 96, 1) bwd_rows_kernel(StepArgs 
             PSW[b * D::PSW + umma::sw32_offset(f, q, 128) / 4] = f < F::GM0 ? 1.f : 0.f;
     }
     if (tid == 0) {
-        for (int i = 0; i < F::NBAR; ++i)
+        for (int i = 0; i < F::XRING; ++i)
             umma::mbar_init(&xfull[i], 1);
+        umma::mbar_init(&mkfull[0], 1);
+        umma::mbar_init(&mkfull[1], 1);
+        umma::mbar_init(g1bar, 1);
+        umma::mbar_init(dpbar, 1);
+        umma::mbar_init(wgbar, 1);
+        umma::mbar_init(wggo, 1);
+        umma::mbar_init(ea_done, F::W_MMA);
+        umma::mbar_init(fe_done, F::W_MMA);
+        *abort = 0;
         umma::fence_mbar_init();
     }
     if (warp == 0) {
@@ -381,7 +419,7 @@ __global__ void __launch_bounds__(128 * NPART + 96, 1) bwd_rows_kernel(StepArgs 
     bool ok = true;
 
     if (warp == F::W_WG) {
-        // ---------------- weight-gradient issuer: one WG group per owned row, in the order of the group's rows
+        // ---------------- weight-gradient issuer: one WG group per owned row, in the order of the rows
         if (lane32 == 0) {
             const uint64_t dA0 = umma::smem_desc(umma::smem_u32(PSW), 128 * 128, 512, umma::LAYOUT_SW128_32B);
             const uint64_t dA1 = umma::smem_desc(umma::smem_u32(PSW + D::PSW), 128 * 128, 512, umma::LAYOUT_SW128_32B);
@@ -392,17 +430,17 @@ __global__ void __launch_bounds__(128 * NPART + 96, 1) bwd_rows_kernel(StepArgs 
             bool started = false;
             int64_t g = g0;
             RowSeg sg;
-            while (ok && next_segment(g, g1, H, sg)) {
+            while (next_segment(g, g1, H, sg)) {
                 const int k = sg.n / a.B, L = sg.r1 - sg.r0 + 2;
                 if (k != wk) {
                     wk = k;
                     started = false;
                 }
                 for (int i = 1; i <= L - 2; ++i) {
-                    ok = umma::mbar_wait(wggo, goph);
+                    ok &= wait_bar(wggo, goph, abort);
                     goph ^= 1;
                     if (!ok)
-                        break;
+                        continue;
                     umma::fence_after_sync();
                     const uint64_t dA = (i & 1) ? dA1 : dA0;
 #pragma unroll
@@ -414,27 +452,27 @@ __global__ void __launch_bounds__(128 * NPART + 96, 1) bwd_rows_kernel(StepArgs 
                     ++issued;
                 }
             }
-            if (issued > 0 && !umma::mbar_wait(wgbar, (uint32_t)((issued - 1) & 1)))  // own MMAs done before teardown
-                ok = false;
+            if (issued > 0)  // this warp's MMAs are complete before the teardown
+                umma::mbar_wait(wgbar, (uint32_t)((issued - 1) & 1));
         }
     } else {
-        // ---------------- compute, MMA and producer warps (named barrier 1)
+        // ---------------- compute, MMA and producer warps
         const uint64_t dW1 = umma::smem_desc(umma::smem_u32(W1s), HID * 16, 128);
         const uint64_t dW1T = umma::smem_desc(umma::smem_u32(W1T), D::PIN * 16, 128);
         const uint64_t dW2T = umma::smem_desc(umma::smem_u32(W2T), HID * 16, 128);
         constexpr uint32_t I1 = umma::idesc_tf32(128, HID, false, false), IP = umma::idesc_tf32(128, D::PIN, false, false);
-        uint32_t xpar = 0, g1ph = 0, dpph = 0, wgph = 0;
-        int cur_k = -1;
-        auto sync = [&]() {
+        uint32_t xpar = 0, mkpar = 0, g1ph = 0, dpph = 0, wgph = 0, eaph = 0, feph = 0;
+        int cur_k = -1, g1_issued = 0, dp_issued = 0, x_issued[F::XRING] = {0, 0, 0};
+        auto group_sync = [&]() {
             umma::fence_before_sync();
             bar_sync(1, F::GROUP);
             umma::fence_after_sync();
         };
-        auto sync_and = [&](bool p) {
+        auto signal = [&](uint64_t *bar) {  // this warp's TMEM and shared-memory writes are complete
             umma::fence_before_sync();
-            const bool r = bar_and(1, F::GROUP, p);
-            umma::fence_after_sync();
-            return r;
+            __syncwarp();
+            if (lane32 == 0)
+                mbar_arrive(bar);
         };
         auto flush = [&](int kk) {  // WG accumulator -> partial slot (blockIdx.x + kk); TMEM lanes 0..63 (warps 0, 1)
             if (!compute || part != 0 || wq >= 2)
@@ -469,120 +507,170 @@ __global__ void __launch_bounds__(128 * NPART + 96, 1) bwd_rows_kernel(StepArgs 
             for (int ks = 0; ks < 2; ++ks)
                 umma::mma_ts(tmem + F::T_DHP, tp + D::PIN + ks * 8, dW2T + (uint64_t)(ks * 2 * HID), I1, ks > 0);
             umma::commit(g1bar);
+            ++g1_issued;
+        };
+        auto ring_wait_x = [&](int &waited, int upto) {  // compute threads: x entries .. upto landed
+            while (waited <= upto) {
+                const int slot = waited % F::XRING;
+                ok &= wait_bar(&xfull[slot], (xpar >> slot) & 1u, abort);
+                xpar ^= 1u << slot;
+                ++waited;
+            }
         };
 
         int64_t g = g0;
         RowSeg sg;
-        while (ok && next_segment(g, g1, H, sg)) {
+        while (next_segment(g, g1, H, sg)) {
             const int n = sg.n, k = n / a.B, L = sg.r1 - sg.r0 + 2;  // sequence: halo, owned rows, halo
             const float *xn = a.x + (size_t)n * C * plane, *gyn = a.gy + (size_t)n * C * plane;
             float *gxn = a.gx + (size_t)n * C * plane;
             auto rowY = [&](int i) { return wrap_index(sg.r0 - 1 + i, H); };
-            auto issue_x = [&](int e) {  // producer warp: x row wrap(r0 - 2 + e) -> slot e % XRING, one lane per channel
+            // producer warp: x row wrap(r0 - 2 + e) -> slot e % XRING (one lane per channel)
+            auto issue_x = [&](int e) {
                 const int slot = e % F::XRING, Y = wrap_index(sg.r0 - 2 + e, H);
-                if (lane32 == 0)
-                    umma::mbar_arrive_expect_tx(&xfull[slot], (uint32_t)(C * W * 4));
-                __syncwarp();
-                if (lane32 < C)
-                    umma::bulk_g2s(XR + ((size_t)slot * C + lane32) * W, xn + ((size_t)lane32 * H + Y) * W,
-                                   (uint32_t)(W * 4), &xfull[slot]);
+                ok = __shfl_sync(~0u, ok, 0);  // lane 0 did the waits: the whole warp takes one path
+                if (ok) {
+                    if (lane32 == 0)
+                        umma::mbar_arrive_expect_tx(&xfull[slot], (uint32_t)(C * W * 4));
+                    __syncwarp();
+                    if (lane32 < C)
+                        umma::bulk_g2s(XR + ((size_t)slot * C + lane32) * W, xn + ((size_t)lane32 * H + Y) * W,
+                                       (uint32_t)(W * 4), &xfull[slot]);
+                    ++x_issued[slot];
+                }
             };
-            auto mask_row = [&](int j) {  // producer warp: update mask of sequence row j -> MK[j % 2]
-                row_mask_warp(MK + (j & 1) * 128, a.seed, a.rate, n + a.n_offset, H, W, rowY(j), lane32);
+            // producer warp: update mask of sequence row j -> MK[j % 2], then mkfull[j % 2]
+            auto draw_mask = [&](int j) {
+                ok = __shfl_sync(~0u, ok, 0);
+                if (ok) {
+                    row_mask_warp(MK + (j & 1) * 128, a.seed, a.rate, n + a.n_offset, H, W, rowY(j), lane32);
+                    __syncwarp();
+                    if (lane32 == 0)
+                        mbar_arrive(&mkfull[j & 1]);
+                }
             };
-            int xwaited = 0;
-            // ---- segment prologue (every WG of earlier rows completed at the last row's B_a)
+            // ---- segment prologue: a new NCA needs its weights (and the old accumulator flushed)
             if (k != cur_k) {
-                if (cur_k >= 0)
+                group_sync();  // every warp finished the previous segment; its tensor-core work completed
+                if (ok && cur_k >= 0)
                     flush(cur_k);
-                sync();
                 stage_bwd_weights<D>(W1s, W1T, W2T, a.w1 + (size_t)k * HID * D::PIN, a.b1 + (size_t)k * HID,
                                      a.w2 + (size_t)k * C * HID, tid, F::GROUP, F::GM0 - D::PIN);
                 umma::fence_proxy_async();
+                group_sync();
                 cur_k = k;
             }
-            float gyA[F::CPP];  // gy of the next front end's row
             if (prod) {
+                // ======== producer: entries 0..2 and masks 0, 1; after every warp's FE(j): entry j + 3, mask j + 2
                 for (int e = 0; e < F::XRING; ++e)
                     issue_x(e);
-                if (lane32 == 0)
-                    ok = ring_wait<F::XRING>(xfull, xwaited, 2, xpar);
-                mask_row(0);
-                mask_row(1);
-            }
-            auto load_gy = [&](int j) {  // gy(Y_j) of this thread's channels (plain loads, used one row later)
-                const float *src = gyn + (size_t)rowY(j) * W + xc;
-#pragma unroll
-                for (int cc = 0; cc < F::CPP; ++cc)
-                    gyA[cc] = __ldg(src + (size_t)(F::CPP * part + cc) * plane);
-            };
-            // front end of sequence row j into buffer bj: p' and gm -> TMEM P[bj] and PSW[bj]
-            auto front_end = [&](int j, int bj) {
-                const float *rm = XR + (size_t)(j % F::XRING) * C * W, *r0 = XR + (size_t)((j + 1) % F::XRING) * C * W,
-                            *rp = XR + (size_t)((j + 2) % F::XRING) * C * W;
-                const float m = MK[(j & 1) * 128 + xc];
-                float *psw = PSW + bj * D::PSW;
-                const uint32_t tp = lane + (bj ? F::T_P1 : F::T_P0);
-#pragma unroll
-                for (int cc = 0; cc < F::CPP; ++cc) {  // warp-uniform channel: tcgen05.st takes one column per warp
-                    const int c = F::CPP * part + cc;
-                    const float *bm = rm + c * W, *b0 = r0 + c * W, *bp = rp + c * W;
-                    const float v[3][3] = {{bm[xl], bm[xc], bm[xr]}, {b0[xl], b0[xc], b0[xr]}, {bp[xl], bp[xc], bp[xr]}};
-                    const float4 p = perceive3x3(v);
-                    const float t4[4] = {tf32_rna(p.x), tf32_rna(p.y), tf32_rna(p.z), tf32_rna(p.w)};
-                    umma::tmem_st4(tp + 4 * c, t4);
-                    *reinterpret_cast<float4 *>(psw + umma::sw32_offset(4 * c, x, 128) / 4) =
-                        make_float4(t4[0], t4[1], t4[2], t4[3]);
-                    const float gmv = (vx && m != 0.f) ? tf32_rna(gyA[cc]) : 0.f;
-                    umma::tmem_st1(tp + F::GM0 + c, gmv);
-                    psw[umma::sw32_offset(F::GM0 + c, x, 128) / 4] = gmv;
+                draw_mask(0);
+                if (L > 1)
+                    draw_mask(1);
+                for (int j = 0; j < L; ++j) {
+                    if (lane32 == 0)
+                        ok &= wait_bar(fe_done, feph, abort);
+                    feph ^= 1;
+                    ok = __shfl_sync(~0u, ok, 0);
+                    if (j + 3 <= L + 1)
+                        issue_x(j + 3);
+                    if (j + 2 < L)
+                        draw_mask(j + 2);
                 }
-                umma::tmem_wait_st();
-                umma::fence_proxy_async();
-            };
-            if (compute)
+            } else if (mma) {
+                // ======== MMA warp: G1(0); per row DP(i), then G1(i+1)
+                if (lane32 == 0) {
+                    ok &= wait_bar(fe_done, feph, abort);
+                    feph ^= 1;
+                    if (ok) {
+                        umma::fence_after_sync();
+                        g1_issue(0);
+                    }
+                    for (int i = 0; i < L; ++i) {
+                        const int b = i & 1;
+                        ok &= wait_bar(ea_done, eaph, abort);
+                        eaph ^= 1;
+                        if (ok) {
+                            umma::fence_after_sync();
+                            const uint32_t tp = tmem + (b ? F::T_P1 : F::T_P0);
+#pragma unroll
+                            for (int ks = 0; ks < HID / 8; ++ks)
+                                umma::mma_ts(tp, tmem + F::T_H + ks * 8, dW1T + (uint64_t)(ks * 2 * D::PIN), IP, ks > 0);
+                            umma::commit(dpbar);
+                            ++dp_issued;
+                            if (i >= 1 && i <= L - 2)
+                                mbar_arrive(wggo);
+                        }
+                        if (i + 1 < L) {
+                            ok &= wait_bar(fe_done, feph, abort);
+                            feph ^= 1;
+                        }
+                        ok &= wait_bar(dpbar, dpph, abort);  // DP(i) read H: G1(i+1) may overwrite it
+                        dpph ^= 1;
+                        if (ok && i + 1 < L) {
+                            umma::fence_after_sync();
+                            g1_issue(b ^ 1);
+                        }
+                    }
+                }
+            } else {
+                // ======== compute warps
+                int xwaited = 0;
+                float gyA[F::CPP];  // gy of the next front end's row
+                auto load_gy = [&](int j) {
+                    const float *src = gyn + (size_t)rowY(j) * W + xc;
+#pragma unroll
+                    for (int cc = 0; cc < F::CPP; ++cc)
+                        gyA[cc] = __ldg(src + (size_t)(F::CPP * part + cc) * plane);
+                };
+                // front end of sequence row j into buffer bj: p' and gm -> TMEM P[bj] and PSW[bj]
+                auto front_end = [&](int j, int bj) {
+                    ring_wait_x(xwaited, j + 2);  // x rows Y_j - 1 .. Y_j + 1
+                    ok &= wait_bar(&mkfull[j & 1], (mkpar >> (j & 1)) & 1u, abort);  // the mask of row j
+                    mkpar ^= 1u << (j & 1);
+                    const float *rm = XR + (size_t)(j % F::XRING) * C * W, *r0 = XR + (size_t)((j + 1) % F::XRING) * C * W,
+                                *rp = XR + (size_t)((j + 2) % F::XRING) * C * W;
+                    const bool m = MK[(j & 1) * 128 + xc] != 0;
+                    float *psw = PSW + bj * D::PSW;
+                    const uint32_t tp = lane + (bj ? F::T_P1 : F::T_P0);
+#pragma unroll
+                    for (int cc = 0; cc < F::CPP; ++cc) {  // warp-uniform channel: tcgen05.st takes one column per warp
+                        const int c = F::CPP * part + cc;
+                        const float *bm = rm + c * W, *b0 = r0 + c * W, *bp = rp + c * W;
+                        const float v[3][3] = {{bm[xl], bm[xc], bm[xr]}, {b0[xl], b0[xc], b0[xr]}, {bp[xl], bp[xc], bp[xr]}};
+                        const float4 p = perceive3x3(v);
+                        const float t4[4] = {tf32_rna(p.x), tf32_rna(p.y), tf32_rna(p.z), tf32_rna(p.w)};
+                        umma::tmem_st4(tp + 4 * c, t4);
+                        *reinterpret_cast<float4 *>(psw + umma::sw32_offset(4 * c, x, 128) / 4) =
+                            make_float4(t4[0], t4[1], t4[2], t4[3]);
+                        const float gmv = (vx && m) ? tf32_rna(gyA[cc]) : 0.f;
+                        umma::tmem_st1(tp + F::GM0 + c, gmv);
+                        psw[umma::sw32_offset(F::GM0 + c, x, 128) / 4] = gmv;
+                    }
+                    umma::tmem_wait_st();
+                    umma::fence_proxy_async();
+                    signal(fe_done);
+                };
                 load_gy(0);
-            ok = sync_and(ok);
-            if (!ok)
-                break;
-            if (compute) {
                 front_end(0, 0);
                 if (L > 1)
                     load_gy(1);
-            }
-            sync();
-            if (mma && lane32 == 0)
-                g1_issue(0);
-            if (prod) {
-                if (F::XRING < L + 2)
-                    issue_x(F::XRING);  // into the slot of entry 0, read only by FE(0)
-                if (L > 2)
-                    mask_row(2);
-            }
-            float accm[F::CPP], acc0[F::CPP], accp[F::CPP];
+                float accm[F::CPP], acc0[F::CPP], accp[F::CPP];
 #pragma unroll
-            for (int cc = 0; cc < F::CPP; ++cc)
-                accm[cc] = acc0[cc] = accp[cc] = 0.f;
+                for (int cc = 0; cc < F::CPP; ++cc)
+                    accm[cc] = acc0[cc] = accp[cc] = 0.f;
 
-            for (int i = 0; i < L; ++i) {
-                const int b = i & 1, Y = rowY(i);
-                const bool owned = i >= 1 && i <= L - 2, next = i + 1 < L, prev_owned = i >= 2;
-                // ---- B_a: G1(i), WG(i-1) complete; x rows of FE(i+1) present
-                if (mma && lane32 == 0) {
-                    ok = umma::mbar_wait(g1bar, g1ph);
-                    if (prev_owned)
-                        ok &= umma::mbar_wait(wgbar, wgph);
-                }
-                if (prod && lane32 == 0 && next)
-                    ok = ring_wait<F::XRING>(xfull, xwaited, i + 3, xpar);
-                g1ph ^= 1;
-                if (prev_owned)
-                    wgph ^= 1;
-                ok = sync_and(ok);
-                if (!ok)
-                    break;
-                // ---- EA(i): relu(h) -> RH, dh -> DH (owned rows) and TMEM H
-                if (compute) {
+                for (int i = 0; i < L; ++i) {
+                    const int b = i & 1, Y = rowY(i);
+                    const bool owned = i >= 1 && i <= L - 2, next = i + 1 < L;
+                    // ---- EA(i): relu(h) -> RH, dh -> DH (owned rows) and TMEM H; needs G1(i) and WG(i-1)
+                    ok &= wait_bar(g1bar, g1ph, abort);
+                    g1ph ^= 1;
+                    if (i >= 2) {
+                        ok &= wait_bar(wgbar, wgph, abort);
+                        wgph ^= 1;
+                    }
+                    umma::fence_after_sync();
 #pragma unroll
                     for (int q = 0; q < F::HPP / 8; ++q) {
                         const int j0 = part * F::HPP + q * 8;
@@ -603,52 +691,37 @@ __global__ void __launch_bounds__(128 * NPART + 96, 1) bwd_rows_kernel(StepArgs 
                     }
                     umma::tmem_wait_st();
                     umma::fence_proxy_async();
-                }
-                sync();  // ---- B_b
-                if (mma && lane32 == 0) {  // DP(i): dp = dh W1 -> P[b] columns 0..PIN-1; then let WG(i) start
-                    const uint32_t tp = tmem + (b ? F::T_P1 : F::T_P0);
-#pragma unroll
-                    for (int ks = 0; ks < HID / 8; ++ks)
-                        umma::mma_ts(tp, tmem + F::T_H + ks * 8, dW1T + (uint64_t)(ks * 2 * D::PIN), IP, ks > 0);
-                    umma::commit(dpbar);
-                    if (owned)
-                        mbar_arrive(wggo);
-                }
-                if (compute && next) {
-                    front_end(i + 1, b ^ 1);
-                    if (i + 2 < L)
-                        load_gy(i + 2);
-                }
-                if (mma && lane32 == 0)
-                    ok = umma::mbar_wait(dpbar, dpph);
-                dpph ^= 1;
-                ok = sync_and(ok);  // ---- B_c
-                if (!ok)
-                    break;
-                if (mma && lane32 == 0 && next)
-                    g1_issue(b ^ 1);
-                if (prod) {
-                    if (i + 4 < L + 2)
-                        issue_x(i + 4);  // slot of entry i + 1, last read by FE(i + 1)
-                    if (i + 3 < L)
-                        mask_row(i + 3);
-                }
-                if (compute) {  // ---- adjoint of dp(i): gx rows Y - 1, Y, Y + 1; gx(Y - 1) final
+                    signal(ea_done);
+                    // ---- FE(i+1)
+                    if (next) {
+                        front_end(i + 1, b ^ 1);
+                        if (i + 2 < L)
+                            load_gy(i + 2);
+                    }
+                    // ---- ADJ(i): dp(i) -> gx rows Y - 1, Y, Y + 1; gx(Y - 1) final
+                    ok &= wait_bar(dpbar, dpph, abort);
+                    dpph ^= 1;
+                    umma::fence_after_sync();
                     float dpv[F::CPP][4];
 #pragma unroll
                     for (int cc = 0; cc < F::CPP; ++cc)
                         umma::tmem_ld4(lane + (b ? F::T_P1 : F::T_P0) + 4 * (F::CPP * part + cc), dpv[cc]);
                     umma::tmem_wait_ld();
+                    float *edge = EDGE + b * (F::EDGE_SLOTS * C * 3);  // double-buffered by row parity
 #pragma unroll
                     for (int cc = 0; cc < F::CPP; ++cc) {  // edge lanes publish (sobel_x, sobel_y, laplacian) parts
                         const int c = F::CPP * part + cc;
-                        const float4 t = make_float4(dpv[cc][1], dpv[cc][2], dpv[cc][3], 0.f);
-                        if (lane32 == 0)
-                            EDGE[wq * C + c] = t;
-                        if (lane32 == 31)
-                            EDGE[(4 + wq) * C + c] = t;
-                        if (x == W - 1)
-                            EDGE[8 * C + c] = t;
+                        const int slot = lane32 == 0 ? wq : lane32 == 31 ? 4 + wq : -1;
+                        if (slot >= 0) {
+                            edge[(slot * C + c) * 3 + 0] = dpv[cc][1];
+                            edge[(slot * C + c) * 3 + 1] = dpv[cc][2];
+                            edge[(slot * C + c) * 3 + 2] = dpv[cc][3];
+                        }
+                        if (x == W - 1) {
+                            edge[(8 * C + c) * 3 + 0] = dpv[cc][1];
+                            edge[(8 * C + c) * 3 + 1] = dpv[cc][2];
+                            edge[(8 * C + c) * 3 + 2] = dpv[cc][3];
+                        }
                     }
                     bar_sync(2 + part, 128);
                     const bool fin = i >= 2 && vx;
@@ -666,16 +739,16 @@ __global__ void __launch_bounds__(128 * NPART + 96, 1) bwd_rows_kernel(StepArgs 
                         float rx = __shfl_down_sync(~0u, dpv[cc][1], 1), ry = __shfl_down_sync(~0u, dpv[cc][2], 1),
                               rz = __shfl_down_sync(~0u, dpv[cc][3], 1);
                         if (lane32 == 0 || x == 0) {
-                            const float4 e = x == 0 ? EDGE[8 * C + c] : EDGE[(4 + wq - 1) * C + c];
-                            lx = e.x;
-                            ly = e.y;
-                            lz = e.z;
+                            const float *e = edge + ((x == 0 ? 8 : 4 + wq - 1) * C + c) * 3;
+                            lx = e[0];
+                            ly = e[1];
+                            lz = e[2];
                         }
                         if (lane32 == 31 || x == W - 1) {
-                            const float4 e = x == W - 1 ? EDGE[c] : EDGE[(wq + 1) * C + c];
-                            rx = e.x;
-                            ry = e.y;
-                            rz = e.z;
+                            const float *e = edge + ((x == W - 1 ? 0 : wq + 1) * C + c) * 3;
+                            rx = e[0];
+                            ry = e[1];
+                            rz = e[2];
                         }
                         const float rsx = lx - rx;                      // horizontal transpose of sobel_x
                         const float rsy = ry + 2.f * dpv[cc][2] + ly;   // ... of sobel_y (smoothing)
@@ -689,20 +762,31 @@ __global__ void __launch_bounds__(128 * NPART + 96, 1) bwd_rows_kernel(StepArgs 
                         acc0[cc] = accp[cc];
                         accp[cc] = 0.f;
                     }
-                    umma::fence_before_sync();
                 }
             }
         }
+        group_sync();  // every warp done; the last WG was waited by the compute warps at their last row
         if (ok && cur_k >= 0)
             flush(cur_k);
+        if (mma && lane32 == 0) {  // this warp's MMAs are complete before the teardown
+            if (g1_issued > 0)
+                umma::mbar_wait(g1bar, (uint32_t)((g1_issued - 1) & 1));
+            if (dp_issued > 0)
+                umma::mbar_wait(dpbar, (uint32_t)((dp_issued - 1) & 1));
+        }
+        if (prod && lane32 == 0)  // and so are this warp's bulk copies
+            for (int s2 = 0; s2 < F::XRING; ++s2)
+                if (x_issued[s2] > 0)
+                    umma::mbar_wait(&xfull[s2], (uint32_t)((x_issued[s2] - 1) & 1));
     }
     umma::fence_before_sync();
     __syncthreads();
     umma::fence_after_sync();
     if (warp == 0)
         umma::tmem_dealloc(tmem, F::TMEM);
-    if (!ok)
-        set_device_error(1);
+    if (*abort || !ok)
+        if (tid == 0)
+            set_device_error(1);
 }
 
 }  // namespace unca
