@@ -228,7 +228,7 @@ int bwd_ctas_per_sm()
 
 // Row-streaming kernels (the benchmark's hot path): TF32 texture NCAs whose rows are whole 16-byte multiples that
 // fit one 128-lane tile; every other case runs the tile kernels.
-constexpr int FWD_ROWS_PARTS = 2, BWD_ROWS_PARTS = 4;
+constexpr int FWD_ROWS_PARTS = 4, BWD_ROWS_PARTS = 4;
 bool rows_path(const Shape &s, bool fp32, bool growing)
 {
     return !fp32 && !growing && s.C == 12 && s.HID == 96 && s.W <= 128 && s.W % 4 == 0;
@@ -239,7 +239,9 @@ int fwd_rows_grid(const Shape &s)
 {
     using FR = FwdRows<12, 96, FWD_ROWS_PARTS>;
     const int per = ctas_per_sm(fwd_rows_kernel<12, 96, FWD_ROWS_PARTS>, FR::smem(), FR::TMEM, FR::THREADS);
-    return grid_for(s.N * s.H, per);
+    const int64_t rows = s.N * s.H;  // each CTA draws the update masks of its rows into shared memory: at most MAXROWS
+    const int64_t need = (rows + FR::MAXROWS - 1) / FR::MAXROWS;
+    return (int)std::max<int64_t>(grid_for(rows, per), std::min<int64_t>(need, rows));
 }
 int bwd_rows_grid(const Shape &s)
 {

@@ -77,192 +77,6 @@ __device__ __forceinline__ void row_mask_warp(T *mk, uint64_t seed, float rate, 
     }
 }
 
-// ================================================================ forward
-template <int C, int HID, int NPART>
-struct FwdRows {
-    using D = Dims<C, HID>;
-    static constexpr int THREADS = 128 * NPART, CPP = C / NPART, HPP = HID / NPART, RING = 4;
-    static constexpr int KPAD = ((D::KP + 15) / 16) * 16;
-    static constexpr int T_P = 0, T_H = 128, T_U = T_H + HID, TMEM = 256;
-    static_assert(C % NPART == 0 && HPP % 8 == 0 && KPAD <= T_H && T_U + 16 <= TMEM, "forward row-kernel layout");
-    static constexpr size_t smem() { return (size_t)(D::W1S + D::W2S + RING * C * 128 + 2 * 128) * 4 + 8 * (RING + 1) + 16; }
-};
-
-template <int C, int HID, int NPART>
-__global__ void __launch_bounds__(128 * NPART, 4 / NPART) fwd_rows_kernel(StepArgs a)
-{
-    using F = FwdRows<C, HID, NPART>;
-    using D = typename F::D;
-    extern __shared__ __align__(128) float smem[];
-    float *W1s = smem, *W2s = W1s + D::W1S, *XR = W2s + D::W2S, *MK = XR + F::RING * C * 128;
-    uint64_t *xfull = reinterpret_cast<uint64_t *>(MK + 2 * 128), *mbar = xfull + F::RING;
-    uint32_t *tslot = reinterpret_cast<uint32_t *>(mbar + 1);
-
-    const int tid = threadIdx.x, warp = tid / 32, part = tid / 128, x = tid % 128;
-    const int lane32 = tid % 32, mask_warp = F::THREADS / 32 - 1;
-    const int H = a.H, W = a.W;
-    const bool vx = x < W;
-    const int xc = vx ? x : 0, xl = xc == 0 ? W - 1 : xc - 1, xr = xc + 1 >= W ? 0 : xc + 1;
-    int64_t g0, g1;
-    cta_range((int64_t)a.N * H, gridDim.x, blockIdx.x, &g0, &g1);
-    const size_t plane = (size_t)H * W;
-
-    if (tid == 0) {
-        for (int i = 0; i < F::RING; ++i)
-            umma::mbar_init(&xfull[i], 1);
-        umma::mbar_init(mbar, 1);
-        umma::fence_mbar_init();
-    }
-    if (warp == 0) {
-        umma::tmem_alloc(tslot, F::TMEM);
-        umma::tmem_relinquish();
-    }
-    umma::fence_before_sync();
-    __syncthreads();
-    umma::fence_after_sync();
-    const uint32_t tmem = *tslot, lane = umma::tmem_addr(tmem, warp, 0);
-    if (part == 0) {  // p' columns past the channel features: bias-hi, bias-lo = 1, zeros (never overwritten)
-        float v[8] = {1.f, 1.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-        umma::tmem_st8(lane + F::T_P + D::PIN, v);
-        const float z[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-        for (int c0 = D::PIN + 8; c0 < F::KPAD; c0 += 8)
-            umma::tmem_st8(lane + F::T_P + c0, z);
-        umma::tmem_wait_st();
-    }
-    uint32_t xpar = 0, mphase = 0;
-    int cur_k = -1;
-    bool ok = true;
-    int64_t g = g0;
-    RowSeg sg;
-    while (ok && next_segment(g, g1, H, sg)) {
-        const int n = sg.n, k = n / a.B, L = sg.r1 - sg.r0;
-        umma::fence_before_sync();
-        __syncthreads();  // the previous segment's ring, mask and TMEM reads are complete
-        if (k != cur_k) {
-            stage_weights<D, true>(W1s, W2s, a.w1 + (size_t)k * HID * D::PIN, a.b1 + (size_t)k * HID,
-                                   a.w2 + (size_t)k * C * HID);
-            umma::fence_proxy_async();
-            cur_k = k;
-        }
-        const float *xn = a.x + (size_t)n * C * plane;
-        auto issue = [&](int e) {  // x row wrap(r0 - 1 + e) -> slot e % RING
-            const int slot = e % F::RING, Y = wrap_index(sg.r0 - 1 + e, H);
-            umma::mbar_arrive_expect_tx(&xfull[slot], (uint32_t)(C * W * 4));
-            for (int c = 0; c < C; ++c)
-                umma::bulk_g2s(XR + ((size_t)slot * C + c) * W, xn + ((size_t)c * H + Y) * W, (uint32_t)(W * 4), &xfull[slot]);
-        };
-        if (tid == 0)
-            for (int e = 0; e < min(L + 2, F::RING); ++e)
-                issue(e);
-        if (warp == mask_warp)
-            row_mask_warp(MK, a.seed, a.rate, n + a.n_offset, H, W, sg.r0, lane32);
-        int waited = 0;
-        for (int i = 0; i < L && ok; ++i) {
-            const int Y = sg.r0 + i;
-            if (tid == 0)
-                ok = ring_wait<F::RING>(xfull, waited, i + 2, xpar);
-            ok = __syncthreads_and(ok);  // rows Y-1 .. Y+1 and the mask of row Y are in shared memory
-            if (!ok)
-                break;
-            umma::fence_after_sync();
-            const float *rm = XR + (size_t)(i % F::RING) * C * W, *r0 = XR + (size_t)((i + 1) % F::RING) * C * W,
-                        *rp = XR + (size_t)((i + 2) % F::RING) * C * W;
-#pragma unroll
-            for (int cc = 0; cc < F::CPP; ++cc) {
-                const int c = part + NPART * cc;
-                const float *bm = rm + c * W, *b0 = r0 + c * W, *bp = rp + c * W;
-                const float v[3][3] = {{bm[xl], bm[xc], bm[xr]}, {b0[xl], b0[xc], b0[xr]}, {bp[xl], bp[xc], bp[xr]}};
-                const float4 p = perceive3x3(v);
-                const float pv[4] = {tf32_rna(p.x), tf32_rna(p.y), tf32_rna(p.z), tf32_rna(p.w)};
-                umma::tmem_st4(lane + F::T_P + 4 * c, pv);
-            }
-            const float m = MK[(i & 1) * 128 + xc];
-            float xv[F::CPP];
-#pragma unroll
-            for (int cc = 0; cc < F::CPP; ++cc)
-                xv[cc] = r0[(part + NPART * cc) * W + xc];
-            umma::tmem_wait_st();
-            umma::fence_before_sync();
-            __syncthreads();  // p' complete; row Y-1 (ring entry i) is no longer read
-            if (tid == 0) {
-                umma::fence_after_sync();
-#pragma unroll
-                for (int ks = 0; ks < D::KP / 8; ++ks)
-                    umma::mma_ts(tmem + F::T_H, tmem + F::T_P + ks * 8,
-                                 umma::smem_desc(umma::smem_u32(W1s) + ks * 2 * HID * 16, HID * 16, 128),
-                                 umma::idesc_tf32(128, HID, false, false), ks > 0);
-                umma::commit(mbar);
-                if (i + 4 < L + 2)
-                    issue(i + 4);
-                ok = umma::mbar_wait(mbar, mphase);
-            }
-            mphase ^= 1;
-            if (warp == mask_warp && i + 1 < L)
-                row_mask_warp(MK + ((i + 1) & 1) * 128, a.seed, a.rate, n + a.n_offset, H, W, Y + 1, lane32);
-            ok = __syncthreads_and(ok);
-            umma::fence_after_sync();
-#pragma unroll
-            for (int q = 0; q < F::HPP / 8; ++q) {
-                float h[8];
-                umma::tmem_ld8(lane + F::T_H + part * F::HPP + q * 8, h);
-                umma::tmem_wait_ld();
-#pragma unroll
-                for (int e = 0; e < 8; ++e)
-                    h[e] = tf32_rna(fmaxf(h[e], 0.f));
-                umma::tmem_st8(lane + F::T_H + part * F::HPP + q * 8, h);
-            }
-            umma::tmem_wait_st();
-            umma::fence_before_sync();
-            __syncthreads();
-            if (tid == 0 && ok) {
-                umma::fence_after_sync();
-#pragma unroll
-                for (int ks = 0; ks < HID / 8; ++ks)
-                    umma::mma_ts(tmem + F::T_U, tmem + F::T_H + ks * 8,
-                                 umma::smem_desc(umma::smem_u32(W2s) + ks * 2 * D::CP * 16, D::CP * 16, 128),
-                                 umma::idesc_tf32(128, 16, false, false), ks > 0);
-                umma::commit(mbar);
-                ok = umma::mbar_wait(mbar, mphase);
-            }
-            mphase ^= 1;
-            ok = __syncthreads_and(ok);
-            umma::fence_after_sync();
-            float u[16];
-            umma::tmem_ld16(lane + F::T_U, u);
-            umma::tmem_wait_ld();
-            if (vx && ok) {
-                float *yn = a.y + (size_t)n * C * plane + (size_t)Y * W + x;
-#pragma unroll
-                for (int cc = 0; cc < F::CPP; ++cc) {
-                    const int c = part + NPART * cc;
-                    yn[(size_t)c * plane] = m != 0.f ? xv[cc] + u[c] : xv[cc];
-                }
-            }
-            umma::fence_before_sync();  // the next row's barriers order these TMEM reads before its MMAs
-        }
-    }
-    umma::fence_before_sync();
-    __syncthreads();
-    umma::fence_after_sync();
-    if (warp == 0)
-        umma::tmem_dealloc(tmem, F::TMEM);
-    if (!ok && tid == 0)
-        set_device_error(1);
-}
-
-// ================================================================ backward with the fused adjoint
-// Eight consecutive values v[0..7] of MN index mn0 (mn0 % 8 == 0) at K row k of a swizzled MN-major tile, as two
-// 16-byte stores whose order alternates with bit 2 of k: a warp's 32 rows then cover all eight 16-byte bank slots of a
-// 128-byte row four times per instruction (the minimum of 4 wavefronts; one fixed order costs 8).
-__device__ __forceinline__ void st_sw32x8_balanced(float *tile, int mn0, int k, int krows, const float *v)
-{
-    float *dst = tile + umma::sw32_offset(mn0, k, krows) / 4;
-    const int flip = (k >> 2) & 1;
-    const float4 lo = make_float4(v[0], v[1], v[2], v[3]), hi = make_float4(v[4], v[5], v[6], v[7]);
-    *reinterpret_cast<float4 *>(dst + 4 * flip) = flip ? hi : lo;
-    *reinterpret_cast<float4 *>(dst + 4 * (1 - flip)) = flip ? lo : hi;
-}
-
 // Named barrier `id` over `count` threads, and the same with an AND over `pred`.
 __device__ __forceinline__ void bar_sync(int id, int count)
 {
@@ -307,6 +121,334 @@ __device__ __forceinline__ bool wait_bar(uint64_t *bar, uint32_t parity, volatil
             return false;
         }
     }
+}
+
+// Update mask of one image row (global image index n, row Y, W <= 128, W % 4 == 0) by one warp as 128 bits in four
+// words: lane l draws the Philox block of pixels 4l .. 4l + 3 and word e collects, by ballot, bit l = mask(4l + e), so
+// mask(x) = (word[x % 4] >> (x / 4)) & 1. Same draws and threshold as row_mask_warp.
+__device__ __forceinline__ void row_mask_bits_warp(uint32_t *dst, uint64_t seed, float rate, int64_t n, int H, int W, int Y,
+                                                   int lane)
+{
+    const int quads = W / 4;
+    bool bits[4] = {false, false, false, false};
+    if (lane < quads) {
+        if (rate >= 1.f) {
+            bits[0] = bits[1] = bits[2] = bits[3] = true;
+        } else {
+            const uint64_t counter = ((uint64_t)n * (uint64_t)H + (uint64_t)Y) * (uint64_t)quads + (uint64_t)lane;
+            const uint4 w = philox4x32_10(seed, counter);
+            const uint32_t words[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e)
+                bits[e] = floorf(__fadd_rn(__fmul_rn((float)(words[e] >> 8), 1.0f / 16777216.0f), rate)) != 0.f;
+        }
+    }
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+        const uint32_t word = __ballot_sync(~0u, bits[e]);
+        if (lane == 0)
+            dst[e] = word;
+    }
+}
+
+// ================================================================ forward
+// Forward, software-pipelined across rows with the warps synchronised by mbarriers only. Warps 0 .. 4 NPART - 1
+// compute (part p owns channels [CPP p, CPP (p+1)) and hidden units [HPP p, HPP (p+1)) of pixel x = its TMEM lane).
+// The tensor-core work is issued from two warps on two different SM sub-partitions (a warp that shares its
+// sub-partition with busy compute warps issues tcgen05.mma at a fraction of the rate): W_M1 issues MMA1
+// (h = [p' 1 1 0..] W1ext^T), W_M2 issues MMA2 (u = relu(h) W2^T). W_PROD keeps an XRING-deep ring of x rows filled
+// with bulk copies (one lane per channel), refilling a slot when every compute warp has released it. The update masks
+// of all of the CTA's rows are drawn in the prologue (at most MAXROWS rows per CTA; the grid grows beyond that) as
+// 128-bit rows. Per row i of the band each compute warp runs
+//   EPI(i)  [MMA1(i)]        h -> tf32(relu(h)) in TMEM H[i%2]                                   -> epi_done
+//   FE(i+1) [x rows]         p' of row i+1 -> TMEM P[(i+1)%2]; centre x and mask kept in registers -> fe_done
+//   OUT(i)  [MMA2(i)]        y = x + m u (m = 0: y = x)
+template <int C, int HID, int NPART>
+struct FwdRows {
+    using D = Dims<C, HID>;
+    static constexpr int CW = 128 * NPART, W_M1 = CW / 32, W_M2 = W_M1 + 1, W_PROD = W_M1 + 2;
+    static constexpr int THREADS = CW + 96, CPP = C / NPART, HPP = HID / NPART, XRING = 6, MAXROWS = 1024;
+    // TMEM: H[2] (h, then tf32(relu(h)) in place), U[2], P[2] (p'; 1, 1 at PIN, PIN+1; zeros to KP)
+    static constexpr int T_H0 = 0, T_H1 = HID, T_U0 = 2 * HID, T_U1 = 2 * HID + 32, T_P0 = 256, T_P1 = 320;
+    static constexpr int TMEM = 512;
+    static_assert(C % NPART == 0 && HPP % 8 == 0 && D::KP <= 64 && T_U1 + 16 <= T_P0 && HID % 32 == 0 &&
+                  D::CP == 16 && C <= 32, "forward row-kernel layout");
+    // shared memory: W1 (K-major, bias folded) | W2 | x ring | mask bits (4 words per row) | mbarriers
+    static constexpr size_t OFF_XR = (size_t)(D::W1S + D::W2S) * 4;
+    static constexpr size_t OFF_MK = OFF_XR + (size_t)XRING * C * 128 * 4;
+    static constexpr size_t OFF_BAR = OFF_MK + (size_t)MAXROWS * 16;
+    static constexpr int NBAR = 2 * XRING + 5;  // x ring full / empty, MMA1, MMA2 per U buffer, epi_done, fe_done
+    static constexpr size_t smem() { return OFF_BAR + 8 * NBAR + 16; }
+    static_assert(OFF_BAR % 8 == 0, "mbarrier alignment");
+};
+
+template <int C, int HID, int NPART>
+__global__ void __launch_bounds__(128 * NPART + 96, 1) fwd_rows_kernel(StepArgs a)
+{
+    using F = FwdRows<C, HID, NPART>;
+    using D = typename F::D;
+    extern __shared__ __align__(128) unsigned char smem_raw[];
+    float *W1s = reinterpret_cast<float *>(smem_raw), *W2s = W1s + D::W1S;
+    float *XR = reinterpret_cast<float *>(smem_raw + F::OFF_XR);
+    uint32_t *MKB = reinterpret_cast<uint32_t *>(smem_raw + F::OFF_MK);
+    uint64_t *xfull = reinterpret_cast<uint64_t *>(smem_raw + F::OFF_BAR), *xempty = xfull + F::XRING,
+             *g1bar = xempty + F::XRING, *g2bar = g1bar + 1, *epi_done = g2bar + 2, *fe_done = epi_done + 1;
+    uint32_t *tslot = reinterpret_cast<uint32_t *>(fe_done + 1);
+    volatile uint32_t *abort = tslot + 1;
+
+    const int tid = threadIdx.x, warp = tid / 32, lane32 = tid % 32;
+    const bool compute = warp < F::W_M1, m1 = warp == F::W_M1, m2 = warp == F::W_M2, prod = warp == F::W_PROD;
+    const int part = compute ? tid / 128 : 0, x = tid % 128;
+    const int H = a.H, W = a.W;
+    const bool vx = compute && x < W;
+    const int xc = x < W ? x : 0, xl = xc == 0 ? W - 1 : xc - 1, xr = xc + 1 >= W ? 0 : xc + 1;
+    int64_t g0, g1;
+    cta_range((int64_t)a.N * H, gridDim.x, blockIdx.x, &g0, &g1);
+    const size_t plane = (size_t)H * W;
+    if (g1 - g0 > F::MAXROWS) {  // the host sizes the grid so that this never happens: refuse rather than overflow
+        if (tid == 0)
+            set_device_error(2);
+        return;
+    }
+
+    if (tid == 0) {
+        for (int i = 0; i < 2 * F::XRING; ++i)
+            umma::mbar_init(&xfull[i], i < F::XRING ? 1 : F::W_M1);  // full: the copy bytes; empty: every compute warp
+        umma::mbar_init(g1bar, 1);
+        umma::mbar_init(&g2bar[0], 1);
+        umma::mbar_init(&g2bar[1], 1);
+        umma::mbar_init(epi_done, F::W_M1);
+        umma::mbar_init(fe_done, F::W_M1);
+        *abort = 0;
+        umma::fence_mbar_init();
+    }
+    if (warp == 0) {
+        umma::tmem_alloc(tslot, F::TMEM);
+        umma::tmem_relinquish();
+    }
+    // update masks of the CTA's rows (g1 - g0 <= MAXROWS: the host sizes the grid so)
+    for (int64_t u = g0 + warp; u < g1; u += blockDim.x / 32)
+        row_mask_bits_warp(MKB + (u - g0) * 4, a.seed, a.rate, u / H + a.n_offset, H, W, (int)(u % H), lane32);
+    umma::fence_before_sync();
+    __syncthreads();
+    umma::fence_after_sync();
+    const uint32_t tmem = *tslot, lane = umma::tmem_addr(tmem, warp, 0);
+    if (compute && part == 0) {  // p' columns past the channel features: bias-hi, bias-lo = 1, zeros (never overwritten)
+        const float v[8] = {1.f, 1.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        umma::tmem_st8(lane + F::T_P0 + D::PIN, v);
+        umma::tmem_st8(lane + F::T_P1 + D::PIN, v);
+        umma::tmem_wait_st();
+    }
+    umma::fence_before_sync();
+    __syncthreads();
+    umma::fence_after_sync();
+
+    const uint64_t dW1 = umma::smem_desc(umma::smem_u32(W1s), HID * 16, 128);
+    const uint64_t dW2 = umma::smem_desc(umma::smem_u32(W2s), D::CP * 16, 128);
+    constexpr uint32_t I1 = umma::idesc_tf32(128, HID, false, false), I2 = umma::idesc_tf32(128, 16, false, false);
+    bool ok = true;
+    uint32_t ecount = 0, epar = 0, g1ph = 0, g2par = 0, eph = 0, feph = 0;  // g2par: one parity bit per U buffer
+    int cur_k = -1, issued = 0, x_uses[F::XRING] = {0, 0, 0, 0, 0, 0};
+    uint64_t *last_bar = nullptr;
+    uint32_t last_par = 0;
+    auto wait_g2 = [&](int bj) {  // MMA2 into U[bj] complete
+        ok &= wait_bar(&g2bar[bj], (g2par >> bj) & 1u, abort);
+        g2par ^= 1u << bj;
+    };
+    int64_t seg_u0 = g0;  // unit index of the current segment's first row
+    auto signal = [&](uint64_t *bar) {  // this warp's TMEM / shared-memory reads and writes are complete
+        umma::fence_before_sync();
+        __syncwarp();
+        if (lane32 == 0)
+            mbar_arrive(bar);
+    };
+
+    int64_t g = g0;
+    RowSeg sg;
+    while (next_segment(g, g1, H, sg)) {
+        const int n = sg.n, k = n / a.B, L = sg.r1 - sg.r0;
+        const float *xn = a.x + (size_t)n * C * plane;
+        float *yn = a.y + (size_t)n * C * plane;
+        if (k != cur_k) {  // every warp finished the previous segment (and its MMAs completed): restage the weights
+            umma::fence_before_sync();
+            __syncthreads();
+            stage_weights<D, true>(W1s, W2s, a.w1 + (size_t)k * HID * D::PIN, a.b1 + (size_t)k * HID,
+                                   a.w2 + (size_t)k * C * HID);
+            umma::fence_proxy_async();
+            __syncthreads();
+            umma::fence_after_sync();
+            cur_k = k;
+        }
+        if (prod) {
+            // ======== producer: x row wrap(r0 - 1 + e) -> slot (running entry count) % XRING, e = 0 .. L + 1
+            if (lane32 == 0) {
+                for (int e = 0; e < L + 2; ++e) {
+                    const int slot = (int)(x_uses[0] + x_uses[1] + x_uses[2] + x_uses[3] + x_uses[4] + x_uses[5]) % F::XRING;
+                    if (x_uses[slot] > 0)  // every compute warp released the slot's previous row
+                        ok &= wait_bar(&xempty[slot], (uint32_t)((x_uses[slot] - 1) & 1), abort);
+                    ++x_uses[slot];
+                    if (ok) {
+                        const int Y = wrap_index(sg.r0 - 1 + e, H);
+                        umma::mbar_arrive_expect_tx(&xfull[slot], (uint32_t)(C * W * 4));
+                        for (int c = 0; c < C; ++c)
+                            umma::bulk_g2s(XR + ((size_t)slot * C + c) * W, xn + ((size_t)c * H + Y) * W,
+                                           (uint32_t)(W * 4), &xfull[slot]);
+                    }
+                }
+            }
+        } else if (m1) {
+            // ======== MMA1 warp: h of row j -> H[j % 2] once FE(j) is done and MMA2(j-1) no longer reads H
+            if (lane32 == 0) {
+                for (int j = 0; j < L; ++j) {
+                    const int bj = j & 1;
+                    ok &= wait_bar(fe_done, feph, abort);
+                    feph ^= 1;
+                    if (j >= 2)  // MMA2(j-2) read H[bj]
+                        wait_g2(bj);
+                    if (ok) {
+                        umma::fence_after_sync();
+                        const uint32_t tp = tmem + (bj ? F::T_P1 : F::T_P0), th = tmem + (bj ? F::T_H1 : F::T_H0);
+#pragma unroll
+                        for (int ks = 0; ks < D::KP / 8; ++ks)
+                            umma::mma_ts(th, tp + ks * 8, dW1 + (uint64_t)(ks * 2 * HID), I1, ks > 0);
+                        umma::commit(g1bar);
+                        ++issued;
+                        last_bar = g1bar;
+                        last_par = (uint32_t)((issued - 1) & 1);
+                    }
+                }
+                for (int j = (L >= 2 ? L - 2 : 0); j < L; ++j)  // MMA2 of the last two rows: every phase waited once
+                    wait_g2(j & 1);
+            }
+        } else if (m2) {
+            // ======== MMA2 warp: u of row i -> U[i % 2] once EPI(i) is done
+            if (lane32 == 0) {
+                for (int i = 0; i < L; ++i) {
+                    const int b = i & 1;
+                    ok &= wait_bar(epi_done, eph, abort);
+                    eph ^= 1;
+                    if (ok) {
+                        umma::fence_after_sync();
+                        const uint32_t th = tmem + (b ? F::T_H1 : F::T_H0), tu = tmem + (b ? F::T_U1 : F::T_U0);
+#pragma unroll
+                        for (int ks = 0; ks < HID / 8; ++ks)
+                            umma::mma_ts(tu, th + ks * 8, dW2 + (uint64_t)(ks * 2 * D::CP), I2, ks > 0);
+                        umma::commit(&g2bar[b]);
+                        last_bar = &g2bar[b];
+                        last_par = (g2par >> b) & 1u;  // this warp counts its own commits per U buffer
+                        g2par ^= 1u << b;
+                    }
+                }
+            }
+        } else if (compute) {
+            // ======== compute warps
+            float xcur[F::CPP], xnext[F::CPP];
+            bool mcur = false, mnext = false;
+            int ewaited = 0;  // entries of this segment waited for
+            auto front_end = [&](int j, int bj) {  // p' of row r0 + j -> P[bj]; its centre x and mask -> xnext, mnext
+                while (ewaited <= j + 2) {  // entries j .. j + 2 (rows Y - 1 .. Y + 1); slots round-robin
+                    const int slot = (int)(ecount % F::XRING);
+                    ok &= wait_bar(&xfull[slot], (epar >> slot) & 1u, abort);
+                    epar ^= 1u << slot;
+                    ++ecount;
+                    ++ewaited;
+                }
+                const int s0 = (int)((ecount - (uint32_t)(ewaited - j)) % F::XRING);  // slot of entry j
+                const float *rm = XR + (size_t)s0 * C * W, *r0 = XR + (size_t)((s0 + 1) % F::XRING) * C * W,
+                            *rp = XR + (size_t)((s0 + 2) % F::XRING) * C * W;
+                const uint32_t *mw = MKB + (seg_u0 - g0 + j) * 4;
+                mnext = ((mw[xc & 3] >> (xc >> 2)) & 1u) != 0;
+                const uint32_t tp = lane + (bj ? F::T_P1 : F::T_P0);
+#pragma unroll
+                for (int cc = 0; cc < F::CPP; ++cc) {  // warp-uniform channel: tcgen05.st takes one column per warp
+                    const int c = F::CPP * part + cc;
+                    const float *bm = rm + c * W, *b0 = r0 + c * W, *bp = rp + c * W;
+                    const float v[3][3] = {{bm[xl], bm[xc], bm[xr]}, {b0[xl], b0[xc], b0[xr]}, {bp[xl], bp[xc], bp[xr]}};
+                    const float4 p = perceive3x3(v);
+                    const float pv[4] = {tf32_rna(p.x), tf32_rna(p.y), tf32_rna(p.z), tf32_rna(p.w)};
+                    umma::tmem_st4(tp + 4 * c, pv);
+                    xnext[cc] = v[1][1];
+                }
+                umma::tmem_wait_st();
+                signal(fe_done);
+                signal(&xempty[s0]);  // entry j is read by no later front end
+                if (j == L - 1) {     // nor are the segment's last two entries
+                    signal(&xempty[(s0 + 1) % F::XRING]);
+                    signal(&xempty[(s0 + 2) % F::XRING]);
+                }
+            };
+            front_end(0, 0);
+            for (int i = 0; i < L; ++i) {
+                const int b = i & 1, Y = sg.r0 + i;
+#pragma unroll
+                for (int cc = 0; cc < F::CPP; ++cc)
+                    xcur[cc] = xnext[cc];
+                mcur = mnext;
+                // ---- EPI(i): h -> tf32(relu(h)) in place
+                ok &= wait_bar(g1bar, g1ph, abort);
+                g1ph ^= 1;
+                umma::fence_after_sync();
+                const uint32_t th = lane + (b ? F::T_H1 : F::T_H0) + part * F::HPP;
+#pragma unroll
+                for (int q = 0; q < F::HPP / 8; ++q) {
+                    float h[8];
+                    umma::tmem_ld8(th + q * 8, h);
+                    umma::tmem_wait_ld();
+#pragma unroll
+                    for (int e = 0; e < 8; ++e)
+                        h[e] = tf32_rna(fmaxf(h[e], 0.f));
+                    umma::tmem_st8(th + q * 8, h);
+                }
+                umma::tmem_wait_st();
+                signal(epi_done);
+                // ---- FE(i+1)
+                if (i + 1 < L)
+                    front_end(i + 1, b ^ 1);
+                // ---- OUT(i): y = x + m u
+                wait_g2(b);
+                umma::fence_after_sync();
+                const uint32_t tu = lane + (b ? F::T_U1 : F::T_U0) + F::CPP * part;
+                float u[F::CPP];
+#pragma unroll
+                for (int cc = 0; cc < F::CPP; ++cc)
+                    u[cc] = umma::tmem_ld1(tu + cc);
+                umma::tmem_wait_ld();  // the loaded registers are defined only after this wait
+                if (vx && ok) {
+                    float *yr = yn + (size_t)Y * W + x;
+#pragma unroll
+                    for (int cc = 0; cc < F::CPP; ++cc)
+                        yr[(size_t)(F::CPP * part + cc) * plane] = mcur ? xcur[cc] + u[cc] : xcur[cc];
+                }
+            }
+        }
+        seg_u0 += L;
+    }
+    if ((m1 || m2) && lane32 == 0 && last_bar != nullptr)  // this warp's MMAs are complete before the teardown
+        umma::mbar_wait(last_bar, last_par);
+    if (prod && lane32 == 0)  // and so are this warp's bulk copies
+        for (int s2 = 0; s2 < F::XRING; ++s2)
+            if (x_uses[s2] > 0)
+                umma::mbar_wait(&xfull[s2], (uint32_t)((x_uses[s2] - 1) & 1));
+    umma::fence_before_sync();
+    __syncthreads();
+    umma::fence_after_sync();
+    if (warp == 0)
+        umma::tmem_dealloc(tmem, F::TMEM);
+    if ((*abort || !ok) && tid == 0)
+        set_device_error(1);
+}
+
+// ================================================================ backward with the fused adjoint
+// Eight consecutive values v[0..7] of MN index mn0 (mn0 % 8 == 0) at K row k of a swizzled MN-major tile, as two
+// 16-byte stores whose order alternates with bit 2 of k: a warp's 32 rows then cover all eight 16-byte bank slots of a
+// 128-byte row four times per instruction (the minimum of 4 wavefronts; one fixed order costs 8).
+__device__ __forceinline__ void st_sw32x8_balanced(float *tile, int mn0, int k, int krows, const float *v)
+{
+    float *dst = tile + umma::sw32_offset(mn0, k, krows) / 4;
+    const int flip = (k >> 2) & 1;
+    const float4 lo = make_float4(v[0], v[1], v[2], v[3]), hi = make_float4(v[4], v[5], v[6], v[7]);
+    *reinterpret_cast<float4 *>(dst + 4 * flip) = flip ? hi : lo;
+    *reinterpret_cast<float4 *>(dst + 4 * (1 - flip)) = flip ? lo : hi;
 }
 
 // Backward, software-pipelined across rows, with the warps synchronised by mbarriers only (no CTA-wide barrier per

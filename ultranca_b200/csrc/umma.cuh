@@ -188,6 +188,13 @@ __device__ __forceinline__ void tmem_ld8(uint32_t taddr, float *v)
     for (int i = 0; i < 8; ++i)
         v[i] = __uint_as_float(r[i]);
 }
+__device__ __forceinline__ float tmem_ld1(uint32_t taddr)
+{
+    uint32_t r;
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x1.b32 {%0}, [%1];" : "=r"(r) : "r"(taddr) : "memory");
+    return __uint_as_float(r);
+}
+
 __device__ __forceinline__ void tmem_ld4(uint32_t taddr, float *v)
 {
     uint32_t r[4];
