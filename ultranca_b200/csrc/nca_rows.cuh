@@ -159,10 +159,13 @@ __device__ __forceinline__ void row_mask_bits_warp(uint32_t *dst, uint64_t seed,
 // (h = [p' 1 1 0..] W1ext^T), W_M2 issues MMA2 (u = relu(h) W2^T). W_PROD keeps an XRING-deep ring of x rows filled
 // with bulk copies (one lane per channel), refilling a slot when every compute warp has released it. The update masks
 // of all of the CTA's rows are drawn in the prologue (at most MAXROWS rows per CTA; the grid grows beyond that) as
-// 128-bit rows. Per row i of the band each compute warp runs
+// 128-bit rows. Per row i of the band each compute warp runs (the front end two rows ahead, so that MMA1 has a row
+// of slack and MMA2 completes under the next front end)
 //   EPI(i)  [MMA1(i)]        h -> tf32(relu(h)) in TMEM H[i%2]                                   -> epi_done
-//   FE(i+1) [x rows]         p' of row i+1 -> TMEM P[(i+1)%2]; centre x and mask kept in registers -> fe_done
+//   FE(i+2) [x rows]         p' of row i+2 -> TMEM P[i%2]; centre x and mask kept in registers   -> fe_done[i%2]
 //   OUT(i)  [MMA2(i)]        y = x + m u (m = 0: y = x)
+// MMA1, MMA2 and the front-end signals use one mbarrier per buffer parity, so that no waiter can see a phase of the
+// row two ahead in place of its own.
 template <int C, int HID, int NPART>
 struct FwdRows {
     using D = Dims<C, HID>;
@@ -177,7 +180,7 @@ struct FwdRows {
     static constexpr size_t OFF_XR = (size_t)(D::W1S + D::W2S) * 4;
     static constexpr size_t OFF_MK = OFF_XR + (size_t)XRING * C * 128 * 4;
     static constexpr size_t OFF_BAR = OFF_MK + (size_t)MAXROWS * 16;
-    static constexpr int NBAR = 2 * XRING + 5;  // x ring full / empty, MMA1, MMA2 per U buffer, epi_done, fe_done
+    static constexpr int NBAR = 2 * XRING + 7;  // x ring full / empty, MMA1, MMA2, fe_done per buffer, epi_done
     static constexpr size_t smem() { return OFF_BAR + 8 * NBAR + 16; }
     static_assert(OFF_BAR % 8 == 0, "mbarrier alignment");
 };
@@ -192,7 +195,7 @@ __global__ void __launch_bounds__(128 * NPART + 96, 1) fwd_rows_kernel(StepArgs 
     float *XR = reinterpret_cast<float *>(smem_raw + F::OFF_XR);
     uint32_t *MKB = reinterpret_cast<uint32_t *>(smem_raw + F::OFF_MK);
     uint64_t *xfull = reinterpret_cast<uint64_t *>(smem_raw + F::OFF_BAR), *xempty = xfull + F::XRING,
-             *g1bar = xempty + F::XRING, *g2bar = g1bar + 1, *epi_done = g2bar + 2, *fe_done = epi_done + 1;
+             *g1bar = xempty + F::XRING, *g2bar = g1bar + 2, *fe_done = g2bar + 2, *epi_done = fe_done + 2;
     uint32_t *tslot = reinterpret_cast<uint32_t *>(fe_done + 1);
     volatile uint32_t *abort = tslot + 1;
 
@@ -214,11 +217,12 @@ __global__ void __launch_bounds__(128 * NPART + 96, 1) fwd_rows_kernel(StepArgs 
     if (tid == 0) {
         for (int i = 0; i < 2 * F::XRING; ++i)
             umma::mbar_init(&xfull[i], i < F::XRING ? 1 : F::W_M1);  // full: the copy bytes; empty: every compute warp
-        umma::mbar_init(g1bar, 1);
-        umma::mbar_init(&g2bar[0], 1);
-        umma::mbar_init(&g2bar[1], 1);
+        for (int b2 = 0; b2 < 2; ++b2) {
+            umma::mbar_init(&g1bar[b2], 1);
+            umma::mbar_init(&g2bar[b2], 1);
+            umma::mbar_init(&fe_done[b2], F::W_M1);
+        }
         umma::mbar_init(epi_done, F::W_M1);
-        umma::mbar_init(fe_done, F::W_M1);
         *abort = 0;
         umma::fence_mbar_init();
     }
@@ -247,14 +251,19 @@ __global__ void __launch_bounds__(128 * NPART + 96, 1) fwd_rows_kernel(StepArgs 
     const uint64_t dW2 = umma::smem_desc(umma::smem_u32(W2s), D::CP * 16, 128);
     constexpr uint32_t I1 = umma::idesc_tf32(128, HID, false, false), I2 = umma::idesc_tf32(128, 16, false, false);
     bool ok = true;
-    uint32_t ecount = 0, epar = 0, g1ph = 0, g2par = 0, eph = 0, feph = 0;  // g2par: one parity bit per U buffer
+    uint32_t ecount = 0, epar = 0, g1par = 0, g2par = 0, eph = 0, fepar = 0;  // *par: one parity bit per buffer
     int cur_k = -1, issued = 0, x_uses[F::XRING] = {0, 0, 0, 0, 0, 0};
     uint64_t *last_bar = nullptr;
     uint32_t last_par = 0;
-    auto wait_g2 = [&](int bj) {  // MMA2 into U[bj] complete
-        ok &= wait_bar(&g2bar[bj], (g2par >> bj) & 1u, abort);
-        g2par ^= 1u << bj;
+    auto wait_par = [&](uint64_t *bars, uint32_t &par, int bj) {  // the next phase of bars[bj] (one thread)
+        ok &= wait_bar(&bars[bj], (par >> bj) & 1u, abort);
+        par ^= 1u << bj;
     };
+    auto warp_wait_par = [&](uint64_t *bars, uint32_t &par, int bj) {  // the same for a whole warp
+        ok &= warp_wait_bar(&bars[bj], (par >> bj) & 1u, abort, lane32);
+        par ^= 1u << bj;
+    };
+    auto wait_g2 = [&](int bj) { wait_par(g2bar, g2par, bj); };  // MMA2 into U[bj] complete
     int64_t seg_u0 = g0;  // unit index of the current segment's first row
     auto signal = [&](uint64_t *bar) {  // this warp's TMEM / shared-memory reads and writes are complete
         umma::fence_before_sync();
@@ -280,20 +289,22 @@ __global__ void __launch_bounds__(128 * NPART + 96, 1) fwd_rows_kernel(StepArgs 
             cur_k = k;
         }
         if (prod) {
-            // ======== producer: x row wrap(r0 - 1 + e) -> slot (running entry count) % XRING, e = 0 .. L + 1
-            if (lane32 == 0) {
-                for (int e = 0; e < L + 2; ++e) {
-                    const int slot = (int)(x_uses[0] + x_uses[1] + x_uses[2] + x_uses[3] + x_uses[4] + x_uses[5]) % F::XRING;
-                    if (x_uses[slot] > 0)  // every compute warp released the slot's previous row
-                        ok &= wait_bar(&xempty[slot], (uint32_t)((x_uses[slot] - 1) & 1), abort);
-                    ++x_uses[slot];
-                    if (ok) {
-                        const int Y = wrap_index(sg.r0 - 1 + e, H);
+            // ======== producer: x row wrap(r0 - 1 + e) -> slot (running entry count) % XRING, e = 0 .. L + 1; lane c
+            // copies channel c (a starved single lane issuing all of them falls behind the compute warps)
+            for (int e = 0; e < L + 2; ++e) {
+                const int slot = (int)(x_uses[0] + x_uses[1] + x_uses[2] + x_uses[3] + x_uses[4] + x_uses[5]) % F::XRING;
+                if (lane32 == 0 && x_uses[slot] > 0)  // every compute warp released the slot's previous row
+                    ok &= wait_bar(&xempty[slot], (uint32_t)((x_uses[slot] - 1) & 1), abort);
+                ++x_uses[slot];
+                ok = __shfl_sync(~0u, ok, 0);
+                if (ok) {
+                    const int Y = wrap_index(sg.r0 - 1 + e, H);
+                    if (lane32 == 0)
                         umma::mbar_arrive_expect_tx(&xfull[slot], (uint32_t)(C * W * 4));
-                        for (int c = 0; c < C; ++c)
-                            umma::bulk_g2s(XR + ((size_t)slot * C + c) * W, xn + ((size_t)c * H + Y) * W,
-                                           (uint32_t)(W * 4), &xfull[slot]);
-                    }
+                    __syncwarp();
+                    if (lane32 < C)
+                        umma::bulk_g2s(XR + ((size_t)slot * C + lane32) * W, xn + ((size_t)lane32 * H + Y) * W,
+                                       (uint32_t)(W * 4), &xfull[slot]);
                 }
             }
         } else if (m1) {
@@ -301,8 +312,7 @@ __global__ void __launch_bounds__(128 * NPART + 96, 1) fwd_rows_kernel(StepArgs 
             if (lane32 == 0) {
                 for (int j = 0; j < L; ++j) {
                     const int bj = j & 1;
-                    ok &= wait_bar(fe_done, feph, abort);
-                    feph ^= 1;
+                    wait_par(fe_done, fepar, bj);
                     if (j >= 2)  // MMA2(j-2) read H[bj]
                         wait_g2(bj);
                     if (ok) {
@@ -311,10 +321,10 @@ __global__ void __launch_bounds__(128 * NPART + 96, 1) fwd_rows_kernel(StepArgs 
 #pragma unroll
                         for (int ks = 0; ks < D::KP / 8; ++ks)
                             umma::mma_ts(th, tp + ks * 8, dW1 + (uint64_t)(ks * 2 * HID), I1, ks > 0);
-                        umma::commit(g1bar);
-                        ++issued;
-                        last_bar = g1bar;
-                        last_par = (uint32_t)((issued - 1) & 1);
+                        umma::commit(&g1bar[bj]);
+                        last_bar = &g1bar[bj];
+                        last_par = (g1par >> bj) & 1u;  // this warp counts its own commits per H buffer
+                        g1par ^= 1u << bj;
                     }
                 }
                 for (int j = (L >= 2 ? L - 2 : 0); j < L; ++j)  // MMA2 of the last two rows: every phase waited once
@@ -342,13 +352,13 @@ __global__ void __launch_bounds__(128 * NPART + 96, 1) fwd_rows_kernel(StepArgs 
             }
         } else if (compute) {
             // ======== compute warps
-            float xcur[F::CPP], xnext[F::CPP];
-            bool mcur = false, mnext = false;
+            float xcur[F::CPP], xn1[F::CPP], xnext[F::CPP];
+            bool mcur = false, mn1 = false, mnext = false;
             int ewaited = 0;  // entries of this segment waited for
             auto front_end = [&](int j, int bj) {  // p' of row r0 + j -> P[bj]; its centre x and mask -> xnext, mnext
                 while (ewaited <= j + 2) {  // entries j .. j + 2 (rows Y - 1 .. Y + 1); slots round-robin
                     const int slot = (int)(ecount % F::XRING);
-                    ok &= wait_bar(&xfull[slot], (epar >> slot) & 1u, abort);
+                    ok &= warp_wait_bar(&xfull[slot], (epar >> slot) & 1u, abort, lane32);
                     epar ^= 1u << slot;
                     ++ecount;
                     ++ewaited;
@@ -370,7 +380,7 @@ __global__ void __launch_bounds__(128 * NPART + 96, 1) fwd_rows_kernel(StepArgs 
                     xnext[cc] = v[1][1];
                 }
                 umma::tmem_wait_st();
-                signal(fe_done);
+                signal(&fe_done[bj]);
                 signal(&xempty[s0]);  // entry j is read by no later front end
                 if (j == L - 1) {     // nor are the segment's last two entries
                     signal(&xempty[(s0 + 1) % F::XRING]);
@@ -378,15 +388,23 @@ __global__ void __launch_bounds__(128 * NPART + 96, 1) fwd_rows_kernel(StepArgs 
                 }
             };
             front_end(0, 0);
+#pragma unroll
+            for (int cc = 0; cc < F::CPP; ++cc)
+                xn1[cc] = xnext[cc];
+            mn1 = mnext;
+            if (L > 1)
+                front_end(1, 1);
             for (int i = 0; i < L; ++i) {
                 const int b = i & 1, Y = sg.r0 + i;
 #pragma unroll
-                for (int cc = 0; cc < F::CPP; ++cc)
-                    xcur[cc] = xnext[cc];
-                mcur = mnext;
+                for (int cc = 0; cc < F::CPP; ++cc) {  // rows i, i + 1 (front end done): xcur, xn1
+                    xcur[cc] = xn1[cc];
+                    xn1[cc] = xnext[cc];
+                }
+                mcur = mn1;
+                mn1 = mnext;
                 // ---- EPI(i): h -> tf32(relu(h)) in place
-                ok &= wait_bar(g1bar, g1ph, abort);
-                g1ph ^= 1;
+                warp_wait_par(g1bar, g1par, b);
                 umma::fence_after_sync();
                 const uint32_t th = lane + (b ? F::T_H1 : F::T_H0) + part * F::HPP;
 #pragma unroll
@@ -401,11 +419,11 @@ __global__ void __launch_bounds__(128 * NPART + 96, 1) fwd_rows_kernel(StepArgs 
                 }
                 umma::tmem_wait_st();
                 signal(epi_done);
-                // ---- FE(i+1)
-                if (i + 1 < L)
-                    front_end(i + 1, b ^ 1);
+                // ---- FE(i+2)
+                if (i + 2 < L)
+                    front_end(i + 2, b);
                 // ---- OUT(i): y = x + m u
-                wait_g2(b);
+                warp_wait_par(g2bar, g2par, b);
                 umma::fence_after_sync();
                 const uint32_t tu = lane + (b ? F::T_U1 : F::T_U0) + F::CPP * part;
                 float u[F::CPP];
@@ -449,6 +467,18 @@ __device__ __forceinline__ void st_sw32x8_balanced(float *tile, int mn0, int k, 
     const float4 lo = make_float4(v[0], v[1], v[2], v[3]), hi = make_float4(v[4], v[5], v[6], v[7]);
     *reinterpret_cast<float4 *>(dst + 4 * flip) = flip ? hi : lo;
     *reinterpret_cast<float4 *>(dst + 4 * (1 - flip)) = flip ? lo : hi;
+}
+
+// wait_bar for a whole warp: lane 0 polls (32 lanes polling one mbarrier word serialise on it), the others take its
+// result; __syncwarp then orders the warp's later accesses after the observed completion.
+__device__ __forceinline__ bool warp_wait_bar(uint64_t *bar, uint32_t parity, volatile uint32_t *abort, int lane)
+{
+    bool r = true;
+    if (lane == 0)
+        r = wait_bar(bar, parity, abort);
+    r = __shfl_sync(~0u, r, 0);
+    __syncwarp();
+    return r;
 }
 
 // Backward, software-pipelined across rows, with the warps synchronised by mbarriers only (no CTA-wide barrier per
