@@ -123,6 +123,18 @@ __device__ __forceinline__ bool wait_bar(uint64_t *bar, uint32_t parity, volatil
     }
 }
 
+// wait_bar for a whole warp: lane 0 polls (32 lanes polling one mbarrier word serialise on it), the others take its
+// result; __syncwarp then orders the warp's later accesses after the observed completion.
+__device__ __forceinline__ bool warp_wait_bar(uint64_t *bar, uint32_t parity, volatile uint32_t *abort, int lane)
+{
+    bool r = true;
+    if (lane == 0)
+        r = wait_bar(bar, parity, abort);
+    r = __shfl_sync(~0u, r, 0);
+    __syncwarp();
+    return r;
+}
+
 // Update mask of one image row (global image index n, row Y, W <= 128, W % 4 == 0) by one warp as 128 bits in four
 // words: lane l draws the Philox block of pixels 4l .. 4l + 3 and word e collects, by ballot, bit l = mask(4l + e), so
 // mask(x) = (word[x % 4] >> (x / 4)) & 1. Same draws and threshold as row_mask_warp.
@@ -467,18 +479,6 @@ __device__ __forceinline__ void st_sw32x8_balanced(float *tile, int mn0, int k, 
     const float4 lo = make_float4(v[0], v[1], v[2], v[3]), hi = make_float4(v[4], v[5], v[6], v[7]);
     *reinterpret_cast<float4 *>(dst + 4 * flip) = flip ? hi : lo;
     *reinterpret_cast<float4 *>(dst + 4 * (1 - flip)) = flip ? lo : hi;
-}
-
-// wait_bar for a whole warp: lane 0 polls (32 lanes polling one mbarrier word serialise on it), the others take its
-// result; __syncwarp then orders the warp's later accesses after the observed completion.
-__device__ __forceinline__ bool warp_wait_bar(uint64_t *bar, uint32_t parity, volatile uint32_t *abort, int lane)
-{
-    bool r = true;
-    if (lane == 0)
-        r = wait_bar(bar, parity, abort);
-    r = __shfl_sync(~0u, r, 0);
-    __syncwarp();
-    return r;
 }
 
 // Backward, software-pipelined across rows, with the warps synchronised by mbarriers only (no CTA-wide barrier per
