@@ -123,18 +123,6 @@ __device__ __forceinline__ bool wait_bar(uint64_t *bar, uint32_t parity, volatil
     }
 }
 
-// wait_bar for a whole warp: lane 0 polls (32 lanes polling one mbarrier word serialise on it), the others take its
-// result; __syncwarp then orders the warp's later accesses after the observed completion.
-__device__ __forceinline__ bool warp_wait_bar(uint64_t *bar, uint32_t parity, volatile uint32_t *abort, int lane)
-{
-    bool r = true;
-    if (lane == 0)
-        r = wait_bar(bar, parity, abort);
-    r = __shfl_sync(~0u, r, 0);
-    __syncwarp();
-    return r;
-}
-
 // Update mask of one image row (global image index n, row Y, W <= 128, W % 4 == 0) by one warp as 128 bits in four
 // words: lane l draws the Philox block of pixels 4l .. 4l + 3 and word e collects, by ballot, bit l = mask(4l + e), so
 // mask(x) = (word[x % 4] >> (x / 4)) & 1. Same draws and threshold as row_mask_warp.
@@ -267,12 +255,8 @@ __global__ void __launch_bounds__(128 * NPART + 96, 1) fwd_rows_kernel(StepArgs 
     int cur_k = -1, issued = 0, x_uses[F::XRING] = {0, 0, 0, 0, 0, 0};
     uint64_t *last_bar = nullptr;
     uint32_t last_par = 0;
-    auto wait_par = [&](uint64_t *bars, uint32_t &par, int bj) {  // the next phase of bars[bj] (one thread)
+    auto wait_par = [&](uint64_t *bars, uint32_t &par, int bj) {  // the next phase of bars[bj]
         ok &= wait_bar(&bars[bj], (par >> bj) & 1u, abort);
-        par ^= 1u << bj;
-    };
-    auto warp_wait_par = [&](uint64_t *bars, uint32_t &par, int bj) {  // the same for a whole warp
-        ok &= warp_wait_bar(&bars[bj], (par >> bj) & 1u, abort, lane32);
         par ^= 1u << bj;
     };
     auto wait_g2 = [&](int bj) { wait_par(g2bar, g2par, bj); };  // MMA2 into U[bj] complete
@@ -370,7 +354,7 @@ __global__ void __launch_bounds__(128 * NPART + 96, 1) fwd_rows_kernel(StepArgs 
             auto front_end = [&](int j, int bj) {  // p' of row r0 + j -> P[bj]; its centre x and mask -> xnext, mnext
                 while (ewaited <= j + 2) {  // entries j .. j + 2 (rows Y - 1 .. Y + 1); slots round-robin
                     const int slot = (int)(ecount % F::XRING);
-                    ok &= warp_wait_bar(&xfull[slot], (epar >> slot) & 1u, abort, lane32);
+                    ok &= wait_bar(&xfull[slot], (epar >> slot) & 1u, abort);
                     epar ^= 1u << slot;
                     ++ecount;
                     ++ewaited;
@@ -416,7 +400,7 @@ __global__ void __launch_bounds__(128 * NPART + 96, 1) fwd_rows_kernel(StepArgs 
                 mcur = mn1;
                 mn1 = mnext;
                 // ---- EPI(i): h -> tf32(relu(h)) in place
-                warp_wait_par(g1bar, g1par, b);
+                wait_par(g1bar, g1par, b);
                 umma::fence_after_sync();
                 const uint32_t th = lane + (b ? F::T_H1 : F::T_H0) + part * F::HPP;
 #pragma unroll
@@ -435,7 +419,7 @@ __global__ void __launch_bounds__(128 * NPART + 96, 1) fwd_rows_kernel(StepArgs 
                 if (i + 2 < L)
                     front_end(i + 2, b);
                 // ---- OUT(i): y = x + m u
-                warp_wait_par(g2bar, g2par, b);
+                wait_g2(b);
                 umma::fence_after_sync();
                 const uint32_t tu = lane + (b ? F::T_U1 : F::T_U0) + F::CPP * part;
                 float u[F::CPP];
