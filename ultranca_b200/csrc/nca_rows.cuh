@@ -151,6 +151,80 @@ __device__ __forceinline__ void row_mask_bits_warp(uint32_t *dst, uint64_t seed,
     }
 }
 
+// Weights of NCA k for the row kernels (TF32), as float4 items whose shared-memory address is linear in the item index:
+//   W1s  (HID x KP, K-major chunk-planar: plane f/4 of HID rows x 4): w1 | b1_hi, b1_lo (the bias as two TF32 columns) | 0
+//   W1T  (backward only; PIN x HID: plane j/4 of PIN rows x 4): w1 transposed
+//   W2x  forward: W2s (CP x HID: plane j/4 of CP rows x 4), channels C..CP-1 zero;
+//        backward: W2T (HID x CP: plane k/4 of HID rows x 4), channel c at k = c + gm_off, other k zero.
+// Each thread loads a batch of items before it rounds and stores any (the loads of a batch are in flight together).
+template <class D, bool BWD>
+__device__ __forceinline__ void stage_rows_weights(float *W1s, float *W1T, float *W2x, const float *w1, const float *b1,
+                                                   const float *w2, int t0, int nt, int gm_off)
+{
+    constexpr int Q = D::PIN / 4, N1 = (D::KP / 4) * D::HID;
+    constexpr int N2 = BWD ? (D::HID / 4) * D::PIN : 0;
+    constexpr int N3 = BWD ? (D::CP / 4) * D::HID : (D::HID / 4) * D::CP;
+    constexpr int NT = N1 + N2 + N3, BATCH = 4;
+    for (int base = t0; base < NT; base += BATCH * nt) {
+        float v[BATCH][4];
+#pragma unroll
+        for (int b = 0; b < BATCH; ++b) {
+            const int it = base + b * nt;
+#pragma unroll
+            for (int t = 0; t < 4; ++t)
+                v[b][t] = 0.f;
+            if (it < N1) {
+                const int q = it / D::HID, j = it % D::HID;
+                if (q < Q) {
+#pragma unroll
+                    for (int t = 0; t < 4; ++t)
+                        v[b][t] = __ldg(w1 + j * D::PIN + 4 * q + t);
+                } else if (q == Q) {
+                    v[b][0] = __ldg(b1 + j);
+                }
+            } else if (it < N1 + N2) {
+                const int r = (it - N1) / D::PIN, f = (it - N1) % D::PIN;
+#pragma unroll
+                for (int t = 0; t < 4; ++t)
+                    v[b][t] = __ldg(w1 + (4 * r + t) * D::PIN + f);
+            } else if (it < NT) {
+                const int i3 = it - N1 - N2;
+                if (BWD) {
+                    const int pl = i3 / D::HID, j = i3 % D::HID;
+#pragma unroll
+                    for (int t = 0; t < 4; ++t) {
+                        const int c = 4 * pl + t - gm_off;
+                        if (c >= 0 && c < D::C)
+                            v[b][t] = __ldg(w2 + c * D::HID + j);
+                    }
+                } else {
+                    const int pl = i3 / D::CP, c = i3 % D::CP;
+                    if (c < D::C)
+#pragma unroll
+                        for (int t = 0; t < 4; ++t)
+                            v[b][t] = __ldg(w2 + c * D::HID + 4 * pl + t);
+                }
+            }
+        }
+#pragma unroll
+        for (int b = 0; b < BATCH; ++b) {
+            const int it = base + b * nt;
+            if (it >= NT)
+                continue;
+            float4 o;
+            if (it < N1 && it / D::HID == Q) {  // bias columns: b1_hi, b1_lo, 0, 0
+                const float hi = tf32_rna(v[b][0]);
+                o = make_float4(hi, tf32_rna(v[b][0] - hi), 0.f, 0.f);
+            } else {
+                o = make_float4(tf32_rna(v[b][0]), tf32_rna(v[b][1]), tf32_rna(v[b][2]), tf32_rna(v[b][3]));
+            }
+            float *dst = it < N1 ? W1s + (size_t)it * 4 : it < N1 + N2 ? W1T + (size_t)(it - N1) * 4
+                                                                        : W2x + (size_t)(it - N1 - N2) * 4;
+            *reinterpret_cast<float4 *>(dst) = o;
+        }
+    }
+}
+
 // ================================================================ forward
 // Forward, software-pipelined across rows with the warps synchronised by mbarriers only. Warps 0 .. 4 NPART - 1
 // compute (part p owns channels [CPP p, CPP (p+1)) and hidden units [HPP p, HPP (p+1)) of pixel x = its TMEM lane).
@@ -277,8 +351,8 @@ __global__ void __launch_bounds__(128 * NPART + 96, 1) fwd_rows_kernel(StepArgs 
         if (k != cur_k) {  // every warp finished the previous segment (and its MMAs completed): restage the weights
             umma::fence_before_sync();
             __syncthreads();
-            stage_weights<D, true>(W1s, W2s, a.w1 + (size_t)k * HID * D::PIN, a.b1 + (size_t)k * HID,
-                                   a.w2 + (size_t)k * C * HID);
+            stage_rows_weights<D, false>(W1s, nullptr, W2s, a.w1 + (size_t)k * HID * D::PIN, a.b1 + (size_t)k * HID,
+                                         a.w2 + (size_t)k * C * HID, tid, blockDim.x, 0);
             umma::fence_proxy_async();
             __syncthreads();
             umma::fence_after_sync();
@@ -630,13 +704,13 @@ __global__ void __launch_bounds__(128 * NPART + 96, 1) bwd_rows_kernel(StepArgs 
             if (lane32 == 0)
                 mbar_arrive(bar);
         };
-        auto flush = [&](int kk) {  // WG accumulator -> partial slot (blockIdx.x + kk); TMEM lanes 0..63 (warps 0, 1)
-            if (!compute || part != 0 || wq >= 2)
+        auto flush = [&](int kk) {  // WG accumulator -> partial slot (blockIdx.x + kk); TMEM lanes 0..63 are read by
+            if (!compute || wq >= 2)  // the warps of lane quadrants 0 and 1, part p taking column chunks p, p + NPART, ..
                 return;
             const int f = x;
             float *out = a.partial + (size_t)(blockIdx.x + kk) * D::PART;
 #pragma unroll 1
-            for (int cc = 0; cc < F::NACC / 16; ++cc) {
+            for (int cc = part; cc < F::NACC / 16; cc += NPART) {
                 float v[16];
                 umma::tmem_ld16(lane + F::T_ACC + cc * 16, v);
                 umma::tmem_wait_ld();
@@ -710,8 +784,8 @@ __global__ void __launch_bounds__(128 * NPART + 96, 1) bwd_rows_kernel(StepArgs 
                 group_sync();  // every warp finished the previous segment; its tensor-core work completed
                 if (ok && cur_k >= 0)
                     flush(cur_k);
-                stage_bwd_weights<D>(W1s, W1T, W2T, a.w1 + (size_t)k * HID * D::PIN, a.b1 + (size_t)k * HID,
-                                     a.w2 + (size_t)k * C * HID, tid, F::GROUP, F::GM0 - D::PIN);
+                stage_rows_weights<D, true>(W1s, W1T, W2T, a.w1 + (size_t)k * HID * D::PIN, a.b1 + (size_t)k * HID,
+                                            a.w2 + (size_t)k * C * HID, tid, F::GROUP, F::GM0 - D::PIN);
                 umma::fence_proxy_async();
                 group_sync();
                 cur_k = k;
