@@ -228,7 +228,7 @@ int bwd_ctas_per_sm()
 
 // Row-streaming kernels (the benchmark's hot path): TF32 texture NCAs whose rows are whole 16-byte multiples that
 // fit one 128-lane tile; every other case runs the tile kernels.
-constexpr int FWD_ROWS_PARTS = 4, BWD_ROWS_PARTS = 4;
+constexpr int FWD_ROWS_PARTS = 2, BWD_ROWS_PARTS = 4;
 bool rows_path(const Shape &s, bool fp32, bool growing)
 {
     return !fp32 && !growing && s.C == 12 && s.HID == 96 && s.W <= 128 && s.W % 4 == 0;
