@@ -326,7 +326,7 @@ __global__ void __launch_bounds__(128 * NPART + 96, 1) fwd_rows_kernel(StepArgs 
     constexpr uint32_t I1 = umma::idesc_tf32(128, HID, false, false), I2 = umma::idesc_tf32(128, 16, false, false);
     bool ok = true;
     uint32_t ecount = 0, epar = 0, g1par = 0, g2par = 0, eph = 0, fepar = 0;  // *par: one parity bit per buffer
-    int cur_k = -1, issued = 0, x_uses[F::XRING] = {0, 0, 0, 0, 0, 0};
+    int cur_k = -1, x_uses[F::XRING] = {0, 0, 0, 0, 0, 0};
     uint64_t *last_bar = nullptr;
     uint32_t last_par = 0;
     auto wait_par = [&](uint64_t *bars, uint32_t &par, int bj) {  // the next phase of bars[bj]
@@ -608,10 +608,11 @@ __global__ void __launch_bounds__(128 * NPART + 96, 1) bwd_rows_kernel(StepArgs 
     const size_t plane = (size_t)H * W;
 
     // constant PSW features of both buffers: 1 at PIN and PIN + 1, 0 at GM0 + C .. 63
-    for (int e = tid; e < 2 * 128 * 64; e += blockDim.x) {
-        const int b = e / (128 * 64), q = (e / 64) % 128, f = e % 64;
-        if (f >= D::PIN && (f < F::GM0 || f >= F::GM0 + C))
-            PSW[b * D::PSW + umma::sw32_offset(f, q, 128) / 4] = f < F::GM0 ? 1.f : 0.f;
+    constexpr int NCONST = 64 - C - D::PIN;  // features PIN .. 63 other than gm
+    for (int e = tid; e < 2 * 128 * NCONST; e += blockDim.x) {
+        const int b = e / (128 * NCONST), q = (e / NCONST) % 128, i = e % NCONST;
+        const int f = i < F::GM0 - D::PIN ? D::PIN + i : F::GM0 + C + (i - (F::GM0 - D::PIN));
+        PSW[b * D::PSW + umma::sw32_offset(f, q, 128) / 4] = f < F::GM0 ? 1.f : 0.f;
     }
     if (tid == 0) {
         for (int i = 0; i < F::XRING; ++i)
@@ -779,7 +780,13 @@ __global__ void __launch_bounds__(128 * NPART + 96, 1) bwd_rows_kernel(StepArgs 
                         mbar_arrive(&mkfull[j & 1]);
                 }
             };
-            // ---- segment prologue: a new NCA needs its weights (and the old accumulator flushed)
+            // ---- segment prologue. The first x rows are requested before any weight work (their slots were consumed
+            // by the previous segment's last front end, which the producer waited for), so that the copies are in
+            // flight while a new NCA's weights are staged.
+            if (prod)
+                for (int e = 0; e < F::XRING; ++e)
+                    issue_x(e);
+            // a new NCA needs its weights (and the old accumulator flushed)
             if (k != cur_k) {
                 group_sync();  // every warp finished the previous segment; its tensor-core work completed
                 if (ok && cur_k >= 0)
@@ -791,9 +798,8 @@ __global__ void __launch_bounds__(128 * NPART + 96, 1) bwd_rows_kernel(StepArgs 
                 cur_k = k;
             }
             if (prod) {
-                // ======== producer: entries 0..2 and masks 0, 1; after every warp's FE(j): entry j + 3, mask j + 2
-                for (int e = 0; e < F::XRING; ++e)
-                    issue_x(e);
+                // ======== producer: entries 0..2 (issued above) and masks 0, 1; after every warp's FE(j): entry j + 3,
+                // mask j + 2
                 draw_mask(0);
                 if (L > 1)
                     draw_mask(1);
