@@ -252,18 +252,20 @@ def main():
             evs.append(('fwd', e0, e1))
         training.synthetic_loss(t.states[STEPS], target, 10.0, t.gy[0], t.loss, t.loss_work)
         cur = t.gy[0]
-        for n, s in enumerate(reversed(range(STEPS))):
+        t.partial.zero_()
+        for s in reversed(range(STEPS)):
             nxt = t.gy[1] if cur is t.gy[0] else t.gy[0]
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             common = (ptr(t.states[s]), ptr(cur), None, ptr(w1), ptr(b1), ptr(w2), ptr(nxt), ptr(t.grads[0]),
                       ptr(t.grads[1]), ptr(t.grads[2]), ptr(t.dp), t.dp_floats, ptr(t.partial), t.partial_floats, t.N, C,
-                      H, W, K, HID, B, nca_ops.step_seed(seed, s), RATE, 0, 0, t.image_offset, int(n > 0))
+                      H, W, K, HID, B, nca_ops.step_seed(seed, s), RATE, 0, 0, t.image_offset, 0)
             e0.record(stream)
-            check(lib.nca_backward_stages(*common, 1, st))
+            check(lib.nca_backward_stages(*common, training.STAGE_MAIN | training.STAGE_PARTIAL_ADD, st))
             e1.record(stream)
-            check(lib.nca_backward_stages(*common, 6, st))
+            check(lib.nca_backward_stages(*common, training.STAGE_ADJOINT, st))  # fused into the main kernel on rows
             evs.append(('bwd_main', e0, e1))
             cur = nxt
+        check(lib.nca_backward_stages(*common, training.STAGE_REDUCE, st))
         t.opt.step(t.grads)
         pending.append(evs)
         return t.loss
@@ -304,8 +306,8 @@ def main():
     cells_per_iter = world * K * B * H * W * STEPS
     value = cells_per_iter * args.steps / (ms / 1000.0)
     rows = nca_ops.launch_info(C, HID, False, K * B, H, W, K)['rows_path']
-    # forward 1 / step; backward: fused kernel + reduce (row path) or main + adjoint + reduce; loss 2; optimiser 2
-    launches_per_iter = STEPS * 1 + 2 + STEPS * (2 if rows else 3) + 2
+    # forward 1 / step; backward: fused kernel (row path) or main + adjoint per step, one reduce; loss 2; optimiser 2
+    launches_per_iter = STEPS * 1 + 2 + STEPS * (1 if rows else 2) + 1 + 2
     # roofline of the dominant kernel (the larger total of the forward kernel and the backward main kernel)
     tot = {k: sum(v) for k, v in stage_times.items()}
     dom = max(tot, key=tot.get)

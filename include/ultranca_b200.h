@@ -84,6 +84,11 @@ int nca_backward(const float *x, const float *gy, const uint8_t *alive, const fl
 #define NCA_STAGE_MAIN 1
 #define NCA_STAGE_ADJOINT 2
 #define NCA_STAGE_REDUCE 4
+/* With NCA_STAGE_MAIN: add this call's weight-gradient partials to the partial workspace instead of replacing them.
+ * A run of calls of one shape (a rollout's backward steps) then needs a single NCA_STAGE_REDUCE at its end; the caller
+ * zeroes the partial workspace before the run's first call. No reference counterpart (the reference reduces the
+ * weight gradients of every step, ncaops/nca_cuda.cu:285-322). */
+#define NCA_STAGE_PARTIAL_ADD 8
 int nca_backward_stages(const float *x, const float *gy, const uint8_t *alive, const float *w1, const float *b1,
                         const float *w2, float *gx, float *dw1, float *db1, float *dw2, float *dp, int64_t dp_floats,
                         float *partial, int64_t partial_floats, int64_t N, int64_t C, int64_t H, int64_t W, int64_t K,

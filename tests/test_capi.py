@@ -75,3 +75,13 @@ def test_ncaops_import_path_is_the_same_module():
     nca_ops.CHUNK = 3
     assert impl.CHUNK == 3
     nca_ops.CHUNK = None
+
+
+def test_partial_add_stage_requires_main():
+    """NCA_STAGE_PARTIAL_ADD (8) modifies NCA_STAGE_MAIN: on its own it is an argument error, found before any device
+    work."""
+    from ultranca_b200._lib import lib
+    p = ctypes.c_void_p(256)
+    st = lib.nca_backward_stages(p, p, None, p, p, p, p, p, p, p, p, 1 << 30, p, 1 << 30, 4, 12, 8, 16, 2, 96, 2, 0, 0.5,
+                                 0, 0, 0, 0, 8, None)
+    assert st == 1 and 'PARTIAL_ADD' in lib.nca_last_error().decode()

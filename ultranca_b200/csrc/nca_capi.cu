@@ -395,8 +395,10 @@ int nca_backward_stages(const float *x, const float *gy, const uint8_t *alive, c
     return guarded([&] {
         const Shape s{N, C, H, W, K, hidden, (int64_t)batch_per_nca};
         validate(s, growing);
-        if (stages <= 0 || stages > 7)
+        if (stages <= 0 || stages > 15)
             fail(NCA_ERR_ARGUMENT, "stages must be a nonzero mask of NCA_STAGE_* bits");
+        if ((stages & NCA_STAGE_PARTIAL_ADD) && !(stages & NCA_STAGE_MAIN))
+            fail(NCA_ERR_ARGUMENT, "NCA_STAGE_PARTIAL_ADD applies to NCA_STAGE_MAIN");
         check_ptr(x, "x"); check_ptr(gy, "gy"); check_ptr(w1, "w1"); check_ptr(b1, "b1"); check_ptr(w2, "w2");
         check_ptr(gx, "gx"); check_ptr(dw1, "dw1"); check_ptr(db1, "db1"); check_ptr(dw2, "dw2"); check_ptr(dp, "dp");
         check_ptr(partial, "partial");
@@ -416,6 +418,7 @@ int nca_backward_stages(const float *x, const float *gy, const uint8_t *alive, c
             a.x = x; a.w1 = w1; a.b1 = b1; a.w2 = w2; a.gy = gy; a.alive = alive; a.dp = dp; a.partial = partial;
             a.N = (int)N; a.B = (int)batch_per_nca; a.H = (int)H; a.W = (int)W;
             a.seed = seed; a.rate = update_rate; a.n_offset = image_offset;
+            a.partial_add = (stages & NCA_STAGE_PARTIAL_ADD) ? 1 : 0;
             const TileGeom g = make_geom((int)H, (int)W);
             const bool rows = rows_path(s, fp32, growing) && aligned16(x) && aligned16(gy) && aligned16(gx);
             int64_t units = N * g.tiles_per_image, units_per_nca = (int64_t)batch_per_nca * g.tiles_per_image;

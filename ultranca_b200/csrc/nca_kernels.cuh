@@ -64,6 +64,7 @@ struct StepArgs {
     uint64_t seed;
     float rate;
     int64_t n_offset;              // global index of image 0 (Philox counter)
+    int partial_add;               // backward: add the weight-gradient partials to the slots instead of storing them
 };
 
 // Stage one NCA's weights: W1' (HID x KP, chunk-planar: plane f/4, row j) with the bias columns, W2 (16 x HID,
@@ -354,13 +355,32 @@ __global__ void alive_kernel(const float *__restrict__ x, const float *__restric
 // dW1' += dh^T p' (column PIN of p' is 1: db1), dW2^T += relu(h)^T gm, accumulated per NCA segment (TMEM in TF32 mode,
 // registers of threads j < HID in fp32 mode) and written to partial slot (CTA + NCA).
 template <class D>
-__device__ __forceinline__ void write_partial_row(float *out, int j, const float *dw1_row, float db1, const float *dw2_col)
+__device__ __forceinline__ void write_partial_row(float *out, int j, const float *dw1_row, float db1, const float *dw2_col,
+                                                  bool add)
 {
+    if (!add) {
+        for (int f = 0; f < D::PIN; ++f)
+            out[j * D::PIN + f] = dw1_row[f];
+        out[D::HID * D::PIN + j] = db1;
+        for (int c = 0; c < D::C; ++c)
+            out[D::HID * (D::PIN + 1) + c * D::HID + j] = dw2_col[c];
+        return;
+    }
+    float o1[D::PIN], o2[D::C];  // the old values first (all in flight), then the sums
+#pragma unroll
     for (int f = 0; f < D::PIN; ++f)
-        out[j * D::PIN + f] = dw1_row[f];
-    out[D::HID * D::PIN + j] = db1;
+        o1[f] = out[j * D::PIN + f];
+    const float ob = out[D::HID * D::PIN + j];
+#pragma unroll
     for (int c = 0; c < D::C; ++c)
-        out[D::HID * (D::PIN + 1) + c * D::HID + j] = dw2_col[c];
+        o2[c] = out[D::HID * (D::PIN + 1) + c * D::HID + j];
+#pragma unroll
+    for (int f = 0; f < D::PIN; ++f)
+        out[j * D::PIN + f] = o1[f] + dw1_row[f];
+    out[D::HID * D::PIN + j] = ob + db1;
+#pragma unroll
+    for (int c = 0; c < D::C; ++c)
+        out[D::HID * (D::PIN + 1) + c * D::HID + j] = o2[c] + dw2_col[c];
 }
 
 // Per tile pixel: gm = gy m (a) (growing: a = the alive mask of the forward), 16 channels, fp32.
@@ -412,7 +432,7 @@ __global__ void __launch_bounds__(128, 1) bwd_kernel_cc(StepArgs a)
     int cur_k = -1;
     auto flush = [&](int k) {
         if (tid < HID)
-            write_partial_row<D>(a.partial + (size_t)(blockIdx.x + k) * D::PART, tid, acc1, accb, acc2);
+            write_partial_row<D>(a.partial + (size_t)(blockIdx.x + k) * D::PART, tid, acc1, accb, acc2, a.partial_add != 0);
 #pragma unroll
         for (int f = 0; f < D::PIN; ++f)
             acc1[f] = 0.f;
@@ -597,7 +617,8 @@ __global__ void __launch_bounds__(128, 1) bwd_kernel_tc(StepArgs a)
         umma::tmem_ld16(lane_base + D::T_ACC2, col);
         umma::tmem_wait_ld();
         if (tid < HID)
-            write_partial_row<D>(a.partial + (size_t)(blockIdx.x + k) * D::PART, tid, row, row[D::PIN], col);
+            write_partial_row<D>(a.partial + (size_t)(blockIdx.x + k) * D::PART, tid, row, row[D::PIN], col,
+                                 a.partial_add != 0);
         umma::fence_before_sync();
     };
 

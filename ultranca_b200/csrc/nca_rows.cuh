@@ -562,7 +562,7 @@ struct BwdRows {
     // TMEM: h / dh, dhp, WG accumulator, P[2] (p' 0..PIN-1 then dp; 1, 1 at PIN, PIN+1; gm at GM0..; zeros)
     static constexpr int T_H = 0, T_DHP = HID, T_ACC = 2 * HID, NACC = 2 * HID, T_P0 = T_ACC + NACC, T_P1 = T_P0 + 64;
     static constexpr int TMEM = 512;
-    static_assert(C % NPART == 0 && HPP % 8 == 0 && D::KP == 56 && GM0 + C <= 62 && T_P1 + 64 <= TMEM &&
+    static_assert(C % NPART == 0 && C <= 16 && HPP % 8 == 0 && D::KP == 56 && GM0 + C <= 62 && T_P1 + 64 <= TMEM &&
                   HID % 32 == 0 && NACC <= 256 && D::NPW == 64, "backward row-kernel layout");
     // shared memory, 1024-aligned base: weights | PSW[2] | RH | DH (swizzled MN-major) | XR | EDGE[2] | MK[2] | bars
     // (WG reads 4 MN blocks of PSW[b] for M = 128: for b = 1 the last two are RH, in bounds and unused)
@@ -710,22 +710,30 @@ __global__ void __launch_bounds__(128 * NPART + 96, 1) bwd_rows_kernel(StepArgs 
                 return;
             const int f = x;
             float *out = a.partial + (size_t)(blockIdx.x + kk) * D::PART;
+            const bool add = a.partial_add != 0;
 #pragma unroll 1
             for (int cc = part; cc < F::NACC / 16; cc += NPART) {
-                float v[16];
+                float v[16], old[16];
                 umma::tmem_ld16(lane + F::T_ACC + cc * 16, v);
+                // this thread's slot element for column j = cc 16 + e, or null: dw2[c][j] (rows GM0.., j < HID),
+                // dw1[j - HID][f] (rows < PIN) and db1[j - HID] (row PIN)
+                auto dst = [&](int e) -> float * {
+                    const int j = cc * 16 + e;
+                    if (j < HID)
+                        return f >= F::GM0 && f < F::GM0 + C ? out + HID * (D::PIN + 1) + (f - F::GM0) * HID + j : nullptr;
+                    return f < D::PIN ? out + (j - HID) * D::PIN + f : f == D::PIN ? out + HID * D::PIN + (j - HID) : nullptr;
+                };
+#pragma unroll
+                for (int e = 0; e < 16; ++e) {  // every old value in flight before the first store
+                    float *o = dst(e);
+                    old[e] = add && o != nullptr ? *o : 0.f;
+                }
                 umma::tmem_wait_ld();
 #pragma unroll
                 for (int e = 0; e < 16; ++e) {
-                    const int j = cc * 16 + e;
-                    if (j < HID) {
-                        if (f >= F::GM0 && f < F::GM0 + C)
-                            out[HID * (D::PIN + 1) + (f - F::GM0) * HID + j] = v[e];  // dw2[c][j]
-                    } else if (f < D::PIN) {
-                        out[(j - HID) * D::PIN + f] = v[e];                          // dw1[j][f]
-                    } else if (f == D::PIN) {
-                        out[HID * D::PIN + (j - HID)] = v[e];                        // db1[j]
-                    }
+                    float *o = dst(e);
+                    if (o != nullptr)
+                        *o = old[e] + v[e];
                 }
             }
         };
@@ -770,6 +778,18 @@ __global__ void __launch_bounds__(128 * NPART + 96, 1) bwd_rows_kernel(StepArgs 
                     ++x_issued[slot];
                 }
             };
+            // producer warp: the x row of entry e and the gy row of sequence row e - 1 (read by the front end of that
+            // row) into L2, some rows before their copy / load: the three-slot ring alone does not cover the latency
+            // of HBM (one lane per channel row)
+            auto prefetch_rows = [&](int e) {
+                if (e > L + 1)
+                    return;
+                if (lane32 < C)
+                    umma::bulk_prefetch_l2(xn + ((size_t)lane32 * H + wrap_index(sg.r0 - 2 + e, H)) * W, (uint32_t)(W * 4));
+                const int c = lane32 - 16;
+                if (c >= 0 && c < C && e >= 1 && e - 1 < L)
+                    umma::bulk_prefetch_l2(gyn + ((size_t)c * H + rowY(e - 1)) * W, (uint32_t)(W * 4));
+            };
             // producer warp: update mask of sequence row j -> MK[j % 2], then mkfull[j % 2]
             auto draw_mask = [&](int j) {
                 ok = __shfl_sync(~0u, ok, 0);
@@ -783,9 +803,12 @@ __global__ void __launch_bounds__(128 * NPART + 96, 1) bwd_rows_kernel(StepArgs 
             // ---- segment prologue. The first x rows are requested before any weight work (their slots were consumed
             // by the previous segment's last front end, which the producer waited for), so that the copies are in
             // flight while a new NCA's weights are staged.
-            if (prod)
+            if (prod) {
                 for (int e = 0; e < F::XRING; ++e)
                     issue_x(e);
+                for (int e = F::XRING; e < 2 * F::XRING; ++e)
+                    prefetch_rows(e);
+            }
             // a new NCA needs its weights (and the old accumulator flushed)
             if (k != cur_k) {
                 group_sync();  // every warp finished the previous segment; its tensor-core work completed
@@ -810,6 +833,7 @@ __global__ void __launch_bounds__(128 * NPART + 96, 1) bwd_rows_kernel(StepArgs 
                     ok = __shfl_sync(~0u, ok, 0);
                     if (j + 3 <= L + 1)
                         issue_x(j + 3);
+                    prefetch_rows(j + 2 * F::XRING);
                     if (j + 2 < L)
                         draw_mask(j + 2);
                 }
@@ -899,6 +923,14 @@ __global__ void __launch_bounds__(128 * NPART + 96, 1) bwd_rows_kernel(StepArgs 
                 for (int i = 0; i < L; ++i) {
                     const int b = i & 1, Y = rowY(i);
                     const bool owned = i >= 1 && i <= L - 2, next = i + 1 < L;
+                    // gy of row Y - 1, for the final gx of that row at the end of this row's adjoint: requested now (an
+                    // L2 hit: its front end read it two rows ago) so that the loads complete under EA and FE
+                    const bool fin = i >= 2 && vx;
+                    const size_t prow = (size_t)wrap_index(Y - 1, H) * W + xc;
+                    float gprev[F::CPP];
+#pragma unroll
+                    for (int cc = 0; cc < F::CPP; ++cc)
+                        gprev[cc] = fin ? __ldg(gyn + prow + (size_t)(F::CPP * part + cc) * plane) : 0.f;
                     // ---- EA(i): relu(h) -> RH, dh -> DH (owned rows) and TMEM H; needs G1(i) and WG(i-1)
                     ok &= wait_bar(g1bar, g1ph, abort);
                     g1ph ^= 1;
@@ -960,12 +992,6 @@ __global__ void __launch_bounds__(128 * NPART + 96, 1) bwd_rows_kernel(StepArgs 
                         }
                     }
                     bar_sync(2 + part, 128);
-                    const bool fin = i >= 2 && vx;
-                    const size_t prow = (size_t)wrap_index(Y - 1, H) * W + xc;
-                    float gprev[F::CPP];  // gy of row Y - 1 (read two rows ago by its front end: an L2 hit)
-#pragma unroll
-                    for (int cc = 0; cc < F::CPP; ++cc)
-                        gprev[cc] = fin ? __ldg(gyn + prow + (size_t)(F::CPP * part + cc) * plane) : 0.f;
 #pragma unroll
                     for (int cc = 0; cc < F::CPP; ++cc) {
                         const int c = F::CPP * part + cc;

@@ -188,6 +188,12 @@ __device__ __forceinline__ void tmem_ld8(uint32_t taddr, float *v)
     for (int i = 0; i < 8; ++i)
         v[i] = __uint_as_float(r[i]);
 }
+// Prefetch `bytes` (a multiple of 16, 16-byte aligned) from global memory into L2, asynchronously.
+__device__ __forceinline__ void bulk_prefetch_l2(const void *src, uint32_t bytes)
+{
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+
 __device__ __forceinline__ float tmem_ld1(uint32_t taddr)
 {
     uint32_t r;

@@ -2,9 +2,10 @@
 driven through the C-ABI without autograd:
 
   pool sample -> `steps` forward steps (each step's input state kept for the backward, as _Step saves x,
-  nca_ops.py:27) -> synthetic loss and its gradient -> `steps` backward steps in reverse, the weight gradients summed
-  in the reduce kernel (accumulate=1) instead of a torch add per step -> per-NCA per-tensor gradient normalisation +
-  Adam + MultiStepLR in one launch (train.py:136-141).
+  nca_ops.py:27) -> synthetic loss and its gradient -> `steps` backward steps in reverse, each adding its per-CTA
+  weight-gradient partials to the partial workspace (zeroed once), then one reduce of the whole rollout's gradient
+  instead of a reduce (or a torch add) per step -> per-NCA per-tensor gradient normalisation + Adam + MultiStepLR in
+  one launch (train.py:136-141).
 
 The synthetic loss replaces the OT texture loss (which needs VGG16 weights and datasets): per NCA, the mean squared
 error of channels 0-2 to a target plus 10 x the overflow |x - clamp(x, -1, 1)| summed (config.yml overflow_weight).
@@ -17,6 +18,7 @@ from ._lib import check, lib, ptr
 from .nca_ops import backward_workspace, step_seed
 
 LOSS_CHUNKS = 64
+STAGE_MAIN, STAGE_ADJOINT, STAGE_REDUCE, STAGE_PARTIAL_ADD = 1, 2, 4, 8  # include/ultranca_b200.h NCA_STAGE_*
 
 
 def _stream(dev):
@@ -105,15 +107,17 @@ class RolloutTrainer:
         s, g = self.states, self.grads
         st = _stream(s.device)
         cur = gy_last
-        for n, i in enumerate(reversed(range(self.steps if steps is None else steps))):
+        self.partial.zero_()  # every step adds its partials; one reduce at the end
+        args = lambda i, cur, nxt: (ptr(s[i]), ptr(cur), ptr(self.alive[i]) if self.growing else None, ptr(self.w1),
+                                    ptr(self.b1), ptr(self.w2), ptr(nxt), ptr(g[0]), ptr(g[1]), ptr(g[2]), ptr(self.dp),
+                                    self.dp_floats, ptr(self.partial), self.partial_floats, self.N, self.C, self.H,
+                                    self.W, self.K, self.HID, self.B, step_seed(seed, i), self.rate, int(self.fp32),
+                                    int(self.growing), self.image_offset, 0)
+        for i in reversed(range(self.steps if steps is None else steps)):
             nxt = self.gy[1] if cur is self.gy[0] else self.gy[0]
-            alive = ptr(self.alive[i]) if self.growing else None
-            check(lib.nca_backward(ptr(s[i]), ptr(cur), alive, ptr(self.w1), ptr(self.b1), ptr(self.w2), ptr(nxt),
-                                   ptr(g[0]), ptr(g[1]), ptr(g[2]), ptr(self.dp), self.dp_floats, ptr(self.partial),
-                                   self.partial_floats, self.N, self.C, self.H, self.W, self.K, self.HID, self.B,
-                                   step_seed(seed, i), self.rate, int(self.fp32), int(self.growing), self.image_offset,
-                                   int(n > 0), st))
+            check(lib.nca_backward_stages(*args(i, cur, nxt), STAGE_MAIN | STAGE_ADJOINT | STAGE_PARTIAL_ADD, st))
             cur = nxt
+        check(lib.nca_backward_stages(*args(0, cur, cur), STAGE_REDUCE, st))  # the rollout's gradient -> grads
         return cur
 
     def iteration(self, x0, target, seed, steps=None):
