@@ -149,6 +149,33 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+def measure_tf32_tflops(dev, n=8192, reps=10):
+    """Dense TF32 throughput of this GPU: torch.matmul of two n x n fp32 matrices with TF32 tensor cores allowed
+    (2 n^3 flop per product), best of `reps` after warm-up, CUDA events. Untimed by the benchmark."""
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = True
+    try:
+        g = torch.Generator(device=dev).manual_seed(0)
+        a = torch.randn(n, n, device=dev, generator=g)
+        b = torch.randn(n, n, device=dev, generator=g)
+        c = torch.empty(n, n, device=dev)
+        for _ in range(3):
+            torch.matmul(a, b, out=c)
+        best = float('inf')
+        for _ in range(reps):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            torch.matmul(a, b, out=c)
+            e1.record()
+            e1.synchronize()
+            best = min(best, e0.elapsed_time(e1))
+        del a, b, c
+        torch.cuda.empty_cache()
+        return 2.0 * n ** 3 / (best / 1000.0) / 1e12
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = prev
+
+
 def config(n, note=None):
     c = {'workload': f'texture NCA training iteration: K={K_PER_GPU * n} NCAs ({K_PER_GPU} per GPU), B={B}, '
                      f'{H}x{W}, {C} ch / {HID} hidden, {STEPS}-step rollout fwd+bwd, p={RATE}, synthetic L2+overflow '
@@ -181,6 +208,7 @@ def main():
         import torch.distributed as dist
         dist.init_process_group('nccl', timeout=datetime.timedelta(seconds=120), device_id=dev)
 
+    tf32_tflops = measure_tf32_tflops(dev)  # before anything else runs: the compute side of the step roofline
     K = K_PER_GPU
     k0 = rank * K  # this rank's first NCA
     # seeded inputs of this shard (NCA k's weights / targets / pool depend on k only)
@@ -330,13 +358,23 @@ def main():
                           'bwd_main': 'bwd_rows_kernel' if rows else 'bwd_kernel_tc'}[dom])
     except (OSError, ValueError):
         pass
+    # the step roofline (per cell-step, p = 0.5: 17,280 flop of the MLP forward and backward, 240 B of state traffic):
+    # the slower of the flops at the TF32 peak measured here and the bytes at the measured HBM bandwidth
+    cell_steps = K * B * H * W * STEPS
+    step_compute_ms = cell_steps * 17280.0 / (tf32_tflops * 1e12) * 1e3
+    step_hbm_ms = cell_steps * 240.0 / (peak * 1e9) * 1e3
+    step_roof_ms = max(step_compute_ms, step_hbm_ms)
     roofline = {'bound': 'hbm', 'achieved': achieved, 'peak': peak, 'unit': 'GB/s', 'frac': achieved / peak,
                 'traffic': traffic,
                 'kernel': {'fwd': 'fwd_rows_kernel<12,96,2>' if rows else 'fwd_kernel<12,96,TC>',
                            'bwd_main': 'bwd_rows_kernel<12,96,4>' if rows else 'bwd_kernel_tc<12,96>'}[dom],
                 'algorithmic_bytes_per_launch': alg_bytes, 'avg_launch_ms': avg_ms,
                 'peak_source': 'MEASURED_PEAKS.json hbm_gbs (of measured)' if 'hbm_gbs' in peaks else 'fallback',
-                'stage_ms_per_iteration': {k: v / args.steps for k, v in tot.items()}}
+                'stage_ms_per_iteration': {k: v / args.steps for k, v in tot.items()},
+                'tf32_tflops_measured': tf32_tflops,
+                'step_roofline': {'compute_ms': step_compute_ms, 'hbm_ms': step_hbm_ms, 'bound_ms': step_roof_ms,
+                                  'bound': 'hbm' if step_hbm_ms >= step_compute_ms else 'tensor',
+                                  'frac_of_iteration': step_roof_ms / (ms / args.steps)}}
 
     # e2e through the public operator API with host buffers
     e2e = None
