@@ -564,14 +564,16 @@ struct BwdRows {
     static constexpr int TMEM = 512;
     static_assert(C % NPART == 0 && C <= 16 && HPP % 8 == 0 && D::KP == 56 && GM0 + C <= 62 && T_P1 + 64 <= TMEM &&
                   HID % 32 == 0 && NACC <= 256 && D::NPW == 64, "backward row-kernel layout");
-    // shared memory, 1024-aligned base: weights | PSW[2] | RH | DH (swizzled MN-major) | XR | EDGE[2] | MK[2] | bars
+    // shared memory, 1024-aligned base: weights | PSW[2] | RH | DH (swizzled MN-major) | XR | EDGE | MK[2] | bars
     // (WG reads 4 MN blocks of PSW[b] for M = 128: for b = 1 the last two are RH, in bounds and unused)
     static constexpr size_t OFF_PSW = (size_t)D::BWD_W;
     static constexpr size_t OFF_RH = OFF_PSW + (size_t)2 * D::PSW * 4;
     static constexpr size_t OFF_XR = OFF_RH + (size_t)2 * D::RHDH * 4;
     static constexpr size_t OFF_EDGE = OFF_XR + (size_t)XRING * C * 128 * 4;
     static constexpr int EDGE_SLOTS = 9;  // left / right edge lane of each of the 4 warps of a part, and x = W - 1
-    static constexpr size_t OFF_MK = OFF_EDGE + (size_t)2 * EDGE_SLOTS * C * 3 * 4;
+    // (one buffer: row i + 1's edges are written only after every warp finished row i's adjoint, since DP(i + 1)
+    // follows every warp's EA(i + 1))
+    static constexpr size_t OFF_MK = OFF_EDGE + (size_t)EDGE_SLOTS * C * 16;
     static constexpr size_t OFF_BAR = OFF_MK + 2 * 128;
     // x ring, mask buffers, g1, dp, wg (tensor-core completions), wg_go, ea_done, fe_done (one arrival per warp)
     static constexpr int NBAR = XRING + 8;
@@ -590,7 +592,7 @@ __global__ void __launch_bounds__(128 * NPART + 96, 1) bwd_rows_kernel(StepArgs 
     float *PSW = reinterpret_cast<float *>(base + F::OFF_PSW), *RH = reinterpret_cast<float *>(base + F::OFF_RH),
           *DH = RH + D::RHDH;
     float *XR = reinterpret_cast<float *>(base + F::OFF_XR);
-    float *EDGE = reinterpret_cast<float *>(base + F::OFF_EDGE);
+    float4 *EDGE = reinterpret_cast<float4 *>(base + F::OFF_EDGE);
     uint8_t *MK = base + F::OFF_MK;
     uint64_t *xfull = reinterpret_cast<uint64_t *>(base + F::OFF_BAR), *g1bar = xfull + F::XRING, *dpbar = g1bar + 1,
              *wgbar = dpbar + 1, *wggo = wgbar + 1, *ea_done = wggo + 1, *fe_done = ea_done + 1, *mkfull = fe_done + 1;
@@ -975,21 +977,16 @@ __global__ void __launch_bounds__(128 * NPART + 96, 1) bwd_rows_kernel(StepArgs 
                     for (int cc = 0; cc < F::CPP; ++cc)
                         umma::tmem_ld4(lane + (b ? F::T_P1 : F::T_P0) + 4 * (F::CPP * part + cc), dpv[cc]);
                     umma::tmem_wait_ld();
-                    float *edge = EDGE + b * (F::EDGE_SLOTS * C * 3);  // double-buffered by row parity
+                    const int my_slot = lane32 == 0 ? wq : lane32 == 31 ? 4 + wq : -1;
+                    const int lsrc = x == 0 ? 8 : lane32 == 0 ? 4 + wq - 1 : -1, rsrc = x == W - 1 ? 0 : lane32 == 31 ? wq + 1 : -1;
 #pragma unroll
                     for (int cc = 0; cc < F::CPP; ++cc) {  // edge lanes publish (sobel_x, sobel_y, laplacian) parts
                         const int c = F::CPP * part + cc;
-                        const int slot = lane32 == 0 ? wq : lane32 == 31 ? 4 + wq : -1;
-                        if (slot >= 0) {
-                            edge[(slot * C + c) * 3 + 0] = dpv[cc][1];
-                            edge[(slot * C + c) * 3 + 1] = dpv[cc][2];
-                            edge[(slot * C + c) * 3 + 2] = dpv[cc][3];
-                        }
-                        if (x == W - 1) {
-                            edge[(8 * C + c) * 3 + 0] = dpv[cc][1];
-                            edge[(8 * C + c) * 3 + 1] = dpv[cc][2];
-                            edge[(8 * C + c) * 3 + 2] = dpv[cc][3];
-                        }
+                        const float4 t = make_float4(dpv[cc][1], dpv[cc][2], dpv[cc][3], 0.f);
+                        if (my_slot >= 0)
+                            EDGE[my_slot * C + c] = t;
+                        if (x == W - 1)
+                            EDGE[8 * C + c] = t;
                     }
                     bar_sync(2 + part, 128);
 #pragma unroll
@@ -1000,17 +997,17 @@ __global__ void __launch_bounds__(128 * NPART + 96, 1) bwd_rows_kernel(StepArgs 
                               lz = __shfl_up_sync(~0u, dpv[cc][3], 1);
                         float rx = __shfl_down_sync(~0u, dpv[cc][1], 1), ry = __shfl_down_sync(~0u, dpv[cc][2], 1),
                               rz = __shfl_down_sync(~0u, dpv[cc][3], 1);
-                        if (lane32 == 0 || x == 0) {
-                            const float *e = edge + ((x == 0 ? 8 : 4 + wq - 1) * C + c) * 3;
-                            lx = e[0];
-                            ly = e[1];
-                            lz = e[2];
+                        if (lsrc >= 0) {
+                            const float4 e = EDGE[lsrc * C + c];
+                            lx = e.x;
+                            ly = e.y;
+                            lz = e.z;
                         }
-                        if (lane32 == 31 || x == W - 1) {
-                            const float *e = edge + ((x == W - 1 ? 0 : wq + 1) * C + c) * 3;
-                            rx = e[0];
-                            ry = e[1];
-                            rz = e[2];
+                        if (rsrc >= 0) {
+                            const float4 e = EDGE[rsrc * C + c];
+                            rx = e.x;
+                            ry = e.y;
+                            rz = e.z;
                         }
                         const float rsx = lx - rx;                      // horizontal transpose of sobel_x
                         const float rsy = ry + 2.f * dpv[cc][2] + ly;   // ... of sobel_y (smoothing)
