@@ -100,13 +100,14 @@ __device__ __forceinline__ void mbar_arrive(uint64_t *bar)
 
 // Bounded mbarrier wait that gives up early once any warp of the CTA has given up (abort != 0), and sets abort when
 // its own 2 s limit runs out: after a failure every warp keeps its loop and barrier sequence (so no named barrier is
-// left short of a participant) while its remaining waits return at once.
+// left short of a participant) while its remaining waits return at once. A phase that has already completed is
+// reported as completed before abort is read (one shared load fewer on the common path).
 __device__ __forceinline__ bool wait_bar(uint64_t *bar, uint32_t parity, volatile uint32_t *abort)
 {
-    if (*abort)
-        return false;
     if (umma::mbar_try_wait(bar, parity))
         return true;
+    if (*abort)
+        return false;
     uint64_t t0;
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
     while (true) {
