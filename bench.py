@@ -11,7 +11,11 @@ each rank owns 32 NCAs (weak scaling, K = 32 N in total); rank 0 broadcasts the 
 the per-NCA losses are all-gathered, as the reference's group loop would log them. Inputs: 64 saved states of 50 MB
 per iteration (3.2 GB) exceed the 126 MB L2, so no flush is needed between iterations.
 
-value: K B H W steps x iterations / (max over ranks of the CUDA-event time of the timed iterations).
+value: K B H W steps x iterations / (max over ranks of the CUDA-event time of the timed iterations). Each iteration
+       is the reference's group-loop iteration run from the device (ultranca_b200.training.PoolTrainer: pool sample
+       with seed injection, rollout, loss, backward, fused reduce + Adam, pool write-back), replayed as one CUDA
+       graph; timing events recorded inside the graph around every 16th step's launches give the per-kernel times
+       of the roofline.
 e2e:   the same metric through the public operator API (ultranca_b200.nca_ops.step under autograd, the call
        train.py makes), with the batch copied host -> device from pinned memory and the losses copied back every
        iteration inside the timed region.
@@ -33,6 +37,7 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 K_PER_GPU, B, C, HID, H, W, STEPS, POOL, RATE = 32, 2, 12, 96, 128, 128, 64, 64, 0.5
+TIMER_STRIDE = 16  # timing events around every 16th step's forward and backward launch (4 + 4 per iteration)
 METRIC = 'cell-updates/s fwd+bwd, 64-step rollout'
 UNIT = 'cell-updates/s'
 
@@ -195,7 +200,6 @@ def main():
         return
     from oracle import nca_oracle as O  # seeded synthetic inputs only (same generator as the tests)
     from ultranca_b200 import nca_ops, training
-    from ultranca_b200._lib import check, lib, ptr
 
     world = int(os.environ.get('WORLD_SIZE', '1'))
     rank = int(os.environ.get('RANK', '0'))
@@ -218,24 +222,30 @@ def main():
     w1, b1, w2, target = (t.to(dev).contiguous() for t in (w1, b1, w2, target))
     trainer = training.RolloutTrainer(w1, b1, w2, B, H, W, STEPS, RATE, growing=False, fp32=False,
                                       image_offset=k0 * B)
-    ks = torch.arange(K, device=dev)[:, None]
+    # the reference's group-loop iteration on the device (pool sample + seed injection every 16 iterations, rollout,
+    # loss, backward, fused reduce + Adam, pool write-back), one CUDA graph replay per iteration; the control block's
+    # key is shared by every rank (broadcast once), so all ranks draw the same rollout seeds, and the pool draws of
+    # NCA k follow its global index
+    key = torch.tensor([20240611], dtype=torch.int64, device=dev)
+    if dist is not None:
+        dist.broadcast(key, 0)
+    loop = training.PoolTrainer(trainer, pool, target, inject_every=16, seed_kind=training.SEED_TEXTURE,
+                                key=int(key.item()), graph=True, timed=TIMER_STRIDE, nca_offset=k0)
     stream = torch.cuda.current_stream(dev)
-    # rank 0 draws (rollout length, seed) per iteration and broadcasts them (the only cross-rank traffic)
-    ctl = torch.zeros(2, dtype=torch.int64, device=dev)
-    seed_gen = torch.Generator().manual_seed(0)
+    # rank 0 draws the rollout length per iteration and broadcasts it (config 1: always STEPS)
+    ctl = torch.zeros(1, dtype=torch.int64, device=dev)
     losses_all = torch.zeros(world * K, device=dev)
 
-    # Control for iteration i + 1 is broadcast on a side stream while iteration i runs, so reading it on the host
+    # The length for iteration i + 1 is broadcast on a side stream while iteration i runs, so reading it on the host
     # never waits for the step kernels (single GPU: drawn on the host, nothing to broadcast).
     side = torch.cuda.Stream(dev)
-    ctl_host = torch.zeros(2, dtype=torch.int64).pin_memory()
+    ctl_host = torch.zeros(1, dtype=torch.int64).pin_memory()
     ctl_ready = torch.cuda.Event()
 
     def prefetch_control():
         with torch.cuda.stream(side):
             if rank == 0:
-                ctl.copy_(torch.tensor([STEPS, int(torch.randint(0, 2 ** 62, (1,), generator=seed_gen).item())]),
-                          non_blocking=False)
+                ctl.fill_(STEPS)
             if dist is not None:
                 dist.broadcast(ctl, 0)
             ctl_host.copy_(ctl, non_blocking=True)
@@ -243,73 +253,24 @@ def main():
 
     def take_control():
         ctl_ready.synchronize()
-        steps, seed = int(ctl_host[0]), int(ctl_host[1])
+        steps = int(ctl_host[0])
         assert steps == STEPS
         prefetch_control()
-        return seed
+        return steps
 
-    stage_times = {'fwd': [], 'bwd_main': []}
-
-    def iteration(i, profile=False):
-        seed = take_control()
-        idx = torch.rand(K, POOL, device=dev).argsort(1)[:, :B]
-        x0 = pool[ks, idx]
-        if i % 16 == 0:
-            x0[:, 0] = 0.0  # the zero seed of a texture NCA replaces the first sample (train.py:131-132)
-        if profile:
-            loss = profiled_iteration(x0, seed)
-        else:
-            loss, xT = trainer.iteration(x0, target, seed)
-        pool[ks, idx] = trainer.states[STEPS]
+    def iteration():
+        loop.iteration(take_control())
         if dist is not None:
             dist.all_gather_into_tensor(losses_all, trainer.loss)
         return trainer.loss
 
-    def profiled_iteration(x0, seed):
-        """trainer.iteration with CUDA events around every forward launch and every backward main-kernel launch."""
-        t = trainer
-        st = ctypes_stream()
-        t.states[0].copy_(x0)
-        evs = []
-        for s in range(STEPS):
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record(stream)
-            check(lib.nca_forward(ptr(t.states[s]), ptr(w1), ptr(b1), ptr(w2), ptr(t.states[s + 1]), None, None, t.N, C,
-                                  H, W, K, HID, B, nca_ops.step_seed(seed, s), RATE, 0, 0, t.image_offset, st))
-            e1.record(stream)
-            evs.append(('fwd', e0, e1))
-        training.synthetic_loss(t.states[STEPS], target, 10.0, t.gy[0], t.loss, t.loss_work)
-        cur = t.gy[0]
-        t.partial.zero_()
-        for s in reversed(range(STEPS)):
-            nxt = t.gy[1] if cur is t.gy[0] else t.gy[0]
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            common = (ptr(t.states[s]), ptr(cur), None, ptr(w1), ptr(b1), ptr(w2), ptr(nxt), ptr(t.grads[0]),
-                      ptr(t.grads[1]), ptr(t.grads[2]), ptr(t.dp), t.dp_floats, ptr(t.partial), t.partial_floats, t.N, C,
-                      H, W, K, HID, B, nca_ops.step_seed(seed, s), RATE, 0, 0, t.image_offset, 0)
-            e0.record(stream)
-            check(lib.nca_backward_stages(*common, training.STAGE_MAIN | training.STAGE_PARTIAL_ADD, st))
-            e1.record(stream)
-            check(lib.nca_backward_stages(*common, training.STAGE_ADJOINT, st))  # fused into the main kernel on rows
-            evs.append(('bwd_main', e0, e1))
-            cur = nxt
-        check(lib.nca_backward_stages(*common, training.STAGE_REDUCE, st))
-        t.opt.step(t.grads)
-        pending.append(evs)
-        return t.loss
-
-    import ctypes
-
-    def ctypes_stream():
-        return ctypes.c_void_p(stream.cuda_stream)
-
-    pending = []
     prefetch_control()
 
-    # warm-up
+    # warm-up (the first iteration launches directly; the graph is recorded at the second)
     for i in range(args.warmup):
-        iteration(i)
+        iteration()
     torch.cuda.synchronize()
+    loop.kernel_times(reset=True)
     if dist is not None:
         dist.barrier()
     torch.cuda.synchronize()
@@ -317,16 +278,14 @@ def main():
     with ClockSampler(local) as clocks:
         start.record(stream)
         for i in range(args.steps):
-            iteration(args.warmup + i, profile=True)
+            iteration()
         end.record(stream)
         torch.cuda.synchronize()
     if dist is not None:
         dist.barrier()
     torch.cuda.synchronize()
     ms = start.elapsed_time(end)
-    for evs in pending:
-        for name, e0, e1 in evs:
-            stage_times[name].append(e0.elapsed_time(e1))
+    stage_times = loop.kernel_times()
     if dist is not None:
         t = torch.tensor([ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -334,12 +293,13 @@ def main():
     cells_per_iter = world * K * B * H * W * STEPS
     value = cells_per_iter * args.steps / (ms / 1000.0)
     rows = nca_ops.launch_info(C, HID, False, K * B, H, W, K)['rows_path']
-    # forward 1 / step; backward: fused kernel (row path) or main + adjoint per step, one reduce; loss 2; optimiser 2
-    launches_per_iter = STEPS * 1 + 2 + STEPS * (1 if rows else 2) + 1 + 2
-    # roofline of the dominant kernel (the larger total of the forward kernel and the backward main kernel)
-    tot = {k: sum(v) for k, v in stage_times.items()}
-    dom = max(tot, key=tot.get)
-    avg_ms = statistics.mean(stage_times[dom])
+    # per iteration: control 1, pool sample 2, forward 1 / step, loss 2, backward 1 / step (row path; main + adjoint
+    # on the tile path), fused reduce + Adam 1, iteration counter 1, pool write-back 1
+    launches_per_iter = 1 + 2 + STEPS + 2 + STEPS * (1 if rows else 2) + 1 + 1 + 1
+    # roofline of the dominant kernel (the larger mean of the sampled forward and backward launches)
+    mean = {k: statistics.mean(v) for k, v in stage_times.items()}
+    dom = max(mean, key=mean.get)
+    avg_ms = mean[dom]
     # algorithmic bytes per cell (fp32, 12 channels): forward reads x and writes y (96 B); the fused backward reads x
     # and gy and writes gx (144 B); the tile-path backward main kernel reads x and gy (96 B)
     alg_per_cell = 96 if dom == 'fwd' else (144 if rows else 96)
@@ -355,7 +315,7 @@ def main():
     try:
         tr = json.load(open(os.path.join(ROOT, 'profiles', 'traffic.json')))
         traffic = tr.get({'fwd': 'fwd_rows_kernel' if rows else 'fwd_kernel',
-                          'bwd_main': 'bwd_rows_kernel' if rows else 'bwd_kernel_tc'}[dom])
+                          'bwd': 'bwd_rows_kernel' if rows else 'bwd_kernel_tc'}[dom])
     except (OSError, ValueError):
         pass
     # the step roofline (per cell-step, p = 0.5: 17,280 flop of the MLP forward and backward, 240 B of state traffic):
@@ -367,10 +327,12 @@ def main():
     roofline = {'bound': 'hbm', 'achieved': achieved, 'peak': peak, 'unit': 'GB/s', 'frac': achieved / peak,
                 'traffic': traffic,
                 'kernel': {'fwd': 'fwd_rows_kernel<12,96,2>' if rows else 'fwd_kernel<12,96,TC>',
-                           'bwd_main': 'bwd_rows_kernel<12,96,4>' if rows else 'bwd_kernel_tc<12,96>'}[dom],
+                           'bwd': 'bwd_rows_kernel<12,96,4>' if rows else 'bwd_kernel_tc<12,96>'}[dom],
                 'algorithmic_bytes_per_launch': alg_bytes, 'avg_launch_ms': avg_ms,
+                'timed_launches': {k: len(v) for k, v in stage_times.items()},
+                'launch_ms': {k: v for k, v in mean.items()},
                 'peak_source': 'MEASURED_PEAKS.json hbm_gbs (of measured)' if 'hbm_gbs' in peaks else 'fallback',
-                'stage_ms_per_iteration': {k: v / args.steps for k, v in tot.items()},
+                'stage_ms_per_iteration': {k: v * STEPS for k, v in mean.items()},
                 'tf32_tflops_measured': tf32_tflops,
                 'step_roofline': {'compute_ms': step_compute_ms, 'hbm_ms': step_hbm_ms, 'bound_ms': step_roof_ms,
                                   'bound': 'hbm' if step_hbm_ms >= step_compute_ms else 'tensor',

@@ -58,6 +58,15 @@ int nca_rollout(const float *x, const float *w1, const float *b1, const float *w
 /* splitmix64 seed of rollout step i (ncaops/nca_cuda.cu:157-164). */
 uint64_t nca_step_seed(uint64_t seed, uint64_t i);
 
+/* nca_forward whose step seed is read from device memory when the kernels run: nca_step_seed(*seed_dev, step), so
+ * that a launch recorded once in a CUDA graph replays with each iteration's rollout seed (seed_dev: a device uint64,
+ * e.g. word 3 of a control block, see nca_control_advance). Otherwise identical to nca_forward. No reference
+ * counterpart (the reference launches every step from the host). */
+int nca_forward_dseed(const float *x, const float *w1, const float *b1, const float *w2, float *y, float *alpha,
+                      uint8_t *alive, int64_t N, int64_t C, int64_t H, int64_t W, int64_t K, int64_t hidden,
+                      uint32_t batch_per_nca, const uint64_t *seed_dev, int64_t step, float update_rate, int fp32,
+                      int growing, int64_t image_offset, void *stream);
+
 /* Workspace sizes of nca_backward for this shape on the current device: dp_floats (the dp scratch, fp32 elements),
  * partial_floats (weight-gradient partials, fp32 elements) and chunk (images per backward launch: always N).
  * Replaces nca_cuda.backward_workspace (ncaops/nca_cuda.cu:235-254, bound at :345-346), whose tuple was
@@ -94,6 +103,15 @@ int nca_backward_stages(const float *x, const float *gy, const uint8_t *alive, c
                         float *partial, int64_t partial_floats, int64_t N, int64_t C, int64_t H, int64_t W, int64_t K,
                         int64_t hidden, uint32_t batch_per_nca, uint64_t seed, float update_rate, int fp32, int growing,
                         int64_t image_offset, int accumulate, int stages, void *stream);
+
+/* nca_backward_stages with the step seed read from device memory (nca_step_seed(*seed_dev, step)), as
+ * nca_forward_dseed. */
+int nca_backward_stages_dseed(const float *x, const float *gy, const uint8_t *alive, const float *w1, const float *b1,
+                              const float *w2, float *gx, float *dw1, float *db1, float *dw2, float *dp,
+                              int64_t dp_floats, float *partial, int64_t partial_floats, int64_t N, int64_t C, int64_t H,
+                              int64_t W, int64_t K, int64_t hidden, uint32_t batch_per_nca, const uint64_t *seed_dev,
+                              int64_t step, float update_rate, int fp32, int growing, int64_t image_offset,
+                              int accumulate, int stages, void *stream);
 
 /* nca_backward for the TF32 texture row kernel (C = 12, hidden = 96, W <= 128 and a multiple of 4; x, gy, gx
  * 16-byte aligned; growing = 0, fp32 = 0) with its scratch held by the library: the weight-gradient partials live in
@@ -135,6 +153,39 @@ int nca_adam_step(float *param0, float *param1, float *param2, const float *grad
                   float *m0, float *m1, float *m2, float *v0, float *v1, float *v2, int64_t K, int64_t numel0,
                   int64_t numel1, int64_t numel2, int64_t *iteration, float lr, float beta1, float beta2, float eps,
                   float gamma, const int64_t *milestones, int n_milestones, void *stream);
+
+/* The weight-gradient reduction of a rollout fused with nca_adam_step: one launch sums, per NCA and in a fixed order,
+ * the partials that backward calls of this shape (NCA_STAGE_MAIN | NCA_STAGE_PARTIAL_ADD, 16-byte-aligned x, gy and
+ * gx) accumulated in `partial`, stores the gradients into dw1 / db1 / dw2, and applies the per-NCA per-tensor
+ * normalisation + Adam + MultiStepLR to w1 / b1 / w2 with moments m_i / v_i (then a one-thread launch increments
+ * iteration). Bitwise equal to nca_backward_stages(NCA_STAGE_REDUCE, accumulate = 0) followed by nca_adam_step.
+ * Replaces the gradient reduction of nca_cuda.backward plus train.py:136-141. */
+int nca_reduce_adam_step(const float *partial, int64_t partial_floats, int64_t N, int64_t C, int64_t H, int64_t W,
+                         int64_t K, int64_t hidden, uint32_t batch_per_nca, int fp32, int growing, float *dw1,
+                         float *db1, float *dw2, float *w1, float *b1, float *w2, float *m0, float *m1, float *m2,
+                         float *v0, float *v1, float *v2, int64_t *iteration, float lr, float beta1, float beta2,
+                         float eps, float gamma, const int64_t *milestones, int n_milestones, void *stream);
+
+/* Training-iteration glue on the device (train.py:126-142), for a loop captured once as a CUDA graph.
+ * Control block ctl: 4 device uint64: [0] key (written by the caller once), [1] iterations started, [2] index of the
+ * current iteration, [3] its rollout seed. nca_control_advance starts the next iteration: [2] = [1]++, [3] =
+ * nca_step_seed([0], 2 [2]); the rollout's step t then uses nca_step_seed([3], t) (nca_*_dseed with seed_dev =
+ * ctl + 3). */
+int nca_control_advance(uint64_t *ctl, void *stream);
+
+/* Batch of the current iteration from the pool: idx (K, B) int64 = B distinct entries of 0..P-1 per NCA (a partial
+ * Fisher-Yates shuffle driven by nca_step_seed(ctl[0], 2 ctl[2] + 1), NCA k's draws indexed by nca_offset + k, the
+ * global index a shard passes; train.py:128 draws them as rand(K, P).argsort(1)[:, :B]), x0 (K, B, C, H, W) =
+ * pool (K, P, C, H, W) [k, idx[k, b]]; when inject_every > 0 and ctl[2] % inject_every == 0, x0[k, 0] is the seed
+ * state instead (train.py:130-131): seed_kind 0 zeros (Texture.seed), 1 the growing seed, 1 in channels 3.. at
+ * (H / 2, W / 2) (Growing.seed). 1 <= B <= 64, B <= P. */
+int nca_pool_sample(const float *pool, float *x0, int64_t *idx, const uint64_t *ctl, int64_t K, int64_t P, int64_t B,
+                    int64_t C, int64_t H, int64_t W, int64_t inject_every, int seed_kind, int64_t nca_offset,
+                    void *stream);
+
+/* pool[k, idx[k, b]] = x[k, b] (train.py:141). */
+int nca_pool_store(float *pool, const float *x, const int64_t *idx, int64_t K, int64_t P, int64_t B, int64_t C,
+                   int64_t H, int64_t W, void *stream);
 
 /* Launch configuration the step kernels use for this shape on the current device, into info[0..11]: row-streaming
  * path (1) or tile path (0), forward grid, forward threads per CTA, backward grid, backward threads per CTA, SM count,

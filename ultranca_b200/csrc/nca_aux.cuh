@@ -94,27 +94,11 @@ struct AdamArgs {
     int n_milestones;
 };
 
-// Block (k, tensor): ||g_k|| in a fixed order, then g / (||g_k|| + 1e-8) through torch.optim.Adam's update
-// (exp_avg.lerp_(g, 1 - beta1); exp_avg_sq = beta2 v + (1 - beta2) g^2; p -= lr / bc1 * m / (sqrt(v) / sqrt(bc2) + eps)).
-__global__ void __launch_bounds__(256) adam_kernel(AdamArgs a)
+// g / norm_eps (norm_eps = ||g_k|| + 1e-8, train.py:139) through torch.optim.Adam's update of NCA k's slice [base,
+// base + numel) of one tensor (exp_avg.lerp_(g, 1 - beta1); exp_avg_sq = beta2 v + (1 - beta2) g^2;
+// p -= lr / bc1 * m / (sqrt(v) / sqrt(bc2) + eps)), with MultiStepLR's lr at the device iteration counter.
+__device__ __forceinline__ void adam_apply(const AdamArgs &a, const AdamTensor &T, int64_t base, float norm_eps)
 {
-    const int k = blockIdx.x;
-    const AdamTensor &T = a.t[blockIdx.y];
-    const int64_t base = (int64_t)k * T.numel;
-    float ss = 0.f;
-    for (int64_t i = threadIdx.x; i < T.numel; i += blockDim.x) {
-        const float g = T.g[base + i];
-        ss = fmaf(g, g, ss);
-    }
-    __shared__ float red[256];
-    red[threadIdx.x] = ss;
-    __syncthreads();
-    for (int w = 128; w > 0; w >>= 1) {
-        if (threadIdx.x < w)
-            red[threadIdx.x] += red[threadIdx.x + w];
-        __syncthreads();
-    }
-    const float norm_eps = sqrtf(red[0]) + 1e-8f;  // train.py:139: p.grad /= ||p.grad_k|| + 1e-8
     const int64_t it = *a.iteration;
     int decays = 0;
     for (int i = 0; i < a.n_milestones; ++i)
@@ -134,6 +118,28 @@ __global__ void __launch_bounds__(256) adam_kernel(AdamArgs a)
         const float denom = sqrtf(v) / bc2_sqrt + a.eps;
         T.p[base + i] -= step_size * m / denom;
     }
+}
+
+// Block (k, tensor): ||g_k|| in a fixed order (strided per thread, then a tree), then adam_apply.
+__global__ void __launch_bounds__(256) adam_kernel(AdamArgs a)
+{
+    const int k = blockIdx.x;
+    const AdamTensor &T = a.t[blockIdx.y];
+    const int64_t base = (int64_t)k * T.numel;
+    float ss = 0.f;
+    for (int64_t i = threadIdx.x; i < T.numel; i += blockDim.x) {
+        const float g = T.g[base + i];
+        ss = fmaf(g, g, ss);
+    }
+    __shared__ float red[256];
+    red[threadIdx.x] = ss;
+    __syncthreads();
+    for (int w = 128; w > 0; w >>= 1) {
+        if (threadIdx.x < w)
+            red[threadIdx.x] += red[threadIdx.x + w];
+        __syncthreads();
+    }
+    adam_apply(a, T, base, sqrtf(red[0]) + 1e-8f);  // train.py:139: p.grad /= ||p.grad_k|| + 1e-8
 }
 
 __global__ void increment_kernel(int64_t *iteration) { *iteration += 1; }

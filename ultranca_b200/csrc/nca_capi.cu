@@ -20,6 +20,7 @@
 #include "nca_kernels.cuh"
 #include "nca_aux.cuh"
 #include "nca_rows.cuh"
+#include "nca_train.cuh"
 #include "../../include/ultranca_b200.h"
 
 namespace unca {
@@ -250,14 +251,16 @@ int bwd_rows_grid(const Shape &s)
     return grid_for(s.N * s.H, per);
 }
 
+// seed_dev != nullptr: the kernels read the rollout seed there and derive step `step`'s seed themselves.
 void launch_forward(const float *x, const float *w1, const float *b1, const float *w2, float *y, float *alpha,
                     uint8_t *alive, const Shape &s, uint64_t seed, float rate, bool fp32, bool growing, int64_t n_offset,
-                    cudaStream_t stream)
+                    cudaStream_t stream, const uint64_t *seed_dev = nullptr, int64_t step = 0)
 {
     StepArgs a{};
     a.x = x; a.w1 = w1; a.b1 = b1; a.w2 = w2; a.y = y; a.alpha = alpha;
     a.N = (int)s.N; a.B = (int)s.B; a.H = (int)s.H; a.W = (int)s.W;
     a.seed = seed; a.rate = rate; a.n_offset = n_offset;
+    a.seed_dev = seed_dev; a.step = step;
     if (rows_path(s, fp32, growing) && aligned16(x)) {
         using FR = FwdRows<12, 96, FWD_ROWS_PARTS>;
         fwd_rows_kernel<12, 96, FWD_ROWS_PARTS><<<fwd_rows_grid(s), FR::THREADS, FR::smem(), stream>>>(a);
@@ -305,6 +308,40 @@ BwdWork backward_work(const Shape &s, bool fp32, bool growing)
     return w;
 }
 
+AdamArgs make_adam_args(float *param0, float *param1, float *param2, const float *grad0, const float *grad1,
+                        const float *grad2, float *m0, float *m1, float *m2, float *v0, float *v1, float *v2, int64_t K,
+                        int64_t numel0, int64_t numel1, int64_t numel2, int64_t *iteration, float lr, float beta1,
+                        float beta2, float eps, float gamma, const int64_t *milestones, int n_milestones)
+{
+    float *p[3] = {param0, param1, param2}, *m[3] = {m0, m1, m2}, *v[3] = {v0, v1, v2};
+    const float *g[3] = {grad0, grad1, grad2};
+    const int64_t ne[3] = {numel0, numel1, numel2};
+    if (K <= 0)
+        fail(NCA_ERR_SHAPE, "K must be positive");
+    if (n_milestones < 0 || n_milestones > 8 || (n_milestones > 0 && !milestones))
+        fail(NCA_ERR_ARGUMENT, "at most 8 milestones");
+    check_ptr(iteration, "iteration");
+    AdamArgs a{};
+    for (int i = 0; i < 3; ++i) {
+        check_ptr(p[i], "param"); check_ptr(g[i], "grad"); check_ptr(m[i], "m"); check_ptr(v[i], "v");
+        if (ne[i] <= 0)
+            fail(NCA_ERR_SHAPE, "numel must be positive");
+        a.t[i] = AdamTensor{p[i], m[i], v[i], g[i], ne[i]};
+    }
+    a.iteration = iteration;
+    a.lr = lr; a.beta1 = beta1; a.beta2 = beta2; a.eps = eps; a.gamma = gamma;
+    a.n_milestones = n_milestones;
+    for (int i = 0; i < n_milestones; ++i)
+        a.milestones[i] = milestones[i];
+    return a;
+}
+
+int grid_stride_blocks(int64_t work)
+{
+    const int64_t cap = (int64_t)device_info().sms * 8;
+    return (int)std::max<int64_t>(1, std::min<int64_t>(cap, (work + 255) / 256));
+}
+
 }  // namespace
 }  // namespace unca
 
@@ -330,6 +367,27 @@ int nca_forward(const float *x, const float *w1, const float *b1, const float *w
         }
         launch_forward(x, w1, b1, w2, y, alpha, alive, s, seed, update_rate, fp32, growing, image_offset,
                        static_cast<cudaStream_t>(stream));
+    });
+}
+
+int nca_forward_dseed(const float *x, const float *w1, const float *b1, const float *w2, float *y, float *alpha,
+                      uint8_t *alive, int64_t N, int64_t C, int64_t H, int64_t W, int64_t K, int64_t hidden,
+                      uint32_t batch_per_nca, const uint64_t *seed_dev, int64_t step, float update_rate, int fp32,
+                      int growing, int64_t image_offset, void *stream)
+{
+    return guarded([&] {
+        const Shape s{N, C, H, W, K, hidden, (int64_t)batch_per_nca};
+        validate(s, growing);
+        check_ptr(x, "x"); check_ptr(w1, "w1"); check_ptr(b1, "b1"); check_ptr(w2, "w2"); check_ptr(y, "y");
+        check_ptr(seed_dev, "seed_dev");
+        if (step < 0)
+            fail(NCA_ERR_ARGUMENT, "step must be >= 0");
+        if (growing) {
+            check_ptr(alpha, "alpha");
+            check_ptr(alive, "alive");
+        }
+        launch_forward(x, w1, b1, w2, y, alpha, alive, s, 0, update_rate, fp32, growing, image_offset,
+                       static_cast<cudaStream_t>(stream), seed_dev, step);
     });
 }
 
@@ -361,13 +419,7 @@ int nca_rollout(const float *x, const float *w1, const float *b1, const float *w
     });
 }
 
-uint64_t nca_step_seed(uint64_t seed, uint64_t i)
-{
-    uint64_t z = seed + (i + 1) * 0x9E3779B97F4A7C15ull;  // splitmix64, ncaops/nca_cuda.cu:157-164
-    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
-    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
-    return z ^ (z >> 31);
-}
+uint64_t nca_step_seed(uint64_t seed, uint64_t i) { return splitmix_step(seed, i); }
 
 int nca_backward_workspace(int64_t C, int64_t hidden, int fp32, int64_t N, int64_t H, int64_t W, int64_t K,
                            float update_rate, int growing, int64_t *dp_floats, int64_t *partial_floats, int64_t *chunk)
@@ -386,11 +438,15 @@ int nca_backward_workspace(int64_t C, int64_t hidden, int fp32, int64_t N, int64
     });
 }
 
-int nca_backward_stages(const float *x, const float *gy, const uint8_t *alive, const float *w1, const float *b1,
-                        const float *w2, float *gx, float *dw1, float *db1, float *dw2, float *dp, int64_t dp_floats,
-                        float *partial, int64_t partial_floats, int64_t N, int64_t C, int64_t H, int64_t W, int64_t K,
-                        int64_t hidden, uint32_t batch_per_nca, uint64_t seed, float update_rate, int fp32, int growing,
-                        int64_t image_offset, int accumulate, int stages, void *stream)
+}  // extern "C"
+
+namespace {
+int backward_stages_impl(const float *x, const float *gy, const uint8_t *alive, const float *w1, const float *b1,
+                         const float *w2, float *gx, float *dw1, float *db1, float *dw2, float *dp, int64_t dp_floats,
+                         float *partial, int64_t partial_floats, int64_t N, int64_t C, int64_t H, int64_t W, int64_t K,
+                         int64_t hidden, uint32_t batch_per_nca, uint64_t seed, const uint64_t *seed_dev, int64_t step,
+                         float update_rate, int fp32, int growing, int64_t image_offset, int accumulate, int stages,
+                         void *stream)
 {
     return guarded([&] {
         const Shape s{N, C, H, W, K, hidden, (int64_t)batch_per_nca};
@@ -418,6 +474,7 @@ int nca_backward_stages(const float *x, const float *gy, const uint8_t *alive, c
             a.x = x; a.w1 = w1; a.b1 = b1; a.w2 = w2; a.gy = gy; a.alive = alive; a.dp = dp; a.partial = partial;
             a.N = (int)N; a.B = (int)batch_per_nca; a.H = (int)H; a.W = (int)W;
             a.seed = seed; a.rate = update_rate; a.n_offset = image_offset;
+            a.seed_dev = seed_dev; a.step = step;
             a.partial_add = (stages & NCA_STAGE_PARTIAL_ADD) ? 1 : 0;
             const TileGeom g = make_geom((int)H, (int)W);
             const bool rows = rows_path(s, fp32, growing) && aligned16(x) && aligned16(gy) && aligned16(gx);
@@ -456,6 +513,34 @@ int nca_backward_stages(const float *x, const float *gy, const uint8_t *alive, c
             }
         });
     });
+}
+}  // namespace
+
+extern "C" {
+
+int nca_backward_stages(const float *x, const float *gy, const uint8_t *alive, const float *w1, const float *b1,
+                        const float *w2, float *gx, float *dw1, float *db1, float *dw2, float *dp, int64_t dp_floats,
+                        float *partial, int64_t partial_floats, int64_t N, int64_t C, int64_t H, int64_t W, int64_t K,
+                        int64_t hidden, uint32_t batch_per_nca, uint64_t seed, float update_rate, int fp32, int growing,
+                        int64_t image_offset, int accumulate, int stages, void *stream)
+{
+    return backward_stages_impl(x, gy, alive, w1, b1, w2, gx, dw1, db1, dw2, dp, dp_floats, partial, partial_floats, N,
+                                C, H, W, K, hidden, batch_per_nca, seed, nullptr, 0, update_rate, fp32, growing,
+                                image_offset, accumulate, stages, stream);
+}
+
+int nca_backward_stages_dseed(const float *x, const float *gy, const uint8_t *alive, const float *w1, const float *b1,
+                              const float *w2, float *gx, float *dw1, float *db1, float *dw2, float *dp,
+                              int64_t dp_floats, float *partial, int64_t partial_floats, int64_t N, int64_t C, int64_t H,
+                              int64_t W, int64_t K, int64_t hidden, uint32_t batch_per_nca, const uint64_t *seed_dev,
+                              int64_t step, float update_rate, int fp32, int growing, int64_t image_offset,
+                              int accumulate, int stages, void *stream)
+{
+    if (!seed_dev)
+        return guarded([] { fail(NCA_ERR_ARGUMENT, "seed_dev is null"); });
+    return backward_stages_impl(x, gy, alive, w1, b1, w2, gx, dw1, db1, dw2, dp, dp_floats, partial, partial_floats, N,
+                                C, H, W, K, hidden, batch_per_nca, 0, seed_dev, step, update_rate, fp32, growing,
+                                image_offset, accumulate, stages, stream);
 }
 
 int nca_backward(const float *x, const float *gy, const uint8_t *alive, const float *w1, const float *b1, const float *w2,
@@ -557,29 +642,105 @@ int nca_adam_step(float *param0, float *param1, float *param2, const float *grad
                   float gamma, const int64_t *milestones, int n_milestones, void *stream)
 {
     return guarded([&] {
-        float *p[3] = {param0, param1, param2}, *m[3] = {m0, m1, m2}, *v[3] = {v0, v1, v2};
-        const float *g[3] = {grad0, grad1, grad2};
-        const int64_t ne[3] = {numel0, numel1, numel2};
-        if (K <= 0)
-            fail(NCA_ERR_SHAPE, "K must be positive");
-        if (n_milestones < 0 || n_milestones > 8 || (n_milestones > 0 && !milestones))
-            fail(NCA_ERR_ARGUMENT, "at most 8 milestones");
-        check_ptr(iteration, "iteration");
-        AdamArgs a{};
-        for (int i = 0; i < 3; ++i) {
-            check_ptr(p[i], "param"); check_ptr(g[i], "grad"); check_ptr(m[i], "m"); check_ptr(v[i], "v");
-            if (ne[i] <= 0)
-                fail(NCA_ERR_SHAPE, "numel must be positive");
-            a.t[i] = AdamTensor{p[i], m[i], v[i], g[i], ne[i]};
-        }
-        a.iteration = iteration;
-        a.lr = lr; a.beta1 = beta1; a.beta2 = beta2; a.eps = eps; a.gamma = gamma;
-        a.n_milestones = n_milestones;
-        for (int i = 0; i < n_milestones; ++i)
-            a.milestones[i] = milestones[i];
+        const AdamArgs a = make_adam_args(param0, param1, param2, grad0, grad1, grad2, m0, m1, m2, v0, v1, v2, K, numel0,
+                                          numel1, numel2, iteration, lr, beta1, beta2, eps, gamma, milestones,
+                                          n_milestones);
         const auto st = static_cast<cudaStream_t>(stream);
         adam_kernel<<<dim3((unsigned)K, 3), 256, 0, st>>>(a);
         CUDA_OK(cudaGetLastError());
+        increment_kernel<<<1, 1, 0, st>>>(iteration);
+        CUDA_OK(cudaGetLastError());
+    });
+}
+
+int nca_control_advance(uint64_t *ctl, void *stream)
+{
+    return guarded([&] {
+        check_ptr(ctl, "ctl");
+        control_advance_kernel<<<1, 1, 0, static_cast<cudaStream_t>(stream)>>>(ctl);
+        CUDA_OK(cudaGetLastError());
+    });
+}
+
+int nca_pool_sample(const float *pool, float *x0, int64_t *idx, const uint64_t *ctl, int64_t K, int64_t P, int64_t B,
+                    int64_t C, int64_t H, int64_t W, int64_t inject_every, int seed_kind, int64_t nca_offset,
+                    void *stream)
+{
+    return guarded([&] {
+        check_ptr(pool, "pool"); check_ptr(x0, "x0"); check_ptr(idx, "idx"); check_ptr(ctl, "ctl");
+        if (K <= 0 || C <= 0 || H <= 0 || W <= 0 || K > INT32_MAX)
+            fail(NCA_ERR_SHAPE, "K, C, H, W must be positive");
+        if (B < 1 || B > POOL_MAX_BATCH || P < B || P > INT32_MAX)
+            fail(NCA_ERR_ARGUMENT, "need 1 <= B <= %d and B <= pool size (B=%lld, P=%lld)", POOL_MAX_BATCH, (long long)B,
+                 (long long)P);
+        if (seed_kind != 0 && seed_kind != 1)
+            fail(NCA_ERR_ARGUMENT, "seed_kind: 0 texture (zeros), 1 growing (centre cell)");
+        if (inject_every < 0 || nca_offset < 0)
+            fail(NCA_ERR_ARGUMENT, "inject_every and nca_offset must be >= 0 (inject_every 0: never)");
+        const auto st = static_cast<cudaStream_t>(stream);
+        const int64_t chw = C * H * W;
+        pool_draw_kernel<<<(unsigned)((K + 127) / 128), 128, 0, st>>>(idx, ctl, (int)K, (int)P, (int)B, nca_offset);
+        CUDA_OK(cudaGetLastError());
+        const bool v4 = chw % 4 == 0 && aligned16(pool) && aligned16(x0);
+        const int blocks = grid_stride_blocks(K * B * chw / (v4 ? 4 : 1));
+        if (v4)
+            pool_gather_kernel<4><<<blocks, 256, 0, st>>>(pool, x0, idx, ctl, (int)K, (int)P, (int)B, (int)H, (int)W,
+                                                          chw, inject_every, seed_kind);
+        else
+            pool_gather_kernel<1><<<blocks, 256, 0, st>>>(pool, x0, idx, ctl, (int)K, (int)P, (int)B, (int)H, (int)W,
+                                                          chw, inject_every, seed_kind);
+        CUDA_OK(cudaGetLastError());
+    });
+}
+
+int nca_pool_store(float *pool, const float *x, const int64_t *idx, int64_t K, int64_t P, int64_t B, int64_t C,
+                   int64_t H, int64_t W, void *stream)
+{
+    return guarded([&] {
+        check_ptr(pool, "pool"); check_ptr(x, "x"); check_ptr(idx, "idx");
+        if (K <= 0 || B <= 0 || P < B || C <= 0 || H <= 0 || W <= 0 || K > INT32_MAX || P > INT32_MAX)
+            fail(NCA_ERR_SHAPE, "need positive K, B <= P, C, H, W");
+        const auto st = static_cast<cudaStream_t>(stream);
+        const int64_t chw = C * H * W;
+        const bool v4 = chw % 4 == 0 && aligned16(pool) && aligned16(x);
+        const int blocks = grid_stride_blocks(K * B * chw / (v4 ? 4 : 1));
+        if (v4)
+            pool_store_kernel<4><<<blocks, 256, 0, st>>>(pool, x, idx, (int)K, (int)P, (int)B, chw);
+        else
+            pool_store_kernel<1><<<blocks, 256, 0, st>>>(pool, x, idx, (int)K, (int)P, (int)B, chw);
+        CUDA_OK(cudaGetLastError());
+    });
+}
+
+int nca_reduce_adam_step(const float *partial, int64_t partial_floats, int64_t N, int64_t C, int64_t H, int64_t W,
+                         int64_t K, int64_t hidden, uint32_t batch_per_nca, int fp32, int growing, float *dw1,
+                         float *db1, float *dw2, float *w1, float *b1, float *w2, float *m0, float *m1, float *m2,
+                         float *v0, float *v1, float *v2, int64_t *iteration, float lr, float beta1, float beta2,
+                         float eps, float gamma, const int64_t *milestones, int n_milestones, void *stream)
+{
+    return guarded([&] {
+        const Shape s{N, C, H, W, K, hidden, (int64_t)batch_per_nca};
+        validate(s, growing);
+        check_ptr(partial, "partial");
+        const BwdWork w = backward_work(s, fp32, growing);
+        if (partial_floats < w.partial_floats)
+            fail(NCA_ERR_SHAPE, "partial workspace too small: %lld floats, need %lld", (long long)partial_floats,
+                 (long long)w.partial_floats);
+        const AdamArgs a = make_adam_args(w1, b1, w2, dw1, db1, dw2, m0, m1, m2, v0, v1, v2, K, hidden * 4 * C, hidden,
+                                          C * hidden, iteration, lr, beta1, beta2, eps, gamma, milestones, n_milestones);
+        const auto st = static_cast<cudaStream_t>(stream);
+        dispatch(C, hidden, fp32, growing, [&](auto I) {
+            using II = decltype(I);
+            // the unit decomposition of the backward launches that wrote the partials (the row kernel when its shape
+            // qualifies: those launches had 16-byte-aligned x, gy and gx)
+            const TileGeom g = make_geom((int)H, (int)W);
+            const bool rows = rows_path(s, fp32, growing);
+            const int64_t units = rows ? N * H : N * g.tiles_per_image;
+            const int64_t per = rows ? (int64_t)batch_per_nca * H : (int64_t)batch_per_nca * g.tiles_per_image;
+            const int grid = rows ? bwd_rows_grid(s) : w.grid;
+            reduce_adam_kernel<II::C, II::HID><<<dim3((unsigned)K, 3), 256, 0, st>>>(partial, units, grid, per, a);
+            CUDA_OK(cudaGetLastError());
+        });
         increment_kernel<<<1, 1, 0, st>>>(iteration);
         CUDA_OK(cudaGetLastError());
     });

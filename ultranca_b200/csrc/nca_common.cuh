@@ -19,6 +19,17 @@ __device__ int g_device_error = 0;
 
 __device__ __forceinline__ void set_device_error(int code) { atomicCAS(&g_device_error, 0, code); }
 
+// ---------------------------------------------------------------- step seeds
+// splitmix64 seed of rollout step i from the rollout's seed (ncaops/nca_cuda.cu:157-164): the host derives it for a
+// host-driven launch, the kernels for a launch that reads its rollout seed from device memory.
+__host__ __device__ __forceinline__ uint64_t splitmix_step(uint64_t seed, uint64_t i)
+{
+    uint64_t z = seed + (i + 1) * 0x9E3779B97F4A7C15ull;
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    return z ^ (z >> 31);
+}
+
 // ---------------------------------------------------------------- Philox mask
 __device__ __forceinline__ uint4 philox4x32_10(uint64_t seed, uint64_t counter)
 {

@@ -65,7 +65,15 @@ struct StepArgs {
     float rate;
     int64_t n_offset;              // global index of image 0 (Philox counter)
     int partial_add;               // backward: add the weight-gradient partials to the slots instead of storing them
+    const uint64_t *seed_dev;      // non-null: the step's seed is splitmix_step(*seed_dev, step), read at run time
+    int64_t step;                  // (a launch recorded once in a CUDA graph and replayed with new rollout seeds)
 };
+
+// The update-mask seed of this launch's step.
+__device__ __forceinline__ uint64_t step_seed_of(const StepArgs &a)
+{
+    return a.seed_dev != nullptr ? splitmix_step(*a.seed_dev, (uint64_t)a.step) : a.seed;
+}
 
 // Stage one NCA's weights: W1' (HID x KP, chunk-planar: plane f/4, row j) with the bias columns, W2 (16 x HID,
 // chunk-planar: plane j/4, row c). TF32 mode rounds (b1 split into hi + lo); fp32 mode keeps fp32 and b1 in column PIN.
@@ -169,6 +177,7 @@ __device__ __forceinline__ TileCoord tile_coord(int64_t t, const TileGeom &g, in
 template <int C, int HID, bool TC, bool GROWING>
 __global__ void __launch_bounds__(128, 1) fwd_kernel(StepArgs a)
 {
+    a.seed = step_seed_of(a);
     using D = Dims<C, HID>;
     extern __shared__ __align__(128) float smem[];
     float *W1s = smem, *W2s = W1s + D::W1S, *P = W2s + D::W2S, *XS = P + D::P;
@@ -409,6 +418,7 @@ __device__ __forceinline__ void load_gm(float (&gm)[16], const StepArgs &a, cons
 template <int C, int HID, bool GROWING>
 __global__ void __launch_bounds__(128, 1) bwd_kernel_cc(StepArgs a)
 {
+    a.seed = step_seed_of(a);
     using D = Dims<C, HID>;
     extern __shared__ __align__(128) float smem[];
     float *W1s = smem, *W2s = W1s + D::W1S, *P = W2s + D::W2S, *G = P + D::P;
@@ -556,6 +566,7 @@ __device__ __forceinline__ void st_sw32x8(float *tile, int mn0, int k, int krows
 template <int C, int HID, bool GROWING>
 __global__ void __launch_bounds__(128, 1) bwd_kernel_tc(StepArgs a)
 {
+    a.seed = step_seed_of(a);
     using D = Dims<C, HID>;
     extern __shared__ __align__(128) unsigned char smem_raw[];
     unsigned char *base = smem_raw + ((1024 - (umma::smem_u32(smem_raw) & 1023)) & 1023);
@@ -830,6 +841,29 @@ __global__ void __launch_bounds__(256) adjoint_kernel(const float *__restrict__ 
     }
 }
 
+// The CTAs [c0, c1] of a G-CTA launch over T units whose unit ranges overlap NCA k's units [k U, (k + 1) U).
+__device__ __forceinline__ void nca_cta_span(int64_t T, int G, int64_t U, int k, int *c0_out, int *c1_out)
+{
+    const int64_t lo = (int64_t)k * U, hi = lo + U;
+    int c0 = (int)(lo * G / T) - 1;
+    c0 = c0 < 0 ? 0 : c0;
+    int64_t a, b;
+    cta_range(T, G, c0, &a, &b);
+    while (b <= lo) {
+        ++c0;
+        cta_range(T, G, c0, &a, &b);
+    }
+    int c1 = c0;
+    while (c1 + 1 < G) {
+        cta_range(T, G, c1 + 1, &a, &b);
+        if (a >= hi)
+            break;
+        ++c1;
+    }
+    *c0_out = c0;
+    *c1_out = c1;
+}
+
 // Fixed-order sum of the partial slots (c + k) of the CTAs c whose tile ranges overlap NCA k -> dw1, db1, dw2
 // (accumulate: added to the outputs). ncaops/nca_step.cuh:1164-1193 sums per-block partials the same way.
 template <int C, int HID>
@@ -839,26 +873,8 @@ __global__ void reduce_kernel(const float *__restrict__ partial, int64_t T, int 
     using D = Dims<C, HID>;
     const int k = blockIdx.y, e = blockIdx.x * blockDim.x + threadIdx.x;
     __shared__ int range[2];
-    if (threadIdx.x == 0) {
-        const int64_t lo = (int64_t)k * tiles_per_nca, hi = lo + tiles_per_nca;
-        int c0 = (int)(lo * G / T) - 1;
-        c0 = c0 < 0 ? 0 : c0;
-        int64_t a, b;
-        cta_range(T, G, c0, &a, &b);
-        while (b <= lo) {
-            ++c0;
-            cta_range(T, G, c0, &a, &b);
-        }
-        int c1 = c0;
-        while (c1 + 1 < G) {
-            cta_range(T, G, c1 + 1, &a, &b);
-            if (a >= hi)
-                break;
-            ++c1;
-        }
-        range[0] = c0;
-        range[1] = c1;
-    }
+    if (threadIdx.x == 0)
+        nca_cta_span(T, G, tiles_per_nca, k, &range[0], &range[1]);
     __syncthreads();
     if (e >= D::PART)
         return;

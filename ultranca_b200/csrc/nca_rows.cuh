@@ -306,8 +306,9 @@ __global__ void __launch_bounds__(128 * NPART + 96, 1) fwd_rows_kernel(StepArgs 
         umma::tmem_relinquish();
     }
     // update masks of the CTA's rows (g1 - g0 <= MAXROWS: the host sizes the grid so)
+    const uint64_t seed = step_seed_of(a);
     for (int64_t u = g0 + warp; u < g1; u += blockDim.x / 32)
-        row_mask_bits_warp(MKB + (u - g0) * 4, a.seed, a.rate, u / H + a.n_offset, H, W, (int)(u % H), lane32);
+        row_mask_bits_warp(MKB + (u - g0) * 4, seed, a.rate, u / H + a.n_offset, H, W, (int)(u % H), lane32);
     umma::fence_before_sync();
     __syncthreads();
     umma::fence_after_sync();
@@ -797,7 +798,7 @@ __global__ void __launch_bounds__(128 * NPART + 96, 1) bwd_rows_kernel(StepArgs 
             auto draw_mask = [&](int j) {
                 ok = __shfl_sync(~0u, ok, 0);
                 if (ok) {
-                    row_mask_warp(MK + (j & 1) * 128, a.seed, a.rate, n + a.n_offset, H, W, rowY(j), lane32);
+                    row_mask_warp(MK + (j & 1) * 128, step_seed_of(a), a.rate, n + a.n_offset, H, W, rowY(j), lane32);
                     __syncwarp();
                     if (lane32 == 0)
                         mbar_arrive(&mkfull[j & 1]);
@@ -880,6 +881,7 @@ __global__ void __launch_bounds__(128 * NPART + 96, 1) bwd_rows_kernel(StepArgs 
                 // ======== compute warps
                 int xwaited = 0;
                 float gyA[F::CPP];  // gy of the next front end's row
+                float win[F::CPP][6];  // rows Y - 1, Y (x[l], x[c], x[r]) of the last front end's channels
                 auto load_gy = [&](int j) {
                     const float *src = gyn + (size_t)rowY(j) * W + xc;
 #pragma unroll
@@ -900,7 +902,14 @@ __global__ void __launch_bounds__(128 * NPART + 96, 1) bwd_rows_kernel(StepArgs 
                     for (int cc = 0; cc < F::CPP; ++cc) {  // warp-uniform channel: tcgen05.st takes one column per warp
                         const int c = F::CPP * part + cc;
                         const float *bm = rm + c * W, *b0 = r0 + c * W, *bp = rp + c * W;
-                        const float v[3][3] = {{bm[xl], bm[xc], bm[xr]}, {b0[xl], b0[xc], b0[xr]}, {bp[xl], bp[xc], bp[xr]}};
+                        if (j == 0) {
+                            win[cc][0] = bm[xl]; win[cc][1] = bm[xc]; win[cc][2] = bm[xr];
+                            win[cc][3] = b0[xl]; win[cc][4] = b0[xc]; win[cc][5] = b0[xr];
+                        }
+                        const float v[3][3] = {{win[cc][0], win[cc][1], win[cc][2]}, {win[cc][3], win[cc][4], win[cc][5]},
+                                               {bp[xl], bp[xc], bp[xr]}};
+                        win[cc][0] = v[1][0]; win[cc][1] = v[1][1]; win[cc][2] = v[1][2];
+                        win[cc][3] = v[2][0]; win[cc][4] = v[2][1]; win[cc][5] = v[2][2];
                         const float4 p = perceive3x3(v);
                         const float t4[4] = {tf32_rna(p.x), tf32_rna(p.y), tf32_rna(p.z), tf32_rna(p.w)};
                         umma::tmem_st4(tp + 4 * c, t4);
