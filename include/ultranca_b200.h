@@ -98,6 +98,12 @@ int nca_backward(const float *x, const float *gy, const uint8_t *alive, const fl
  * zeroes the partial workspace before the run's first call. No reference counterpart (the reference reduces the
  * weight gradients of every step, ncaops/nca_cuda.cu:285-322). */
 #define NCA_STAGE_PARTIAL_ADD 8
+/* The row kernels are launched as programmatic dependents of the previous kernel on the stream: their set-up overlaps
+ * the tail of a previous step kernel, and they wait for it before touching the state it may write. With this bit
+ * the caller declares that x was written before the last launch on this stream of a kernel other than this library's
+ * step kernels (for a rollout's saved states: the loss kernel, or the zeroing of the partial workspace, came later),
+ * so the backward may start copying x before that wait. No reference counterpart. */
+#define NCA_STAGE_X_STABLE 16
 int nca_backward_stages(const float *x, const float *gy, const uint8_t *alive, const float *w1, const float *b1,
                         const float *w2, float *gx, float *dw1, float *db1, float *dw2, float *dp, int64_t dp_floats,
                         float *partial, int64_t partial_floats, int64_t N, int64_t C, int64_t H, int64_t W, int64_t K,

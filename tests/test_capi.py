@@ -85,3 +85,14 @@ def test_partial_add_stage_requires_main():
     st = lib.nca_backward_stages(p, p, None, p, p, p, p, p, p, p, p, 1 << 30, p, 1 << 30, 4, 12, 8, 16, 2, 96, 2, 0, 0.5,
                                  0, 0, 0, 0, 8, None)
     assert st == 1 and 'PARTIAL_ADD' in lib.nca_last_error().decode()
+
+
+@pytest.mark.parametrize('stages', [0, 16, 32, 16 | 32])
+def test_stage_mask_needs_a_stage_and_known_bits(stages):
+    """NCA_STAGE_X_STABLE (16) qualifies the stages; a mask without a stage bit or with an unknown bit is rejected
+    before any device work."""
+    from ultranca_b200._lib import lib
+    p = ctypes.c_void_p(256)
+    st = lib.nca_backward_stages(p, p, None, p, p, p, p, p, p, p, p, 1 << 30, p, 1 << 30, 4, 12, 8, 16, 2, 96, 2, 0, 0.5,
+                                 0, 0, 0, 0, stages, None)
+    assert st == 1 and 'stage' in lib.nca_last_error().decode()

@@ -236,6 +236,28 @@ bool rows_path(const Shape &s, bool fp32, bool growing)
 }
 bool aligned16(const void *p) { return ((uintptr_t)p & 15) == 0; }
 
+// Launch of a row kernel as a programmatic dependent of the previous kernel on the stream: once every CTA of that
+// kernel has started (the row kernels signal it first thing), this one is launched; its CTAs take the SMs the
+// previous kernel's CTAs free and run their set-up (barriers, TMEM, update masks, the first NCA's weights) under the
+// previous kernel's tail, then wait for it to complete (griddepcontrol.wait) before touching the state it writes.
+// The grids are persistent (at most the resident CTA slots), so a waiting dependent never holds an SM that an
+// unstarted CTA of the previous kernel needs. In a captured CUDA graph the dependency becomes a programmatic edge.
+template <class Kern>
+void launch_pdl(Kern kern, int grid, int threads, size_t smem, cudaStream_t st, const StepArgs &a)
+{
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3((unsigned)grid);
+    cfg.blockDim = dim3((unsigned)threads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    CUDA_OK(cudaLaunchKernelEx(&cfg, kern, a));
+}
+
 int fwd_rows_grid(const Shape &s)
 {
     using FR = FwdRows<12, 96, FWD_ROWS_PARTS>;
@@ -247,7 +269,7 @@ int fwd_rows_grid(const Shape &s)
 int bwd_rows_grid(const Shape &s)
 {
     using BR = BwdRows<12, 96, BWD_ROWS_PARTS>;
-    const int per = ctas_per_sm(bwd_rows_kernel<12, 96, BWD_ROWS_PARTS>, BR::smem(), BR::TMEM, BR::THREADS);
+    const int per = ctas_per_sm(bwd_rows_kernel<12, 96, BWD_ROWS_PARTS, false>, BR::smem(), BR::TMEM, BR::THREADS);
     return grid_for(s.N * s.H, per);
 }
 
@@ -263,7 +285,7 @@ void launch_forward(const float *x, const float *w1, const float *b1, const floa
     a.seed_dev = seed_dev; a.step = step;
     if (rows_path(s, fp32, growing) && aligned16(x)) {
         using FR = FwdRows<12, 96, FWD_ROWS_PARTS>;
-        fwd_rows_kernel<12, 96, FWD_ROWS_PARTS><<<fwd_rows_grid(s), FR::THREADS, FR::smem(), stream>>>(a);
+        launch_pdl(fwd_rows_kernel<12, 96, FWD_ROWS_PARTS>, fwd_rows_grid(s), FR::THREADS, FR::smem(), stream, a);
         CUDA_OK(cudaGetLastError());
         return;
     }
@@ -451,8 +473,8 @@ int backward_stages_impl(const float *x, const float *gy, const uint8_t *alive, 
     return guarded([&] {
         const Shape s{N, C, H, W, K, hidden, (int64_t)batch_per_nca};
         validate(s, growing);
-        if (stages <= 0 || stages > 15)
-            fail(NCA_ERR_ARGUMENT, "stages must be a nonzero mask of NCA_STAGE_* bits");
+        if ((stages & 15) == 0 || stages > 31)
+            fail(NCA_ERR_ARGUMENT, "stages must be a mask of NCA_STAGE_* bits with at least one stage");
         if ((stages & NCA_STAGE_PARTIAL_ADD) && !(stages & NCA_STAGE_MAIN))
             fail(NCA_ERR_ARGUMENT, "NCA_STAGE_PARTIAL_ADD applies to NCA_STAGE_MAIN");
         check_ptr(x, "x"); check_ptr(gy, "gy"); check_ptr(w1, "w1"); check_ptr(b1, "b1"); check_ptr(w2, "w2");
@@ -487,7 +509,13 @@ int backward_stages_impl(const float *x, const float *gy, const uint8_t *alive, 
                 units_per_nca = (int64_t)batch_per_nca * H;
                 a.gx = gx;
                 if (stages & NCA_STAGE_MAIN) {
-                    bwd_rows_kernel<12, 96, BWD_ROWS_PARTS><<<grid, BR::THREADS, BR::smem(), st>>>(a);
+                    if (stages & NCA_STAGE_X_STABLE) {
+                        set_smem_once(bwd_rows_kernel<12, 96, BWD_ROWS_PARTS, true>, BR::smem());
+                        launch_pdl(bwd_rows_kernel<12, 96, BWD_ROWS_PARTS, true>, grid, BR::THREADS, BR::smem(), st, a);
+                    } else {
+                        launch_pdl(bwd_rows_kernel<12, 96, BWD_ROWS_PARTS, false>, grid, BR::THREADS, BR::smem(), st,
+                                   a);
+                    }
                     CUDA_OK(cudaGetLastError());
                 }
             } else {
@@ -831,7 +859,7 @@ extern "C" int nca_backward_static_scratch(const float *x, const float *gy, cons
         a.N = (int)N; a.B = (int)batch_per_nca; a.H = (int)H; a.W = (int)W;
         a.seed = seed; a.rate = update_rate; a.n_offset = image_offset;
         // every partial slot the reduction reads is written by the row kernel of the same call: nothing to clear
-        bwd_rows_kernel<12, 96, BWD_ROWS_PARTS><<<grid, BR::THREADS, BR::smem(), st>>>(a);
+        bwd_rows_kernel<12, 96, BWD_ROWS_PARTS, false><<<grid, BR::THREADS, BR::smem(), st>>>(a);
         CUDA_OK(cudaGetLastError());
         reduce_kernel<12, 96><<<dim3((D::PART + 255) / 256, (unsigned)K), 256, 0, st>>>(
             partial, N * H, grid, (int64_t)batch_per_nca * H, dw1, db1, dw2, accumulate);

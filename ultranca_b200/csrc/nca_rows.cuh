@@ -265,6 +265,8 @@ __global__ void __launch_bounds__(128 * NPART + 96, 1) fwd_rows_kernel(StepArgs 
 {
     using F = FwdRows<C, HID, NPART>;
     using D = typename F::D;
+    // the next step's kernel may launch now (it waits for this one before reading the state it writes)
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     extern __shared__ __align__(128) unsigned char smem_raw[];
     float *W1s = reinterpret_cast<float *>(smem_raw), *W2s = W1s + D::W1S;
     float *XR = reinterpret_cast<float *>(smem_raw + F::OFF_XR);
@@ -337,6 +339,7 @@ __global__ void __launch_bounds__(128 * NPART + 96, 1) fwd_rows_kernel(StepArgs 
     };
     auto wait_g2 = [&](int bj) { wait_par(g2bar, g2par, bj); };  // MMA2 into U[bj] complete
     int64_t seg_u0 = g0;  // unit index of the current segment's first row
+    bool dep_waited = false;
     auto signal = [&](uint64_t *bar) {  // this warp's TMEM / shared-memory reads and writes are complete
         umma::fence_before_sync();
         __syncwarp();
@@ -359,6 +362,10 @@ __global__ void __launch_bounds__(128 * NPART + 96, 1) fwd_rows_kernel(StepArgs 
             __syncthreads();
             umma::fence_after_sync();
             cur_k = k;
+        }
+        if (!dep_waited) {  // set-up done: wait for the previous step's kernel (launched as its programmatic
+            asm volatile("griddepcontrol.wait;" ::: "memory");  // dependent) before reading x, which it wrote
+            dep_waited = true;
         }
         if (prod) {
             // ======== producer: x row wrap(r0 - 1 + e) -> slot (running entry count) % XRING, e = 0 .. L + 1; lane c
@@ -583,11 +590,15 @@ struct BwdRows {
     static_assert(OFF_BAR % 8 == 0, "mbarrier alignment");
 };
 
-template <int C, int HID, int NPART>
+// X_STABLE: x was written before the previous non-step kernel on the stream, so its first rows may be copied before
+// the wait for the previous kernel (a compile-time choice: the two instances keep the same register allocation).
+template <int C, int HID, int NPART, bool X_STABLE>
 __global__ void __launch_bounds__(128 * NPART + 96, 1) bwd_rows_kernel(StepArgs a)
 {
     using F = BwdRows<C, HID, NPART>;
     using D = typename F::D;
+    // the next step's kernel may launch now (it waits for this one before reading the state it writes)
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     extern __shared__ __align__(128) unsigned char smem_raw[];
     unsigned char *base = smem_raw + ((1024 - (umma::smem_u32(smem_raw) & 1023)) & 1023);
     float *W1s = reinterpret_cast<float *>(base), *W1T = W1s + D::W1S, *W2T = W1T + D::W1T;
@@ -698,6 +709,7 @@ __global__ void __launch_bounds__(128 * NPART + 96, 1) bwd_rows_kernel(StepArgs 
         constexpr uint32_t I1 = umma::idesc_tf32(128, HID, false, false), IP = umma::idesc_tf32(128, D::PIN, false, false);
         uint32_t xpar = 0, mkpar = 0, g1ph = 0, dpph = 0, wgph = 0, eaph = 0, feph = 0;
         int cur_k = -1, g1_issued = 0, dp_issued = 0, x_issued[F::XRING] = {0, 0, 0};
+        bool dep_waited = false;
         auto group_sync = [&]() {
             umma::fence_before_sync();
             bar_sync(1, F::GROUP);
@@ -806,7 +818,13 @@ __global__ void __launch_bounds__(128 * NPART + 96, 1) bwd_rows_kernel(StepArgs 
             };
             // ---- segment prologue. The first x rows are requested before any weight work (their slots were consumed
             // by the previous segment's last front end, which the producer waited for), so that the copies are in
-            // flight while a new NCA's weights are staged.
+            // flight while a new NCA's weights are staged. The first wait for the previous kernel on the stream (this
+            // one is launched as its programmatic dependent; it may have written x or gy and adds to the same partial
+            // slots) comes before them, or, when the caller declared x stable, after the weight staging.
+            if (!X_STABLE && !dep_waited) {
+                asm volatile("griddepcontrol.wait;" ::: "memory");
+                dep_waited = true;
+            }
             if (prod) {
                 for (int e = 0; e < F::XRING; ++e)
                     issue_x(e);
@@ -823,6 +841,10 @@ __global__ void __launch_bounds__(128 * NPART + 96, 1) bwd_rows_kernel(StepArgs 
                 umma::fence_proxy_async();
                 group_sync();
                 cur_k = k;
+            }
+            if (X_STABLE && !dep_waited) {
+                asm volatile("griddepcontrol.wait;" ::: "memory");
+                dep_waited = true;
             }
             if (prod) {
                 // ======== producer: entries 0..2 (issued above) and masks 0, 1; after every warp's FE(j): entry j + 3,

@@ -22,7 +22,7 @@ from ._lib import check, lib, ptr
 from .nca_ops import backward_workspace, step_seed
 
 LOSS_CHUNKS = 64
-STAGE_MAIN, STAGE_ADJOINT, STAGE_REDUCE, STAGE_PARTIAL_ADD = 1, 2, 4, 8  # include/ultranca_b200.h NCA_STAGE_*
+STAGE_MAIN, STAGE_ADJOINT, STAGE_REDUCE, STAGE_PARTIAL_ADD, STAGE_X_STABLE = 1, 2, 4, 8, 16  # NCA_STAGE_*
 
 
 def _stream(dev):
@@ -151,8 +151,9 @@ class RolloutTrainer:
 
         for i in reversed(range(self.steps if steps is None else steps)):
             nxt = self.gy[1] if cur is self.gy[0] else self.gy[0]
-            _timed(timers, 'bwd', lambda: call(i, cur, nxt, STAGE_MAIN | STAGE_ADJOINT | STAGE_PARTIAL_ADD),
-                   i % timer_stride == timer_stride // 2)
+            # the saved states were written before the zeroing above (a kernel of its own): stable for the backward
+            _timed(timers, 'bwd', lambda: call(i, cur, nxt, STAGE_MAIN | STAGE_ADJOINT | STAGE_PARTIAL_ADD |
+                                               STAGE_X_STABLE), i % timer_stride == timer_stride // 2)
             cur = nxt
         if reduce:
             call(0, cur, cur, STAGE_REDUCE)  # the rollout's gradient -> grads
