@@ -766,6 +766,9 @@ int nca_reduce_adam_step(const float *partial, int64_t partial_floats, int64_t N
             const int64_t units = rows ? N * H : N * g.tiles_per_image;
             const int64_t per = rows ? (int64_t)batch_per_nca * H : (int64_t)batch_per_nca * g.tiles_per_image;
             const int grid = rows ? bwd_rows_grid(s) : w.grid;
+            if (grid > REDUCE_MAX_SLOTS)
+                fail(NCA_ERR_UNSUPPORTED, "backward grid of %d CTAs exceeds the fused reduction's %d slots", grid,
+                     REDUCE_MAX_SLOTS);
             reduce_adam_kernel<II::C, II::HID><<<dim3((unsigned)K, 3), 256, 0, st>>>(partial, units, grid, per, a);
             CUDA_OK(cudaGetLastError());
         });

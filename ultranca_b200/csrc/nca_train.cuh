@@ -121,35 +121,69 @@ __global__ void pool_store_kernel(float *__restrict__ pool, const float *__restr
     }
 }
 
+constexpr int REDUCE_MAX_SLOTS = 4096;  // partial slots one NCA may span (CTAs of the backward grid)
+
 // Block (k, tensor t): gradient element e of NCA k = the fixed-order sum (CTAs ascending) of the partial slots of the
 // backward CTAs that covered NCA k's units (as reduce_kernel), stored into the gradient output, then ||g_k|| and the
-// Adam update exactly as adam_kernel (same per-thread order and tree), so the result is bitwise that of reduce_kernel
-// followed by adam_kernel, in one pass over the partials.
+// Adam update exactly as adam_kernel (same per-thread element order and tree over 256 threads), so the result is
+// bitwise that of reduce_kernel followed by adam_kernel, in one pass over the partials. A thread keeps up to 8 slots x 4
+// elements of loads in flight (the sums are then taken in slot order).
 template <int C, int HID>
 __global__ void __launch_bounds__(256) reduce_adam_kernel(const float *__restrict__ partial, int64_t T, int G,
                                                           int64_t units_per_nca, AdamArgs a)
 {
     using D = Dims<C, HID>;
+    constexpr int U = 4, S = 8;
     const int k = blockIdx.x, t = blockIdx.y;
     const AdamTensor &Tt = a.t[t];
     const int64_t off = t == 0 ? 0 : t == 1 ? (int64_t)HID * D::PIN : (int64_t)HID * (D::PIN + 1);
     const int64_t base = (int64_t)k * Tt.numel;
-    __shared__ int range[2];
-    if (threadIdx.x == 0)
-        nca_cta_span(T, G, units_per_nca, k, &range[0], &range[1]);
-    __syncthreads();
-    float *g = const_cast<float *>(Tt.g);
-    float ss = 0.f;
-    for (int64_t i = threadIdx.x; i < Tt.numel; i += blockDim.x) {
-        float s = 0.f;
-        for (int c = range[0]; c <= range[1]; ++c) {
+    __shared__ int slots[REDUCE_MAX_SLOTS];
+    __shared__ int nslots;
+    if (threadIdx.x == 0) {
+        int c0, c1, n = 0;
+        nca_cta_span(T, G, units_per_nca, k, &c0, &c1);
+        for (int c = c0; c <= c1 && n < REDUCE_MAX_SLOTS; ++c) {
             int64_t lo, hi;
             cta_range(T, G, c, &lo, &hi);
             if (hi > lo)
-                s += partial[(size_t)(c + k) * D::PART + off + i];
+                slots[n++] = c + k;
         }
-        g[base + i] = s;
-        ss = fmaf(s, s, ss);
+        nslots = n;
+    }
+    __syncthreads();
+    const int ns = nslots;
+    float *g = const_cast<float *>(Tt.g);
+    float ss = 0.f;
+    for (int64_t i0 = threadIdx.x; i0 < Tt.numel; i0 += U * blockDim.x) {
+        float sum[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u)
+            sum[u] = 0.f;
+        for (int cb = 0; cb < ns; cb += S) {
+            float v[S][U];
+#pragma unroll
+            for (int j = 0; j < S; ++j)
+#pragma unroll
+                for (int u = 0; u < U; ++u) {
+                    const int64_t i = i0 + (int64_t)u * blockDim.x;
+                    v[j][u] = cb + j < ns && i < Tt.numel ? partial[(size_t)slots[cb + j] * D::PART + off + i] : 0.f;
+                }
+#pragma unroll
+            for (int j = 0; j < S; ++j)
+#pragma unroll
+                for (int u = 0; u < U; ++u)
+                    if (cb + j < ns)
+                        sum[u] += v[j][u];
+        }
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const int64_t i = i0 + (int64_t)u * blockDim.x;
+            if (i < Tt.numel) {
+                g[base + i] = sum[u];
+                ss = fmaf(sum[u], sum[u], ss);
+            }
+        }
     }
     __shared__ float red[256];
     red[threadIdx.x] = ss;
