@@ -258,13 +258,25 @@ void launch_pdl(Kern kern, int grid, int threads, size_t smem, cudaStream_t st, 
     CUDA_OK(cudaLaunchKernelEx(&cfg, kern, a));
 }
 
+// Switch costs (quarter rows) of the cost-balanced row bands, measured per CTA on the B200 (config 1): a band that
+// crosses into another image costs the forward ~2.4 rows and the backward ~3.4 rows more, one that crosses into
+// another NCA ~9 and ~8 rows in all.
+constexpr int FWD_BAND_S4 = 10, FWD_BAND_N4 = 26, BWD_BAND_S4 = 14, BWD_BAND_N4 = 19;
+
+Bands fwd_bands(const Shape &s, int G) { return Bands{s.N * s.H, s.H, s.B * s.H, G, FWD_BAND_S4, FWD_BAND_N4}; }
+Bands bwd_bands(const Shape &s, int G) { return Bands{s.N * s.H, s.H, s.B * s.H, G, BWD_BAND_S4, BWD_BAND_N4}; }
+
 int fwd_rows_grid(const Shape &s)
 {
     using FR = FwdRows<12, 96, FWD_ROWS_PARTS>;
     const int per = ctas_per_sm(fwd_rows_kernel<12, 96, FWD_ROWS_PARTS>, FR::smem(), FR::TMEM, FR::THREADS);
     const int64_t rows = s.N * s.H;  // each CTA draws the update masks of its rows into shared memory: at most MAXROWS
-    const int64_t need = (rows + FR::MAXROWS - 1) / FR::MAXROWS;
-    return (int)std::max<int64_t>(grid_for(rows, per), std::min<int64_t>(need, rows));
+    int64_t G = std::max<int64_t>(grid_for(rows, per), std::min<int64_t>((rows + FR::MAXROWS - 1) / FR::MAXROWS, rows));
+    // a band holds at most cost(T) / (4 G) + (4 + s4 + n4) / 4 + 1 rows: grow the grid until that fits MAXROWS
+    while (G < rows && band_cost(fwd_bands(s, (int)G), rows) / (4 * G) + (4 + FWD_BAND_S4 + FWD_BAND_N4) / 4 + 1 >
+                           FR::MAXROWS)
+        ++G;
+    return (int)G;
 }
 int bwd_rows_grid(const Shape &s)
 {
@@ -283,8 +295,10 @@ void launch_forward(const float *x, const float *w1, const float *b1, const floa
     a.N = (int)s.N; a.B = (int)s.B; a.H = (int)s.H; a.W = (int)s.W;
     a.seed = seed; a.rate = rate; a.n_offset = n_offset;
     a.seed_dev = seed_dev; a.step = step;
-    if (rows_path(s, fp32, growing) && aligned16(x)) {
+    if (rows_path(s, fp32, growing) && aligned16(x) && aligned16(y)) {
         using FR = FwdRows<12, 96, FWD_ROWS_PARTS>;
+        a.band_s4 = FWD_BAND_S4;
+        a.band_n4 = FWD_BAND_N4;
         launch_pdl(fwd_rows_kernel<12, 96, FWD_ROWS_PARTS>, fwd_rows_grid(s), FR::THREADS, FR::smem(), stream, a);
         CUDA_OK(cudaGetLastError());
         return;
@@ -502,9 +516,13 @@ int backward_stages_impl(const float *x, const float *gy, const uint8_t *alive, 
             const bool rows = rows_path(s, fp32, growing) && aligned16(x) && aligned16(gy) && aligned16(gx);
             int64_t units = N * g.tiles_per_image, units_per_nca = (int64_t)batch_per_nca * g.tiles_per_image;
             int grid = w.grid;
+            Bands bands{units, 1, 1, grid, 0, 0};  // tile path: the uniform split
             if (rows) {  // one launch: backward + fused adjoint; the dp scratch is not used
                 using BR = BwdRows<12, 96, BWD_ROWS_PARTS>;
                 grid = bwd_rows_grid(s);
+                bands = bwd_bands(s, grid);
+                a.band_s4 = BWD_BAND_S4;
+                a.band_n4 = BWD_BAND_N4;
                 units = N * H;
                 units_per_nca = (int64_t)batch_per_nca * H;
                 a.gx = gx;
@@ -536,7 +554,7 @@ int backward_stages_impl(const float *x, const float *gy, const uint8_t *alive, 
             }
             if (stages & NCA_STAGE_REDUCE) {
                 reduce_kernel<II::C, II::HID><<<dim3((D::PART + 255) / 256, (unsigned)K), 256, 0, st>>>(
-                    partial, units, grid, units_per_nca, dw1, db1, dw2, accumulate);
+                    partial, bands, units_per_nca, dw1, db1, dw2, accumulate);
                 CUDA_OK(cudaGetLastError());
             }
         });
@@ -769,7 +787,8 @@ int nca_reduce_adam_step(const float *partial, int64_t partial_floats, int64_t N
             if (grid > REDUCE_MAX_SLOTS)
                 fail(NCA_ERR_UNSUPPORTED, "backward grid of %d CTAs exceeds the fused reduction's %d slots", grid,
                      REDUCE_MAX_SLOTS);
-            reduce_adam_kernel<II::C, II::HID><<<dim3((unsigned)K, 3), 256, 0, st>>>(partial, units, grid, per, a);
+            const Bands bands = rows ? bwd_bands(s, grid) : Bands{units, 1, 1, grid, 0, 0};
+            reduce_adam_kernel<II::C, II::HID><<<dim3((unsigned)K, 3), 256, 0, st>>>(partial, bands, per, a);
             CUDA_OK(cudaGetLastError());
         });
         increment_kernel<<<1, 1, 0, st>>>(iteration);
@@ -861,11 +880,13 @@ extern "C" int nca_backward_static_scratch(const float *x, const float *gy, cons
         a.x = x; a.w1 = w1; a.b1 = b1; a.w2 = w2; a.gy = gy; a.gx = gx; a.partial = partial;
         a.N = (int)N; a.B = (int)batch_per_nca; a.H = (int)H; a.W = (int)W;
         a.seed = seed; a.rate = update_rate; a.n_offset = image_offset;
+        a.band_s4 = BWD_BAND_S4;
+        a.band_n4 = BWD_BAND_N4;
         // every partial slot the reduction reads is written by the row kernel of the same call: nothing to clear
         bwd_rows_kernel<12, 96, BWD_ROWS_PARTS, false><<<grid, BR::THREADS, BR::smem(), st>>>(a);
         CUDA_OK(cudaGetLastError());
         reduce_kernel<12, 96><<<dim3((D::PART + 255) / 256, (unsigned)K), 256, 0, st>>>(
-            partial, N * H, grid, (int64_t)batch_per_nca * H, dw1, db1, dw2, accumulate);
+            partial, bwd_bands(s, grid), (int64_t)batch_per_nca * H, dw1, db1, dw2, accumulate);
         CUDA_OK(cudaGetLastError());
     });
 }

@@ -122,4 +122,36 @@ __host__ __device__ inline void cta_range(int64_t T, int G, int c, int64_t *a, i
     *b = T * (c + 1) / G;
 }
 
+// Cost-balanced bands of a row-kernel launch over T = N H image rows (images of H rows, NCAs of BH rows): CTA c gets
+// rows [band_lo(c), band_lo(c + 1)), band_lo(c) = the last row u with cost(u) G <= c cost(T), where cost(u) = 4 u +
+// s4 (image starts in (0, u)) + n4 (NCA starts in (0, u)) in quarter rows: a band that switches to another image
+// inside costs its kernel s4 / 4 rows more (halo rows, pipeline drain and refill), one that switches to another NCA
+// n4 / 4 rows more again (weights restaged). s4 = n4 = 0: the uniform split of cta_range.
+struct Bands {
+    int64_t T, H, BH;
+    int G, s4, n4;
+};
+__host__ __device__ inline int64_t band_cost(const Bands &b, int64_t u)  // T < 2^31 rows: 32-bit divisions
+{
+    const uint32_t v = u > 0 ? (uint32_t)(u - 1) : 0u;
+    return 4 * u + (u > 0 ? (int64_t)b.s4 * (v / (uint32_t)b.H) + (int64_t)b.n4 * (v / (uint32_t)b.BH) : 0);
+}
+__host__ __device__ inline int64_t band_lo(const Bands &b, int c)
+{
+    int64_t u = b.T * c / b.G;  // the uniform split; the balanced start lies within about (s4 + n4) / 4 rows of it
+    if (b.s4 == 0 && b.n4 == 0)
+        return u;
+    const int64_t target = band_cost(b, b.T) * c;  // the last u with cost(u) G <= target (cost rises >= 4 per row)
+    while (u > 0 && band_cost(b, u) * b.G > target)
+        --u;
+    while (u < b.T && band_cost(b, u + 1) * b.G <= target)
+        ++u;
+    return u;
+}
+__host__ __device__ inline void band_range(const Bands &b, int c, int64_t *lo, int64_t *hi)
+{
+    *lo = band_lo(b, c);
+    *hi = band_lo(b, c + 1);
+}
+
 }  // namespace unca

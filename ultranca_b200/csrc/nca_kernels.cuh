@@ -67,7 +67,14 @@ struct StepArgs {
     int partial_add;               // backward: add the weight-gradient partials to the slots instead of storing them
     const uint64_t *seed_dev;      // non-null: the step's seed is splitmix_step(*seed_dev, step), read at run time
     int64_t step;                  // (a launch recorded once in a CUDA graph and replayed with new rollout seeds)
+    int band_s4, band_n4;          // row kernels: switch costs of the cost-balanced bands (Bands)
 };
+
+// The row bands of a row-kernel launch of `a` over `G` CTAs.
+__host__ __device__ inline Bands row_bands(const StepArgs &a, int G)
+{
+    return Bands{(int64_t)a.N * a.H, a.H, (int64_t)a.B * a.H, G, a.band_s4, a.band_n4};
+}
 
 // The update-mask seed of this launch's step.
 __device__ __forceinline__ uint64_t step_seed_of(const StepArgs &a)
@@ -841,25 +848,21 @@ __global__ void __launch_bounds__(256) adjoint_kernel(const float *__restrict__ 
     }
 }
 
-// The CTAs [c0, c1] of a G-CTA launch over T units whose unit ranges overlap NCA k's units [k U, (k + 1) U).
-__device__ __forceinline__ void nca_cta_span(int64_t T, int G, int64_t U, int k, int *c0_out, int *c1_out)
+// The CTAs [c0, c1] of a launch whose unit ranges (bands bd) overlap NCA k's units [k U, (k + 1) U): c0 holds unit
+// k U (first, from the uniform estimate, step down while the band starts after it, then up while it ends at or before
+// it), c1 the last CTA that starts before (k + 1) U.
+__device__ __forceinline__ void nca_cta_span(const Bands &bd, int64_t U, int k, int *c0_out, int *c1_out)
 {
     const int64_t lo = (int64_t)k * U, hi = lo + U;
-    int c0 = (int)(lo * G / T) - 1;
-    c0 = c0 < 0 ? 0 : c0;
-    int64_t a, b;
-    cta_range(T, G, c0, &a, &b);
-    while (b <= lo) {
+    int c0 = (int)(lo * bd.G / bd.T);
+    c0 = c0 >= bd.G ? bd.G - 1 : c0;
+    while (c0 > 0 && band_lo(bd, c0) > lo)
+        --c0;
+    while (c0 + 1 < bd.G && band_lo(bd, c0 + 1) <= lo)
         ++c0;
-        cta_range(T, G, c0, &a, &b);
-    }
     int c1 = c0;
-    while (c1 + 1 < G) {
-        cta_range(T, G, c1 + 1, &a, &b);
-        if (a >= hi)
-            break;
+    while (c1 + 1 < bd.G && band_lo(bd, c1 + 1) < hi)
         ++c1;
-    }
     *c0_out = c0;
     *c1_out = c1;
 }
@@ -867,21 +870,21 @@ __device__ __forceinline__ void nca_cta_span(int64_t T, int G, int64_t U, int k,
 // Fixed-order sum of the partial slots (c + k) of the CTAs c whose tile ranges overlap NCA k -> dw1, db1, dw2
 // (accumulate: added to the outputs). ncaops/nca_step.cuh:1164-1193 sums per-block partials the same way.
 template <int C, int HID>
-__global__ void reduce_kernel(const float *__restrict__ partial, int64_t T, int G, int64_t tiles_per_nca,
+__global__ void reduce_kernel(const float *__restrict__ partial, Bands bd, int64_t tiles_per_nca,
                               float *__restrict__ dw1, float *__restrict__ db1, float *__restrict__ dw2, int accumulate)
 {
     using D = Dims<C, HID>;
     const int k = blockIdx.y, e = blockIdx.x * blockDim.x + threadIdx.x;
     __shared__ int range[2];
     if (threadIdx.x == 0)
-        nca_cta_span(T, G, tiles_per_nca, k, &range[0], &range[1]);
+        nca_cta_span(bd, tiles_per_nca, k, &range[0], &range[1]);
     __syncthreads();
     if (e >= D::PART)
         return;
     float s = 0.f;
     for (int c = range[0]; c <= range[1]; ++c) {
         int64_t a, b;
-        cta_range(T, G, c, &a, &b);
+        band_range(bd, c, &a, &b);
         if (b > a)
             s += partial[(size_t)(c + k) * D::PART + e];
     }

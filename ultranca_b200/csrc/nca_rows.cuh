@@ -227,37 +227,103 @@ __device__ __forceinline__ void stage_rows_weights(float *W1s, float *W1T, float
 }
 
 // ================================================================ forward
-// Forward, software-pipelined across rows with the warps synchronised by mbarriers only. Warps 0 .. 4 NPART - 1
-// compute (part p owns channels [CPP p, CPP (p+1)) and hidden units [HPP p, HPP (p+1)) of pixel x = its TMEM lane).
-// The tensor-core work is issued from two warps on two different SM sub-partitions (a warp that shares its
-// sub-partition with busy compute warps issues tcgen05.mma at a fraction of the rate): W_M1 issues MMA1
-// (h = [p' 1 1 0..] W1ext^T), W_M2 issues MMA2 (u = relu(h) W2^T). W_PROD keeps an XRING-deep ring of x rows filled
-// with bulk copies (one lane per channel), refilling a slot when every compute warp has released it. The update masks
-// of all of the CTA's rows are drawn in the prologue (at most MAXROWS rows per CTA; the grid grows beyond that) as
-// 128-bit rows. Per row i of the band each compute warp runs (the front end two rows ahead, so that MMA1 has a row
-// of slack and MMA2 completes under the next front end)
-//   EPI(i)  [MMA1(i)]        h -> tf32(relu(h)) in TMEM H[i%2]                                   -> epi_done
-//   FE(i+2) [x rows]         p' of row i+2 -> TMEM P[i%2]; centre x and mask kept in registers   -> fe_done[i%2]
-//   OUT(i)  [MMA2(i)]        y = x + m u (m = 0: y = x)
+// Update mask of one image row (global image index n, row Y, W <= 128, W % 4 == 0) by one warp as 128 bits in x order:
+// word w holds pixels 32 w .. 32 w + 31 (bit x % 32), so mask(x) = (word[x / 32] >> (x % 32)) & 1. Lane l draws the
+// Philox block of pixels 4l .. 4l + 3 (the reference's counter layout, one call per 4 pixels) and the 4-bit groups of
+// 8 lanes are merged by shuffles. Same draws and threshold as row_mask_warp.
+__device__ __forceinline__ void row_mask_xorder_warp(uint32_t *dst, uint64_t seed, float rate, int64_t n, int H, int W,
+                                                     int Y, int lane)
+{
+    const int quads = W / 4;
+    uint32_t nib = 0;
+    if (lane < quads) {
+        if (rate >= 1.f) {
+            nib = 0xFu;
+        } else {
+            const uint64_t counter = ((uint64_t)n * (uint64_t)H + (uint64_t)Y) * (uint64_t)quads + (uint64_t)lane;
+            const uint4 w = philox4x32_10(seed, counter);
+            const uint32_t words[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e)
+                nib |= (floorf(__fadd_rn(__fmul_rn((float)(words[e] >> 8), 1.0f / 16777216.0f), rate)) != 0.f ? 1u : 0u)
+                       << e;
+        }
+    }
+    uint32_t v = nib << (4 * (lane & 7));
+    v |= __shfl_xor_sync(~0u, v, 1);
+    v |= __shfl_xor_sync(~0u, v, 2);
+    v |= __shfl_xor_sync(~0u, v, 4);
+    if ((lane & 7) == 0)
+        dst[lane >> 3] = v;
+}
+
+// Position of the n-th (0-based) set bit of w (n < popc(w)).
+__device__ __forceinline__ int nth_set_bit(uint32_t w, int n)
+{
+    int pos = 0, c = __popc(w & 0xFFFFu);
+    if (n >= c) { n -= c; w >>= 16; pos += 16; }
+    c = __popc(w & 0xFFu);
+    if (n >= c) { n -= c; w >>= 8; pos += 8; }
+    c = __popc(w & 0xFu);
+    if (n >= c) { n -= c; w >>= 4; pos += 4; }
+    c = __popc(w & 0x3u);
+    if (n >= c) { n -= c; w >>= 2; pos += 2; }
+    return pos + (n >= (int)(w & 1u) ? 1 : 0);
+}
+
+// Column of the n-th updating pixel of a row (x-order mask words m[0..3]).
+__device__ __forceinline__ int nth_pixel(const uint32_t *m, int n)
+{
+    int w = 0;
+#pragma unroll
+    for (int i = 0; i < 3; ++i) {
+        const int c = __popc(m[w]);
+        if (n >= c) {
+            n -= c;
+            ++w;
+        }
+    }
+    return 32 * w + nth_set_bit(m[w], n);
+}
+
+// Forward over the updating pixels only (the reference's forward also runs the MLP on the updating pixels alone,
+// ncaops/nca_step.cuh:344-349): the pixels with m = 1 of a segment of rows, in row-major order, are cut into tiles of
+// up to 128 (one MMA tile, lane = queue position) that span at most SPAN rows; the other pixels get y = x. Warps
+// 0 .. 4 NPART - 1 compute (part p owns channels [CPP p, CPP (p+1)) and hidden units [HPP p, HPP (p+1)) of its lane's
+// pixel); W_M1 issues MMA1 (h = [p' 1 1 0..] W1ext^T) and W_M2 issues MMA2 (u = relu(h) W2^T), from two different SM
+// sub-partitions; W_PROD keeps an XRING-deep ring of x rows filled with bulk copies (one lane per channel), refilling
+// a slot when every compute warp has released it. The prologue draws the update masks of all of the CTA's rows (at
+// most MAXROWS rows per CTA; the grid grows beyond that) as 128-bit rows and builds the tile table (per segment:
+// prefix counts of the rows, then tiles greedily). Per tile t each compute warp runs (the front end two tiles ahead)
+//   EPI(t)  [MMA1(t)]        h -> tf32(relu(h)) in TMEM H[t%2]                                       -> epi_done
+//   FE(t+2) [x rows]         lane -> (row, column) of its pixel; p' -> TMEM P[t%2]; centre x kept     -> fe_done[t%2]
+//           then the ring entries no later front end reads are retired: the non-updating pixels of their rows are
+//           copied (y = x) and the slots released
+//   OUT(t)  [MMA2(t)]        y = x + u at the lane's pixel
 // MMA1, MMA2 and the front-end signals use one mbarrier per buffer parity, so that no waiter can see a phase of the
-// row two ahead in place of its own.
+// tile two ahead in place of its own. A tile's rows and the front end's lag keep at most SPAN + 2 ring entries live.
 template <int C, int HID, int NPART>
 struct FwdRows {
     using D = Dims<C, HID>;
     static constexpr int CW = 128 * NPART, W_M1 = CW / 32, W_M2 = W_M1 + 1, W_PROD = W_M1 + 2;
-    static constexpr int THREADS = CW + 96, CPP = C / NPART, HPP = HID / NPART, XRING = 6, MAXROWS = 1024;
+    static constexpr int THREADS = CW + 96, CPP = C / NPART, HPP = HID / NPART, XRING = 8, MAXROWS = 1024, SPAN = 4;
     // TMEM: H[2] (h, then tf32(relu(h)) in place), U[2], P[2] (p'; 1, 1 at PIN, PIN+1; zeros to KP)
     static constexpr int T_H0 = 0, T_H1 = HID, T_U0 = 2 * HID, T_U1 = 2 * HID + 32, T_P0 = 256, T_P1 = 320;
     static constexpr int TMEM = 512;
     static_assert(C % NPART == 0 && HPP % 8 == 0 && D::KP <= 64 && T_U1 + 16 <= T_P0 && HID % 32 == 0 &&
-                  D::CP == 16 && C <= 32, "forward row-kernel layout");
-    // shared memory: W1 (K-major, bias folded) | W2 | x ring | mask bits (4 words per row) | mbarriers
+                  D::CP == 16 && C <= 32 && (XRING & (XRING - 1)) == 0 && XRING >= SPAN + 3, "forward row-kernel layout");
+    // shared memory: W1 (K-major, bias folded) | W2 | x ring | masks (4 words per row) | prefix counts (per row) |
+    // tiles (int2 per tile: queue start; count | first row << 8 | last row << 20) | tiles per segment (cumulative) |
+    // mbarriers
     static constexpr size_t OFF_XR = (size_t)(D::W1S + D::W2S) * 4;
     static constexpr size_t OFF_MK = OFF_XR + (size_t)XRING * C * 128 * 4;
-    static constexpr size_t OFF_BAR = OFF_MK + (size_t)MAXROWS * 16;
+    static constexpr size_t OFF_CUM = OFF_MK + (size_t)MAXROWS * 16;
+    static constexpr size_t OFF_TILE = OFF_CUM + (size_t)MAXROWS * 4;
+    static constexpr size_t OFF_SEGT = OFF_TILE + (size_t)MAXROWS * 8;
+    static constexpr size_t OFF_BAR = OFF_SEGT + (size_t)MAXROWS * 4;
     static constexpr int NBAR = 2 * XRING + 7;  // x ring full / empty, MMA1, MMA2, fe_done per buffer, epi_done
     static constexpr size_t smem() { return OFF_BAR + 8 * NBAR + 16; }
-    static_assert(OFF_BAR % 8 == 0, "mbarrier alignment");
+    static_assert(OFF_BAR % 8 == 0 && OFF_TILE % 8 == 0, "alignment");
 };
 
 template <int C, int HID, int NPART>
@@ -270,28 +336,23 @@ __global__ void __launch_bounds__(128 * NPART + 96, 1) fwd_rows_kernel(StepArgs 
     extern __shared__ __align__(128) unsigned char smem_raw[];
     float *W1s = reinterpret_cast<float *>(smem_raw), *W2s = W1s + D::W1S;
     float *XR = reinterpret_cast<float *>(smem_raw + F::OFF_XR);
-    uint32_t *MKB = reinterpret_cast<uint32_t *>(smem_raw + F::OFF_MK);
+    uint32_t *MKX = reinterpret_cast<uint32_t *>(smem_raw + F::OFF_MK);
+    int *CUM = reinterpret_cast<int *>(smem_raw + F::OFF_CUM), *SEGT = reinterpret_cast<int *>(smem_raw + F::OFF_SEGT);
+    int2 *TILE = reinterpret_cast<int2 *>(smem_raw + F::OFF_TILE);
     uint64_t *xfull = reinterpret_cast<uint64_t *>(smem_raw + F::OFF_BAR), *xempty = xfull + F::XRING,
              *g1bar = xempty + F::XRING, *g2bar = g1bar + 2, *fe_done = g2bar + 2, *epi_done = fe_done + 2;
-    uint32_t *tslot = reinterpret_cast<uint32_t *>(fe_done + 1);
+    uint32_t *tslot = reinterpret_cast<uint32_t *>(epi_done + 1);
     volatile uint32_t *abort = tslot + 1;
 
     const int tid = threadIdx.x, warp = tid / 32, lane32 = tid % 32;
     const bool compute = warp < F::W_M1, m1 = warp == F::W_M1, m2 = warp == F::W_M2, prod = warp == F::W_PROD;
     const int part = compute ? tid / 128 : 0, x = tid % 128;
     const int H = a.H, W = a.W;
-    const bool vx = compute && x < W;
-    const int xc = x < W ? x : 0, xl = xc == 0 ? W - 1 : xc - 1, xr = xc + 1 >= W ? 0 : xc + 1;
-    int64_t g0, g1;
-    cta_range((int64_t)a.N * H, gridDim.x, blockIdx.x, &g0, &g1);
     const size_t plane = (size_t)H * W;
-    if (g1 - g0 > F::MAXROWS) {  // the host sizes the grid so that this never happens: refuse rather than overflow
-        if (tid == 0)
-            set_device_error(2);
-        return;
-    }
+    __shared__ int64_t band[2];  // this CTA's rows [g0, g1), found by thread 0
 
     if (tid == 0) {
+        band_range(row_bands(a, gridDim.x), blockIdx.x, &band[0], &band[1]);
         for (int i = 0; i < 2 * F::XRING; ++i)
             umma::mbar_init(&xfull[i], i < F::XRING ? 1 : F::W_M1);  // full: the copy bytes; empty: every compute warp
         for (int b2 = 0; b2 < 2; ++b2) {
@@ -303,6 +364,13 @@ __global__ void __launch_bounds__(128 * NPART + 96, 1) fwd_rows_kernel(StepArgs 
         *abort = 0;
         umma::fence_mbar_init();
     }
+    __syncthreads();
+    const int64_t g0 = band[0], g1 = band[1];
+    if (g1 - g0 > F::MAXROWS) {  // the host sizes the grid so that this never happens: refuse rather than overflow
+        if (tid == 0)
+            set_device_error(2);
+        return;
+    }
     if (warp == 0) {
         umma::tmem_alloc(tslot, F::TMEM);
         umma::tmem_relinquish();
@@ -310,10 +378,65 @@ __global__ void __launch_bounds__(128 * NPART + 96, 1) fwd_rows_kernel(StepArgs 
     // update masks of the CTA's rows (g1 - g0 <= MAXROWS: the host sizes the grid so)
     const uint64_t seed = step_seed_of(a);
     for (int64_t u = g0 + warp; u < g1; u += blockDim.x / 32)
-        row_mask_bits_warp(MKB + (u - g0) * 4, seed, a.rate, u / H + a.n_offset, H, W, (int)(u % H), lane32);
-    umma::fence_before_sync();
+        row_mask_xorder_warp(MKX + (u - g0) * 4, seed, a.rate, u / H + a.n_offset, H, W, (int)(u % H), lane32);
     __syncthreads();
-    umma::fence_after_sync();
+    if (warp == 0) {  // tile table: per segment, the prefix counts of its rows, then tiles of <= 128 pixels, <= SPAN rows
+        int64_t g = g0;
+        RowSeg sg;
+        int s = 0, nt = 0, u0 = 0;
+        while (next_segment(g, g1, H, sg)) {
+            const int L = sg.r1 - sg.r0;
+            int run = 0;
+            for (int b = 0; b < L; b += 32) {
+                const int j = b + lane32;
+                int cnt = 0;
+                if (j < L) {
+                    const uint32_t *m = MKX + (size_t)(u0 + j) * 4;
+                    cnt = __popc(m[0]) + __popc(m[1]) + __popc(m[2]) + __popc(m[3]);
+                }
+                int inc = cnt;
+#pragma unroll
+                for (int d = 1; d < 32; d <<= 1) {
+                    const int t = __shfl_up_sync(~0u, inc, d);
+                    if (lane32 >= d)
+                        inc += t;
+                }
+                if (j < L)
+                    CUM[u0 + j] = run + inc - cnt;
+                run += __shfl_sync(~0u, inc, 31);
+            }
+            __syncwarp();
+            // greedy tiles, warp-parallel: lanes hold the prefix counts of a 64-row window [wb, wb + 64) (rows past
+            // the segment: Q); the row holding queue position p is the last row whose prefix count is <= p
+            const int Q = run;
+            auto cx = [&](int jj) { return jj < L ? CUM[u0 + jj] : Q; };
+            int wb = 0, cw0 = cx(lane32), cw1 = cx(32 + lane32);
+            auto row_of = [&](int p) {
+                const uint32_t b0 = __ballot_sync(~0u, cw0 <= p), b1 = __ballot_sync(~0u, cw1 <= p);
+                return wb + (b1 ? 63 - __clz(b1) : 31 - __clz(b0));
+            };
+            int q = 0;
+            while (q < Q) {
+                while (__shfl_sync(~0u, cw1, 0) <= q) {  // the tile's first row is past the window's first half
+                    wb += 32;
+                    cw0 = cw1;
+                    cw1 = cx(wb + 32 + lane32);
+                }
+                const int j = row_of(q);  // in [wb, wb + 32): the tile's rows stay inside the window
+                const int lim = __shfl_sync(~0u, j + F::SPAN - wb < 32 ? cw0 : cw1, (j + F::SPAN - wb) & 31);
+                const int end = min(q + 128, lim), jh = row_of(end - 1);
+                if (lane32 == 0)
+                    TILE[nt] = make_int2(q, (end - q) | (j << 8) | (jh << 20));
+                ++nt;
+                q = end;
+            }
+            if (lane32 == 0)
+                SEGT[s] = nt;
+            __syncwarp();
+            ++s;
+            u0 += L;
+        }
+    }
     const uint32_t tmem = *tslot, lane = umma::tmem_addr(tmem, warp, 0);
     if (compute && part == 0) {  // p' columns past the channel features: bias-hi, bias-lo = 1, zeros (never overwritten)
         const float v[8] = {1.f, 1.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
@@ -329,8 +452,8 @@ __global__ void __launch_bounds__(128 * NPART + 96, 1) fwd_rows_kernel(StepArgs 
     const uint64_t dW2 = umma::smem_desc(umma::smem_u32(W2s), D::CP * 16, 128);
     constexpr uint32_t I1 = umma::idesc_tf32(128, HID, false, false), I2 = umma::idesc_tf32(128, 16, false, false);
     bool ok = true;
-    uint32_t ecount = 0, epar = 0, g1par = 0, g2par = 0, eph = 0, fepar = 0;  // *par: one parity bit per buffer
-    int cur_k = -1, x_uses[F::XRING] = {0, 0, 0, 0, 0, 0};
+    uint32_t epar = 0, g1par = 0, g2par = 0, eph = 0, fepar = 0;  // *par: one parity bit per buffer / ring slot
+    int cur_k = -1, x_uses[F::XRING] = {0, 0, 0, 0, 0, 0, 0, 0};
     uint64_t *last_bar = nullptr;
     uint32_t last_par = 0;
     auto wait_par = [&](uint64_t *bars, uint32_t &par, int bj) {  // the next phase of bars[bj]
@@ -338,8 +461,6 @@ __global__ void __launch_bounds__(128 * NPART + 96, 1) fwd_rows_kernel(StepArgs 
         par ^= 1u << bj;
     };
     auto wait_g2 = [&](int bj) { wait_par(g2bar, g2par, bj); };  // MMA2 into U[bj] complete
-    int64_t seg_u0 = g0;  // unit index of the current segment's first row
-    bool dep_waited = false;
     auto signal = [&](uint64_t *bar) {  // this warp's TMEM / shared-memory reads and writes are complete
         umma::fence_before_sync();
         __syncwarp();
@@ -349,8 +470,11 @@ __global__ void __launch_bounds__(128 * NPART + 96, 1) fwd_rows_kernel(StepArgs 
 
     int64_t g = g0;
     RowSeg sg;
+    int seg = 0, u0 = 0, ebase = 0;  // segment ordinal, its first row (CTA-relative), ring entries of earlier segments
+    bool dep_waited = false;
     while (next_segment(g, g1, H, sg)) {
         const int n = sg.n, k = n / a.B, L = sg.r1 - sg.r0;
+        const int tb = seg == 0 ? 0 : SEGT[seg - 1], T = SEGT[seg] - tb;
         const float *xn = a.x + (size_t)n * C * plane;
         float *yn = a.y + (size_t)n * C * plane;
         if (k != cur_k) {  // every warp finished the previous segment (and its MMAs completed): restage the weights
@@ -368,10 +492,10 @@ __global__ void __launch_bounds__(128 * NPART + 96, 1) fwd_rows_kernel(StepArgs 
             dep_waited = true;
         }
         if (prod) {
-            // ======== producer: x row wrap(r0 - 1 + e) -> slot (running entry count) % XRING, e = 0 .. L + 1; lane c
-            // copies channel c (a starved single lane issuing all of them falls behind the compute warps)
+            // ======== producer: x row wrap(r0 - 1 + e) -> slot (ebase + e) % XRING, e = 0 .. L + 1; lane c copies
+            // channel c (a starved single lane issuing all of them falls behind the compute warps)
             for (int e = 0; e < L + 2; ++e) {
-                const int slot = (int)(x_uses[0] + x_uses[1] + x_uses[2] + x_uses[3] + x_uses[4] + x_uses[5]) % F::XRING;
+                const int slot = (ebase + e) & (F::XRING - 1);
                 if (lane32 == 0 && x_uses[slot] > 0)  // every compute warp released the slot's previous row
                     ok &= wait_bar(&xempty[slot], (uint32_t)((x_uses[slot] - 1) & 1), abort);
                 ++x_uses[slot];
@@ -387,9 +511,9 @@ __global__ void __launch_bounds__(128 * NPART + 96, 1) fwd_rows_kernel(StepArgs 
                 }
             }
         } else if (m1) {
-            // ======== MMA1 warp: h of row j -> H[j % 2] once FE(j) is done and MMA2(j-1) no longer reads H
+            // ======== MMA1 warp: h of tile j -> H[j % 2] once FE(j) is done and MMA2(j-2) no longer reads H
             if (lane32 == 0) {
-                for (int j = 0; j < L; ++j) {
+                for (int j = 0; j < T; ++j) {
                     const int bj = j & 1;
                     wait_par(fe_done, fepar, bj);
                     if (j >= 2)  // MMA2(j-2) read H[bj]
@@ -406,13 +530,13 @@ __global__ void __launch_bounds__(128 * NPART + 96, 1) fwd_rows_kernel(StepArgs 
                         g1par ^= 1u << bj;
                     }
                 }
-                for (int j = (L >= 2 ? L - 2 : 0); j < L; ++j)  // MMA2 of the last two rows: every phase waited once
+                for (int j = (T >= 2 ? T - 2 : 0); j < T; ++j)  // MMA2 of the last two tiles: every phase waited once
                     wait_g2(j & 1);
             }
         } else if (m2) {
-            // ======== MMA2 warp: u of row i -> U[i % 2] once EPI(i) is done
+            // ======== MMA2 warp: u of tile i -> U[i % 2] once EPI(i) is done
             if (lane32 == 0) {
-                for (int i = 0; i < L; ++i) {
+                for (int i = 0; i < T; ++i) {
                     const int b = i & 1;
                     ok &= wait_bar(epi_done, eph, abort);
                     eph ^= 1;
@@ -432,56 +556,87 @@ __global__ void __launch_bounds__(128 * NPART + 96, 1) fwd_rows_kernel(StepArgs 
         } else if (compute) {
             // ======== compute warps
             float xcur[F::CPP], xn1[F::CPP], xnext[F::CPP];
-            bool mcur = false, mn1 = false, mnext = false;
-            int ewaited = 0;  // entries of this segment waited for
-            auto front_end = [&](int j, int bj) {  // p' of row r0 + j -> P[bj]; its centre x and mask -> xnext, mnext
-                while (ewaited <= j + 2) {  // entries j .. j + 2 (rows Y - 1 .. Y + 1); slots round-robin
-                    const int slot = (int)(ecount % F::XRING);
+            int pcur = -1, pn1 = -1, pnext = -1;  // the lane's pixel of a tile (row << 8 | column), -1: no pixel
+            int ewaited = 0, released = 0;        // ring entries of this segment waited for / released
+            const uint32_t *mseg = MKX + (size_t)u0 * 4;
+            auto slot_of = [&](int e) { return (ebase + e) & (F::XRING - 1); };
+            auto wait_entries = [&](int upto) {  // ring entries .. upto landed
+                while (ewaited <= upto) {
+                    const int slot = slot_of(ewaited);
                     ok &= wait_bar(&xfull[slot], (epar >> slot) & 1u, abort);
                     epar ^= 1u << slot;
-                    ++ecount;
                     ++ewaited;
                 }
-                const int s0 = (int)((ecount - (uint32_t)(ewaited - j)) % F::XRING);  // slot of entry j
-                const float *rm = XR + (size_t)s0 * C * W, *r0 = XR + (size_t)((s0 + 1) % F::XRING) * C * W,
-                            *rp = XR + (size_t)((s0 + 2) % F::XRING) * C * W;
-                const uint32_t *mw = MKB + (seg_u0 - g0 + j) * 4;
-                mnext = ((mw[xc & 3] >> (xc >> 2)) & 1u) != 0;
+            };
+            // release ring entries < target (no later front end reads them), copying y = x at the non-updating pixels
+            // of the owned row each one holds first
+            auto retire = [&](int target) {
+                for (; released < target; ++released) {
+                    const int e = released, j = e - 1;
+                    wait_entries(e);
+                    if (j >= 0 && j < L && x < W && ok) {
+                        const float *src = XR + (size_t)slot_of(e) * C * W + x;
+                        float *dst = yn + (size_t)(sg.r0 + j) * W + x;
+                        if (!((mseg[j * 4 + (x >> 5)] >> (x & 31)) & 1u)) {
+#pragma unroll
+                            for (int cc = 0; cc < F::CPP; ++cc) {
+                                const int c = F::CPP * part + cc;
+                                dst[(size_t)c * plane] = src[(size_t)c * W];
+                            }
+                        }
+                    }
+                    signal(&xempty[slot_of(e)]);
+                }
+            };
+            auto front_end = [&](int t, int bj) {  // p' of tile t's pixels -> P[bj]; centre x and pixel kept
+                const int2 tl = TILE[tb + t];
+                const int nq = tl.y & 0xFF, jlo = (tl.y >> 8) & 0x3FF, jhi = (tl.y >> 20) & 0x3FF;
+                wait_entries(jhi + 2);  // rows Y - 1 .. Y + 1 of the tile's rows
+                const bool valid = x < nq;
+                const int q = tl.x + (valid ? x : 0);
+                int j = jlo;
+                while (j < jhi && CUM[u0 + j + 1] <= q)
+                    ++j;
+                const int px = nth_pixel(mseg + j * 4, q - CUM[u0 + j]);
+                const int pl = px == 0 ? W - 1 : px - 1, pr = px + 1 >= W ? 0 : px + 1;
+                const float *rm = XR + (size_t)slot_of(j) * C * W, *r0 = XR + (size_t)slot_of(j + 1) * C * W,
+                            *rp = XR + (size_t)slot_of(j + 2) * C * W;
                 const uint32_t tp = lane + (bj ? F::T_P1 : F::T_P0);
 #pragma unroll
                 for (int cc = 0; cc < F::CPP; ++cc) {  // warp-uniform channel: tcgen05.st takes one column per warp
                     const int c = F::CPP * part + cc;
                     const float *bm = rm + c * W, *b0 = r0 + c * W, *bp = rp + c * W;
-                    const float v[3][3] = {{bm[xl], bm[xc], bm[xr]}, {b0[xl], b0[xc], b0[xr]}, {bp[xl], bp[xc], bp[xr]}};
+                    const float v[3][3] = {{bm[pl], bm[px], bm[pr]}, {b0[pl], b0[px], b0[pr]}, {bp[pl], bp[px], bp[pr]}};
                     const float4 p = perceive3x3(v);
                     const float pv[4] = {tf32_rna(p.x), tf32_rna(p.y), tf32_rna(p.z), tf32_rna(p.w)};
                     umma::tmem_st4(tp + 4 * c, pv);
                     xnext[cc] = v[1][1];
                 }
+                pnext = valid ? (((sg.r0 + j) << 8) | px) : -1;
                 umma::tmem_wait_st();
                 signal(&fe_done[bj]);
-                signal(&xempty[s0]);  // entry j is read by no later front end
-                if (j == L - 1) {     // nor are the segment's last two entries
-                    signal(&xempty[(s0 + 1) % F::XRING]);
-                    signal(&xempty[(s0 + 2) % F::XRING]);
-                }
+                retire(t + 1 < T ? ((TILE[tb + t + 1].y >> 8) & 0x3FF) : L + 2);
             };
-            front_end(0, 0);
+            if (T > 0) {
+                front_end(0, 0);
 #pragma unroll
-            for (int cc = 0; cc < F::CPP; ++cc)
-                xn1[cc] = xnext[cc];
-            mn1 = mnext;
-            if (L > 1)
-                front_end(1, 1);
-            for (int i = 0; i < L; ++i) {
-                const int b = i & 1, Y = sg.r0 + i;
+                for (int cc = 0; cc < F::CPP; ++cc)
+                    xn1[cc] = xnext[cc];
+                pn1 = pnext;
+                if (T > 1)
+                    front_end(1, 1);
+            } else {
+                retire(L + 2);  // no updating pixel: y = x everywhere
+            }
+            for (int i = 0; i < T; ++i) {
+                const int b = i & 1;
 #pragma unroll
-                for (int cc = 0; cc < F::CPP; ++cc) {  // rows i, i + 1 (front end done): xcur, xn1
+                for (int cc = 0; cc < F::CPP; ++cc) {  // tiles i, i + 1 (front end done): xcur, xn1
                     xcur[cc] = xn1[cc];
                     xn1[cc] = xnext[cc];
                 }
-                mcur = mn1;
-                mn1 = mnext;
+                pcur = pn1;
+                pn1 = pnext;
                 // ---- EPI(i): h -> tf32(relu(h)) in place
                 wait_par(g1bar, g1par, b);
                 umma::fence_after_sync();
@@ -499,9 +654,9 @@ __global__ void __launch_bounds__(128 * NPART + 96, 1) fwd_rows_kernel(StepArgs 
                 umma::tmem_wait_st();
                 signal(epi_done);
                 // ---- FE(i+2)
-                if (i + 2 < L)
+                if (i + 2 < T)
                     front_end(i + 2, b);
-                // ---- OUT(i): y = x + m u
+                // ---- OUT(i): y = x + u at the lane's pixel
                 wait_g2(b);
                 umma::fence_after_sync();
                 const uint32_t tu = lane + (b ? F::T_U1 : F::T_U0) + F::CPP * part;
@@ -510,15 +665,17 @@ __global__ void __launch_bounds__(128 * NPART + 96, 1) fwd_rows_kernel(StepArgs 
                 for (int cc = 0; cc < F::CPP; ++cc)
                     u[cc] = umma::tmem_ld1(tu + cc);
                 umma::tmem_wait_ld();  // the loaded registers are defined only after this wait
-                if (vx && ok) {
-                    float *yr = yn + (size_t)Y * W + x;
+                if (pcur >= 0 && ok) {
+                    float *yr = yn + (size_t)(pcur >> 8) * W + (pcur & 0xFF);
 #pragma unroll
                     for (int cc = 0; cc < F::CPP; ++cc)
-                        yr[(size_t)(F::CPP * part + cc) * plane] = mcur ? xcur[cc] + u[cc] : xcur[cc];
+                        yr[(size_t)(F::CPP * part + cc) * plane] = xcur[cc] + u[cc];
                 }
             }
         }
-        seg_u0 += L;
+        ebase += L + 2;
+        u0 += L;
+        ++seg;
     }
     if ((m1 || m2) && lane32 == 0 && last_bar != nullptr)  // this warp's MMAs are complete before the teardown
         umma::mbar_wait(last_bar, last_par);
@@ -618,9 +775,8 @@ __global__ void __launch_bounds__(128 * NPART + 96, 1) bwd_rows_kernel(StepArgs 
     const int H = a.H, W = a.W;
     const bool vx = compute && x < W;
     const int xc = x < W ? x : 0, xl = xc == 0 ? W - 1 : xc - 1, xr = xc + 1 >= W ? 0 : xc + 1;
-    int64_t g0, g1;
-    cta_range((int64_t)a.N * H, gridDim.x, blockIdx.x, &g0, &g1);
     const size_t plane = (size_t)H * W;
+    __shared__ int64_t band[2];  // this CTA's rows [g0, g1), found by thread 0
 
     // constant PSW features of both buffers: 1 at PIN and PIN + 1, 0 at GM0 + C .. 63
     constexpr int NCONST = 64 - C - D::PIN;  // features PIN .. 63 other than gm
@@ -630,6 +786,7 @@ __global__ void __launch_bounds__(128 * NPART + 96, 1) bwd_rows_kernel(StepArgs 
         PSW[b * D::PSW + umma::sw32_offset(f, q, 128) / 4] = f < F::GM0 ? 1.f : 0.f;
     }
     if (tid == 0) {
+        band_range(row_bands(a, gridDim.x), blockIdx.x, &band[0], &band[1]);
         for (int i = 0; i < F::XRING; ++i)
             umma::mbar_init(&xfull[i], 1);
         umma::mbar_init(&mkfull[0], 1);
@@ -650,6 +807,7 @@ __global__ void __launch_bounds__(128 * NPART + 96, 1) bwd_rows_kernel(StepArgs 
     umma::fence_before_sync();
     __syncthreads();
     umma::fence_after_sync();
+    const int64_t g0 = band[0], g1 = band[1];
     const uint32_t tmem = *tslot, lane = umma::tmem_addr(tmem, warp, 0);
     if (compute && part == 0) {  // constant P columns of both buffers: 1, 1 at PIN, PIN + 1; 0 up to 63
         const float v[8] = {1.f, 1.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f}, z[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};

@@ -129,7 +129,7 @@ constexpr int REDUCE_MAX_SLOTS = 4096;  // partial slots one NCA may span (CTAs 
 // bitwise that of reduce_kernel followed by adam_kernel, in one pass over the partials. A thread keeps up to 8 slots x 4
 // elements of loads in flight (the sums are then taken in slot order).
 template <int C, int HID>
-__global__ void __launch_bounds__(256) reduce_adam_kernel(const float *__restrict__ partial, int64_t T, int G,
+__global__ void __launch_bounds__(256) reduce_adam_kernel(const float *__restrict__ partial, Bands bd,
                                                           int64_t units_per_nca, AdamArgs a)
 {
     using D = Dims<C, HID>;
@@ -142,10 +142,10 @@ __global__ void __launch_bounds__(256) reduce_adam_kernel(const float *__restric
     __shared__ int nslots;
     if (threadIdx.x == 0) {
         int c0, c1, n = 0;
-        nca_cta_span(T, G, units_per_nca, k, &c0, &c1);
+        nca_cta_span(bd, units_per_nca, k, &c0, &c1);
         for (int c = c0; c <= c1 && n < REDUCE_MAX_SLOTS; ++c) {
             int64_t lo, hi;
-            cta_range(T, G, c, &lo, &hi);
+            band_range(bd, c, &lo, &hi);
             if (hi > lo)
                 slots[n++] = c + k;
         }
