@@ -97,6 +97,18 @@ __device__ __forceinline__ int wrap_index(int i, int n)
     return i < 0 ? i + n : i;
 }
 
+// wrap_index for i at most one period outside [0, n) without a division (general i falls back to it).
+__device__ __forceinline__ int wrap_near(int i, int n)
+{
+    if (i >= 0 && i < n)
+        return i;
+    if (i < 0 && i >= -n)
+        return i + n;
+    if (i >= n && i < 2 * n)
+        return i - n;
+    return wrap_index(i, n);
+}
+
 // ---------------------------------------------------------------- tile geometry
 // A tile is R rows x S columns (R S <= 128) of one image: S = min(W, 128) columns, R = 128 / W rows when W <= 128
 // (else one row of a 128-column strip). Tile pixel i (0..127) is (i / S, i % S); tiles of an image are strips-fastest.

@@ -501,7 +501,7 @@ __global__ void __launch_bounds__(128 * NPART + 96, 1) fwd_rows_kernel(StepArgs 
                 ++x_uses[slot];
                 ok = __shfl_sync(~0u, ok, 0);
                 if (ok) {
-                    const int Y = wrap_index(sg.r0 - 1 + e, H);
+                    const int Y = wrap_near(sg.r0 - 1 + e, H);
                     if (lane32 == 0)
                         umma::mbar_arrive_expect_tx(&xfull[slot], (uint32_t)(C * W * 4));
                     __syncwarp();
