@@ -299,3 +299,55 @@ def test_fused_adam_matches_torch(ops):
         opt.step(gpu(g['g_w1'][i], g['g_b1'][i], g['g_w2'][i]))
         for p, name in zip(params, ('w1_after', 'b1_after', 'w2_after')):
             assert O.rel(p.cpu(), g[name][i]) < 1e-6, (i, name)
+
+
+@pytest.mark.parametrize('rate', [0.02, 0.1, 0.3, 0.9])
+@pytest.mark.parametrize('K,B,H,W', [(2, 2, 1, 128), (3, 1, 2, 8), (2, 3, 3, 4), (4, 2, 16, 128), (1, 2, 64, 124)])
+def test_row_forward_sparse_tiles(ops, rate, K, B, H, W):
+    """The row forward queues the updating pixels into tiles of up to 128 over at most 4 rows: low rates (tiles over
+    many sparse rows), one- to three-row images (every row a segment with wrapped halos), narrow rows. Updating
+    pixels match the TF32 oracle; the others are copied exactly."""
+    C, HID = 12, 96
+    assert ops.launch_info(C, HID, False, K * B, H, W, K)['rows_path'] == 1
+    x, w1, b1, w2 = O.make(K, B, C, HID, H, W, seed=7 * H + W)
+    mask = O.mask_for(K, B, H, W, 99, rate)
+    out = ops.step(*gpu(x, w1, b1, w2), rate, seed=99).cpu()
+    ref = O.reference_step(x, w1, b1, w2, mask, False, tf32=True)
+    keep = (mask == 0).expand_as(x)
+    assert torch.equal(out[keep], x[keep])
+    assert O.rel(out, ref) < 1e-3
+    assert device_error_clear()
+
+
+@pytest.mark.parametrize('K,B,H,W', [(400, 2, 4, 32), (160, 8, 128, 8)])
+def test_row_forward_many_segments_and_grown_grid(ops, K, B, H, W):
+    """Bands of several segments (4-row images, two or three NCAs per band: weights restaged, ring and queue kept per
+    segment), and more rows than 148 CTAs of MAXROWS rows hold (the grid grows)."""
+    C, HID = 12, 96
+    info = ops.launch_info(C, HID, False, K * B, H, W, K)
+    assert info['rows_path'] == 1
+    if K * B * H > 148 * 1024:
+        assert info['fwd_grid'] > 148
+    x, w1, b1, w2 = O.make(K, B, C, HID, H, W, seed=3)
+    mask = O.mask_for(K, B, H, W, 5, 0.5)
+    out = ops.step(*gpu(x, w1, b1, w2), 0.5, seed=5).cpu()
+    ref = O.reference_step(x, w1, b1, w2, mask, False, tf32=True)
+    assert O.rel(out, ref) < 1e-3
+    assert device_error_clear()
+
+
+def test_row_backward_many_segments(ops):
+    """Backward bands over many 4-row images and two or three NCAs each (the weight-gradient accumulator flushed to a
+    new partial slot and the weights restaged at every NCA switch, halo rows at every image switch; the cost-balanced
+    bands differ from the uniform split): TF32 gradients vs the TF32 oracle."""
+    C, HID, K, B, H, W = 12, 96, 300, 2, 4, 32
+    assert ops.launch_info(C, HID, False, K * B, H, W, K)['rows_path'] == 1
+    x, w1, b1, w2 = O.make(K, B, C, HID, H, W, seed=11)
+    R0 = torch.randn(x.shape, generator=torch.Generator().manual_seed(4))
+    R, n_amb = unambiguous(x, w1, b1, R0)
+    mask = O.mask_for(K, B, H, W, 77, 0.5)
+    got, _ = grads_gpu(ops, x, w1, b1, w2, R, 0.5, False, False, 77)
+    ref = O.step_backward(x, w1, b1, w2, mask, R, False, tf32=True)
+    for a, b, name in zip(got, ref, ('gx', 'dw1', 'db1', 'dw2')):
+        assert O.rel(a, b) < 1e-3, name
+    assert device_error_clear()
