@@ -874,19 +874,35 @@ __global__ void reduce_kernel(const float *__restrict__ partial, Bands bd, int64
                               float *__restrict__ dw1, float *__restrict__ db1, float *__restrict__ dw2, int accumulate)
 {
     using D = Dims<C, HID>;
+    constexpr int MAXS = 1024;  // slots listed in shared memory; a longer span is summed in the same order from bd
     const int k = blockIdx.y, e = blockIdx.x * blockDim.x + threadIdx.x;
-    __shared__ int range[2];
-    if (threadIdx.x == 0)
+    __shared__ int range[2], nslots;
+    __shared__ int slots[MAXS];  // the non-empty CTAs of the span (thread 0 finds them once)
+    if (threadIdx.x == 0) {
         nca_cta_span(bd, tiles_per_nca, k, &range[0], &range[1]);
+        int n = 0;
+        for (int c = range[0]; c <= range[1] && n < MAXS; ++c) {
+            int64_t a, b;
+            band_range(bd, c, &a, &b);
+            if (b > a)
+                slots[n++] = c;
+        }
+        nslots = range[1] - range[0] + 1 <= MAXS ? n : -1;
+    }
     __syncthreads();
     if (e >= D::PART)
         return;
     float s = 0.f;
-    for (int c = range[0]; c <= range[1]; ++c) {
-        int64_t a, b;
-        band_range(bd, c, &a, &b);
-        if (b > a)
-            s += partial[(size_t)(c + k) * D::PART + e];
+    if (nslots >= 0) {
+        for (int i = 0; i < nslots; ++i)
+            s += partial[(size_t)(slots[i] + k) * D::PART + e];
+    } else {
+        for (int c = range[0]; c <= range[1]; ++c) {
+            int64_t a, b;
+            band_range(bd, c, &a, &b);
+            if (b > a)
+                s += partial[(size_t)(c + k) * D::PART + e];
+        }
     }
     float *dst;
     if (e < HID * D::PIN)
