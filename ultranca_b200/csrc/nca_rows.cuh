@@ -1020,6 +1020,10 @@ __global__ void __launch_bounds__(128 * NPART + 96, 1) bwd_rows_kernel(StepArgs 
                     prefetch_rows(j + 2 * F::XRING);
                     if (j + 2 < L)
                         draw_mask(j + 2);
+                    // the partial slot this NCA's accumulator is added to when the segment ends: into L2 a few rows
+                    // ahead, so that the flush's reads of the old values hit
+                    if (a.partial_add && lane32 == 0 && j == (L > 4 ? L - 4 : 0))
+                        umma::bulk_prefetch_l2(a.partial + (size_t)(blockIdx.x + k) * D::PART, (uint32_t)(D::PART * 4));
                 }
             } else if (mma) {
                 // ======== MMA warp: G1(0); per row DP(i), then G1(i+1)
