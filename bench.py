@@ -412,16 +412,36 @@ def reference_kernels_b200(args, dev):
 
 def run_e2e(args, dev, rank, world, dist, K, w1, b1, w2, target, nca_ops, training):
     """The training iteration as train.py runs it on the drop-in operator: nca_ops.step per step under autograd,
-    backward through _Step, the fused optimiser; batch H2D from pinned host memory, losses D2H, every iteration."""
+    backward through _Step, the fused optimiser; batch H2D from pinned host memory, losses D2H, every iteration. The
+    batch of iteration i + 1 is copied on a side stream while iteration i computes (two device buffers; a buffer is
+    refilled once the iteration that read it, whose autograd graph keeps it, has finished)."""
     g = torch.Generator().manual_seed(77 + rank)
     host = ((torch.rand(K, B, C, H, W, generator=g) * 2 - 1) * 0.1).pin_memory()
     ws = [t.clone().requires_grad_() for t in (w1, b1, w2)]
     opt = training.FusedAdam(ws)
     loss_host = torch.empty(K).pin_memory()
     stream = torch.cuda.current_stream(dev)
+    copy_stream = torch.cuda.Stream(dev)
+    dbuf = [torch.empty(host.shape, device=dev) for _ in range(2)]
+    ready = [torch.cuda.Event() for _ in range(2)]
+    done = [torch.cuda.Event() for _ in range(2)]
+    pending = set()
+
+    def prefetch(i):
+        b = i % 2
+        with torch.cuda.stream(copy_stream):
+            if b in pending:
+                copy_stream.wait_event(done[b])  # the iteration that last read this buffer has finished
+            dbuf[b].copy_(host, non_blocking=True)
+            ready[b].record(copy_stream)
 
     def it(i):
-        x = host.to(dev, non_blocking=True)
+        b = i % 2
+        if i == first[0]:
+            prefetch(i)
+        prefetch(i + 1)
+        stream.wait_event(ready[b])
+        x = dbuf[b]
         for s in range(STEPS):
             x = nca_ops.step(x, *ws, RATE, seed=1000 * i + s, image_offset=rank * K * B)
         loss, gy = training.synthetic_loss(x.detach(), target)
@@ -430,13 +450,18 @@ def run_e2e(args, dev, rank, world, dist, K, w1, b1, w2, target, nca_ops, traini
         for w in ws:
             w.grad = None
         loss_host.copy_(loss, non_blocking=True)
+        done[b].record(stream)
+        pending.add(b)
 
+    first = [0]
     for i in range(args.warmup):
         it(i)
     torch.cuda.synchronize()
     if dist is not None:
         dist.barrier()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    first[0] = args.warmup  # the timed region copies its own first batch too
+    pending.clear()
     start.record(stream)
     for i in range(args.steps):
         it(args.warmup + i)
