@@ -351,3 +351,28 @@ def test_row_backward_many_segments(ops):
     for a, b, name in zip(got, ref, ('gx', 'dw1', 'db1', 'dw2')):
         assert O.rel(a, b) < 1e-3, name
     assert device_error_clear()
+
+
+@pytest.mark.parametrize('K,B,H,W,rate', [(2, 1, 6, 256, 0.5), (1, 2, 5, 384, 0.5), (2, 1, 1, 256, 1.0),
+                                          (1, 1, 3, 512, 0.3), (3, 2, 7, 256, 0.5), (40, 2, 4, 256, 0.5)])
+def test_strip_backward_parity(ops, K, B, H, W, rate):
+    """Rows wider than 128 (W = 128 S) run the backward row kernel over column strips of 128 with the cross-strip
+    adjoint terms added by the edge fix-up: TF32 gradients vs the TF32 oracle, on the whole of gx and on the strip edge
+    columns alone (where the fix-up adds), at two to four strips, one-row images, a rate of 1 and bands of many 4-row
+    images over several NCAs; repeated calls are bitwise equal."""
+    C, HID = 12, 96
+    assert ops.launch_info(C, HID, False, K * B, H, W, K)['rows_path'] == 2
+    x, w1, b1, w2 = O.make(K, B, C, HID, H, W, seed=5 * H + W + K)
+    R0 = torch.randn(x.shape, generator=torch.Generator().manual_seed(6))
+    R, n_amb = unambiguous(x, w1, b1, R0)
+    assert n_amb <= 0.05 * K * B * H * W
+    mask = O.mask_for(K, B, H, W, 31, rate)
+    got, _ = grads_gpu(ops, x, w1, b1, w2, R, rate, False, False, 31)
+    ref = O.step_backward(x, w1, b1, w2, mask, R, False, tf32=True)
+    for a, b, name in zip(got, ref, ('gx', 'dw1', 'db1', 'dw2')):
+        assert O.rel(a, b) < 1e-3, (name, O.rel(a, b))
+    edges = [c for s in range(W // 128) for c in (128 * s, 128 * s + 127)]
+    assert O.rel(got[0][..., edges], ref[0][..., edges]) < 1e-3
+    again, _ = grads_gpu(ops, x, w1, b1, w2, R, rate, False, False, 31)
+    assert all(torch.equal(a, b) for a, b in zip(got, again))
+    assert device_error_clear()

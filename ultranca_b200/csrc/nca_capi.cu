@@ -234,6 +234,14 @@ bool rows_path(const Shape &s, bool fp32, bool growing)
 {
     return !fp32 && !growing && s.C == 12 && s.HID == 96 && s.W <= 128 && s.W % 4 == 0;
 }
+// Wider rows (W a multiple of 128 from 256 on): the backward row kernel over column strips of 128 plus the edge
+// fix-up; the forward keeps the tile kernel.
+bool strip_path(const Shape &s, bool fp32, bool growing)
+{
+    return !fp32 && !growing && s.C == 12 && s.HID == 96 && s.W >= 256 && s.W % 128 == 0;
+}
+// The backward runs a row kernel (one tile per row, or strips) for this shape.
+bool bwd_rows_path(const Shape &s, bool fp32, bool growing) { return rows_path(s, fp32, growing) || strip_path(s, fp32, growing); }
 bool aligned16(const void *p) { return ((uintptr_t)p & 15) == 0; }
 
 // Launch of a row kernel as a programmatic dependent of the previous kernel on the stream: once every CTA of that
@@ -338,8 +346,8 @@ BwdWork backward_work(const Shape &s, bool fp32, bool growing)
         w.grid = grid_for(s.N * g.tiles_per_image, bwd_ctas_per_sm<II>());
         w.dp_floats = s.N * D::PIN * s.H * s.W;
         int slots = w.grid;
-        if (rows_path(s, fp32, growing))  // either kernel may run (the row kernel needs 16-byte aligned rows)
-            slots = std::max(slots, bwd_rows_grid(s));
+        if (bwd_rows_path(s, fp32, growing))  // either kernel may run (the row kernel needs 16-byte aligned rows);
+            slots = std::max(slots, bwd_rows_grid(s));  // the strip kernel's edge scratch fits in the dp scratch
         w.partial_floats = (int64_t)(slots + s.K - 1) * D::PART;
     });
     return w;
@@ -514,7 +522,9 @@ int backward_stages_impl(const float *x, const float *gy, const uint8_t *alive, 
             a.seed_dev = seed_dev; a.step = step;
             a.partial_add = (stages & NCA_STAGE_PARTIAL_ADD) ? 1 : 0;
             const TileGeom g = make_geom((int)H, (int)W);
-            const bool rows = rows_path(s, fp32, growing) && aligned16(x) && aligned16(gy) && aligned16(gx);
+            const bool strip = strip_path(s, fp32, growing) && aligned16(x) && aligned16(gy) && aligned16(gx) &&
+                               aligned16(dp);
+            const bool rows = strip || (rows_path(s, fp32, growing) && aligned16(x) && aligned16(gy) && aligned16(gx));
             int64_t units = N * g.tiles_per_image, units_per_nca = (int64_t)batch_per_nca * g.tiles_per_image;
             int grid = w.grid;
             Bands bands{units, 1, 1, grid, 0, 0};  // tile path: the uniform split
@@ -527,7 +537,28 @@ int backward_stages_impl(const float *x, const float *gy, const uint8_t *alive, 
                 units = N * H;
                 units_per_nca = (int64_t)batch_per_nca * H;
                 a.gx = gx;
-                if (stages & NCA_STAGE_MAIN) {
+                if (strip) {  // column strips; the adjoint stage adds the cross-strip terms from the edge scratch (dp)
+                    using BS = BwdRows<12, 96, BWD_ROWS_PARTS, true>;
+                    if (stages & NCA_STAGE_MAIN) {
+                        if (stages & NCA_STAGE_X_STABLE) {
+                            set_smem_once(bwd_rows_kernel<12, 96, BWD_ROWS_PARTS, true, true>, BS::smem());
+                            launch_pdl(bwd_rows_kernel<12, 96, BWD_ROWS_PARTS, true, true>, grid, BS::THREADS,
+                                       BS::smem(), st, a);
+                        } else {
+                            set_smem_once(bwd_rows_kernel<12, 96, BWD_ROWS_PARTS, false, true>, BS::smem());
+                            launch_pdl(bwd_rows_kernel<12, 96, BWD_ROWS_PARTS, false, true>, grid, BS::THREADS,
+                                       BS::smem(), st, a);
+                        }
+                        CUDA_OK(cudaGetLastError());
+                    }
+                    if (stages & NCA_STAGE_ADJOINT) {
+                        const int64_t total = N * H * (W / 128) * 2 * 12;
+                        const int blocks = (int)std::min<int64_t>((total + 255) / 256, (int64_t)device_info().sms * 8);
+                        strip_edge_fixup_kernel<12><<<blocks, 256, 0, st>>>(reinterpret_cast<const float4 *>(dp), gx,
+                                                                           (int)N, (int)H, (int)W);
+                        CUDA_OK(cudaGetLastError());
+                    }
+                } else if (stages & NCA_STAGE_MAIN) {
                     if (stages & NCA_STAGE_X_STABLE) {
                         set_smem_once(bwd_rows_kernel<12, 96, BWD_ROWS_PARTS, true>, BR::smem());
                         launch_pdl(bwd_rows_kernel<12, 96, BWD_ROWS_PARTS, true>, grid, BR::THREADS, BR::smem(), st, a);
@@ -608,7 +639,7 @@ int nca_launch_info(int64_t C, int64_t hidden, int fp32, int growing, int64_t N,
         check_ptr(info, "info");
         const Shape s{N, C, H, W, K, hidden, K > 0 ? N / K : 0};
         validate(s, growing);
-        const bool rows = rows_path(s, fp32, growing);
+        const bool rows = rows_path(s, fp32, growing), brows = bwd_rows_path(s, fp32, growing);
         const BwdWork w = backward_work(s, fp32, growing);
         int fwd_grid = 0, fwd_per = 0;
         dispatch(C, hidden, fp32, growing, [&](auto I) {
@@ -617,11 +648,11 @@ int nca_launch_info(int64_t C, int64_t hidden, int fp32, int growing, int64_t N,
             fwd_per = fwd_ctas_per_sm<II>();
             fwd_grid = grid_for(N * g.tiles_per_image, fwd_per);
         });
-        info[0] = rows ? 1 : 0;
+        info[0] = rows ? 1 : brows ? 2 : 0;
         info[1] = rows ? fwd_rows_grid(s) : fwd_grid;
         info[2] = rows ? FwdRows<12, 96, FWD_ROWS_PARTS>::THREADS : 128;
-        info[3] = rows ? bwd_rows_grid(s) : w.grid;
-        info[4] = rows ? BwdRows<12, 96, BWD_ROWS_PARTS>::THREADS : 128;
+        info[3] = brows ? bwd_rows_grid(s) : w.grid;
+        info[4] = brows ? BwdRows<12, 96, BWD_ROWS_PARTS>::THREADS : 128;
         info[5] = device_info().sms;
         info[6] = fwd_per;
         info[7] = w.grid;
@@ -781,7 +812,7 @@ int nca_reduce_adam_step(const float *partial, int64_t partial_floats, int64_t N
             // the unit decomposition of the backward launches that wrote the partials (the row kernel when its shape
             // qualifies: those launches had 16-byte-aligned x, gy and gx)
             const TileGeom g = make_geom((int)H, (int)W);
-            const bool rows = rows_path(s, fp32, growing);
+            const bool rows = bwd_rows_path(s, fp32, growing);
             const int64_t units = rows ? N * H : N * g.tiles_per_image;
             const int64_t per = rows ? (int64_t)batch_per_nca * H : (int64_t)batch_per_nca * g.tiles_per_image;
             const int grid = rows ? bwd_rows_grid(s) : w.grid;

@@ -77,6 +77,25 @@ __device__ __forceinline__ void row_mask_warp(T *mk, uint64_t seed, float rate, 
     }
 }
 
+// The same for the 128 pixels x0 .. x0 + 127 of a wider row (x0 % 4 == 0, x0 + 128 <= W): lane l draws the Philox
+// block of pixels x0 + 4l .. x0 + 4l + 3 and writes mk[x - x0].
+template <class T>
+__device__ __forceinline__ void row_mask_strip_warp(T *mk, uint64_t seed, float rate, int64_t n, int H, int W, int Y,
+                                                    int lane, int x0)
+{
+    if (rate >= 1.f) {
+        for (int x = lane; x < 128; x += 32)
+            mk[x] = T(1);
+        return;
+    }
+    const uint64_t counter = ((uint64_t)n * (uint64_t)H + (uint64_t)Y) * (uint64_t)(W / 4) + (uint64_t)(x0 / 4 + lane);
+    const uint4 w = philox4x32_10(seed, counter);
+    const uint32_t words[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e)
+        mk[4 * lane + e] = floorf(__fadd_rn(__fmul_rn((float)(words[e] >> 8), 1.0f / 16777216.0f), rate)) != 0.f ? T(1) : T(0);
+}
+
 // Named barrier `id` over `count` threads, and the same with an AND over `pred`.
 __device__ __forceinline__ void bar_sync(int id, int count)
 {
@@ -719,12 +738,17 @@ __device__ __forceinline__ void st_sw32x8_balanced(float *tile, int mn0, int k, 
 // WG is one chain of M = 128 (features of PSW: p' 0..PIN-1, the constant 1 at PIN, gm at GM0..GM0+C-1), N = 2 HID
 // (relu(h) | dh), K = 128 pixels: columns [0, HID) of rows GM0.. hold dW2, columns [HID, 2 HID) of rows 0..PIN hold
 // dW1 and db1 (transposed); the other blocks are not used.
-template <int C, int HID, int NPART>
+// STRIP: rows wider than one tile (W = 128 S, S >= 2) are processed as S column strips of 128, one after the other
+// over the rows of a segment. A strip's x rows carry 4 halo columns on each side (ring rows of XS = 136 floats); the
+// adjoint treats the columns next to a strip as zero and publishes the strip's first and last columns of dp for every
+// owned row to the edge scratch, from which strip_edge_fixup_kernel adds the cross-strip terms.
+template <int C, int HID, int NPART, bool STRIP = false>
 struct BwdRows {
     using D = Dims<C, HID>;
     static constexpr int CW = 128 * NPART, W_MMA = CW / 32, W_PROD = W_MMA + 1, W_WG = W_MMA + 2;
     static constexpr int THREADS = CW + 96, GROUP = CW + 64;  // GROUP: the warps on named barrier 1 (all but W_WG)
     static constexpr int CPP = C / NPART, HPP = HID / NPART, XRING = 3, GM0 = D::PIN + 2;
+    static constexpr int XS = STRIP ? 136 : 128;  // ring row stride (floats)
     // TMEM: h / dh, dhp, WG accumulator, P[2] (p' 0..PIN-1 then dp; 1, 1 at PIN, PIN+1; gm at GM0..; zeros)
     static constexpr int T_H = 0, T_DHP = HID, T_ACC = 2 * HID, NACC = 2 * HID, T_P0 = T_ACC + NACC, T_P1 = T_P0 + 64;
     static constexpr int TMEM = 512;
@@ -735,28 +759,41 @@ struct BwdRows {
     static constexpr size_t OFF_PSW = (size_t)D::BWD_W;
     static constexpr size_t OFF_RH = OFF_PSW + (size_t)2 * D::PSW * 4;
     static constexpr size_t OFF_XR = OFF_RH + (size_t)2 * D::RHDH * 4;
-    static constexpr size_t OFF_EDGE = OFF_XR + (size_t)XRING * C * 128 * 4;
-    static constexpr int EDGE_SLOTS = 9;  // left / right edge lane of each of the 4 warps of a part, and x = W - 1
+    static constexpr size_t OFF_EDGE = OFF_XR + (size_t)XRING * C * XS * 4;
+    // left / right edge lane of each of the 4 warps of a part, and (not STRIP) x = W - 1
     // (one buffer: row i + 1's edges are written only after every warp finished row i's adjoint, since DP(i + 1)
     // follows every warp's EA(i + 1))
+    static constexpr int EDGE_SLOTS = STRIP ? 8 : 9;
     static constexpr size_t OFF_MK = OFF_EDGE + (size_t)EDGE_SLOTS * C * 16;
     static constexpr size_t OFF_BAR = OFF_MK + 2 * 128;
     // x ring, mask buffers, g1, dp, wg (tensor-core completions), wg_go, ea_done, fe_done (one arrival per warp)
     static constexpr int NBAR = XRING + 8;
-    static constexpr size_t smem() { return 1024 + OFF_BAR + 8 * NBAR + 16; }
+    // then the TMEM slot and abort words (8 bytes) and this CTA's row band (two int64)
+    static constexpr size_t OFF_BAND = OFF_BAR + 8 * NBAR + 8;
+    // The swizzled operands need a 1024-byte aligned base. The strip layout leaves no room for alignment slack: its
+    // kernel requires the dynamic shared memory to start 1024-aligned (it does when the kernel has no static shared
+    // memory) and reports a device error otherwise.
+    static constexpr size_t ALIGN_SLACK = STRIP ? 0 : 1024;
+    static constexpr size_t smem() { return ALIGN_SLACK + OFF_BAND + 16; }
     static_assert(OFF_BAR % 8 == 0, "mbarrier alignment");
+    static_assert(smem() <= 232448, "227 KB of shared memory per CTA");
 };
 
 // X_STABLE: x was written before the previous non-step kernel on the stream, so its first rows may be copied before
 // the wait for the previous kernel (a compile-time choice: the two instances keep the same register allocation).
-template <int C, int HID, int NPART, bool X_STABLE>
+template <int C, int HID, int NPART, bool X_STABLE, bool STRIP = false>
 __global__ void __launch_bounds__(128 * NPART + 96, 1) bwd_rows_kernel(StepArgs a)
 {
-    using F = BwdRows<C, HID, NPART>;
+    using F = BwdRows<C, HID, NPART, STRIP>;
     using D = typename F::D;
     // the next step's kernel may launch now (it waits for this one before reading the state it writes)
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     extern __shared__ __align__(128) unsigned char smem_raw[];
+    if (STRIP && (umma::smem_u32(smem_raw) & 1023) != 0) {  // no room for alignment slack (the layout would overrun)
+        if (threadIdx.x == 0)
+            set_device_error(3);
+        return;
+    }
     unsigned char *base = smem_raw + ((1024 - (umma::smem_u32(smem_raw) & 1023)) & 1023);
     float *W1s = reinterpret_cast<float *>(base), *W1T = W1s + D::W1S, *W2T = W1T + D::W1T;
     float *PSW = reinterpret_cast<float *>(base + F::OFF_PSW), *RH = reinterpret_cast<float *>(base + F::OFF_RH),
@@ -773,10 +810,18 @@ __global__ void __launch_bounds__(128 * NPART + 96, 1) bwd_rows_kernel(StepArgs 
     const bool compute = warp < F::W_MMA, mma = warp == F::W_MMA, prod = warp == F::W_PROD;
     const int part = compute ? tid / 128 : 0, x = tid % 128, wq = warp & 3;
     const int H = a.H, W = a.W;
-    const bool vx = compute && x < W;
-    const int xc = x < W ? x : 0, xl = xc == 0 ? W - 1 : xc - 1, xr = xc + 1 >= W ? 0 : xc + 1;
+    const int S = STRIP ? W / 128 : 1;  // column strips per row
+    const bool vx = compute && (STRIP || x < W);
+    const int xc = STRIP ? x : x < W ? x : 0;
+    // the lane's left, centre and right columns in a ring row (STRIP: 4 halo columns precede the strip's first)
+    const int il = STRIP ? x + 3 : xc == 0 ? W - 1 : xc - 1, ic = STRIP ? x + 4 : xc,
+              ir = STRIP ? x + 5 : xc + 1 >= W ? 0 : xc + 1;
+    const int RS = STRIP ? F::XS : W;  // ring row stride
     const size_t plane = (size_t)H * W;
-    __shared__ int64_t band[2];  // this CTA's rows [g0, g1), found by thread 0
+    // this CTA's rows [g0, g1), found by thread 0 (STRIP: in the dynamic shared memory, so that the kernel has no static
+    // shared memory and its dynamic shared memory starts 1024-aligned)
+    __shared__ int64_t band_static[2];
+    int64_t *band = STRIP ? reinterpret_cast<int64_t *>(base + F::OFF_BAND) : band_static;
 
     // constant PSW features of both buffers: 1 at PIN and PIN + 1, 0 at GM0 + C .. 63
     constexpr int NCONST = 64 - C - D::PIN;  // features PIN .. 63 other than gm
@@ -840,21 +885,22 @@ __global__ void __launch_bounds__(128 * NPART + 96, 1) bwd_rows_kernel(StepArgs 
                     wk = k;
                     started = false;
                 }
-                for (int i = 1; i <= L - 2; ++i) {
-                    ok &= wait_bar(wggo, goph, abort);
-                    goph ^= 1;
-                    if (!ok)
-                        continue;
-                    umma::fence_after_sync();
-                    const uint64_t dA = (i & 1) ? dA1 : dA0;
+                for (int s = 0; s < S; ++s)
+                    for (int i = 1; i <= L - 2; ++i) {
+                        ok &= wait_bar(wggo, goph, abort);
+                        goph ^= 1;
+                        if (!ok)
+                            continue;
+                        umma::fence_after_sync();
+                        const uint64_t dA = (i & 1) ? dA1 : dA0;
 #pragma unroll
-                    for (int ks = 0; ks < 16; ++ks)
-                        umma::mma_ss(tmem + F::T_ACC, dA + (uint64_t)(ks * 64), dB + (uint64_t)(ks * 64), IWG,
-                                     started || ks > 0);
-                    umma::commit(wgbar);
-                    started = true;
-                    ++issued;
-                }
+                        for (int ks = 0; ks < 16; ++ks)
+                            umma::mma_ss(tmem + F::T_ACC, dA + (uint64_t)(ks * 64), dB + (uint64_t)(ks * 64), IWG,
+                                         started || ks > 0);
+                        umma::commit(wgbar);
+                        started = true;
+                        ++issued;
+                    }
             }
             if (issued > 0)  // this warp's MMAs are complete before the teardown
                 umma::mbar_wait(wgbar, (uint32_t)((issued - 1) & 1));
@@ -933,42 +979,63 @@ __global__ void __launch_bounds__(128 * NPART + 96, 1) bwd_rows_kernel(StepArgs 
 
         int64_t g = g0;
         RowSeg sg;
-        while (next_segment(g, g1, H, sg)) {
+        while (next_segment(g, g1, H, sg))
+          for (int s = 0; s < S; ++s) {  // the column strips of the segment (one pass unless STRIP)
             const int n = sg.n, k = n / a.B, L = sg.r1 - sg.r0 + 2;  // sequence: halo, owned rows, halo
+            const int c0 = 128 * s, gcol = c0 + xc;  // the strip's first column; the lane's column in the image
             const float *xn = a.x + (size_t)n * C * plane, *gyn = a.gy + (size_t)n * C * plane;
             float *gxn = a.gx + (size_t)n * C * plane;
             auto rowY = [&](int i) { return wrap_index(sg.r0 - 1 + i, H); };
-            // producer warp: x row wrap(r0 - 2 + e) -> slot e % XRING (one lane per channel)
+            // producer warp: x row wrap(r0 - 2 + e) -> slot e % XRING (one lane per channel). STRIP: columns
+            // c0 - 4 .. c0 + 131 (circular) -> ring columns 0 .. 135, as one copy or two where the range wraps (every
+            // piece starts and ends on a 16-byte boundary: W and c0 are multiples of 128)
             auto issue_x = [&](int e) {
                 const int slot = e % F::XRING, Y = wrap_index(sg.r0 - 2 + e, H);
                 ok = __shfl_sync(~0u, ok, 0);  // lane 0 did the waits: the whole warp takes one path
                 if (ok) {
                     if (lane32 == 0)
-                        umma::mbar_arrive_expect_tx(&xfull[slot], (uint32_t)(C * W * 4));
+                        umma::mbar_arrive_expect_tx(&xfull[slot], (uint32_t)(C * RS * 4));
                     __syncwarp();
-                    if (lane32 < C)
-                        umma::bulk_g2s(XR + ((size_t)slot * C + lane32) * W, xn + ((size_t)lane32 * H + Y) * W,
-                                       (uint32_t)(W * 4), &xfull[slot]);
+                    if (lane32 < C) {
+                        float *dst = XR + ((size_t)slot * C + lane32) * RS;
+                        const float *src = xn + ((size_t)lane32 * H + Y) * W;
+                        if (!STRIP) {
+                            umma::bulk_g2s(dst, src, (uint32_t)(W * 4), &xfull[slot]);
+                        } else if (s == 0) {
+                            umma::bulk_g2s(dst, src + W - 4, 16u, &xfull[slot]);
+                            umma::bulk_g2s(dst + 4, src, 132u * 4u, &xfull[slot]);
+                        } else if (s == S - 1) {
+                            umma::bulk_g2s(dst, src + c0 - 4, 132u * 4u, &xfull[slot]);
+                            umma::bulk_g2s(dst + 132, src, 16u, &xfull[slot]);
+                        } else {
+                            umma::bulk_g2s(dst, src + c0 - 4, 136u * 4u, &xfull[slot]);
+                        }
+                    }
                     ++x_issued[slot];
                 }
             };
             // producer warp: the x row of entry e and the gy row of sequence row e - 1 (read by the front end of that
             // row) into L2, some rows before their copy / load: the three-slot ring alone does not cover the latency
-            // of HBM (one lane per channel row)
+            // of HBM (one lane per channel row; STRIP: the strip's 128 columns)
             auto prefetch_rows = [&](int e) {
                 if (e > L + 1)
                     return;
+                const uint32_t bytes = STRIP ? 512u : (uint32_t)(W * 4);
                 if (lane32 < C)
-                    umma::bulk_prefetch_l2(xn + ((size_t)lane32 * H + wrap_index(sg.r0 - 2 + e, H)) * W, (uint32_t)(W * 4));
+                    umma::bulk_prefetch_l2(xn + ((size_t)lane32 * H + wrap_index(sg.r0 - 2 + e, H)) * W + c0, bytes);
                 const int c = lane32 - 16;
                 if (c >= 0 && c < C && e >= 1 && e - 1 < L)
-                    umma::bulk_prefetch_l2(gyn + ((size_t)c * H + rowY(e - 1)) * W, (uint32_t)(W * 4));
+                    umma::bulk_prefetch_l2(gyn + ((size_t)c * H + rowY(e - 1)) * W + c0, bytes);
             };
-            // producer warp: update mask of sequence row j -> MK[j % 2], then mkfull[j % 2]
+            // producer warp: update mask of sequence row j (the strip's columns) -> MK[j % 2], then mkfull[j % 2]
             auto draw_mask = [&](int j) {
                 ok = __shfl_sync(~0u, ok, 0);
                 if (ok) {
-                    row_mask_warp(MK + (j & 1) * 128, step_seed_of(a), a.rate, n + a.n_offset, H, W, rowY(j), lane32);
+                    if (STRIP)
+                        row_mask_strip_warp(MK + (j & 1) * 128, step_seed_of(a), a.rate, n + a.n_offset, H, W, rowY(j),
+                                            lane32, c0);
+                    else
+                        row_mask_warp(MK + (j & 1) * 128, step_seed_of(a), a.rate, n + a.n_offset, H, W, rowY(j), lane32);
                     __syncwarp();
                     if (lane32 == 0)
                         mbar_arrive(&mkfull[j & 1]);
@@ -1067,7 +1134,7 @@ __global__ void __launch_bounds__(128 * NPART + 96, 1) bwd_rows_kernel(StepArgs 
                 float gyA[F::CPP];  // gy of the next front end's row
                 float win[F::CPP][6];  // rows Y - 1, Y (x[l], x[c], x[r]) of the last front end's channels
                 auto load_gy = [&](int j) {
-                    const float *src = gyn + (size_t)rowY(j) * W + xc;
+                    const float *src = gyn + (size_t)rowY(j) * W + gcol;
 #pragma unroll
                     for (int cc = 0; cc < F::CPP; ++cc)
                         gyA[cc] = __ldg(src + (size_t)(F::CPP * part + cc) * plane);
@@ -1077,21 +1144,21 @@ __global__ void __launch_bounds__(128 * NPART + 96, 1) bwd_rows_kernel(StepArgs 
                     ring_wait_x(xwaited, j + 2);  // x rows Y_j - 1 .. Y_j + 1
                     ok &= wait_bar(&mkfull[j & 1], (mkpar >> (j & 1)) & 1u, abort);  // the mask of row j
                     mkpar ^= 1u << (j & 1);
-                    const float *rm = XR + (size_t)(j % F::XRING) * C * W, *r0 = XR + (size_t)((j + 1) % F::XRING) * C * W,
-                                *rp = XR + (size_t)((j + 2) % F::XRING) * C * W;
+                    const float *rm = XR + (size_t)(j % F::XRING) * C * RS, *r0 = XR + (size_t)((j + 1) % F::XRING) * C * RS,
+                                *rp = XR + (size_t)((j + 2) % F::XRING) * C * RS;
                     const bool m = MK[(j & 1) * 128 + xc] != 0;
                     float *psw = PSW + bj * D::PSW;
                     const uint32_t tp = lane + (bj ? F::T_P1 : F::T_P0);
 #pragma unroll
                     for (int cc = 0; cc < F::CPP; ++cc) {  // warp-uniform channel: tcgen05.st takes one column per warp
                         const int c = F::CPP * part + cc;
-                        const float *bm = rm + c * W, *b0 = r0 + c * W, *bp = rp + c * W;
+                        const float *bm = rm + c * RS, *b0 = r0 + c * RS, *bp = rp + c * RS;
                         if (j == 0) {
-                            win[cc][0] = bm[xl]; win[cc][1] = bm[xc]; win[cc][2] = bm[xr];
-                            win[cc][3] = b0[xl]; win[cc][4] = b0[xc]; win[cc][5] = b0[xr];
+                            win[cc][0] = bm[il]; win[cc][1] = bm[ic]; win[cc][2] = bm[ir];
+                            win[cc][3] = b0[il]; win[cc][4] = b0[ic]; win[cc][5] = b0[ir];
                         }
                         const float v[3][3] = {{win[cc][0], win[cc][1], win[cc][2]}, {win[cc][3], win[cc][4], win[cc][5]},
-                                               {bp[xl], bp[xc], bp[xr]}};
+                                               {bp[il], bp[ic], bp[ir]}};
                         win[cc][0] = v[1][0]; win[cc][1] = v[1][1]; win[cc][2] = v[1][2];
                         win[cc][3] = v[2][0]; win[cc][4] = v[2][1]; win[cc][5] = v[2][2];
                         const float4 p = perceive3x3(v);
@@ -1122,7 +1189,7 @@ __global__ void __launch_bounds__(128 * NPART + 96, 1) bwd_rows_kernel(StepArgs 
                     // gy of row Y - 1, for the final gx of that row at the end of this row's adjoint: requested now (an
                     // L2 hit: its front end read it two rows ago) so that the loads complete under EA and FE
                     const bool fin = i >= 2 && vx;
-                    const size_t prow = (size_t)wrap_index(Y - 1, H) * W + xc;
+                    const size_t prow = (size_t)wrap_index(Y - 1, H) * W + gcol;
                     float gprev[F::CPP];
 #pragma unroll
                     for (int cc = 0; cc < F::CPP; ++cc)
@@ -1172,15 +1239,25 @@ __global__ void __launch_bounds__(128 * NPART + 96, 1) bwd_rows_kernel(StepArgs 
                         umma::tmem_ld4(lane + (b ? F::T_P1 : F::T_P0) + 4 * (F::CPP * part + cc), dpv[cc]);
                     umma::tmem_wait_ld();
                     const int my_slot = lane32 == 0 ? wq : lane32 == 31 ? 4 + wq : -1;
-                    const int lsrc = x == 0 ? 8 : lane32 == 0 ? 4 + wq - 1 : -1, rsrc = x == W - 1 ? 0 : lane32 == 31 ? wq + 1 : -1;
+                    // neighbour source: an edge slot, -1 a shuffle, -2 (STRIP: the strip's first and last columns)
+                    // none: the other strip's term is added by the edge fix-up
+                    const int lsrc = x == 0 ? (STRIP ? -2 : 8) : lane32 == 0 ? 4 + wq - 1 : -1;
+                    const int rsrc = STRIP ? (x == 127 ? -2 : lane32 == 31 ? wq + 1 : -1)
+                                           : (x == W - 1 ? 0 : lane32 == 31 ? wq + 1 : -1);
+                    // STRIP: the edge columns of an owned row -> edge scratch [n][Y][strip][first / last][c]
+                    float4 *eg = STRIP && owned && (x == 0 || x == 127)
+                                     ? reinterpret_cast<float4 *>(a.dp) + ((((size_t)n * H + Y) * S + s) * 2 + (x == 127)) * C
+                                     : nullptr;
 #pragma unroll
                     for (int cc = 0; cc < F::CPP; ++cc) {  // edge lanes publish (sobel_x, sobel_y, laplacian) parts
                         const int c = F::CPP * part + cc;
                         const float4 t = make_float4(dpv[cc][1], dpv[cc][2], dpv[cc][3], 0.f);
                         if (my_slot >= 0)
                             EDGE[my_slot * C + c] = t;
-                        if (x == W - 1)
+                        if (!STRIP && x == W - 1)
                             EDGE[8 * C + c] = t;
+                        if (STRIP && eg != nullptr)
+                            eg[c] = t;
                     }
                     bar_sync(2 + part, 128);
 #pragma unroll
@@ -1202,6 +1279,16 @@ __global__ void __launch_bounds__(128 * NPART + 96, 1) bwd_rows_kernel(StepArgs 
                             rx = e.x;
                             ry = e.y;
                             rz = e.z;
+                        }
+                        if (STRIP && lsrc == -2) {
+                            lx = 0.f;
+                            ly = 0.f;
+                            lz = 0.f;
+                        }
+                        if (STRIP && rsrc == -2) {
+                            rx = 0.f;
+                            ry = 0.f;
+                            rz = 0.f;
                         }
                         const float rsx = lx - rx;                      // horizontal transpose of sobel_x
                         const float rsy = ry + 2.f * dpv[cc][2] + ly;   // ... of sobel_y (smoothing)
@@ -1240,6 +1327,37 @@ __global__ void __launch_bounds__(128 * NPART + 96, 1) bwd_rows_kernel(StepArgs 
     if (*abort || !ok)
         if (tid == 0)
             set_device_error(1);
+}
+
+// Cross-strip terms of the adjoint after bwd_rows_kernel<..., STRIP> (W = 128 S): the first column of strip s
+// (x = 128 s) receives the terms of its left neighbour x - 1 (the last column of strip s - 1, circular) and the last
+// column (x = 128 s + 127) those of its right neighbour x + 1 (the first column of strip s + 1), from the edge
+// scratch edge[n][Y][strip][first / last][c] = (sobel_x, sobel_y, laplacian) parts of dp. With L = such a part vector
+// of the left neighbour in row Y', gx(Y) += (Lx - Ly + Lz)(Y + 1) + 2 (Lx + Lz)(Y) + (Lx + Ly + Lz)(Y - 1) (rows
+// circular); a right neighbour R enters as (-Rx - Ry + Rz)(Y + 1) + 2 (Rz - Rx)(Y) + (-Rx + Ry + Rz)(Y - 1): the
+// horizontal transposes of sobel_x, sobel_y and the laplacian times their vertical weights, as in the row kernel's
+// adjoint. One thread per (image, row, strip, side, channel).
+template <int C>
+__global__ void strip_edge_fixup_kernel(const float4 *__restrict__ edge, float *gx, int N, int H, int W)
+{
+    const int S = W / 128;
+    const int64_t total = (int64_t)N * H * S * 2 * C;
+    for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < total; t += (int64_t)gridDim.x * blockDim.x) {
+        const int c = (int)(t % C);
+        int64_t r = t / C;
+        const int side = (int)(r % 2);
+        r /= 2;
+        const int s = (int)(r % S);
+        r /= S;
+        const int Y = (int)(r % H);
+        const int64_t n = r / H;
+        const int sn = side == 0 ? (s == 0 ? S - 1 : s - 1) : (s + 1 == S ? 0 : s + 1);  // the neighbour's strip
+        auto at = [&](int yy) { return __ldg(edge + (((n * H + yy) * S + sn) * 2 + (1 - side)) * C + c); };
+        const float4 up = at(Y == 0 ? H - 1 : Y - 1), mid = at(Y), dn = at(Y + 1 == H ? 0 : Y + 1);
+        const float v = side == 0 ? (dn.x - dn.y + dn.z) + 2.f * (mid.x + mid.z) + (up.x + up.y + up.z)
+                                  : (-dn.x - dn.y + dn.z) + 2.f * (mid.z - mid.x) + (-up.x + up.y + up.z);
+        gx[((n * C + c) * H + Y) * W + 128 * s + (side ? 127 : 0)] += v;
+    }
 }
 
 }  // namespace unca
