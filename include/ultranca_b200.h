@@ -194,7 +194,7 @@ int nca_pool_store(float *pool, const float *x, const int64_t *idx, int64_t K, i
                    int64_t H, int64_t W, void *stream);
 
 /* Launch configuration the step kernels use for this shape on the current device, into info[0..11]: row-streaming
- * path (1), backward row kernel over column strips with the forward on the tile path (2) or tile path (0), forward
+ * path (1), row kernels over column strips of 128 (2: W a multiple of 128 from 256 on) or tile path (0), forward
  * grid, forward threads per CTA, backward grid, backward threads per CTA, SM count,
  * tile-path forward CTAs per SM, tile-path backward grid, and the occupancy query, registers, dynamic shared memory
  * limit and carveout of the row-streaming forward kernel. Diagnostic; no reference counterpart. */

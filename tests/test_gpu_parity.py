@@ -376,3 +376,37 @@ def test_strip_backward_parity(ops, K, B, H, W, rate):
     again, _ = grads_gpu(ops, x, w1, b1, w2, R, rate, False, False, 31)
     assert all(torch.equal(a, b) for a, b in zip(got, again))
     assert device_error_clear()
+
+
+@pytest.mark.parametrize('K,B,H,W,rate', [(2, 1, 6, 256, 0.5), (1, 2, 5, 384, 0.3), (2, 1, 1, 256, 1.0),
+                                          (1, 1, 3, 512, 0.02), (40, 2, 4, 256, 0.5), (1, 2, 130, 256, 0.9)])
+def test_strip_forward_parity(ops, K, B, H, W, rate):
+    """Rows wider than 128 run the row forward over column strips of 128 (masks, prefix counts and tiles per strip;
+    4 halo columns on each side of a strip, wrapped at the row's ends): updating pixels match the TF32 oracle, the
+    others are copied exactly; two to four strips, one-row images, rates 0.02 to 1, many images and NCAs per band."""
+    C, HID = 12, 96
+    assert ops.launch_info(C, HID, False, K * B, H, W, K)['rows_path'] == 2
+    x, w1, b1, w2 = O.make(K, B, C, HID, H, W, seed=3 * H + W + K)
+    mask = O.mask_for(K, B, H, W, 41, rate)
+    out = ops.step(*gpu(x, w1, b1, w2), rate, seed=41).cpu()
+    ref = O.reference_step(x, w1, b1, w2, mask, False, tf32=True)
+    keep = (mask == 0).expand_as(x)
+    assert torch.equal(out[keep], x[keep])
+    assert O.rel(out, ref) < 1e-3
+    edges = [c for s in range(W // 128) for c in (128 * s, 128 * s + 127)]
+    assert O.rel(out[..., edges], ref[..., edges]) < 1e-3
+    assert device_error_clear()
+
+
+def test_strip_rollout_equals_repeated_steps(ops):
+    """rollout() over column strips equals repeated step() calls bitwise, x unmodified (test_nca.py:128-149)."""
+    x, w1, b1, w2 = gpu(*O.make(2, 2, 12, 96, 9, 256, seed=8))
+    original = x.clone()
+    for rate in (0.5, 1.0):
+        ref = x
+        for steps in range(5):
+            if steps:
+                ref = ops.step(ref, w1, b1, w2, rate, seed=O.step_seed(123, steps - 1))
+            assert torch.equal(ops.rollout(x, w1, b1, w2, rate, steps, seed=123), ref)
+    assert torch.equal(x, original)
+    assert device_error_clear()

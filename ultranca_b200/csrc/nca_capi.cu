@@ -234,8 +234,8 @@ bool rows_path(const Shape &s, bool fp32, bool growing)
 {
     return !fp32 && !growing && s.C == 12 && s.HID == 96 && s.W <= 128 && s.W % 4 == 0;
 }
-// Wider rows (W a multiple of 128 from 256 on): the backward row kernel over column strips of 128 plus the edge
-// fix-up; the forward keeps the tile kernel.
+// Wider rows (W a multiple of 128 from 256 on): both row kernels over column strips of 128 (the backward plus the
+// edge fix-up).
 bool strip_path(const Shape &s, bool fp32, bool growing)
 {
     return !fp32 && !growing && s.C == 12 && s.HID == 96 && s.W >= 256 && s.W % 128 == 0;
@@ -278,12 +278,16 @@ Bands bwd_bands(const Shape &s, int G) { return Bands{s.N * s.H, s.H, s.B * s.H,
 int fwd_rows_grid(const Shape &s)
 {
     using FR = FwdRows<12, 96, FWD_ROWS_PARTS>;
-    const int per = ctas_per_sm(fwd_rows_kernel<12, 96, FWD_ROWS_PARTS>, FR::smem(), FR::TMEM, FR::THREADS);
-    const int64_t rows = s.N * s.H;  // each CTA draws the update masks of its rows into shared memory: at most MAXROWS
-    int64_t G = std::max<int64_t>(grid_for(rows, per), std::min<int64_t>((rows + FR::MAXROWS - 1) / FR::MAXROWS, rows));
-    // a band holds at most cost(T) / (4 G) + (4 + s4 + n4) / 4 + 1 rows: grow the grid until that fits MAXROWS
+    using FS = FwdRows<12, 96, FWD_ROWS_PARTS, true>;
+    const bool strip = s.W > 128;
+    const int per = strip ? ctas_per_sm(fwd_rows_kernel<12, 96, FWD_ROWS_PARTS, true>, FS::smem(), FS::TMEM, FS::THREADS)
+                          : ctas_per_sm(fwd_rows_kernel<12, 96, FWD_ROWS_PARTS>, FR::smem(), FR::TMEM, FR::THREADS);
+    // each CTA draws the update masks of its rows (times the column strips) into shared memory: at most MAXROWS
+    const int64_t rows = s.N * s.H, maxrows = strip ? FS::MAXROWS / (s.W / 128) : FR::MAXROWS;
+    int64_t G = std::max<int64_t>(grid_for(rows, per), std::min<int64_t>((rows + maxrows - 1) / maxrows, rows));
+    // a band holds at most cost(T) / (4 G) + (4 + s4 + n4) / 4 + 1 rows: grow the grid until that fits
     while (G < rows && band_cost(fwd_bands(s, (int)G), rows) / (4 * G) + (4 + FWD_BAND_S4 + FWD_BAND_N4) / 4 + 1 >
-                           FR::MAXROWS)
+                           maxrows)
         ++G;
     return (int)G;
 }
@@ -309,6 +313,15 @@ void launch_forward(const float *x, const float *w1, const float *b1, const floa
         a.band_s4 = FWD_BAND_S4;
         a.band_n4 = FWD_BAND_N4;
         launch_pdl(fwd_rows_kernel<12, 96, FWD_ROWS_PARTS>, fwd_rows_grid(s), FR::THREADS, FR::smem(), stream, a);
+        CUDA_OK(cudaGetLastError());
+        return;
+    }
+    if (strip_path(s, fp32, growing) && aligned16(x) && aligned16(y)) {  // column strips of 128
+        using FS = FwdRows<12, 96, FWD_ROWS_PARTS, true>;
+        a.band_s4 = FWD_BAND_S4;
+        a.band_n4 = FWD_BAND_N4;
+        const int grid = fwd_rows_grid(s);  // sets the kernel's shared-memory limit (occupancy query) first
+        launch_pdl(fwd_rows_kernel<12, 96, FWD_ROWS_PARTS, true>, grid, FS::THREADS, FS::smem(), stream, a);
         CUDA_OK(cudaGetLastError());
         return;
     }
@@ -649,8 +662,8 @@ int nca_launch_info(int64_t C, int64_t hidden, int fp32, int growing, int64_t N,
             fwd_grid = grid_for(N * g.tiles_per_image, fwd_per);
         });
         info[0] = rows ? 1 : brows ? 2 : 0;
-        info[1] = rows ? fwd_rows_grid(s) : fwd_grid;
-        info[2] = rows ? FwdRows<12, 96, FWD_ROWS_PARTS>::THREADS : 128;
+        info[1] = brows ? fwd_rows_grid(s) : fwd_grid;
+        info[2] = brows ? FwdRows<12, 96, FWD_ROWS_PARTS>::THREADS : 128;
         info[3] = brows ? bwd_rows_grid(s) : w.grid;
         info[4] = brows ? BwdRows<12, 96, BWD_ROWS_PARTS>::THREADS : 128;
         info[5] = device_info().sms;

@@ -276,6 +276,28 @@ __device__ __forceinline__ void row_mask_xorder_warp(uint32_t *dst, uint64_t see
         dst[lane >> 3] = v;
 }
 
+// The same for the 128 pixels x0 .. x0 + 127 of a wider row (x0 % 128 == 0, x0 + 128 <= W): bit x - x0.
+__device__ __forceinline__ void row_mask_xorder_strip_warp(uint32_t *dst, uint64_t seed, float rate, int64_t n, int H,
+                                                           int W, int Y, int lane, int x0)
+{
+    uint32_t nib = 0xFu;
+    if (rate < 1.f) {
+        const uint64_t counter = ((uint64_t)n * (uint64_t)H + (uint64_t)Y) * (uint64_t)(W / 4) + (uint64_t)(x0 / 4 + lane);
+        const uint4 w = philox4x32_10(seed, counter);
+        const uint32_t words[4] = {w.x, w.y, w.z, w.w};
+        nib = 0;
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+            nib |= (floorf(__fadd_rn(__fmul_rn((float)(words[e] >> 8), 1.0f / 16777216.0f), rate)) != 0.f ? 1u : 0u) << e;
+    }
+    uint32_t v = nib << (4 * (lane & 7));
+    v |= __shfl_xor_sync(~0u, v, 1);
+    v |= __shfl_xor_sync(~0u, v, 2);
+    v |= __shfl_xor_sync(~0u, v, 4);
+    if ((lane & 7) == 0)
+        dst[lane >> 3] = v;
+}
+
 // Position of the n-th (0-based) set bit of w (n < popc(w)).
 __device__ __forceinline__ int nth_set_bit(uint32_t w, int n)
 {
@@ -321,11 +343,15 @@ __device__ __forceinline__ int nth_pixel(const uint32_t *m, int n)
 //   OUT(t)  [MMA2(t)]        y = x + u at the lane's pixel
 // MMA1, MMA2 and the front-end signals use one mbarrier per buffer parity, so that no waiter can see a phase of the
 // tile two ahead in place of its own. A tile's rows and the front end's lag keep at most SPAN + 2 ring entries live.
-template <int C, int HID, int NPART>
+// STRIP: rows wider than one tile (W = 128 S, S >= 2) run as S column strips of 128 per segment ("passes": the
+// rows of a segment at the strip's columns; masks, prefix counts and tiles per pass), with ring rows of XS = 136
+// floats (4 halo columns on each side of the strip). MAXROWS then counts rows times strips.
+template <int C, int HID, int NPART, bool STRIP = false>
 struct FwdRows {
     using D = Dims<C, HID>;
     static constexpr int CW = 128 * NPART, W_M1 = CW / 32, W_M2 = W_M1 + 1, W_PROD = W_M1 + 2;
-    static constexpr int THREADS = CW + 96, CPP = C / NPART, HPP = HID / NPART, XRING = 8, MAXROWS = 1024, SPAN = 4;
+    static constexpr int THREADS = CW + 96, CPP = C / NPART, HPP = HID / NPART, XRING = 8, SPAN = 4;
+    static constexpr int MAXROWS = STRIP ? 4096 : 1024, XS = STRIP ? 136 : 128;
     // TMEM: H[2] (h, then tf32(relu(h)) in place), U[2], P[2] (p'; 1, 1 at PIN, PIN+1; zeros to KP)
     static constexpr int T_H0 = 0, T_H1 = HID, T_U0 = 2 * HID, T_U1 = 2 * HID + 32, T_P0 = 256, T_P1 = 320;
     static constexpr int TMEM = 512;
@@ -335,7 +361,7 @@ struct FwdRows {
     // tiles (int2 per tile: queue start; count | first row << 8 | last row << 20) | tiles per segment (cumulative) |
     // mbarriers
     static constexpr size_t OFF_XR = (size_t)(D::W1S + D::W2S) * 4;
-    static constexpr size_t OFF_MK = OFF_XR + (size_t)XRING * C * 128 * 4;
+    static constexpr size_t OFF_MK = OFF_XR + (size_t)XRING * C * XS * 4;
     static constexpr size_t OFF_CUM = OFF_MK + (size_t)MAXROWS * 16;
     static constexpr size_t OFF_TILE = OFF_CUM + (size_t)MAXROWS * 4;
     static constexpr size_t OFF_SEGT = OFF_TILE + (size_t)MAXROWS * 8;
@@ -343,12 +369,13 @@ struct FwdRows {
     static constexpr int NBAR = 2 * XRING + 7;  // x ring full / empty, MMA1, MMA2, fe_done per buffer, epi_done
     static constexpr size_t smem() { return OFF_BAR + 8 * NBAR + 16; }
     static_assert(OFF_BAR % 8 == 0 && OFF_TILE % 8 == 0, "alignment");
+    static_assert(smem() <= 232448, "227 KB of shared memory per CTA");
 };
 
-template <int C, int HID, int NPART>
+template <int C, int HID, int NPART, bool STRIP = false>
 __global__ void __launch_bounds__(128 * NPART + 96, 1) fwd_rows_kernel(StepArgs a)
 {
-    using F = FwdRows<C, HID, NPART>;
+    using F = FwdRows<C, HID, NPART, STRIP>;
     using D = typename F::D;
     // the next step's kernel may launch now (it waits for this one before reading the state it writes)
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
@@ -367,6 +394,8 @@ __global__ void __launch_bounds__(128 * NPART + 96, 1) fwd_rows_kernel(StepArgs 
     const bool compute = warp < F::W_M1, m1 = warp == F::W_M1, m2 = warp == F::W_M2, prod = warp == F::W_PROD;
     const int part = compute ? tid / 128 : 0, x = tid % 128;
     const int H = a.H, W = a.W;
+    const int S = STRIP ? W / 128 : 1;  // column strips per row
+    const int RS = STRIP ? F::XS : W;   // ring row stride
     const size_t plane = (size_t)H * W;
     __shared__ int64_t band[2];  // this CTA's rows [g0, g1), found by thread 0
 
@@ -385,7 +414,7 @@ __global__ void __launch_bounds__(128 * NPART + 96, 1) fwd_rows_kernel(StepArgs 
     }
     __syncthreads();
     const int64_t g0 = band[0], g1 = band[1];
-    if (g1 - g0 > F::MAXROWS) {  // the host sizes the grid so that this never happens: refuse rather than overflow
+    if ((g1 - g0) * S > F::MAXROWS) {  // the host sizes the grid so that this never happens: refuse rather than overflow
         if (tid == 0)
             set_device_error(2);
         return;
@@ -396,14 +425,25 @@ __global__ void __launch_bounds__(128 * NPART + 96, 1) fwd_rows_kernel(StepArgs 
     }
     // update masks of the CTA's rows (g1 - g0 <= MAXROWS: the host sizes the grid so)
     const uint64_t seed = step_seed_of(a);
-    for (int64_t u = g0 + warp; u < g1; u += blockDim.x / 32)
-        row_mask_xorder_warp(MKX + (u - g0) * 4, seed, a.rate, u / H + a.n_offset, H, W, (int)(u % H), lane32);
+    if (!STRIP) {
+        for (int64_t u = g0 + warp; u < g1; u += blockDim.x / 32)
+            row_mask_xorder_warp(MKX + (u - g0) * 4, seed, a.rate, u / H + a.n_offset, H, W, (int)(u % H), lane32);
+    } else {
+        // pass-major: row u of the segment [lo, hi) (CTA-relative) at strip s is mask row S lo + s (hi - lo) + u - lo
+        for (int64_t u = g0 + warp; u < g1; u += blockDim.x / 32) {
+            const int64_t img = u / H, lo = max(g0, img * H) - g0, hi = min(g1, (img + 1) * H) - g0;
+            for (int s = 0; s < S; ++s)
+                row_mask_xorder_strip_warp(MKX + (S * lo + s * (hi - lo) + (u - g0 - lo)) * 4, seed, a.rate,
+                                           img + a.n_offset, H, W, (int)(u % H), lane32, 128 * s);
+        }
+    }
     __syncthreads();
-    if (warp == 0) {  // tile table: per segment, the prefix counts of its rows, then tiles of <= 128 pixels, <= SPAN rows
-        int64_t g = g0;
+    if (warp == 0) {  // tile table: per segment (pass), the prefix counts of its rows, then tiles of <= 128 pixels,
+        int64_t g = g0;  // <= SPAN rows
         RowSeg sg;
         int s = 0, nt = 0, u0 = 0;
-        while (next_segment(g, g1, H, sg)) {
+        while (next_segment(g, g1, H, sg))
+          for (int strip = 0; strip < S; ++strip) {
             const int L = sg.r1 - sg.r0;
             int run = 0;
             for (int b = 0; b < L; b += 32) {
@@ -470,6 +510,7 @@ __global__ void __launch_bounds__(128 * NPART + 96, 1) fwd_rows_kernel(StepArgs 
     const uint64_t dW1 = umma::smem_desc(umma::smem_u32(W1s), HID * 16, 128);
     const uint64_t dW2 = umma::smem_desc(umma::smem_u32(W2s), D::CP * 16, 128);
     constexpr uint32_t I1 = umma::idesc_tf32(128, HID, false, false), I2 = umma::idesc_tf32(128, 16, false, false);
+    constexpr int JM = STRIP ? 0xFFF : 0x3FF;  // row fields of a tile entry
     bool ok = true;
     uint32_t epar = 0, g1par = 0, g2par = 0, eph = 0, fepar = 0;  // *par: one parity bit per buffer / ring slot
     int cur_k = -1, x_uses[F::XRING] = {0, 0, 0, 0, 0, 0, 0, 0};
@@ -491,8 +532,9 @@ __global__ void __launch_bounds__(128 * NPART + 96, 1) fwd_rows_kernel(StepArgs 
     RowSeg sg;
     int seg = 0, u0 = 0, ebase = 0;  // segment ordinal, its first row (CTA-relative), ring entries of earlier segments
     bool dep_waited = false;
-    while (next_segment(g, g1, H, sg)) {
-        const int n = sg.n, k = n / a.B, L = sg.r1 - sg.r0;
+    while (next_segment(g, g1, H, sg))
+      for (int s = 0; s < S; ++s) {  // the column strips of the segment, one pass each (one pass unless STRIP)
+        const int n = sg.n, k = n / a.B, L = sg.r1 - sg.r0, c0 = 128 * s;
         const int tb = seg == 0 ? 0 : SEGT[seg - 1], T = SEGT[seg] - tb;
         const float *xn = a.x + (size_t)n * C * plane;
         float *yn = a.y + (size_t)n * C * plane;
@@ -522,11 +564,27 @@ __global__ void __launch_bounds__(128 * NPART + 96, 1) fwd_rows_kernel(StepArgs 
                 if (ok) {
                     const int Y = wrap_near(sg.r0 - 1 + e, H);
                     if (lane32 == 0)
-                        umma::mbar_arrive_expect_tx(&xfull[slot], (uint32_t)(C * W * 4));
+                        umma::mbar_arrive_expect_tx(&xfull[slot], (uint32_t)(C * RS * 4));
                     __syncwarp();
-                    if (lane32 < C)
-                        umma::bulk_g2s(XR + ((size_t)slot * C + lane32) * W, xn + ((size_t)lane32 * H + Y) * W,
-                                       (uint32_t)(W * 4), &xfull[slot]);
+                    if (!STRIP) {
+                        if (lane32 < C)
+                            umma::bulk_g2s(XR + ((size_t)slot * C + lane32) * W, xn + ((size_t)lane32 * H + Y) * W,
+                                           (uint32_t)(W * 4), &xfull[slot]);
+                    } else if (lane32 < C) {
+                        // columns c0 - 4 .. c0 + 131 (circular) -> ring columns 0 .. 135, one piece or two where the
+                        // range wraps (16-byte aligned: W and c0 are multiples of 128)
+                        float *dst = XR + ((size_t)slot * C + lane32) * RS;
+                        const float *src = xn + ((size_t)lane32 * H + Y) * W;
+                        if (s == 0) {
+                            umma::bulk_g2s(dst, src + W - 4, 16u, &xfull[slot]);
+                            umma::bulk_g2s(dst + 4, src, 132u * 4u, &xfull[slot]);
+                        } else if (s == S - 1) {
+                            umma::bulk_g2s(dst, src + c0 - 4, 132u * 4u, &xfull[slot]);
+                            umma::bulk_g2s(dst + 132, src, 16u, &xfull[slot]);
+                        } else {
+                            umma::bulk_g2s(dst, src + c0 - 4, 136u * 4u, &xfull[slot]);
+                        }
+                    }
                 }
             }
         } else if (m1) {
@@ -593,14 +651,14 @@ __global__ void __launch_bounds__(128 * NPART + 96, 1) fwd_rows_kernel(StepArgs 
                 for (; released < target; ++released) {
                     const int e = released, j = e - 1;
                     wait_entries(e);
-                    if (j >= 0 && j < L && x < W && ok) {
-                        const float *src = XR + (size_t)slot_of(e) * C * W + x;
-                        float *dst = yn + (size_t)(sg.r0 + j) * W + x;
+                    if (j >= 0 && j < L && (STRIP || x < W) && ok) {
+                        const float *src = XR + (size_t)slot_of(e) * C * RS + (STRIP ? x + 4 : x);
+                        float *dst = yn + (size_t)(sg.r0 + j) * W + c0 + x;
                         if (!((mseg[j * 4 + (x >> 5)] >> (x & 31)) & 1u)) {
 #pragma unroll
                             for (int cc = 0; cc < F::CPP; ++cc) {
                                 const int c = F::CPP * part + cc;
-                                dst[(size_t)c * plane] = src[(size_t)c * W];
+                                dst[(size_t)c * plane] = src[(size_t)c * RS];
                             }
                         }
                     }
@@ -609,7 +667,7 @@ __global__ void __launch_bounds__(128 * NPART + 96, 1) fwd_rows_kernel(StepArgs 
             };
             auto front_end = [&](int t, int bj) {  // p' of tile t's pixels -> P[bj]; centre x and pixel kept
                 const int2 tl = TILE[tb + t];
-                const int nq = tl.y & 0xFF, jlo = (tl.y >> 8) & 0x3FF, jhi = (tl.y >> 20) & 0x3FF;
+                const int nq = tl.y & 0xFF, jlo = (tl.y >> 8) & JM, jhi = (tl.y >> 20) & JM;
                 wait_entries(jhi + 2);  // rows Y - 1 .. Y + 1 of the tile's rows
                 const bool valid = x < nq;
                 const int q = tl.x + (valid ? x : 0);
@@ -617,15 +675,17 @@ __global__ void __launch_bounds__(128 * NPART + 96, 1) fwd_rows_kernel(StepArgs 
                 while (j < jhi && CUM[u0 + j + 1] <= q)
                     ++j;
                 const int px = nth_pixel(mseg + j * 4, q - CUM[u0 + j]);
-                const int pl = px == 0 ? W - 1 : px - 1, pr = px + 1 >= W ? 0 : px + 1;
-                const float *rm = XR + (size_t)slot_of(j) * C * W, *r0 = XR + (size_t)slot_of(j + 1) * C * W,
-                            *rp = XR + (size_t)slot_of(j + 2) * C * W;
+                // the pixel's left, centre and right columns in a ring row (STRIP: 4 halo columns precede the strip)
+                const int pl = STRIP ? px + 3 : px == 0 ? W - 1 : px - 1, pc = STRIP ? px + 4 : px,
+                          pr = STRIP ? px + 5 : px + 1 >= W ? 0 : px + 1;
+                const float *rm = XR + (size_t)slot_of(j) * C * RS, *r0 = XR + (size_t)slot_of(j + 1) * C * RS,
+                            *rp = XR + (size_t)slot_of(j + 2) * C * RS;
                 const uint32_t tp = lane + (bj ? F::T_P1 : F::T_P0);
 #pragma unroll
                 for (int cc = 0; cc < F::CPP; ++cc) {  // warp-uniform channel: tcgen05.st takes one column per warp
                     const int c = F::CPP * part + cc;
-                    const float *bm = rm + c * W, *b0 = r0 + c * W, *bp = rp + c * W;
-                    const float v[3][3] = {{bm[pl], bm[px], bm[pr]}, {b0[pl], b0[px], b0[pr]}, {bp[pl], bp[px], bp[pr]}};
+                    const float *bm = rm + c * RS, *b0 = r0 + c * RS, *bp = rp + c * RS;
+                    const float v[3][3] = {{bm[pl], bm[pc], bm[pr]}, {b0[pl], b0[pc], b0[pr]}, {bp[pl], bp[pc], bp[pr]}};
                     const float4 p = perceive3x3(v);
                     const float pv[4] = {tf32_rna(p.x), tf32_rna(p.y), tf32_rna(p.z), tf32_rna(p.w)};
                     umma::tmem_st4(tp + 4 * c, pv);
@@ -634,7 +694,7 @@ __global__ void __launch_bounds__(128 * NPART + 96, 1) fwd_rows_kernel(StepArgs 
                 pnext = valid ? (((sg.r0 + j) << 8) | px) : -1;
                 umma::tmem_wait_st();
                 signal(&fe_done[bj]);
-                retire(t + 1 < T ? ((TILE[tb + t + 1].y >> 8) & 0x3FF) : L + 2);
+                retire(t + 1 < T ? ((TILE[tb + t + 1].y >> 8) & JM) : L + 2);
             };
             if (T > 0) {
                 front_end(0, 0);
@@ -685,7 +745,7 @@ __global__ void __launch_bounds__(128 * NPART + 96, 1) fwd_rows_kernel(StepArgs 
                     u[cc] = umma::tmem_ld1(tu + cc);
                 umma::tmem_wait_ld();  // the loaded registers are defined only after this wait
                 if (pcur >= 0 && ok) {
-                    float *yr = yn + (size_t)(pcur >> 8) * W + (pcur & 0xFF);
+                    float *yr = yn + (size_t)(pcur >> 8) * W + c0 + (pcur & 0xFF);
 #pragma unroll
                     for (int cc = 0; cc < F::CPP; ++cc)
                         yr[(size_t)(F::CPP * part + cc) * plane] = xcur[cc] + u[cc];
