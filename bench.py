@@ -21,6 +21,9 @@ e2e:   the same metric through the public operator API (ultranca_b200.nca_ops.st
        iteration inside the timed region.
 --impl reference: the reference's eager PyTorch step (the CPU restatement in oracle/, fp32, all host threads) on a
        bounded sample of the same workload; it prints its own JSON line and no GPU is used.
+--config 4: a supplemental line (not the default): BASELINE configuration 4 per GPU, i.e. its 8-GPU shard of 64
+       texture NCAs, B = 4, 256 x 256 (the row kernels over column strips), 96-step rollout, pool of 16 states per
+       NCA; 64 NCAs per GPU at any N (weak scaling: K = 512 at N = 8).
 """
 import argparse
 import json
@@ -48,6 +51,7 @@ def parse():
     ap.add_argument('--steps', type=int, default=10)
     ap.add_argument('--warmup', type=int, default=3)
     ap.add_argument('--impl', default='ours', choices=['ours', 'reference'])
+    ap.add_argument('--config', type=int, default=1, choices=[1, 4])
     ap.add_argument('--no-e2e', action='store_true')
     ap.add_argument('--no-cpu', action='store_true')
     ap.add_argument('--no-ref-kernels', action='store_true')
@@ -181,12 +185,27 @@ def measure_tf32_tflops(dev, n=8192, reps=10):
         torch.backends.cuda.matmul.allow_tf32 = prev
 
 
+def use_config(cfg):
+    """Switch the workload constants to BASELINE configuration `cfg` (1: the default; 4: its 8-GPU shard per GPU)."""
+    global K_PER_GPU, B, H, W, STEPS, POOL, METRIC, CONFIG
+    CONFIG = cfg
+    if cfg == 4:
+        K_PER_GPU, B, H, W, STEPS, POOL = 64, 4, 256, 256, 96, 16
+        METRIC = 'cell-updates/s fwd+bwd, 96-step rollout'
+
+
+CONFIG = 1
+
+
 def config(n, note=None):
+    state_mb = K_PER_GPU * B * C * H * W * 4 / 1e6
     c = {'workload': f'texture NCA training iteration: K={K_PER_GPU * n} NCAs ({K_PER_GPU} per GPU), B={B}, '
                      f'{H}x{W}, {C} ch / {HID} hidden, {STEPS}-step rollout fwd+bwd, p={RATE}, synthetic L2+overflow '
-                     f'loss, grad-norm + Adam (BASELINE config 1)',
+                     f'loss, grad-norm + Adam (BASELINE config {CONFIG}'
+                     f'{"" if CONFIG == 1 else ", the per-GPU shard of K=512 over 8 GPUs"})',
          'K': K_PER_GPU * n, 'B': B, 'H': H, 'W': W, 'steps_per_rollout': STEPS, 'update_rate': RATE,
-         'parallelism': f'K-sharded x{n}', 'l2': 'inputs larger than L2 (64 saved states of 50 MB per iteration)'}
+         'parallelism': f'K-sharded x{n}',
+         'l2': f'inputs larger than L2 ({STEPS} saved states of {state_mb:.0f} MB per iteration)'}
     if note:
         c['note'] = note
     return c
@@ -195,6 +214,7 @@ def config(n, note=None):
 # ------------------------------------------------------------------------------------------------ GPU arm
 def main():
     args = parse()
+    use_config(args.config)
     if args.impl == 'reference':
         run_reference(args)
         return
@@ -294,8 +314,9 @@ def main():
     value = cells_per_iter * args.steps / (ms / 1000.0)
     rows = nca_ops.launch_info(C, HID, False, K * B, H, W, K)['rows_path']
     # per iteration: control 1, pool sample 2, forward 1 / step, loss 2, backward 1 / step (row path; main + adjoint
-    # on the tile path), fused reduce + Adam 1, iteration counter 1, pool write-back 1
-    launches_per_iter = 1 + 2 + STEPS + 2 + STEPS * (1 if rows else 2) + 1 + 1 + 1
+    # on the tile path, main + edge fix-up over column strips), fused reduce + Adam 1, iteration counter 1, pool
+    # write-back 1
+    launches_per_iter = 1 + 2 + STEPS + 2 + STEPS * (1 if rows == 1 else 2) + 1 + 1 + 1
     # roofline of the dominant kernel (the larger mean of the sampled forward and backward launches)
     mean = {k: statistics.mean(v) for k, v in stage_times.items()}
     dom = max(mean, key=mean.get)
@@ -312,10 +333,11 @@ def main():
     peak = peaks.get('hbm_gbs', 6650.0)
     achieved = alg_bytes / (avg_ms / 1000.0) / 1e9
     traffic = None
-    try:
+    try:  # per-launch DRAM bytes of one ncu capture of the config-1 step
         tr = json.load(open(os.path.join(ROOT, 'profiles', 'traffic.json')))
-        traffic = tr.get({'fwd': 'fwd_rows_kernel' if rows else 'fwd_kernel',
-                          'bwd': 'bwd_rows_kernel' if rows else 'bwd_kernel_tc'}[dom])
+        if CONFIG == 1:
+            traffic = tr.get({'fwd': 'fwd_rows_kernel' if rows else 'fwd_kernel',
+                              'bwd': 'bwd_rows_kernel' if rows else 'bwd_kernel_tc'}[dom])
     except (OSError, ValueError):
         pass
     # the step roofline (per cell-step, p = 0.5: 17,280 flop of the MLP forward and backward, 240 B of state traffic):
@@ -327,7 +349,8 @@ def main():
     roofline = {'bound': 'hbm', 'achieved': achieved, 'peak': peak, 'unit': 'GB/s', 'frac': achieved / peak,
                 'traffic': traffic,
                 'kernel': {'fwd': 'fwd_rows_kernel<12,96,2>' if rows else 'fwd_kernel<12,96,TC>',
-                           'bwd': 'bwd_rows_kernel<12,96,4>' if rows else 'bwd_kernel_tc<12,96>'}[dom],
+                           'bwd': 'bwd_rows_kernel<12,96,4>' if rows else 'bwd_kernel_tc<12,96>'}[dom] +
+                          (' (column strips)' if rows == 2 else ''),
                 'algorithmic_bytes_per_launch': alg_bytes, 'avg_launch_ms': avg_ms,
                 'timed_launches': {k: len(v) for k, v in stage_times.items()},
                 'launch_ms': {k: v for k, v in mean.items()},
