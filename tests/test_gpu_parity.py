@@ -410,3 +410,42 @@ def test_strip_rollout_equals_repeated_steps(ops):
             assert torch.equal(ops.rollout(x, w1, b1, w2, rate, steps, seed=123), ref)
     assert torch.equal(x, original)
     assert device_error_clear()
+
+
+@pytest.mark.parametrize('fp32', [False, True])
+def test_growing_sparse_seed(ops, fp32):
+    """Growing NCAs from single live seed cells (the start state of BASELINE config 2: channels 3.. = 1 at one cell,
+    16 channels / 128 hidden, 72 x 72), where most tiles are dead and skipped (forward: no cell within two pixels alive
+    before the step; backward and adjoint: no alive cell). Over 6 steps: the step output is exactly the dense update
+    times the exact alive mask, the dense update matches the oracle; then the gradients of the last step match the
+    oracle, and rollout() equals the repeated steps bitwise."""
+    C, HID, K, B, H, W = 16, 128, 2, 2, 72, 72
+    x = torch.zeros(K, B, C, H, W)
+    x[:, :, 3:, H // 2, W // 2] = 1.0
+    x[:, 1, 3:, 5, 66] = 1.0  # a second seed near the top-right border
+    _, w1, b1, w2 = O.make(K, B, C, HID, 4, 4, seed=21)
+    w1d, b1d, w2d = gpu(w1, b1, w2)
+    cur = x
+    tol = 1e-5 if fp32 else 1e-3
+    for i in range(6):
+        seed = O.step_seed(17, i)
+        xd = cur.to(DEV)
+        out = ops.step(xd, w1d, b1d, w2d, 0.5, True, fp32=fp32, seed=seed).cpu()
+        raw = ops.step(xd, w1d, b1d, w2d, 0.5, False, fp32=fp32, seed=seed).cpu()
+        assert torch.equal(out, raw * (O.alive(cur) & O.alive(raw))), i
+        ref_raw = O.reference_step(cur, w1, b1, w2, O.mask_for(K, B, H, W, seed, 0.5), False, tf32=not fp32)
+        assert O.rel(raw, ref_raw) < tol, i
+        cur = out
+    assert (cur[:, :, 3] > 0.1).any()  # still alive somewhere
+    roll = ops.rollout(x.to(DEV), w1d, b1d, w2d, 0.5, 6, True, fp32, seed=17).cpu()
+    assert torch.equal(roll, cur)
+    # gradients of one step from the grown state
+    R0 = torch.randn(cur.shape, generator=torch.Generator().manual_seed(9))
+    R, _ = unambiguous(cur, w1, b1, R0, tf32=not fp32)
+    got, _ = grads_gpu(ops, cur, w1, b1, w2, R, 0.5, True, fp32, 23)
+    _, alive = ops._forward(*gpu(cur, w1, b1, w2), 0.5, 23, fp32, True)
+    ref = O.step_backward(cur, w1, b1, w2, O.mask_for(K, B, H, W, 23, 0.5), R, True, tf32=not fp32,
+                          alive_mask=alive.cpu().view(K, B, 1, H, W))
+    for a_, b_, name in zip(got, ref, ('gx', 'dw1', 'db1', 'dw2')):
+        assert O.rel(a_, b_) < tol, (name, O.rel(a_, b_))
+    assert device_error_clear()

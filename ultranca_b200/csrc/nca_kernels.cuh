@@ -181,6 +181,50 @@ __device__ __forceinline__ TileCoord tile_coord(int64_t t, const TileGeom &g, in
 // ================================================================ forward
 // One CTA per SM slot, tiles [T c / G, T (c+1) / G). Writes y (growing: the unmasked y and its alpha plane, the alive
 // kernel then masks it).
+// Growing NCAs, active tiles (block-wide, every thread calls it): whether some cell of the grid within two pixels of
+// the tile (no wrap: the alive pooling pads with zeros) has x_alpha > 0.1. If none has, every cell within one pixel of
+// the tile is dead before the step (3x3 max-pool of x_alpha <= 0.1), so the alive mask is 0 on the tile whatever the
+// update computes (the alive pass then writes y = 0 there), and the post-step alpha of the tile's cells only enters
+// the pooling of cells that are dead already: the tile's MLP can be skipped without changing any output.
+// XS: the tile's halo copy (one pixel, circular: its out-of-grid positions are skipped here); the ring at distance two
+// is read from global memory only when the halo holds no live alpha.
+template <int C>
+__device__ __forceinline__ bool tile_live_before(const StepArgs &a, const TileCoord &tc, const TileGeom &g,
+                                                 const float *XS)
+{
+    const int RR = g.R + 2, SS = g.S + 2;
+    const float *xs = XS + 3 * RR * SS;  // the alpha channel of the halo copy
+    bool live = false;
+    for (int e = threadIdx.x; e < RR * SS; e += blockDim.x) {
+        const int rr = e / SS, Y = tc.y0 - 1 + rr, X = tc.x0 - 1 + (e - rr * SS);
+        live |= Y >= 0 && Y < a.H && X >= 0 && X < a.W && xs[e] > 0.1f;
+    }
+    if (__syncthreads_or(live))
+        return true;
+    const int RO = g.R + 4, SO = g.S + 4;
+    const float *xa = a.x + ((size_t)tc.n * C + 3) * (size_t)a.H * a.W;
+    for (int e = threadIdx.x; e < RO * SO; e += blockDim.x) {
+        const int rr = e / SO, ss = e - rr * SO, Y = tc.y0 - 2 + rr, X = tc.x0 - 2 + ss;
+        const bool ring = rr == 0 || rr == RO - 1 || ss == 0 || ss == SO - 1;
+        if (ring && Y >= 0 && Y < a.H && X >= 0 && X < a.W)
+            live |= __ldg(xa + (size_t)Y * a.W + X) > 0.1f;
+    }
+    return __syncthreads_or(live) != 0;
+}
+
+// Growing NCAs, backward: a tile with no pixel alive after its forward step has gm = gy m a = 0 throughout, so it adds
+// nothing to the weight gradients and its dp is 0; the backward skips it without writing its dp, and the adjoint
+// reads dp at alive cells only. This thread's pixel of tile t alive (false when the pixel is outside the image); the
+// backward loads it one tile ahead, so that the skip decision does not wait for memory.
+__device__ __forceinline__ bool pixel_alive(const StepArgs &a, const TileGeom &g, int64_t t)
+{
+    const int64_t n = t / g.tiles_per_image;
+    const int ti = (int)(t - n * g.tiles_per_image);
+    const int r = threadIdx.x / g.S, s = threadIdx.x - r * g.S;
+    const int Y = (ti / g.strips) * g.R + r, X = (ti % g.strips) * g.S + s;
+    return threadIdx.x < g.R * g.S && Y < a.H && X < a.W && a.alive[((size_t)n * a.H + Y) * a.W + X] != 0;
+}
+
 template <int C, int HID, bool TC, bool GROWING>
 __global__ void __launch_bounds__(128, 1) fwd_kernel(StepArgs a)
 {
@@ -229,6 +273,12 @@ __global__ void __launch_bounds__(128, 1) fwd_kernel(StepArgs a)
         __syncthreads();
         const int r = tid / g.S, s = tid - r * g.S;
         const bool valid = tid < g.R * g.S && tc.y0 + r < a.H && tc.x0 + s < a.W;
+        // dead tile: no MLP (the alive pass zeroes y); the check's closing barrier follows its last read of XS
+        if (GROWING && !tile_live_before<C>(a, tc, g, XS)) {
+            if (valid)
+                a.alpha[(size_t)tc.n * plane + (size_t)(tc.y0 + r) * a.W + tc.x0 + s] = 0.f;
+            continue;
+        }
         perceive_tile<D, TC>(P, XS, g, tid, valid);
         float u[16];
         if constexpr (TC) {
@@ -399,26 +449,29 @@ __device__ __forceinline__ void write_partial_row(float *out, int j, const float
         out[D::HID * (D::PIN + 1) + c * D::HID + j] = o2[c] + dw2_col[c];
 }
 
-// Per tile pixel: gm = gy m (a) (growing: a = the alive mask of the forward), 16 channels, fp32.
+// Per tile pixel: gm = gy m (a) (growing: a = the alive mask of the forward), 16 channels, fp32. Returns whether the
+// pixel is valid and (growing) alive.
 template <int C, bool GROWING>
-__device__ __forceinline__ void load_gm(float (&gm)[16], const StepArgs &a, const TileCoord &tc, int Y, int X,
+__device__ __forceinline__ bool load_gm(float (&gm)[16], const StepArgs &a, const TileCoord &tc, int Y, int X,
                                         bool valid, bool stoch)
 {
 #pragma unroll
     for (int c = 0; c < 16; ++c)
         gm[c] = 0.f;
     if (!valid)
-        return;
+        return false;
     const size_t plane = (size_t)a.H * a.W;
     float m = stoch ? update_mask_at(a.seed, a.rate, tc.n + a.n_offset, a.H, a.W, Y, X) : 1.f;
-    if (GROWING && !a.alive[(size_t)tc.n * plane + (size_t)Y * a.W + X])
+    const bool live = !GROWING || a.alive[(size_t)tc.n * plane + (size_t)Y * a.W + X];
+    if (!live)
         m = 0.f;
     if (m == 0.f)
-        return;
+        return live;
     const float *gyn = a.gy + (size_t)tc.n * C * plane + (size_t)Y * a.W + X;
 #pragma unroll
     for (int c = 0; c < C; ++c)
         gm[c] = __ldg(gyn + (size_t)c * plane);
+    return live;
 }
 
 // fp32 mode: the MLP on CUDA cores in fp32, weight gradients accumulated by threads j < HID in registers.
@@ -458,6 +511,7 @@ __global__ void __launch_bounds__(128, 1) bwd_kernel_cc(StepArgs a)
             acc2[c] = 0.f;
         accb = 0.f;
     };
+    bool alive_next = GROWING && t0 < t1 && pixel_alive(a, g, t0);  // growing: this pixel of the next tile
     for (int64_t t = t0; t < t1; ++t) {
         const TileCoord tc = tile_coord(t, g, a.B);
         if (tc.k != cur_k) {
@@ -467,6 +521,13 @@ __global__ void __launch_bounds__(128, 1) bwd_kernel_cc(StepArgs a)
             stage_weights<D, false>(W1s, W2s, a.w1 + (size_t)tc.k * HID * D::PIN, a.b1 + (size_t)tc.k * HID,
                                     a.w2 + (size_t)tc.k * C * HID);
             cur_k = tc.k;
+        }
+        if (GROWING) {  // dead tile: nothing to add, its dp is not read
+            const bool here = alive_next;
+            if (t + 1 < t1)
+                alive_next = pixel_alive(a, g, t + 1);
+            if (!__syncthreads_or(here))
+                continue;
         }
         load_halo_async<D>(XS, a.x, tc.n, g, tc.y0, tc.x0);
         const int r = tid / g.S, s = tid - r * g.S;
@@ -630,16 +691,20 @@ __global__ void __launch_bounds__(128, 1) bwd_kernel_tc(StepArgs a)
             umma::tmem_wait_ld();
 #pragma unroll
             for (int e = 0; e < 16; ++e)
-                row[cc * 16 + e] = v[e];
+                row[cc * 16 + e] = started ? v[e] : 0.f;  // no tile of NCA k ran an MMA (growing: all dead)
         }
         umma::tmem_ld16(lane_base + D::T_ACC2, col);
         umma::tmem_wait_ld();
+#pragma unroll
+        for (int e = 0; e < 16; ++e)
+            col[e] = started ? col[e] : 0.f;
         if (tid < HID)
             write_partial_row<D>(a.partial + (size_t)(blockIdx.x + k) * D::PART, tid, row, row[D::PIN], col,
                                  a.partial_add != 0);
         umma::fence_before_sync();
     };
 
+    bool alive_next = GROWING && t0 < t1 && pixel_alive(a, g, t0);  // growing: this pixel of the next tile
     for (int64_t t = t0; t < t1; ++t) {
         const TileCoord tc = tile_coord(t, g, a.B);
         if (tc.k != cur_k) {
@@ -650,6 +715,13 @@ __global__ void __launch_bounds__(128, 1) bwd_kernel_tc(StepArgs a)
                                  a.w2 + (size_t)tc.k * C * HID);
             cur_k = tc.k;
             started = false;
+        }
+        if (GROWING) {  // dead tile: nothing to add, its dp is not read
+            const bool here = alive_next;
+            if (t + 1 < t1)
+                alive_next = pixel_alive(a, g, t + 1);
+            if (!__syncthreads_or(here))
+                continue;
         }
         // ---- 1. inputs
         load_halo_async<D>(XS, a.x, tc.n, g, tc.y0, tc.x0);
@@ -814,14 +886,45 @@ __global__ void __launch_bounds__(256) adjoint_kernel(const float *__restrict__ 
 {
     constexpr int PIN = 4 * C, HW_ = ADJ_TW + 2, HH_ = ADJ_TH + 2;
     extern __shared__ __align__(16) float sdp[];  // [PIN][HH_][HW_]
+    __shared__ uint8_t sal[GROWING ? HH_ * HW_ : 1];  // growing: the alive mask of the halo
     const int tiles_x = (W + ADJ_TW - 1) / ADJ_TW;
     const int x0 = (blockIdx.x % tiles_x) * ADJ_TW, y0 = (blockIdx.x / tiles_x) * ADJ_TH;
     const int64_t n = blockIdx.y, plane = (int64_t)H * W;
     const float *dpn = dp + n * PIN * plane;
-    for (int e = threadIdx.x; e < PIN * HH_ * HW_; e += blockDim.x) {
-        const int f = e / (HH_ * HW_), rem = e - f * HH_ * HW_, r = rem / HW_, s = rem - r * HW_;
-        const int Y = wrap_index(y0 - 1 + r, H), X = wrap_index(x0 - 1 + s, W);
-        sdp[e] = dpn[(int64_t)f * plane + (int64_t)Y * W + X];
+    bool gate = false;  // growing, block with dead cells in its halo: read dp at alive cells only
+    if (GROWING) {
+        // dp is 0 wherever the cell is dead (gm = 0 there); the backward skips all-dead tiles without writing their
+        // dp, so dp is read at alive cells only, and a block with no alive cell in its halo has gx = 0
+        bool some = false, all = true;  // of this thread's halo cells
+        for (int e = threadIdx.x; e < HH_ * HW_; e += blockDim.x) {
+            const int r = e / HW_, s = e - r * HW_;
+            const uint8_t v = alive[n * plane + (int64_t)wrap_index(y0 - 1 + r, H) * W + wrap_index(x0 - 1 + s, W)];
+            sal[e] = v;
+            some |= v != 0;
+            all &= v != 0;
+        }
+        const bool any_alive = __syncthreads_or(some), all_alive = __syncthreads_and(all);
+        if (!any_alive) {
+            const int r = threadIdx.x / ADJ_TW, s = threadIdx.x % ADJ_TW, Y = y0 + r, X = x0 + s;
+            if (Y < H && X < W)
+                for (int c = 0; c < C; ++c)
+                    gx[(n * C + c) * plane + (int64_t)Y * W + X] = 0.f;
+            return;
+        }
+        gate = !all_alive;
+    }
+    if (gate) {
+        for (int e = threadIdx.x; e < PIN * HH_ * HW_; e += blockDim.x) {
+            const int f = e / (HH_ * HW_), rem = e - f * HH_ * HW_, r = rem / HW_, s = rem - r * HW_;
+            const int Y = wrap_index(y0 - 1 + r, H), X = wrap_index(x0 - 1 + s, W);
+            sdp[e] = sal[GROWING ? rem : 0] ? dpn[(int64_t)f * plane + (int64_t)Y * W + X] : 0.f;
+        }
+    } else {
+        for (int e = threadIdx.x; e < PIN * HH_ * HW_; e += blockDim.x) {
+            const int f = e / (HH_ * HW_), rem = e - f * HH_ * HW_, r = rem / HW_, s = rem - r * HW_;
+            const int Y = wrap_index(y0 - 1 + r, H), X = wrap_index(x0 - 1 + s, W);
+            sdp[e] = dpn[(int64_t)f * plane + (int64_t)Y * W + X];
+        }
     }
     __syncthreads();
     const int r = threadIdx.x / ADJ_TW, s = threadIdx.x % ADJ_TW, Y = y0 + r, X = x0 + s;
