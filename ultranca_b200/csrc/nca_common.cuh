@@ -67,6 +67,11 @@ __device__ __forceinline__ float tf32_rna(float v)
     return __uint_as_float((__float_as_uint(v) + 0x1000u) & 0xFFFFE000u);
 }
 
+// tf32_rna for a value that only tcgen05.mma kind::tf32 reads: the MMA takes the upper 19 bits of an fp32 operand
+// (sign, exponent, 10 mantissa bits) and ignores the other 13, so adding the rounding bias is enough (one integer
+// operation). Measured on the B200: the step kernels' outputs are bitwise those of tf32_rna operands.
+__device__ __forceinline__ float tf32_bias(float v) { return __uint_as_float(__float_as_uint(v) + 0x1000u); }
+
 // ---------------------------------------------------------------- perception
 // The four filters of one channel from its 3x3 neighbourhood v (rows dy = -1..1, columns dx = -1..1), summed in the
 // reference's grouping (ncaops/nca_step.cuh:317-320).

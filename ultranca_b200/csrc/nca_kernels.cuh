@@ -155,7 +155,7 @@ __device__ __forceinline__ void perceive_tile(float *P, const float *XS, const T
                     v[dy][dx] = b[dy * SS + dx];
             p = perceive3x3(v);
             if (TC)
-                p = make_float4(tf32_rna(p.x), tf32_rna(p.y), tf32_rna(p.z), tf32_rna(p.w));
+                p = make_float4(tf32_bias(p.x), tf32_bias(p.y), tf32_bias(p.z), tf32_bias(p.w));
         }
         *reinterpret_cast<float4 *>(P + c * D::PLANE + i * 4) = p;
     }
@@ -310,7 +310,7 @@ __global__ void __launch_bounds__(128, 1) fwd_kernel(StepArgs a)
                 umma::tmem_wait_ld();
 #pragma unroll
                 for (int e = 0; e < 16; ++e)
-                    v[e] = tf32_rna(fmaxf(v[e], 0.f));
+                    v[e] = tf32_bias(fmaxf(v[e], 0.f));
                 umma::tmem_st16(ad, v);
             }
             umma::tmem_wait_st();
@@ -732,7 +732,7 @@ __global__ void __launch_bounds__(128, 1) bwd_kernel_tc(StepArgs a)
         load_gm<C, GROWING>(gm, a, tc, Y, X, valid, stoch);
 #pragma unroll
         for (int c = 0; c < 16; ++c)
-            gm[c] = tf32_rna(gm[c]);
+            gm[c] = tf32_bias(gm[c]);
         umma::tmem_st16(lane_base + D::T_G, gm);
         st_sw32x8(GSW, 0, tid, 128, gm);
         st_sw32x8(GSW, 8, tid, 128, gm + 8);
@@ -754,8 +754,8 @@ __global__ void __launch_bounds__(128, 1) bwd_kernel_tc(StepArgs a)
                             v[dy][dx] = b[dy * SS + dx];
                     p = perceive3x3(v);
                 }
-                pv[4 * c] = tf32_rna(p.x); pv[4 * c + 1] = tf32_rna(p.y);
-                pv[4 * c + 2] = tf32_rna(p.z); pv[4 * c + 3] = tf32_rna(p.w);
+                pv[4 * c] = tf32_bias(p.x); pv[4 * c + 1] = tf32_bias(p.y);
+                pv[4 * c + 2] = tf32_bias(p.z); pv[4 * c + 3] = tf32_bias(p.w);
             }
 #pragma unroll
             for (int f = D::PIN; f < ((D::KP + 15) / 16) * 16; ++f)
@@ -800,8 +800,8 @@ __global__ void __launch_bounds__(128, 1) bwd_kernel_tc(StepArgs a)
             umma::tmem_wait_ld();
 #pragma unroll
             for (int e = 0; e < 16; ++e) {
-                d[e] = h[e] > 0.f ? tf32_rna(d[e]) : 0.f;
-                h[e] = tf32_rna(fmaxf(h[e], 0.f));
+                d[e] = h[e] > 0.f ? tf32_bias(d[e]) : 0.f;
+                h[e] = tf32_bias(fmaxf(h[e], 0.f));
             }
             st_sw32x8(RHDH, cc * 16, tid, 128, h);
             st_sw32x8(RHDH, cc * 16 + 8, tid, 128, h + 8);

@@ -687,7 +687,7 @@ __global__ void __launch_bounds__(128 * NPART + 96, 1) fwd_rows_kernel(StepArgs 
                     const float *bm = rm + c * RS, *b0 = r0 + c * RS, *bp = rp + c * RS;
                     const float v[3][3] = {{bm[pl], bm[pc], bm[pr]}, {b0[pl], b0[pc], b0[pr]}, {bp[pl], bp[pc], bp[pr]}};
                     const float4 p = perceive3x3(v);
-                    const float pv[4] = {tf32_rna(p.x), tf32_rna(p.y), tf32_rna(p.z), tf32_rna(p.w)};
+                    const float pv[4] = {tf32_bias(p.x), tf32_bias(p.y), tf32_bias(p.z), tf32_bias(p.w)};
                     umma::tmem_st4(tp + 4 * c, pv);
                     xnext[cc] = v[1][1];
                 }
@@ -727,7 +727,7 @@ __global__ void __launch_bounds__(128 * NPART + 96, 1) fwd_rows_kernel(StepArgs 
                     umma::tmem_wait_ld();
 #pragma unroll
                     for (int e = 0; e < 8; ++e)
-                        h[e] = tf32_rna(fmaxf(h[e], 0.f));
+                        h[e] = tf32_bias(fmaxf(h[e], 0.f));
                     umma::tmem_st8(th + q * 8, h);
                 }
                 umma::tmem_wait_st();
@@ -1222,11 +1222,11 @@ __global__ void __launch_bounds__(128 * NPART + 96, 1) bwd_rows_kernel(StepArgs 
                         win[cc][0] = v[1][0]; win[cc][1] = v[1][1]; win[cc][2] = v[1][2];
                         win[cc][3] = v[2][0]; win[cc][4] = v[2][1]; win[cc][5] = v[2][2];
                         const float4 p = perceive3x3(v);
-                        const float t4[4] = {tf32_rna(p.x), tf32_rna(p.y), tf32_rna(p.z), tf32_rna(p.w)};
+                        const float t4[4] = {tf32_bias(p.x), tf32_bias(p.y), tf32_bias(p.z), tf32_bias(p.w)};
                         umma::tmem_st4(tp + 4 * c, t4);
                         *reinterpret_cast<float4 *>(psw + umma::sw32_offset(4 * c, x, 128) / 4) =
                             make_float4(t4[0], t4[1], t4[2], t4[3]);
-                        const float gmv = (vx && m) ? tf32_rna(gyA[cc]) : 0.f;
+                        const float gmv = (vx && m) ? tf32_bias(gyA[cc]) : 0.f;
                         umma::tmem_st1(tp + F::GM0 + c, gmv);
                         psw[umma::sw32_offset(F::GM0 + c, x, 128) / 4] = gmv;
                     }
@@ -1271,8 +1271,8 @@ __global__ void __launch_bounds__(128 * NPART + 96, 1) bwd_rows_kernel(StepArgs 
                         umma::tmem_wait_ld();
 #pragma unroll
                         for (int e = 0; e < 8; ++e) {
-                            d[e] = h[e] > 0.f ? tf32_rna(d[e]) : 0.f;
-                            h[e] = tf32_rna(fmaxf(h[e], 0.f));
+                            d[e] = h[e] > 0.f ? tf32_bias(d[e]) : 0.f;
+                            h[e] = tf32_bias(fmaxf(h[e], 0.f));
                         }
                         if (owned) {
                             st_sw32x8_balanced(RH, j0, x, 128, h);
