@@ -186,18 +186,20 @@ __device__ __forceinline__ TileCoord tile_coord(int64_t t, const TileGeom &g, in
 // the tile is dead before the step (3x3 max-pool of x_alpha <= 0.1), so the alive mask is 0 on the tile whatever the
 // update computes (the alive pass then writes y = 0 there), and the post-step alpha of the tile's cells only enters
 // the pooling of cells that are dead already: the tile's MLP can be skipped without changing any output.
-// XS: the tile's halo copy (one pixel, circular: its out-of-grid positions are skipped here); the ring at distance two
-// is read from global memory only when the halo holds no live alpha.
+// XS: the tile's halo copy (one pixel, circular: its out-of-grid positions are skipped here); hr, hc: the row and column
+// in the halo copy of this thread's positions threadIdx.x + 128 i (hr < 0: none; blocks of 128 threads, and
+// (R + 2)(S + 2) <= 390 positions). The ring at distance two is read from global memory only when the halo holds no
+// live alpha.
 template <int C>
 __device__ __forceinline__ bool tile_live_before(const StepArgs &a, const TileCoord &tc, const TileGeom &g,
-                                                 const float *XS)
+                                                 const float *XS, const int (&hr)[4], const int (&hc)[4])
 {
-    const int RR = g.R + 2, SS = g.S + 2;
-    const float *xs = XS + 3 * RR * SS;  // the alpha channel of the halo copy
+    const float *xs = XS + 3 * (g.R + 2) * (g.S + 2);  // the alpha channel of the halo copy
     bool live = false;
-    for (int e = threadIdx.x; e < RR * SS; e += blockDim.x) {
-        const int rr = e / SS, Y = tc.y0 - 1 + rr, X = tc.x0 - 1 + (e - rr * SS);
-        live |= Y >= 0 && Y < a.H && X >= 0 && X < a.W && xs[e] > 0.1f;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int Y = tc.y0 - 1 + hr[i], X = tc.x0 - 1 + hc[i];
+        live |= hr[i] >= 0 && Y >= 0 && Y < a.H && X >= 0 && X < a.W && xs[threadIdx.x + 128 * i] > 0.1f;
     }
     if (__syncthreads_or(live))
         return true;
@@ -242,6 +244,13 @@ __global__ void __launch_bounds__(128, 1) fwd_kernel(StepArgs a)
     cta_range(T, gridDim.x, blockIdx.x, &t0, &t1);
     const bool stoch = a.rate < 1.f;
     const size_t plane = (size_t)a.H * a.W;
+    int hr[4], hc[4];  // growing: this thread's positions in the halo copy (row, column; row < 0: none)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int e = tid + 128 * i, ss = g.S + 2;
+        hr[i] = GROWING && e < (g.R + 2) * ss ? e / ss : -1;
+        hc[i] = e - (hr[i] < 0 ? 0 : hr[i]) * ss;
+    }
 
     uint32_t tmem = 0;
     if constexpr (TC) {
@@ -274,7 +283,7 @@ __global__ void __launch_bounds__(128, 1) fwd_kernel(StepArgs a)
         const int r = tid / g.S, s = tid - r * g.S;
         const bool valid = tid < g.R * g.S && tc.y0 + r < a.H && tc.x0 + s < a.W;
         // dead tile: no MLP (the alive pass zeroes y); the check's closing barrier follows its last read of XS
-        if (GROWING && !tile_live_before<C>(a, tc, g, XS)) {
+        if (GROWING && !tile_live_before<C>(a, tc, g, XS, hr, hc)) {
             if (valid)
                 a.alpha[(size_t)tc.n * plane + (size_t)(tc.y0 + r) * a.W + tc.x0 + s] = 0.f;
             continue;
