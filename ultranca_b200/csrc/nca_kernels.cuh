@@ -963,20 +963,53 @@ __global__ void __launch_bounds__(256) adjoint_kernel(const float *__restrict__ 
 // The CTAs [c0, c1] of a launch whose unit ranges (bands bd) overlap NCA k's units [k U, (k + 1) U): c0 holds unit
 // k U (first, from the uniform estimate, step down while the band starts after it, then up while it ends at or before
 // it), c1 the last CTA that starts before (k + 1) U.
-__device__ __forceinline__ void nca_cta_span(const Bands &bd, int64_t U, int k, int *c0_out, int *c1_out)
+// blo(c): the first unit of CTA c (band_lo, or a table of it).
+template <class BandLo>
+__device__ __forceinline__ void nca_cta_span(const Bands &bd, int64_t U, int k, int *c0_out, int *c1_out, BandLo blo)
 {
     const int64_t lo = (int64_t)k * U, hi = lo + U;
     int c0 = (int)(lo * bd.G / bd.T);
     c0 = c0 >= bd.G ? bd.G - 1 : c0;
-    while (c0 > 0 && band_lo(bd, c0) > lo)
+    while (c0 > 0 && blo(c0) > lo)
         --c0;
-    while (c0 + 1 < bd.G && band_lo(bd, c0 + 1) <= lo)
+    while (c0 + 1 < bd.G && blo(c0 + 1) <= lo)
         ++c0;
     int c1 = c0;
-    while (c1 + 1 < bd.G && band_lo(bd, c1 + 1) < hi)
+    while (c1 + 1 < bd.G && blo(c1 + 1) < hi)
         ++c1;
     *c0_out = c0;
     *c1_out = c1;
+}
+__device__ __forceinline__ void nca_cta_span(const Bands &bd, int64_t U, int k, int *c0_out, int *c1_out)
+{
+    nca_cta_span(bd, U, k, c0_out, c1_out, [&](int c) { return band_lo(bd, c); });
+}
+
+// Block-wide (every thread calls it): the non-empty CTAs of NCA k's span, in increasing order, into slots[0 .. n);
+// returns n, or -1 (range = the span) when the span has more than cap CTAs. For a launch of at most SPAN_TABLE CTAs
+// the band starts are computed in parallel (one band_lo per thread, into the shared table blo) and thread 0 lists
+// from the table: band_lo of cost-balanced bands is a search of a few steps and the listing needs two per CTA, which
+// serially on one thread made a reduce launch take ~27 us.
+constexpr int SPAN_TABLE = 1024;
+__device__ __forceinline__ int nca_span_slots(const Bands &bd, int64_t U, int k, int *slots, int cap, int64_t *blo,
+                                              int *range, int *nslots)
+{
+    const bool table = bd.G < SPAN_TABLE;
+    if (table)
+        for (int c = threadIdx.x; c <= bd.G; c += blockDim.x)
+            blo[c] = band_lo(bd, c);
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        auto lo_of = [&](int c) { return table ? blo[c] : band_lo(bd, c); };
+        nca_cta_span(bd, U, k, &range[0], &range[1], lo_of);
+        int n = 0;
+        for (int c = range[0]; c <= range[1] && n < cap; ++c)
+            if (lo_of(c + 1) > lo_of(c))
+                slots[n++] = c;
+        *nslots = range[1] - range[0] + 1 <= cap ? n : -1;
+    }
+    __syncthreads();
+    return *nslots;
 }
 
 // Fixed-order sum of the partial slots (c + k) of the CTAs c whose tile ranges overlap NCA k -> dw1, db1, dw2
@@ -988,20 +1021,10 @@ __global__ void reduce_kernel(const float *__restrict__ partial, Bands bd, int64
     using D = Dims<C, HID>;
     constexpr int MAXS = 1024;  // slots listed in shared memory; a longer span is summed in the same order from bd
     const int k = blockIdx.y, e = blockIdx.x * blockDim.x + threadIdx.x;
-    __shared__ int range[2], nslots;
-    __shared__ int slots[MAXS];  // the non-empty CTAs of the span (thread 0 finds them once)
-    if (threadIdx.x == 0) {
-        nca_cta_span(bd, tiles_per_nca, k, &range[0], &range[1]);
-        int n = 0;
-        for (int c = range[0]; c <= range[1] && n < MAXS; ++c) {
-            int64_t a, b;
-            band_range(bd, c, &a, &b);
-            if (b > a)
-                slots[n++] = c;
-        }
-        nslots = range[1] - range[0] + 1 <= MAXS ? n : -1;
-    }
-    __syncthreads();
+    __shared__ int range[2], nslots_s;
+    __shared__ int slots[MAXS];  // the non-empty CTAs of the span
+    __shared__ int64_t blo[SPAN_TABLE];
+    const int nslots = nca_span_slots(bd, tiles_per_nca, k, slots, MAXS, blo, range, &nslots_s);
     if (e >= D::PART)
         return;
     float s = 0.f;

@@ -139,20 +139,10 @@ __global__ void __launch_bounds__(256) reduce_adam_kernel(const float *__restric
     const int64_t off = t == 0 ? 0 : t == 1 ? (int64_t)HID * D::PIN : (int64_t)HID * (D::PIN + 1);
     const int64_t base = (int64_t)k * Tt.numel;
     __shared__ int slots[REDUCE_MAX_SLOTS];
-    __shared__ int nslots;
-    if (threadIdx.x == 0) {
-        int c0, c1, n = 0;
-        nca_cta_span(bd, units_per_nca, k, &c0, &c1);
-        for (int c = c0; c <= c1 && n < REDUCE_MAX_SLOTS; ++c) {
-            int64_t lo, hi;
-            band_range(bd, c, &lo, &hi);
-            if (hi > lo)
-                slots[n++] = c + k;
-        }
-        nslots = n;
-    }
-    __syncthreads();
-    const int ns = nslots;
+    __shared__ int range[2], nslots;
+    __shared__ int64_t blo[SPAN_TABLE];
+    // the host launches this only for grids of at most REDUCE_MAX_SLOTS CTAs, so the span always fits
+    const int ns = nca_span_slots(bd, units_per_nca, k, slots, REDUCE_MAX_SLOTS, blo, range, &nslots);
     float *g = const_cast<float *>(Tt.g);
     float ss = 0.f;
     for (int64_t i0 = threadIdx.x; i0 < Tt.numel; i0 += U * blockDim.x) {
@@ -167,7 +157,7 @@ __global__ void __launch_bounds__(256) reduce_adam_kernel(const float *__restric
 #pragma unroll
                 for (int u = 0; u < U; ++u) {
                     const int64_t i = i0 + (int64_t)u * blockDim.x;
-                    v[j][u] = cb + j < ns && i < Tt.numel ? partial[(size_t)slots[cb + j] * D::PART + off + i] : 0.f;
+                    v[j][u] = cb + j < ns && i < Tt.numel ? partial[(size_t)(slots[cb + j] + k) * D::PART + off + i] : 0.f;
                 }
 #pragma unroll
             for (int j = 0; j < S; ++j)
