@@ -1,7 +1,8 @@
-// Row-streaming step kernels (TF32, texture NCAs, W <= 128 and W % 4 == 0): the hot path of the benchmark configs.
+// Row-streaming step kernels (TF32, texture NCAs, W <= 128 and W % 4 == 0, or W a multiple of 128 as column strips):
+// the hot path of the benchmark configs.
 //
-// A CTA owns a contiguous band of global rows [NH c / G, NH (c+1) / G) of the N images; one image row is one
-// 128-lane MMA tile (lane = column). Rows of x (and, in the backward, gy) stream through shared-memory rings by
+// A CTA owns a contiguous band of global rows of the N images (cost-balanced bands, Bands); one image row (or one
+// 128-column strip of it) is one 128-lane MMA tile (lane = column). Rows of x (and, in the backward, gy) stream through shared-memory rings by
 // bulk-async copies (the TMA engine), one row per channel per copy, completing on mbarriers; consecutive rows of a
 // band share their neighbours, so every x row is read from HBM once per band.
 //
