@@ -150,6 +150,13 @@ int nca_update_mask(float *mask, int64_t n, int64_t h, int64_t w, uint64_t seed,
 int nca_synthetic_loss(const float *x, const float *target, float *gy, float *loss, float *work, int64_t K, int64_t B,
                        int64_t C, int64_t H, int64_t W, float overflow_weight, void *stream);
 
+/* The same loss over the first target_channels channels (target: K x target_channels x H x W): per NCA the mean
+ * squared error to the target plus overflow_weight x the summed overflow. target_channels = 4 with overflow_weight = 0
+ * is the growing NCA's loss, L2 to a premultiplied RGBA target (train.py:97-99, Growing.loss); nca_synthetic_loss is
+ * target_channels = 3. */
+int nca_task_loss(const float *x, const float *target, float *gy, float *loss, float *work, int64_t K, int64_t B,
+                  int64_t C, int64_t H, int64_t W, int64_t target_channels, float overflow_weight, void *stream);
+
 /* Per-NCA, per-tensor gradient normalisation followed by Adam with a MultiStepLR schedule, for the three weight
  * tensors at once, in one launch (train.py:120-122 and :136-141: g /= ||g_k||_2 + 1e-8; torch.optim.Adam; lr x gamma
  * at each milestone). param_i / grad_i / m_i / v_i: K x numel_i fp32 (i = 0, 1, 2 for w1, b1, w2). iteration: device
@@ -212,6 +219,14 @@ int nca_device_error(int *code, int reset);
  * N in 16..128 (multiple of 16), K in 8..128 (multiple of 8). No reference counterpart (the reference has no
  * tcgen05 path). */
 int nca_umma_selftest(int form, int N, int K, const float *A, const float *B, float *D, void *stream);
+
+/* Failure-detection self-test of the kernels' bounded waits: one CTA waits on an mbarrier that nothing arrives on,
+ * one warp with a limit of limit_ns (in (0, 1 s]) and a second warp with the step kernels' 2 s limit; the second must
+ * give up as soon as the first has (the shared abort word). The kernel then frees its Tensor Memory, sets the device
+ * error word to 1 (as a step kernel whose wait ran out does) and returns: no trap, the context stays usable.
+ * out (4 x u64, device memory): nanoseconds each warp waited and whether its wait reported success (0 expected).
+ * No reference counterpart (the reference's kernels have no bounded waits). */
+int nca_wait_selftest(int64_t limit_ns, unsigned long long *out, void *stream);
 
 #ifdef __cplusplus
 }

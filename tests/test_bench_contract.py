@@ -1,6 +1,6 @@
 """The benchmark's JSON-line contract on CPU: the reference arm (the reference's eager PyTorch step, restated in
 oracle/, on the host cores) prints one line with the metric, unit, config and the cpu_baseline / e2e objects the
-driver reads, for the default configuration and the supplemental configuration-4 shard."""
+driver reads, for every configuration (1, the default; 2, growing; 3, no-grad rollouts; 4, the 256 x 256 shard)."""
 import json
 import os
 import subprocess
@@ -12,6 +12,8 @@ ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
 
 @pytest.mark.parametrize('config,metric,hw', [(1, 'cell-updates/s fwd+bwd, 64-step rollout', 128),
+                                              (2, 'cell-updates/s fwd+bwd, 80-step rollout', 72),
+                                              (3, 'cell-updates/s no-grad, 128-step rollout', 256),
                                               (4, 'cell-updates/s fwd+bwd, 96-step rollout', 256)])
 def test_reference_arm_prints_one_contract_line(config, metric, hw):
     out = subprocess.run([sys.executable, os.path.join(ROOT, 'bench.py'), '--impl', 'reference', '--steps', '1',

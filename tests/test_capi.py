@@ -96,3 +96,12 @@ def test_stage_mask_needs_a_stage_and_known_bits(stages):
     st = lib.nca_backward_stages(p, p, None, p, p, p, p, p, p, p, p, 1 << 30, p, 1 << 30, 4, 12, 8, 16, 2, 96, 2, 0, 0.5,
                                  0, 0, 0, 0, stages, None)
     assert st == 1 and 'stage' in lib.nca_last_error().decode()
+
+
+def test_wait_selftest_validates_its_arguments():
+    """The failure-detection self-test refuses a limit outside (0, 1 s] and a null output before any launch."""
+    from ultranca_b200._lib import lib
+    assert lib.nca_wait_selftest(0, ctypes.c_void_p(256), None) == 1
+    assert lib.nca_wait_selftest(2_000_000_000, ctypes.c_void_p(256), None) == 1
+    assert lib.nca_wait_selftest(1000, None, None) == 1
+    assert 'out must not be null' in lib.nca_last_error().decode()

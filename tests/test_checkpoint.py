@@ -49,6 +49,36 @@ def test_not_a_checkpoint_is_rejected(tmp_path):
         ck.load_nca(str(tmp_path / 'x.pt'))
 
 
+def _fake_trainer(seed):
+    """The attributes of a RolloutTrainer that the group state reads and writes, as CPU tensors."""
+    import ctypes
+    from types import SimpleNamespace
+    g = torch.Generator().manual_seed(seed)
+    K, C, Hd = 2, 12, 96
+    ws = [torch.randn(K, Hd, 4 * C, generator=g), torch.randn(K, Hd, generator=g), torch.randn(K, C, Hd, generator=g)]
+    opt = SimpleNamespace(m=[torch.randn_like(w) for w in ws], v=[torch.rand_like(w) for w in ws],
+                          iteration=torch.tensor([5]), lr=1e-3, betas=(0.9, 0.999), eps=1e-8, gamma=0.5,
+                          milestones=(ctypes.c_int64 * 8)(256, 512), n_milestones=2)
+    return SimpleNamespace(w1=ws[0], b1=ws[1], w2=ws[2], opt=opt)
+
+
+def test_group_state_with_other_moments_is_rejected_untouched():
+    """A group state whose Adam moments differ in number or shape from the trainer's is refused before anything is
+    overwritten (weights and moments keep their values)."""
+    src, dst = _fake_trainer(1), _fake_trainer(2)
+    sd = ck.state_dict(src)
+    before = [t.clone() for t in (dst.w1, dst.b1, dst.w2, *dst.opt.m, *dst.opt.v)]
+    bad_count = dict(sd, m=sd['m'][:2])
+    bad_shape = dict(sd, v=[sd['v'][0], sd['v'][1][:, :-1], sd['v'][2]])
+    for bad in (bad_count, bad_shape):
+        with pytest.raises(ValueError):
+            ck.load_state_dict(dst, bad)
+        after = (dst.w1, dst.b1, dst.w2, *dst.opt.m, *dst.opt.v)
+        assert all(torch.equal(a, b) for a, b in zip(before, after))
+    ck.load_state_dict(dst, sd)  # the matching state restores every tensor
+    assert all(torch.equal(a, b) for a, b in zip((dst.w1, *dst.opt.m, *dst.opt.v), (src.w1, *src.opt.m, *src.opt.v)))
+
+
 @pytest.mark.gpu
 def test_resumed_group_continues_bitwise(tmp_path):
     from oracle import nca_oracle as O

@@ -1,0 +1,166 @@
+"""GPU parity of the benchmarked paths against the CPU oracle (oracle/nca_oracle.py), end to end.
+
+1. BASELINE configuration 0 exactly (K = 1 texture NCA, B = 2, 128 x 128, 32 steps, p = 0.5, the synthetic
+   L2 + 10 x overflow loss, TF32), through the drop-in operator (nca_ops.step under autograd, the call train.py makes)
+   and through the device-driven RolloutTrainer, against the oracle's TF32-emulating rollout with its backward chained
+   step by step, with no masking of any pixel:
+   - end to end (two independent trajectories): the state after every step, the per-NCA loss and dw1, db1, dw2 within
+     1e-3 relative (the parity bar for TF32). The gradient at the initial state is ill-conditioned at this
+     configuration: it grows about 2x per backward step (|gx0| ~ 2e4 from a loss gradient of ~1e-5), so a relative
+     perturbation of 1e-6 of x0 moves the oracle's own gx0 by ~1e-2. gx0 is held to the oracle's own sensitivity (at
+     most twice the change that perturbation makes, and 1e-3 if that is smaller);
+   - pinned (the oracle's backward chain evaluated on the GPU's own forward states, from the oracle's loss gradient
+     at the GPU's final state): gx0, dw1, db1 and dw2 within 1e-3 relative. This separates the kernels' backward from
+     the chaotic sensitivity of the trajectory.
+   The error of the states grows with the step count; the test prints it per step.
+2. One backward step at the benchmark's shape (K = 32, B = 2, 128 x 128: one launch of 148 CTAs whose cost-balanced
+   row bands cross image and NCA boundaries) against the oracle, for both instances of the row kernel (the caller's x
+   written by the previous kernel, and x declared stable, the instance the training graph replays).
+
+Reference: ncaops/testing/test_nca.py:111-149 (gradients vs the eager math, rollout == repeated steps), the
+north-star's parity clause (states, losses and gradients within 1e-3 relative for TF32).
+"""
+import ctypes
+
+import pytest
+import torch
+
+from oracle import nca_oracle as O
+
+pytestmark = pytest.mark.gpu
+DEV = 'cuda'
+TOL = 1e-3
+
+
+def oracle_backward_chain(states, w1, b1, w2, masks, target):
+    """The synthetic loss at states[-1] and its gradient, then the oracle's TF32 backward chained through the steps in
+    reverse (step_backward per step, evaluated at the given states). Returns (per-NCA loss, (gx0, dw1, db1, dw2))."""
+    xT = states[-1].detach().clone().requires_grad_()
+    obj, per = O.synthetic_loss(xT, target)
+    (g,) = torch.autograd.grad(obj, xT)
+    dw1, db1, dw2 = torch.zeros_like(w1), torch.zeros_like(b1), torch.zeros_like(w2)
+    for i in reversed(range(len(masks))):
+        g, a, b, c = O.step_backward(states[i], w1, b1, w2, masks[i], g, tf32=True)
+        dw1 += a
+        db1 += b
+        dw2 += c
+    return per, (g, dw1, db1, dw2)
+
+
+def oracle_rollout_grads(x0, w1, b1, w2, target, steps, seed, rate):
+    """The oracle's TF32-emulating rollout (reference_step per step, masks of step_seed(seed, i)), the synthetic loss
+    and the backward chained through the steps. Returns (states [steps + 1], per-NCA loss, (gx0, dw1, db1, dw2))."""
+    K, B, C, H, W = x0.shape
+    masks = oracle_masks(K, B, H, W, steps, seed, rate)
+    states = [x0]
+    for i in range(steps):
+        states.append(O.reference_step(states[-1], w1, b1, w2, masks[i], tf32=True))
+    per, grads = oracle_backward_chain(states, w1, b1, w2, masks, target)
+    return states, per, grads
+
+
+def oracle_masks(K, B, H, W, steps, seed, rate):
+    return [O.mask_for(K, B, H, W, O.step_seed(seed, i), rate) for i in range(steps)]
+
+
+GRADS = ('gx0', 'dw1', 'db1', 'dw2')
+
+
+@pytest.fixture(scope='module')
+def config0():
+    """Configuration 0's inputs, the oracle's rollout of them and the oracle's own sensitivity of its gradients to a
+    1e-6 relative perturbation of x0 (computed once for both GPU paths)."""
+    K, B, C, HID, H, W, steps, rate, seed = 1, 2, 12, 96, 128, 128, 32, 0.5, 2024
+    x0, w1, b1, w2, target = O.make_config_inputs(K, B, C, HID, H, W, seed=0)
+    ref = oracle_rollout_grads(x0, w1, b1, w2, target, steps, seed, rate)
+    x0p = x0 * (1 + 1e-6 * torch.randn(x0.shape, generator=torch.Generator().manual_seed(1)))
+    pert = oracle_rollout_grads(x0p, w1, b1, w2, target, steps, seed, rate)
+    sens = {n: O.rel(a, b) for n, a, b in zip(GRADS, pert[2], ref[2])}
+    print('\noracle sensitivity to a 1e-6 relative perturbation of x0: ' +
+          ', '.join(f'{n} {e:.1e}' for n, e in sens.items()))
+    return dict(x0=x0, w1=w1, b1=b1, w2=w2, target=target, steps=steps, rate=rate, seed=seed, ref=ref, sens=sens,
+                masks=oracle_masks(K, B, H, W, steps, seed, rate))
+
+
+def check_rollout(states, loss, grads, c, label):
+    ref_states, ref_loss, ref_grads = c['ref']
+    errs = [O.rel(a.cpu(), b) for a, b in zip(states, ref_states)]
+    print(f'\n{label}: state rel err by step ' + ' '.join(f'{e:.1e}' for e in errs))
+    gerr = {n: O.rel(a.cpu(), b) for a, b, n in zip(grads, ref_grads, GRADS)}
+    lerr = O.rel(loss.cpu(), ref_loss)
+    print(f'{label}: end to end: loss rel err {lerr:.1e}; gradients ' +
+          ', '.join(f'{n} {e:.1e}' for n, e in gerr.items()))
+    assert max(errs) < TOL, errs
+    assert lerr < TOL, lerr
+    for n in ('dw1', 'db1', 'dw2'):
+        assert gerr[n] < TOL, (n, gerr[n])
+    assert gerr['gx0'] < max(TOL, 2 * c['sens']['gx0']), (gerr['gx0'], c['sens']['gx0'])
+    # pinned: the oracle's backward on the GPU's own trajectory
+    cpu_states = [s.detach().cpu() for s in states]
+    _, pinned = oracle_backward_chain(cpu_states, c['w1'], c['b1'], c['w2'], c['masks'], c['target'])
+    perr = {n: O.rel(a.cpu(), b) for a, b, n in zip(grads, pinned, GRADS)}
+    print(f'{label}: pinned to the GPU states: gradients ' + ', '.join(f'{n} {e:.1e}' for n, e in perr.items()))
+    for n, e in perr.items():
+        assert e < TOL, (n, e)
+
+
+def test_config0_rollout_through_the_operator_under_autograd(config0):
+    """train.py's call pattern: nca_ops.step per step under autograd, the loss's gradient pushed through _Step."""
+    from ultranca_b200 import nca_ops, training
+    c = config0
+    w = [t.to(DEV).requires_grad_() for t in (c['w1'], c['b1'], c['w2'])]
+    x0 = c['x0'].to(DEV).requires_grad_()
+    states = [x0]
+    for i in range(c['steps']):
+        states.append(nca_ops.step(states[-1], *w, c['rate'], seed=nca_ops.step_seed(c['seed'], i)))
+    loss, gy = training.synthetic_loss(states[-1].detach(), c['target'].to(DEV))
+    grads = torch.autograd.grad(states[-1], [x0] + w, gy)
+    torch.cuda.synchronize()
+    check_rollout([s.detach() for s in states], loss, grads, c, 'nca_ops.step + autograd')
+
+
+def test_config0_rollout_through_the_rollout_trainer(config0):
+    """The training path the benchmark replays: RolloutTrainer's forward steps, the fused loss kernel, the backward
+    steps adding their partials (x declared stable) and one reduction at the end."""
+    from ultranca_b200 import training
+    c = config0
+    w1, b1, w2 = (t.to(DEV).contiguous() for t in (c['w1'], c['b1'], c['w2']))
+    B, H, W = c['x0'].shape[1], c['x0'].shape[3], c['x0'].shape[4]
+    t = training.RolloutTrainer(w1, b1, w2, B, H, W, c['steps'], c['rate'])
+    t.states[0].copy_(c['x0'].to(DEV))
+    t.forward_steps(c['seed'])
+    training.synthetic_loss(t.states[c['steps']], c['target'].to(DEV), t.overflow_weight, t.gy[0], t.loss, t.loss_work)
+    gx0 = t.backward_steps(c['seed'], t.gy[0], reduce=True)
+    torch.cuda.synchronize()
+    check_rollout(list(t.states), t.loss, (gx0, *t.grads), c, 'RolloutTrainer')
+
+
+@pytest.mark.parametrize('x_stable', [False, True])
+def test_backward_step_at_the_benchmark_shape(x_stable):
+    """K = 32, B = 2, 128 x 128 in one launch (148 CTAs over cost-balanced bands that cross image and NCA boundaries,
+    the weight-gradient accumulator flushed at every NCA switch) vs the oracle's TF32 backward, no pixel masked."""
+    from ultranca_b200 import nca_ops
+    from ultranca_b200._lib import check, lib, ptr
+    K, B, C, HID, H, W, rate, seed = 32, 2, 12, 96, 128, 128, 0.5, 777
+    N = K * B
+    info = nca_ops.launch_info(C, HID, False, N, H, W, K)
+    assert info['rows_path'] == 1 and info['bwd_grid'] == info['sms']
+    x, w1, b1, w2, _ = O.make_config_inputs(K, B, C, HID, H, W, seed=3)
+    gy = torch.randn(x.shape, generator=torch.Generator().manual_seed(4)) * 1e-3
+    mask = O.mask_for(K, B, H, W, seed, rate)
+    ref = O.step_backward(x, w1, b1, w2, mask, gy, tf32=True)
+    xd, gyd, w1d, b1d, w2d = (t.to(DEV).contiguous() for t in (x, gy, w1, b1, w2))
+    dpf, pf, _ = nca_ops.backward_workspace(C, HID, False, N, H, W, K, rate, False)
+    dp, partial = torch.empty(dpf, device=DEV), torch.empty(pf, device=DEV)
+    out = [torch.full_like(t, float('nan')) for t in (xd, w1d, b1d, w2d)]
+    stages = 1 | 2 | 4 | (16 if x_stable else 0)  # main, adjoint, reduce (+ x stable)
+    st = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    check(lib.nca_backward_stages(ptr(xd), ptr(gyd), None, ptr(w1d), ptr(b1d), ptr(w2d), *map(ptr, out), ptr(dp), dpf,
+                                  ptr(partial), pf, N, C, H, W, K, HID, B, seed, rate, 0, 0, 0, 0, stages, st))
+    torch.cuda.synchronize()
+    code = ctypes.c_int()
+    assert lib.nca_device_error(ctypes.byref(code), 1) == 0 and code.value == 0
+    for a, b, name in zip(out, ref, ('gx', 'dw1', 'db1', 'dw2')):
+        e = O.rel(a.cpu(), b)
+        print(f'x_stable={x_stable} {name}: rel err {e:.1e}')
+        assert e < TOL, (name, e)

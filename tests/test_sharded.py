@@ -10,7 +10,7 @@ import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
 
-from ultranca_b200.sharded import ControlChannel, shard_range
+from ultranca_b200.sharded import ControlChannel, RolloutLengths, shard_range
 
 
 def free_port():
@@ -41,6 +41,22 @@ def _worker(rank, world, port, out, mode):
             k0, k1 = shard_range(8, world, rank)
             losses = torch.arange(k0, k1, dtype=torch.float32) * 10
             out[rank] = (seq, ch.gather_losses(losses).tolist())
+        elif mode == 'uneven':
+            # K = 7 over 2 ranks: shards of 3 and 4 NCAs; the gather pads to 4 and trims
+            K = 7
+            ch = ControlChannel((32, 96), seed=123, K=K)
+            k0, k1 = shard_range(K, world, rank)
+            first = ch.gather_losses(torch.arange(k0, k1, dtype=torch.float32) + 0.5).tolist()
+            second = ch.gather_losses(torch.arange(k0, k1, dtype=torch.float32) * -2).tolist()
+            try:  # a rank whose loss count contradicts its shard is refused before the collective
+                ch.gather_losses(torch.zeros(k1 - k0 + 1))
+                refused = False
+            except ValueError:
+                refused = True
+            out[rank] = (first, second, refused)
+        elif mode == 'lengths':
+            rl = RolloutLengths((32, 96), seed=9)
+            out[rank] = [rl.next() for _ in range(6)]
         elif mode == 'dead_peer':
             if rank == 1:
                 return  # leaves without joining the broadcast
@@ -51,7 +67,7 @@ def _worker(rank, world, port, out, mode):
             except Exception as e:  # the collective must fail, not hang
                 out[rank] = f'error: {type(e).__name__}'
     finally:
-        if mode == 'control':
+        if mode in ('control', 'uneven', 'lengths'):
             dist.destroy_process_group()
 
 
@@ -82,3 +98,20 @@ def test_control_broadcast_and_loss_gather():
 def test_dead_peer_fails_fast():
     out = _run('dead_peer')
     assert out[0].startswith('error'), out
+
+
+def test_uneven_shards_gather_in_nca_order():
+    """K not divisible by the world size (7 NCAs on 2 ranks): every rank receives all 7 losses in NCA order, twice in
+    a row (no stale padding), and a loss count that contradicts the rank's shard is refused."""
+    out = _run('uneven')
+    for r in (0, 1):
+        first, second, refused = out[r]
+        assert first == [k + 0.5 for k in range(7)]
+        assert second == [-2.0 * k for k in range(7)]
+        assert refused
+
+
+def test_rollout_lengths_identical_on_every_rank():
+    out = _run('lengths')
+    assert out[0] == out[1]
+    assert all(32 <= n < 96 for n in out[0]) and len(set(out[0])) > 1

@@ -29,24 +29,34 @@ def inputs(K, B, H, W, seed):
     return [t.cuda() for t in (x, gy, w1, b1, w2)]
 
 
-def with_workspace(lib, P, x, gy, w1, b1, w2, K, B, seed, rate, st):
+def outputs(x, w1, b1, w2, init):
+    """gx (never read by either entry point) and the weight gradients; init: values the weight gradients start from
+    (accumulate = 1 adds to them), or None."""
+    gx = torch.full_like(x, float('nan'))
+    grads = [torch.full_like(t, float('nan')) if init is None else i.clone() for t, i in
+             zip((w1, b1, w2), init if init is not None else (None,) * 3)]
+    return [gx] + grads
+
+
+def with_workspace(lib, P, x, gy, w1, b1, w2, K, B, seed, rate, st, offset=0, init=None):
     N, C, H, W = x.shape
     HID = w1.shape[1]
     dpf, pf, ch = ctypes.c_int64(), ctypes.c_int64(), ctypes.c_int64()
     assert lib.nca_backward_workspace(C, HID, 0, N, H, W, K, rate, 0, ctypes.byref(dpf), ctypes.byref(pf),
                                       ctypes.byref(ch)) == 0
     dp, partial = torch.empty(dpf.value, device='cuda'), torch.empty(pf.value, device='cuda')
-    out = [torch.empty_like(t) for t in (x, w1, b1, w2)]
+    out = outputs(x, w1, b1, w2, init)
     assert lib.nca_backward(P(x), P(gy), None, P(w1), P(b1), P(w2), *map(P, out), P(dp), dpf.value, P(partial),
-                            pf.value, N, C, H, W, K, HID, B, seed, rate, 0, 0, 0, 0, st) == 0, lib.nca_last_error()
+                            pf.value, N, C, H, W, K, HID, B, seed, rate, 0, 0, offset, int(init is not None),
+                            st) == 0, lib.nca_last_error()
     return out
 
 
-def static_scratch(lib, P, x, gy, w1, b1, w2, K, B, seed, rate, st):
+def static_scratch(lib, P, x, gy, w1, b1, w2, K, B, seed, rate, st, offset=0, init=None):
     N, C, H, W = x.shape
-    out = [torch.full_like(t, float('nan')) for t in (x, w1, b1, w2)]
+    out = outputs(x, w1, b1, w2, init)
     assert lib.nca_backward_static_scratch(P(x), P(gy), P(w1), P(b1), P(w2), *map(P, out), N, C, H, W, K, w1.shape[1],
-                                           B, seed, rate, 0, 0, st) == 0, lib.nca_last_error()
+                                           B, seed, rate, offset, int(init is not None), st) == 0, lib.nca_last_error()
     return out
 
 
@@ -62,6 +72,33 @@ def test_static_scratch_backward_matches_workspace_backward_twice():
         for a, b, name in zip(got, ref, ('gx', 'dw1', 'db1', 'dw2')):
             assert torch.isfinite(a).all(), (name, (K, B, H, W))
             assert rel(a, b) < TOL, (name, (K, B, H, W), rel(a, b))
+
+
+def test_static_scratch_backward_accumulates_and_follows_the_shard_offset():
+    """accumulate = 1 adds the step's weight gradients to the values the outputs hold (the autograd accumulation of a
+    rollout), and a nonzero image offset (a shard of a multi-GPU job) selects the shard's update masks: both as the
+    workspace backward does, with outputs pre-filled with the same values on both paths."""
+    from ultranca_b200._lib import lib, ptr as P
+    st = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    K, B, H, W, seed, rate, offset = 3, 2, 40, 64, 12345, 0.5, 6
+    x, gy, w1, b1, w2 = inputs(K, B, H, W, seed)
+    g = torch.Generator().manual_seed(5)
+    init = [torch.randn(t.shape, generator=g).cuda() for t in (w1, b1, w2)]
+    for off, acc in ((offset, None), (offset, init), (0, init)):
+        ref = with_workspace(lib, P, x, gy, w1, b1, w2, K, B, seed, rate, st, off, acc)
+        got = static_scratch(lib, P, x, gy, w1, b1, w2, K, B, seed, rate, st, off, acc)
+        torch.cuda.synchronize()
+        for a, b, name in zip(got, ref, ('gx', 'dw1', 'db1', 'dw2')):
+            assert torch.isfinite(a).all(), (name, off, acc is not None)
+            assert rel(a, b) < TOL, (name, off, acc is not None, rel(a, b))
+    # the offset changes the masks (the case above is not the unsharded one) and accumulation adds the init values
+    plain = with_workspace(lib, P, x, gy, w1, b1, w2, K, B, seed, rate, st, 0, None)
+    shifted = with_workspace(lib, P, x, gy, w1, b1, w2, K, B, seed, rate, st, offset, None)
+    added = with_workspace(lib, P, x, gy, w1, b1, w2, K, B, seed, rate, st, 0, init)
+    torch.cuda.synchronize()
+    assert not torch.equal(plain[0], shifted[0])
+    for a, b, i in zip(added[1:], plain[1:], init):
+        assert rel(a - i, b) < 1e-5
 
 
 def test_static_scratch_backward_rejects_what_it_cannot_hold():

@@ -42,12 +42,15 @@ SIGNATURES = {
     'nca_update_mask': (c_int, [c_f32p, c_i64, c_i64, c_i64, c_u64, c_float, c_i64, c_vp]),
     'nca_synthetic_loss': (c_int, [c_f32p, c_f32p, c_f32p, c_f32p, c_f32p, c_i64, c_i64, c_i64, c_i64, c_i64, c_float,
                                    c_vp]),
+    'nca_task_loss': (c_int, [c_f32p, c_f32p, c_f32p, c_f32p, c_f32p, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64,
+                              c_float, c_vp]),
     'nca_adam_step': (c_int, [c_f32p, c_f32p, c_f32p, c_f32p, c_f32p, c_f32p, c_f32p, c_f32p, c_f32p, c_f32p, c_f32p,
                               c_f32p, c_i64, c_i64, c_i64, c_i64, c_vp, c_float, c_float, c_float, c_float, c_float,
                               ctypes.POINTER(c_i64), c_int, c_vp]),
     'nca_launch_info': (c_int, [c_i64, c_i64, c_int, c_int, c_i64, c_i64, c_i64, c_i64, ctypes.POINTER(ctypes.c_int32)]),
     'nca_device_error': (c_int, [ctypes.POINTER(c_int), c_int]),
     'nca_umma_selftest': (c_int, [c_int, c_int, c_int, c_f32p, c_f32p, c_f32p, c_vp]),
+    'nca_wait_selftest': (c_int, [c_i64, c_vp, c_vp]),
     'nca_forward_dseed': (c_int, [c_f32p, c_f32p, c_f32p, c_f32p, c_f32p, c_f32p, c_u8p, c_i64, c_i64, c_i64, c_i64,
                                   c_i64, c_i64, c_u32, c_vp, c_i64, c_float, c_int, c_int, c_i64, c_vp]),
     'nca_backward_stages_dseed': (c_int, [c_f32p, c_f32p, c_u8p, c_f32p, c_f32p, c_f32p, c_f32p, c_f32p, c_f32p,

@@ -76,12 +76,16 @@ def load_state_dict(trainer, sd, pool=None):
     mine = [int(opt.milestones[i]) for i in range(opt.n_milestones)]
     if list(sd['milestones']) != mine or float(sd['lr']) != float(opt.lr) or float(sd['gamma']) != float(opt.gamma):
         raise ValueError('checkpoint schedule (lr, gamma, milestones) differs from the trainer\'s')
+    for name, mine_t in (('m', opt.m), ('v', opt.v)):
+        if len(sd[name]) != len(mine_t):
+            raise ValueError(f'checkpoint holds {len(sd[name])} Adam {name} tensors, the trainer {len(mine_t)}')
+    pairs = [(trainer.w1, sd['w1']), (trainer.b1, sd['b1']), (trainer.w2, sd['w2'])]
+    pairs += list(zip(opt.m + opt.v, list(sd['m']) + list(sd['v'])))
+    for dst, src in pairs:  # every shape checked before anything is overwritten
+        if dst.shape != src.shape:
+            raise ValueError(f'checkpoint shape {tuple(src.shape)} != trainer shape {tuple(dst.shape)}')
     with torch.no_grad():
-        for dst, src in ((trainer.w1, sd['w1']), (trainer.b1, sd['b1']), (trainer.w2, sd['w2'])):
-            if dst.shape != src.shape:
-                raise ValueError(f'checkpoint shape {tuple(src.shape)} != trainer shape {tuple(dst.shape)}')
-            dst.copy_(src)
-        for dst, src in zip(opt.m + opt.v, list(sd['m']) + list(sd['v'])):
+        for dst, src in pairs:
             dst.copy_(src)
         opt.iteration.copy_(sd['iteration'])
         if pool is not None and 'pool' in sd:

@@ -18,18 +18,21 @@ __global__ void mask_kernel(float *__restrict__ mask, int64_t N, int H, int W, u
 }
 
 // ---------------------------------------------------------------- synthetic loss
-// Block (chunk, k) sums a fixed slice of NCA k's elements (fixed order: strided per thread, then a tree), writes
-// gy for the slice; loss_final sums the chunks of each NCA in order.
+// Per NCA k: mean over (B, TC, H, W) of (x[:, :TC] - target_k)^2 plus overflow_weight * sum over (B, C, H, W) of
+// |x - clamp(x, -1, 1)|, and its gradient gy. TC = 3 with overflow: the texture configurations (the OT loss replaced
+// by an L2 to a synthetic target, train.py:67-72); TC = 4 without: the growing NCA's loss, L2 to a premultiplied RGBA
+// target (train.py:97-99). Block (chunk, k) sums a fixed slice of NCA k's elements (fixed order: strided per thread,
+// then a tree), writes gy for the slice; loss_final sums the chunks of each NCA in order.
 constexpr int LOSS_CHUNKS = 64;
 
 __global__ void __launch_bounds__(256) loss_kernel(const float *__restrict__ x, const float *__restrict__ target,
                                                    float *__restrict__ gy, float *__restrict__ work, int B, int C, int H,
-                                                   int W, float overflow_weight)
+                                                   int W, int TC, float overflow_weight)
 {
     const int k = blockIdx.y, chunk = blockIdx.x;
     const int64_t plane = (int64_t)H * W, per = (int64_t)B * C * plane;
     const int64_t lo = per * chunk / LOSS_CHUNKS, hi = per * (chunk + 1) / LOSS_CHUNKS;
-    const float inv = 1.f / (float)((int64_t)B * 3 * plane);
+    const float inv = 1.f / (float)((int64_t)B * TC * plane);
     const float *xk = x + (int64_t)k * per;
     float *gk = gy + (int64_t)k * per;
     float l2 = 0.f, of = 0.f;
@@ -37,8 +40,8 @@ __global__ void __launch_bounds__(256) loss_kernel(const float *__restrict__ x, 
         const int64_t pix = i % plane, c = (i / plane) % C;
         const float v = xk[i];
         float g = 0.f;
-        if (c < 3) {
-            const float d = v - target[((int64_t)k * 3 + c) * plane + pix];
+        if (c < TC) {
+            const float d = v - target[((int64_t)k * TC + c) * plane + pix];
             l2 = fmaf(d, d, l2);
             g = 2.f * d * inv;
         }

@@ -711,20 +711,28 @@ int nca_update_mask(float *mask, int64_t n, int64_t h, int64_t w, uint64_t seed,
     });
 }
 
-int nca_synthetic_loss(const float *x, const float *target, float *gy, float *loss, float *work, int64_t K, int64_t B,
-                       int64_t C, int64_t H, int64_t W, float overflow_weight, void *stream)
+int nca_task_loss(const float *x, const float *target, float *gy, float *loss, float *work, int64_t K, int64_t B,
+                  int64_t C, int64_t H, int64_t W, int64_t target_channels, float overflow_weight, void *stream)
 {
     return guarded([&] {
         check_ptr(x, "x"); check_ptr(target, "target"); check_ptr(gy, "gy"); check_ptr(loss, "loss"); check_ptr(work, "work");
-        if (K <= 0 || B <= 0 || C < 3 || H <= 0 || W <= 0)
-            fail(NCA_ERR_SHAPE, "loss sizes must be positive with at least 3 channels");
+        if (K <= 0 || B <= 0 || H <= 0 || W <= 0 || target_channels < 1 || C < target_channels)
+            fail(NCA_ERR_SHAPE, "loss sizes must be positive with 1 <= target_channels <= C (got C=%lld, target "
+                 "channels %lld)", (long long)C, (long long)target_channels);
         const auto st = static_cast<cudaStream_t>(stream);
         loss_kernel<<<dim3(LOSS_CHUNKS, (unsigned)K), 256, 0, st>>>(x, target, gy, work, (int)B, (int)C, (int)H, (int)W,
-                                                                   overflow_weight);
+                                                                   (int)target_channels, overflow_weight);
         CUDA_OK(cudaGetLastError());
-        loss_final_kernel<<<(unsigned)((K + 127) / 128), 128, 0, st>>>(work, loss, (int)K, B * 3 * H * W, overflow_weight);
+        loss_final_kernel<<<(unsigned)((K + 127) / 128), 128, 0, st>>>(work, loss, (int)K, B * target_channels * H * W,
+                                                                      overflow_weight);
         CUDA_OK(cudaGetLastError());
     });
+}
+
+int nca_synthetic_loss(const float *x, const float *target, float *gy, float *loss, float *work, int64_t K, int64_t B,
+                       int64_t C, int64_t H, int64_t W, float overflow_weight, void *stream)
+{
+    return nca_task_loss(x, target, gy, loss, work, K, B, C, H, W, 3, overflow_weight, stream);
 }
 
 int nca_adam_step(float *param0, float *param1, float *param2, const float *grad0, const float *grad1, const float *grad2,
@@ -852,6 +860,17 @@ int nca_umma_selftest(int form, int N, int K, const float *A, const float *B, fl
         const size_t smem = 2 * 128 * 128 * sizeof(float) + 1024 + 16;
         set_smem_once(umma_selftest_kernel, smem);
         umma_selftest_kernel<<<1, 128, smem, static_cast<cudaStream_t>(stream)>>>(form, N, K, A, B, D);
+        CUDA_OK(cudaGetLastError());
+    });
+}
+
+int nca_wait_selftest(int64_t limit_ns, unsigned long long *out, void *stream)
+{
+    return guarded([&] {
+        if (limit_ns <= 0 || limit_ns > 1000000000ll)
+            fail(NCA_ERR_ARGUMENT, "wait self-test limit must be in (0, 1 s], got %lld ns", (long long)limit_ns);
+        check_ptr(out, "out");
+        wait_selftest_kernel<<<1, 64, 0, static_cast<cudaStream_t>(stream)>>>((uint64_t)limit_ns, out);
         CUDA_OK(cudaGetLastError());
     });
 }

@@ -122,7 +122,8 @@ __device__ __forceinline__ void mbar_arrive(uint64_t *bar)
 // its own 2 s limit runs out: after a failure every warp keeps its loop and barrier sequence (so no named barrier is
 // left short of a participant) while its remaining waits return at once. A phase that has already completed is
 // reported as completed before abort is read (one shared load fewer on the common path).
-__device__ __forceinline__ bool wait_bar(uint64_t *bar, uint32_t parity, volatile uint32_t *abort)
+__device__ __forceinline__ bool wait_bar(uint64_t *bar, uint32_t parity, volatile uint32_t *abort,
+                                         uint64_t limit_ns = 2000000000ull)
 {
     if (umma::mbar_try_wait(bar, parity))
         return true;
@@ -137,11 +138,54 @@ __device__ __forceinline__ bool wait_bar(uint64_t *bar, uint32_t parity, volatil
             return false;
         uint64_t t;
         asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-        if (t - t0 > 2000000000ull) {
+        if (t - t0 > limit_ns) {
             *abort = 1;
             return false;
         }
     }
+}
+
+// Failure-detection self-test of the bounded waits (one CTA of 64 threads): warp 0 holds a Tensor Memory allocation and
+// waits on an mbarrier that nothing arrives on, with a limit of limit_ns; warp 1 waits on the same barrier with the
+// kernels' 2 s limit and must return as soon as warp 0 has given up (the abort word). Both then take the kernels'
+// teardown: Tensor Memory freed, the device error word set (code 1). out[0] / out[2]: nanoseconds warp 0 / warp 1
+// waited; out[1] / out[3]: 1 if the wait of warp 0 / warp 1 reported success (it must not).
+__global__ void __launch_bounds__(64, 1) wait_selftest_kernel(uint64_t limit_ns, unsigned long long *out)
+{
+    __shared__ uint64_t never;
+    __shared__ uint32_t tslot;
+    __shared__ uint32_t abort_word;
+    volatile uint32_t *abort = &abort_word;
+    const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+    if (threadIdx.x == 0) {
+        umma::mbar_init(&never, 1);
+        *abort = 0;
+        umma::fence_mbar_init();
+    }
+    if (warp == 0) {
+        umma::tmem_alloc(&tslot, 32);
+        umma::tmem_relinquish();
+    }
+    umma::fence_before_sync();
+    __syncthreads();
+    umma::fence_after_sync();
+    uint64_t t0, t1;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+    bool ok = true;
+    if (lane == 0)
+        ok = warp == 0 ? wait_bar(&never, 0, abort, limit_ns) : wait_bar(&never, 0, abort);
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t1));
+    if (lane == 0) {
+        out[2 * warp] = t1 - t0;
+        out[2 * warp + 1] = ok ? 1ull : 0ull;
+    }
+    umma::fence_before_sync();
+    __syncthreads();
+    umma::fence_after_sync();
+    if (warp == 0)
+        umma::tmem_dealloc(tslot, 32);
+    if (*abort && threadIdx.x == 0)
+        set_device_error(1);
 }
 
 // Update mask of one image row (global image index n, row Y, W <= 128, W % 4 == 0) by one warp as 128 bits in four

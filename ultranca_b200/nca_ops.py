@@ -100,7 +100,11 @@ def _backward(x, gy, alive, w1, b1, w2, update_rate, seed, fp32, growing, image_
         dw1, db1, dw2, acc = torch.empty_like(w1), torch.empty_like(b1), torch.empty_like(w2), 0
     else:
         (dw1, db1, dw2), acc = grads, 1
-    gy = gy.contiguous()
+    _check('gy', gy, 5, dtype=gy.dtype)
+    if gy.shape != x.shape or gy.device != x.device:
+        raise RuntimeError(f'gy must have the shape and device of x {tuple(x.shape)} on {x.device}, got '
+                           f'{tuple(gy.shape)} on {gy.device}')
+    gy = gy.float().contiguous()  # an upstream gradient in another precision (e.g. under autocast) is read as fp32
     with torch.cuda.device(x.device):
         check(lib.nca_backward(ptr(x), ptr(gy), ptr(alive) if growing else None, ptr(w1), ptr(b1), ptr(w2), ptr(gx),
                                ptr(dw1), ptr(db1), ptr(dw2), ptr(dp), dp_floats, ptr(partial), partial_floats, N, C, H, W,

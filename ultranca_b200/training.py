@@ -44,14 +44,17 @@ def _timed(timers, kind, launch, on=True):
 
 
 def synthetic_loss(x, target, overflow_weight=10.0, gy=None, loss=None, work=None):
-    """x (K, B, C, H, W), target (K, 3, H, W) -> (loss (K,), gy = d sum(loss) / dx), deterministic."""
+    """x (K, B, C, H, W), target (K, TC, H, W) -> (loss (K,), gy = d sum(loss) / dx), deterministic: per NCA the mean
+    squared error of channels 0 .. TC-1 to the target + overflow_weight x the summed overflow |x - clamp(x, -1, 1)|.
+    TC = 3 with overflow_weight = 10: the texture configurations; TC = 4 with overflow_weight = 0: the growing NCA's
+    L2 to a premultiplied RGBA target (train.py:97-99)."""
     K, B, C, H, W = x.shape
     gy = torch.empty_like(x) if gy is None else gy
     loss = torch.empty(K, device=x.device) if loss is None else loss
     work = torch.empty(K * LOSS_CHUNKS * 2, device=x.device) if work is None else work
     with torch.cuda.device(x.device):
-        check(lib.nca_synthetic_loss(ptr(x), ptr(target), ptr(gy), ptr(loss), ptr(work), K, B, C, H, W,
-                                     float(overflow_weight), _stream(x.device)))
+        check(lib.nca_task_loss(ptr(x), ptr(target), ptr(gy), ptr(loss), ptr(work), K, B, C, H, W, target.shape[1],
+                                float(overflow_weight), _stream(x.device)))
     return loss, gy
 
 
