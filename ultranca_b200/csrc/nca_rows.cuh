@@ -464,25 +464,34 @@ __global__ void __launch_bounds__(128 * NPART + 96, 1) fwd_rows_kernel(StepArgs 
             set_device_error(2);
         return;
     }
+    // Set-up, in two phases whose parts run on different warps (this set-up is the part of a step a launch cannot hide
+    // under the previous step's tail on the SMs that previous step frees last):
+    //   1. warp 0 allocates the Tensor Memory; warps 1.. draw the update masks of the CTA's rows;
+    //   2. warp 0 builds the tile table; warps 1.. stage the first NCA's weights.
+    const int nrows = (int)(g1 - g0);  // <= MAXROWS / S (the host sizes the grid so)
+    const int64_t n0 = g0 / H;         // the band's first image and row
+    const int r0 = (int)(g0 - n0 * H), nw = blockDim.x / 32;
     if (warp == 0) {
         umma::tmem_alloc(tslot, F::TMEM);
         umma::tmem_relinquish();
-    }
-    // update masks of the CTA's rows (g1 - g0 <= MAXROWS: the host sizes the grid so)
-    const uint64_t seed = step_seed_of(a);
-    if (!STRIP) {
-        for (int64_t u = g0 + warp; u < g1; u += blockDim.x / 32)
-            row_mask_xorder_warp(MKX + (u - g0) * 4, seed, a.rate, u / H + a.n_offset, H, W, (int)(u % H), lane32);
     } else {
-        // pass-major: row u of the segment [lo, hi) (CTA-relative) at strip s is mask row S lo + s (hi - lo) + u - lo
-        for (int64_t u = g0 + warp; u < g1; u += blockDim.x / 32) {
-            const int64_t img = u / H, lo = max(g0, img * H) - g0, hi = min(g1, (img + 1) * H) - g0;
-            for (int s = 0; s < S; ++s)
-                row_mask_xorder_strip_warp(MKX + (S * lo + s * (hi - lo) + (u - g0 - lo)) * 4, seed, a.rate,
-                                           img + a.n_offset, H, W, (int)(u % H), lane32, 128 * s);
+        const uint64_t seed = step_seed_of(a);
+        for (int rel = warp - 1; rel < nrows; rel += nw - 1) {
+            const int yy = r0 + rel, dn = yy / H, Y = yy - dn * H;
+            if (!STRIP) {
+                row_mask_xorder_warp(MKX + (size_t)rel * 4, seed, a.rate, n0 + dn + a.n_offset, H, W, Y, lane32);
+            } else {
+                // pass-major: row rel of the segment [lo, hi) (CTA-relative) at strip s is mask row S lo + s (hi - lo) +
+                // rel - lo
+                const int lo = max(0, dn * H - r0), hi = min(nrows, (dn + 1) * H - r0);
+                for (int s = 0; s < S; ++s)
+                    row_mask_xorder_strip_warp(MKX + (size_t)(S * lo + s * (hi - lo) + (rel - lo)) * 4, seed, a.rate,
+                                               n0 + dn + a.n_offset, H, W, Y, lane32, 128 * s);
+            }
         }
     }
     __syncthreads();
+    int cur_k = -1;
     if (warp == 0) {  // tile table: per segment (pass), the prefix counts of its rows, then tiles of <= 128 pixels,
         int64_t g = g0;  // <= SPAN rows
         RowSeg sg;
@@ -510,29 +519,64 @@ __global__ void __launch_bounds__(128 * NPART + 96, 1) fwd_rows_kernel(StepArgs 
                 run += __shfl_sync(~0u, inc, 31);
             }
             __syncwarp();
-            // greedy tiles, warp-parallel: lanes hold the prefix counts of a 64-row window [wb, wb + 64) (rows past
-            // the segment: Q); the row holding queue position p is the last row whose prefix count is <= p
             const int Q = run;
-            auto cx = [&](int jj) { return jj < L ? CUM[u0 + jj] : Q; };
-            int wb = 0, cw0 = cx(lane32), cw1 = cx(32 + lane32);
-            auto row_of = [&](int p) {
-                const uint32_t b0 = __ballot_sync(~0u, cw0 <= p), b1 = __ballot_sync(~0u, cw1 <= p);
-                return wb + (b1 ? 63 - __clz(b1) : 31 - __clz(b0));
-            };
-            int q = 0;
-            while (q < Q) {
-                while (__shfl_sync(~0u, cw1, 0) <= q) {  // the tile's first row is past the window's first half
-                    wb += 32;
-                    cw0 = cw1;
-                    cw1 = cx(wb + 32 + lane32);
+            // The tiles are the greedy cut of the queue: from q, up to 128 pixels, ending before the pixels of row
+            // j(q) + SPAN, where j(p) is the row holding queue position p (the last row whose prefix count is <= p).
+            // Usually no tile is cut short by the SPAN rule, and then the tiles are the fixed cut q = 128 t: every lane
+            // builds one fixed tile (binary searches in the prefix counts) and checks the rule; only a segment where
+            // some tile would be cut short takes the sequential greedy pass, which rewrites its entries.
+            auto row_bs = [&](int p) {
+                int lo = 0, hi = L - 1;
+                while (lo < hi) {
+                    const int mid = (lo + hi + 1) >> 1;
+                    if (CUM[u0 + mid] <= p)
+                        lo = mid;
+                    else
+                        hi = mid - 1;
                 }
-                const int j = row_of(q);  // in [wb, wb + 32): the tile's rows stay inside the window
-                const int lim = __shfl_sync(~0u, j + F::SPAN - wb < 32 ? cw0 : cw1, (j + F::SPAN - wb) & 31);
-                const int end = min(q + 128, lim), jh = row_of(end - 1);
-                if (lane32 == 0)
-                    TILE[nt] = make_int2(q, (end - q) | (j << 8) | (jh << 20));
-                ++nt;
-                q = end;
+                return lo;
+            };
+            const int TF = (Q + 127) / 128;
+            bool fixed = true;
+            for (int t0 = 0; t0 < TF; t0 += 32) {
+                const int t = t0 + lane32;
+                bool fits = true;
+                if (t < TF) {
+                    const int q = 128 * t, end = min(q + 128, Q);
+                    const int j = row_bs(q), jh = row_bs(end - 1);
+                    const int lim = j + F::SPAN < L ? CUM[u0 + j + F::SPAN] : Q;
+                    fits = lim >= end;
+                    TILE[nt + t] = make_int2(q, (end - q) | (j << 8) | (jh << 20));
+                }
+                fixed &= __all_sync(~0u, fits);
+            }
+            if (fixed) {
+                nt += TF;
+            } else {
+                // greedy tiles, warp-parallel: lanes hold the prefix counts of a 64-row window [wb, wb + 64) (rows past
+                // the segment: Q)
+                auto cx = [&](int jj) { return jj < L ? CUM[u0 + jj] : Q; };
+                int wb = 0, cw0 = cx(lane32), cw1 = cx(32 + lane32);
+                auto row_of = [&](int p) {
+                    const uint32_t b0 = __ballot_sync(~0u, cw0 <= p), b1 = __ballot_sync(~0u, cw1 <= p);
+                    return wb + (b1 ? 63 - __clz(b1) : 31 - __clz(b0));
+                };
+                int q = 0;
+                while (q < Q) {
+                    while (__shfl_sync(~0u, cw1, 0) <= q) {  // the tile's first row is past the window's first half
+                        wb += 32;
+                        cw0 = cw1;
+                        cw1 = cx(wb + 32 + lane32);
+                    }
+                    const int j = row_of(q);  // in [wb, wb + 32): the tile's rows stay inside the window
+                    const int lim = __shfl_sync(~0u, j + F::SPAN - wb < 32 ? cw0 : cw1, (j + F::SPAN - wb) & 31);
+                    const int end = min(q + 128, lim), jh = row_of(end - 1);
+                    __syncwarp();
+                    if (lane32 == 0)
+                        TILE[nt] = make_int2(q, (end - q) | (j << 8) | (jh << 20));
+                    ++nt;
+                    q = end;
+                }
             }
             if (lane32 == 0)
                 SEGT[s] = nt;
@@ -540,7 +584,14 @@ __global__ void __launch_bounds__(128 * NPART + 96, 1) fwd_rows_kernel(StepArgs 
             ++s;
             u0 += L;
         }
+    } else if (nrows > 0) {  // the first segment's NCA: its weights, by warps 1..
+        const int k = (int)(n0 / a.B);
+        stage_rows_weights<D, false>(W1s, nullptr, W2s, a.w1 + (size_t)k * HID * D::PIN, a.b1 + (size_t)k * HID,
+                                     a.w2 + (size_t)k * C * HID, tid - 32, blockDim.x - 32, 0);
+        umma::fence_proxy_async();
     }
+    if (nrows > 0)
+        cur_k = (int)(n0 / a.B);
     const uint32_t tmem = *tslot, lane = umma::tmem_addr(tmem, warp, 0);
     if (compute && part == 0) {  // p' columns past the channel features: bias-hi, bias-lo = 1, zeros (never overwritten)
         const float v[8] = {1.f, 1.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
@@ -558,7 +609,7 @@ __global__ void __launch_bounds__(128 * NPART + 96, 1) fwd_rows_kernel(StepArgs 
     constexpr int JM = STRIP ? 0xFFF : 0x3FF;  // row fields of a tile entry
     bool ok = true;
     uint32_t epar = 0, g1par = 0, g2par = 0, eph = 0, fepar = 0;  // *par: one parity bit per buffer / ring slot
-    int cur_k = -1, x_uses[F::XRING] = {0, 0, 0, 0, 0, 0, 0, 0};
+    int x_uses[F::XRING] = {0, 0, 0, 0, 0, 0, 0, 0};
     uint64_t *last_bar = nullptr;
     uint32_t last_par = 0;
     auto wait_par = [&](uint64_t *bars, uint32_t &par, int bj) {  // the next phase of bars[bj]
