@@ -29,6 +29,7 @@ value: cell-updates (K B H W steps, all ranks) per second of the timed iteration
 e2e:   the same metric through the public operator API (nca_ops.step under autograd + fused Adam, or nca_ops.rollout)
        with the batch copied host -> device from pinned memory and the result (losses, or the final states) copied
        back every step inside the timed region.
+--fp32: the accuracy mode (nca_ops.step(..., fp32=True), which train.py selects with tf32: false) instead of TF32.
 --impl reference: the reference's eager PyTorch step (its CPU restatement in oracle/, fp32, all host threads) on a
        bounded sample of the same workload; rank 0 prints its own JSON line, no GPU is used.
 """
@@ -77,6 +78,8 @@ def parse():
     ap.add_argument('--no-cpu', action='store_true')
     ap.add_argument('--no-ref-kernels', action='store_true')
     ap.add_argument('--no-extra', action='store_true', help='skip the configurations 2 and 3 of the default run')
+    ap.add_argument('--fp32', action='store_true', help="the reference's fp32=True accuracy mode (here: the MLP in "
+                    'fp32 on CUDA cores) instead of TF32 tensor cores')
     return ap.parse_args()
 
 
@@ -332,7 +335,7 @@ def launches_per_iteration(cfg, steps, rows_path, growing):
     return 1 + 2 + steps * fwd + 2 + steps * bwd + 1 + 1 + 1
 
 
-def measure_train(cfg, cid, ctx, steps_timed, warmup, rate, e2e=True, cpu=True, ref_kernels=False):
+def measure_train(cfg, cid, ctx, steps_timed, warmup, rate, e2e=True, cpu=True, ref_kernels=False, fp32=False):
     """One configuration's training iteration at one update rate: the JSON fields of its line."""
     from ultranca_b200 import nca_ops, sharded
     K_total, k0, Kr = shard_of(cfg, ctx)
@@ -340,7 +343,8 @@ def measure_train(cfg, cid, ctx, steps_timed, warmup, rate, e2e=True, cpu=True, 
     w1, b1, w2, target, pool = train_inputs(cfg, ctx, k0, Kr)
     job = sharded.ShardedPoolTrainer(w1, b1, w2, pool, target, B, H, W, S, K_total, rollout=(S, S + 1),
                                      key=KEY, inject_every=16, seed_kind=cfg['seed_kind'], timed=TIMER_STRIDE,
-                                     update_rate=rate, growing=cfg['growing'], overflow_weight=cfg['overflow'])
+                                     update_rate=rate, growing=cfg['growing'], overflow_weight=cfg['overflow'],
+                                     fp32=fp32)
     stream = torch.cuda.current_stream(ctx.dev)
     for _ in range(warmup):  # the first iteration launches directly, the graph is recorded at the second
         job.iteration()
@@ -359,7 +363,7 @@ def measure_train(cfg, cid, ctx, steps_timed, warmup, rate, e2e=True, cpu=True, 
     stage_times = job.loop.kernel_times()
     cells_per_iter = K_total * B * H * W * S
     value = cells_per_iter * steps_timed / (ms / 1000.0)
-    info = nca_ops.launch_info(C, HID, False, Kr * B, H, W, Kr, growing=cfg['growing'])
+    info = nca_ops.launch_info(C, HID, fp32, Kr * B, H, W, Kr, growing=cfg['growing'])
     rows = info['rows_path'] if not cfg['growing'] else 0
     # the dominant kernel (the larger mean of the sampled forward and backward launches)
     mean = {k: statistics.mean(v) for k, v in stage_times.items()}
@@ -370,12 +374,14 @@ def measure_train(cfg, cid, ctx, steps_timed, warmup, rate, e2e=True, cpu=True, 
     # (16 channels): forward 128 B + 1 B alive map; backward x, gy in, gx out 192 B + 1 B alive map
     if cfg['growing']:
         alg_per_cell = {'fwd': 129, 'bwd': 193}[dom]
+    elif fp32:  # the tile path: forward x in, y out; backward main x, gy in + dp out, adjoint dp, gy in, gx out
+        alg_per_cell = {'fwd': 96, 'bwd': 96}[dom]
     else:
         alg_per_cell = {'fwd': 96, 'bwd': 144 if rows else 96}[dom]
     cells = Kr * B * H * W
     achieved = cells * alg_per_cell / (avg_ms / 1000.0) / 1e9
     traffic = None
-    if cid == 1 and not cfg['growing']:
+    if cid == 1 and not cfg['growing'] and not fp32:
         try:  # per-launch DRAM bytes of one ncu capture of the benchmark's kernels (profiles/traffic.json)
             tr = json.load(open(os.path.join(ROOT, 'profiles', 'traffic.json')))
             traffic = tr.get({'fwd': 'fwd_rows_kernel', 'bwd': 'bwd_rows_kernel_x_stable'}[dom])
@@ -391,6 +397,8 @@ def measure_train(cfg, cid, ctx, steps_timed, warmup, rate, e2e=True, cpu=True, 
     kname = {'fwd': {1: 'fwd_rows_kernel<12,96,2>', 2: 'fwd_rows_kernel<12,96,2,strip>', 0: 'fwd_kernel'},
              'bwd': {1: 'bwd_rows_kernel<12,96,4,x_stable>', 2: 'bwd_rows_kernel<12,96,4,x_stable,strip>',
                      0: 'bwd_kernel_tc + adjoint_kernel'}}[dom][rows]
+    if fp32:
+        kname = {'fwd': 'fwd_kernel<12,96,fp32>', 'bwd': 'bwd_kernel_cc<12,96> + adjoint_kernel'}[dom]
     roofline = {'bound': 'hbm', 'achieved': achieved, 'peak': ctx.hbm, 'unit': 'GB/s', 'frac': achieved / ctx.hbm,
                 'traffic': traffic, 'kernel': kname, 'algorithmic_bytes_per_launch': cells * alg_per_cell,
                 'avg_launch_ms': avg_ms, 'timed_launches': {k: len(v) for k, v in stage_times.items()},
@@ -415,7 +423,7 @@ def measure_train(cfg, cid, ctx, steps_timed, warmup, rate, e2e=True, cpu=True, 
            'launch': info, 'losses_finite': bool(torch.isfinite(job.trainer.loss).all().item())}
     del job
     if e2e:
-        out['e2e'] = run_e2e_train(cfg, ctx, K_total, k0, Kr, w1, b1, w2, target, rate, steps_timed, warmup)
+        out['e2e'] = run_e2e_train(cfg, ctx, K_total, k0, Kr, w1, b1, w2, target, rate, steps_timed, warmup, fp32)
     if cpu and ctx.rank == 0 and ctx.world == 1:
         out['cpu_baseline'] = cpu_baseline(cfg)
     if ref_kernels and ctx.rank == 0 and ctx.world == 1:
@@ -424,7 +432,7 @@ def measure_train(cfg, cid, ctx, steps_timed, warmup, rate, e2e=True, cpu=True, 
     return out
 
 
-def run_e2e_train(cfg, ctx, K_total, k0, Kr, w1, b1, w2, target, rate, steps_timed, warmup):
+def run_e2e_train(cfg, ctx, K_total, k0, Kr, w1, b1, w2, target, rate, steps_timed, warmup, fp32=False):
     """The training iteration as train.py runs it on the drop-in operator: nca_ops.step per step under autograd,
     backward through _Step, the fused optimiser; batch H2D from pinned host memory, losses D2H, every iteration. The
     batch of iteration i + 1 is copied on a side stream while iteration i computes (two device buffers; a buffer is
@@ -464,7 +472,7 @@ def run_e2e_train(cfg, ctx, K_total, k0, Kr, w1, b1, w2, target, rate, steps_tim
         stream.wait_event(ready[b])
         x = dbuf[b]
         for s in range(S):
-            x = nca_ops.step(x, *ws, rate, cfg['growing'], seed=1000 * i + s, image_offset=k0 * B)
+            x = nca_ops.step(x, *ws, rate, cfg['growing'], fp32, seed=1000 * i + s, image_offset=k0 * B)
         loss, gy = training.synthetic_loss(x.detach(), target, cfg['overflow'])
         x.backward(gy)
         opt.step([w.grad for w in ws])
@@ -630,8 +638,10 @@ def measure(cid, ctx, steps_timed, warmup, args, main=True):
     cfg = CONFIGS[cid]
     if cfg['kind'] == 'infer':
         return measure_infer(cfg, cid, ctx, steps_timed, warmup, e2e=not args.no_e2e, cpu=not args.no_cpu)
+    fp32 = bool(getattr(args, 'fp32', False)) and main
     out = measure_train(cfg, cid, ctx, steps_timed, warmup, cfg['rates'][0], e2e=not args.no_e2e,
-                        cpu=not args.no_cpu, ref_kernels=main and cid == 1 and not args.no_ref_kernels)
+                        cpu=not args.no_cpu and not fp32, ref_kernels=main and cid == 1 and not args.no_ref_kernels
+                        and not fp32, fp32=fp32)
     for rate in cfg['rates'][1:]:  # further update rates (configuration 2): value, time, roofline and clocks
         r = measure_train(cfg, cid, ctx, steps_timed, warmup, rate, e2e=False, cpu=False)
         out[f'rate_{rate}'] = {k: r[k] for k in ('value', 'ms_per_step', 'roofline', 'clocks', 'gpu_launches')}
@@ -647,7 +657,7 @@ def main():
     ctx = Ctx()
     res = measure(args.config, ctx, args.steps, args.warmup, args)
     extra = {}
-    if args.config == 1 and not args.no_extra:
+    if args.config == 1 and not args.no_extra and not args.fp32:
         # configurations 2 and 3 with fewer iterations, outside the line's own timed region
         for cid, (n, w) in ((2, (3, 3)), (3, (3, 3))):
             r = measure(cid, ctx, n, w, args, main=False)
@@ -657,7 +667,8 @@ def main():
     if ctx.rank == 0:
         line = {'metric': metric_of(cfg), 'value': res['value'], 'unit': UNIT, 'n_gpus': ctx.world,
                 'steps': args.steps, 'warmup': args.warmup, 'ms_per_step': res['ms_per_step'],
-                'higher_is_better': True, 'scaling': cfg['scaling'], 'vs_baseline': None, 'dtype': 'tf32',
+                'higher_is_better': True, 'scaling': cfg['scaling'], 'vs_baseline': None,
+                'dtype': 'fp32' if args.fp32 else 'tf32',
                 'data': 'synthetic', 'config': config_dict(cfg, args.config, ctx.world)}
         line.update({k: v for k, v in res.items() if k not in ('value', 'ms_per_step')})
         line.setdefault('cpu_baseline', None)
