@@ -167,6 +167,18 @@ struct TileCoord {
     int n, k, y0, x0;
 };
 
+// Block-wide OR (blocks of 128 threads, every thread calls it) of a 32-bit word; sw: 4 words of shared memory.
+__device__ __forceinline__ uint32_t block_or_128(uint32_t v, uint32_t *sw)
+{
+    v = __reduce_or_sync(~0u, v);
+    if ((threadIdx.x & 31) == 0)
+        sw[threadIdx.x >> 5] = v;
+    __syncthreads();
+    const uint32_t r = sw[0] | sw[1] | sw[2] | sw[3];
+    __syncthreads();  // sw is reused by the next call
+    return r;
+}
+
 __device__ __forceinline__ TileCoord tile_coord(int64_t t, const TileGeom &g, int B)
 {
     TileCoord tc;
@@ -186,32 +198,48 @@ __device__ __forceinline__ TileCoord tile_coord(int64_t t, const TileGeom &g, in
 // the tile is dead before the step (3x3 max-pool of x_alpha <= 0.1), so the alive mask is 0 on the tile whatever the
 // update computes (the alive pass then writes y = 0 there), and the post-step alpha of the tile's cells only enters
 // the pooling of cells that are dead already: the tile's MLP can be skipped without changing any output.
-// XS: the tile's halo copy (one pixel, circular: its out-of-grid positions are skipped here); hr, hc: the row and column
-// in the halo copy of this thread's positions threadIdx.x + 128 i (hr < 0: none; blocks of 128 threads, and
-// (R + 2)(S + 2) <= 390 positions). The ring at distance two is read from global memory only when the halo holds no
-// live alpha.
+// The liveness of 32 consecutive tiles [t, t + 32) (tiles >= t1 count as dead) in one pass, one bit per tile: every
+// thread reads its share of each tile's (R + 4) x (S + 4) window of x_alpha (no wrap), all of them in flight together,
+// then a block-wide OR; every thread of the block calls it. Deciding one tile at a time cost a memory latency per tile,
+// which dominated growing steps where most tiles are dead.
 template <int C>
-__device__ __forceinline__ bool tile_live_before(const StepArgs &a, const TileCoord &tc, const TileGeom &g,
-                                                 const float *XS, const int (&hr)[4], const int (&hc)[4])
+__device__ __forceinline__ uint32_t tiles_live_before(const StepArgs &a, const TileGeom &g, int64_t t, int64_t t1,
+                                                      uint32_t *sw)
 {
-    const float *xs = XS + 3 * (g.R + 2) * (g.S + 2);  // the alpha channel of the halo copy
-    bool live = false;
+    // window positions threadIdx.x + 128 q, q < 6 ((R + 4)(S + 4) <= 660 for R S <= 128): their offsets are the same
+    // for every tile, so they are computed once
+    const int RO = g.R + 4, SO = g.S + 4, WIN = RO * SO;
+    int dr[6], dc[6];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        const int Y = tc.y0 - 1 + hr[i], X = tc.x0 - 1 + hc[i];
-        live |= hr[i] >= 0 && Y >= 0 && Y < a.H && X >= 0 && X < a.W && xs[threadIdx.x + 128 * i] > 0.1f;
+    for (int q = 0; q < 6; ++q) {
+        const int e = threadIdx.x + 128 * q;
+        dr[q] = e < WIN ? e / SO - 2 : -1000000;
+        dc[q] = e < WIN ? e % SO - 2 : 0;
     }
-    if (__syncthreads_or(live))
-        return true;
-    const int RO = g.R + 4, SO = g.S + 4;
-    const float *xa = a.x + ((size_t)tc.n * C + 3) * (size_t)a.H * a.W;
-    for (int e = threadIdx.x; e < RO * SO; e += blockDim.x) {
-        const int rr = e / SO, ss = e - rr * SO, Y = tc.y0 - 2 + rr, X = tc.x0 - 2 + ss;
-        const bool ring = rr == 0 || rr == RO - 1 || ss == 0 || ss == SO - 1;
-        if (ring && Y >= 0 && Y < a.H && X >= 0 && X < a.W)
-            live |= __ldg(xa + (size_t)Y * a.W + X) > 0.1f;
+    uint32_t mine = 0;
+    for (int i0 = 0; i0 < 32; i0 += 8) {  // 8 tiles x 6 positions in flight per round
+        float v[8][6];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const bool tile_ok = t + i0 + i < t1;
+            const TileCoord tc = tile_coord(tile_ok ? t + i0 + i : t, g, a.B);
+            const float *xa = a.x + ((size_t)tc.n * C + 3) * (size_t)a.H * a.W;
+#pragma unroll
+            for (int q = 0; q < 6; ++q) {
+                const int Y = tc.y0 + dr[q], X = tc.x0 + dc[q];
+                v[i][q] = tile_ok && Y >= 0 && Y < a.H && X >= 0 && X < a.W ? __ldg(xa + (size_t)Y * a.W + X) : 0.f;
+            }
+        }
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            bool live = false;
+#pragma unroll
+            for (int q = 0; q < 6; ++q)
+                live |= v[i][q] > 0.1f;
+            mine |= live ? 1u << (i0 + i) : 0u;
+        }
     }
-    return __syncthreads_or(live) != 0;
+    return block_or_128(mine, sw);
 }
 
 // Growing NCAs, backward: a tile with no pixel alive after its forward step has gm = gy m a = 0 throughout, so it adds
@@ -244,13 +272,9 @@ __global__ void __launch_bounds__(128, 1) fwd_kernel(StepArgs a)
     cta_range(T, gridDim.x, blockIdx.x, &t0, &t1);
     const bool stoch = a.rate < 1.f;
     const size_t plane = (size_t)a.H * a.W;
-    int hr[4], hc[4];  // growing: this thread's positions in the halo copy (row, column; row < 0: none)
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        const int e = tid + 128 * i, ss = g.S + 2;
-        hr[i] = GROWING && e < (g.R + 2) * ss ? e / ss : -1;
-        hc[i] = e - (hr[i] < 0 ? 0 : hr[i]) * ss;
-    }
+    __shared__ uint32_t sw[4];
+    uint32_t live_bits = 0;  // growing: liveness of tiles [live_base, live_base + 32)
+    int64_t live_base = t0 - 64;
 
     uint32_t tmem = 0;
     if constexpr (TC) {
@@ -272,7 +296,20 @@ __global__ void __launch_bounds__(128, 1) fwd_kernel(StepArgs a)
     bool failed = false;
     for (int64_t t = t0; t < t1 && !failed; ++t) {
         const TileCoord tc = tile_coord(t, g, a.B);
-        if (tc.k != cur_k) {
+        const int r = tid / g.S, s = tid - r * g.S;
+        const bool valid = tid < g.R * g.S && tc.y0 + r < a.H && tc.x0 + s < a.W;
+        if (GROWING) {  // dead tile (block-uniform): no MLP, no halo copy; the alive pass zeroes y
+            if (t >= live_base + 32) {
+                live_base = t;
+                live_bits = tiles_live_before<C>(a, g, t, t1, sw);
+            }
+            if (!((live_bits >> (t - live_base)) & 1u)) {
+                if (valid)
+                    a.alpha[(size_t)tc.n * plane + (size_t)(tc.y0 + r) * a.W + tc.x0 + s] = 0.f;
+                continue;
+            }
+        }
+        if (tc.k != cur_k) {  // staged at the NCA's first live tile
             stage_weights<D, TC>(W1s, W2s, a.w1 + (size_t)tc.k * HID * D::PIN, a.b1 + (size_t)tc.k * HID,
                                  a.w2 + (size_t)tc.k * C * HID);
             cur_k = tc.k;
@@ -280,14 +317,6 @@ __global__ void __launch_bounds__(128, 1) fwd_kernel(StepArgs a)
         load_halo_async<D>(XS, a.x, tc.n, g, tc.y0, tc.x0);
         cp_async_wait_all();
         __syncthreads();
-        const int r = tid / g.S, s = tid - r * g.S;
-        const bool valid = tid < g.R * g.S && tc.y0 + r < a.H && tc.x0 + s < a.W;
-        // dead tile: no MLP (the alive pass zeroes y); the check's closing barrier follows its last read of XS
-        if (GROWING && !tile_live_before<C>(a, tc, g, XS, hr, hc)) {
-            if (valid)
-                a.alpha[(size_t)tc.n * plane + (size_t)(tc.y0 + r) * a.W + tc.x0 + s] = 0.f;
-            continue;
-        }
         perceive_tile<D, TC>(P, XS, g, tid, valid);
         float u[16];
         if constexpr (TC) {
@@ -520,23 +549,35 @@ __global__ void __launch_bounds__(128, 1) bwd_kernel_cc(StepArgs a)
             acc2[c] = 0.f;
         accb = 0.f;
     };
-    bool alive_next = GROWING && t0 < t1 && pixel_alive(a, g, t0);  // growing: this pixel of the next tile
+    __shared__ uint32_t sw[4];
+    uint32_t live_bits = 0;  // growing: whether tiles [live_base, live_base + 32) hold an alive pixel
+    int64_t live_base = t0 - 64;
+    bool staged = false;
     for (int64_t t = t0; t < t1; ++t) {
         const TileCoord tc = tile_coord(t, g, a.B);
         if (tc.k != cur_k) {
             if (cur_k >= 0)
                 flush(cur_k);
             __syncthreads();
+            cur_k = tc.k;
+            staged = false;
+        }
+        if (GROWING) {  // dead tile (block-uniform): nothing to add, its dp is not read
+            if (t >= live_base + 32) {  // the alive bytes of 32 tiles' pixels, all loads in flight together
+                live_base = t;
+                uint32_t mine = 0;
+#pragma unroll
+                for (int i = 0; i < 32; ++i)
+                    mine |= t + i < t1 && pixel_alive(a, g, t + i) ? 1u << i : 0u;
+                live_bits = block_or_128(mine, sw);
+            }
+            if (!((live_bits >> (t - live_base)) & 1u))
+                continue;
+        }
+        if (!staged) {  // the NCA's weights, at its first live tile
             stage_weights<D, false>(W1s, W2s, a.w1 + (size_t)tc.k * HID * D::PIN, a.b1 + (size_t)tc.k * HID,
                                     a.w2 + (size_t)tc.k * C * HID);
-            cur_k = tc.k;
-        }
-        if (GROWING) {  // dead tile: nothing to add, its dp is not read
-            const bool here = alive_next;
-            if (t + 1 < t1)
-                alive_next = pixel_alive(a, g, t + 1);
-            if (!__syncthreads_or(here))
-                continue;
+            staged = true;
         }
         load_halo_async<D>(XS, a.x, tc.n, g, tc.y0, tc.x0);
         const int r = tid / g.S, s = tid - r * g.S;
@@ -713,24 +754,36 @@ __global__ void __launch_bounds__(128, 1) bwd_kernel_tc(StepArgs a)
         umma::fence_before_sync();
     };
 
-    bool alive_next = GROWING && t0 < t1 && pixel_alive(a, g, t0);  // growing: this pixel of the next tile
+    __shared__ uint32_t sw[4];
+    uint32_t live_bits = 0;  // growing: whether tiles [live_base, live_base + 32) hold an alive pixel
+    int64_t live_base = t0 - 64;
+    bool staged = false;
     for (int64_t t = t0; t < t1; ++t) {
         const TileCoord tc = tile_coord(t, g, a.B);
         if (tc.k != cur_k) {
             if (cur_k >= 0)
                 flush(cur_k);
             __syncthreads();
-            stage_bwd_weights<D>(W1s, W1T, W2T, a.w1 + (size_t)tc.k * HID * D::PIN, a.b1 + (size_t)tc.k * HID,
-                                 a.w2 + (size_t)tc.k * C * HID);
             cur_k = tc.k;
             started = false;
+            staged = false;
         }
-        if (GROWING) {  // dead tile: nothing to add, its dp is not read
-            const bool here = alive_next;
-            if (t + 1 < t1)
-                alive_next = pixel_alive(a, g, t + 1);
-            if (!__syncthreads_or(here))
+        if (GROWING) {  // dead tile (block-uniform): nothing to add, its dp is not read
+            if (t >= live_base + 32) {  // the alive bytes of 32 tiles' pixels, all loads in flight together
+                live_base = t;
+                uint32_t mine = 0;
+#pragma unroll
+                for (int i = 0; i < 32; ++i)
+                    mine |= t + i < t1 && pixel_alive(a, g, t + i) ? 1u << i : 0u;
+                live_bits = block_or_128(mine, sw);
+            }
+            if (!((live_bits >> (t - live_base)) & 1u))
                 continue;
+        }
+        if (!staged) {  // the NCA's weights, at its first live tile (the flush above needs none)
+            stage_bwd_weights<D>(W1s, W1T, W2T, a.w1 + (size_t)tc.k * HID * D::PIN, a.b1 + (size_t)tc.k * HID,
+                                 a.w2 + (size_t)tc.k * C * HID);
+            staged = true;
         }
         // ---- 1. inputs
         load_halo_async<D>(XS, a.x, tc.n, g, tc.y0, tc.x0);
