@@ -328,7 +328,7 @@ void launch_forward(const float *x, const float *w1, const float *b1, const floa
     dispatch(s.C, s.HID, fp32, growing, [&](auto I) {
         using II = decltype(I);
         using D = Dims<II::C, II::HID>;
-        const TileGeom g = make_geom((int)s.H, (int)s.W);
+        const TileGeom g = make_geom((int)s.H, (int)s.W, II::GROW);
         const int G = grid_for(s.N * g.tiles_per_image, fwd_ctas_per_sm<II>());
         if (II::FP32)
             fwd_kernel<II::C, II::HID, false, II::GROW><<<G, 128, D::fwd_smem(), stream>>>(a);
@@ -355,7 +355,7 @@ BwdWork backward_work(const Shape &s, bool fp32, bool growing)
     dispatch(s.C, s.HID, fp32, growing, [&](auto I) {
         using II = decltype(I);
         using D = Dims<II::C, II::HID>;
-        const TileGeom g = make_geom((int)s.H, (int)s.W);
+        const TileGeom g = make_geom((int)s.H, (int)s.W, II::GROW);
         w.grid = grid_for(s.N * g.tiles_per_image, bwd_ctas_per_sm<II>());
         w.dp_floats = s.N * D::PIN * s.H * s.W;
         int slots = w.grid;
@@ -534,7 +534,7 @@ int backward_stages_impl(const float *x, const float *gy, const uint8_t *alive, 
             a.seed = seed; a.rate = update_rate; a.n_offset = image_offset;
             a.seed_dev = seed_dev; a.step = step;
             a.partial_add = (stages & NCA_STAGE_PARTIAL_ADD) ? 1 : 0;
-            const TileGeom g = make_geom((int)H, (int)W);
+            const TileGeom g = make_geom((int)H, (int)W, II::GROW);
             const bool strip = strip_path(s, fp32, growing) && aligned16(x) && aligned16(gy) && aligned16(gx) &&
                                aligned16(dp);
             const bool rows = strip || (rows_path(s, fp32, growing) && aligned16(x) && aligned16(gy) && aligned16(gx));
@@ -657,7 +657,7 @@ int nca_launch_info(int64_t C, int64_t hidden, int fp32, int growing, int64_t N,
         int fwd_grid = 0, fwd_per = 0;
         dispatch(C, hidden, fp32, growing, [&](auto I) {
             using II = decltype(I);
-            const TileGeom g = make_geom((int)H, (int)W);
+            const TileGeom g = make_geom((int)H, (int)W, II::GROW);
             fwd_per = fwd_ctas_per_sm<II>();
             fwd_grid = grid_for(N * g.tiles_per_image, fwd_per);
         });
@@ -832,7 +832,7 @@ int nca_reduce_adam_step(const float *partial, int64_t partial_floats, int64_t N
             using II = decltype(I);
             // the unit decomposition of the backward launches that wrote the partials (the row kernel when its shape
             // qualifies: those launches had 16-byte-aligned x, gy and gx)
-            const TileGeom g = make_geom((int)H, (int)W);
+            const TileGeom g = make_geom((int)H, (int)W, II::GROW);
             const bool rows = bwd_rows_path(s, fp32, growing);
             const int64_t units = rows ? N * H : N * g.tiles_per_image;
             const int64_t per = rows ? (int64_t)batch_per_nca * H : (int64_t)batch_per_nca * g.tiles_per_image;

@@ -116,17 +116,19 @@ __device__ __forceinline__ int wrap_near(int i, int n)
 
 // ---------------------------------------------------------------- tile geometry
 // A tile is R rows x S columns (R S <= 128) of one image: S = min(W, 128) columns, R = 128 / W rows when W <= 128
-// (else one row of a 128-column strip). Tile pixel i (0..127) is (i / S, i % S); tiles of an image are strips-fastest.
+// (else one row of a 128-column strip). Compact tiles (growing NCAs, W >= 16): 8 rows x 16 columns, so that the tiles
+// around a small living region are few (a growing grid is mostly dead, and dead tiles are skipped). Tile pixel i
+// (0..127) is (i / S, i % S); tiles of an image are strips-fastest.
 struct TileGeom {
     int H, W, S, R, strips, tiles_per_image;
 };
 
-__host__ __device__ inline TileGeom make_geom(int H, int W)
+__host__ __device__ inline TileGeom make_geom(int H, int W, bool compact = false)
 {
     TileGeom g;
     g.H = H; g.W = W;
-    g.S = W <= 128 ? W : 128;
-    g.R = W <= 128 ? 128 / W : 1;
+    g.S = compact && W >= 16 ? 16 : W <= 128 ? W : 128;
+    g.R = compact && W >= 16 ? 8 : W <= 128 ? 128 / W : 1;
     g.strips = (W + g.S - 1) / g.S;
     g.tiles_per_image = g.strips * ((H + g.R - 1) / g.R);
     return g;

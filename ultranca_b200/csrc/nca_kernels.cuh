@@ -266,7 +266,7 @@ __global__ void __launch_bounds__(128, 1) fwd_kernel(StepArgs a)
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bar + 1);
 
     const int tid = threadIdx.x, warp = tid / 32;
-    const TileGeom g = make_geom(a.H, a.W);
+    const TileGeom g = make_geom(a.H, a.W, GROWING);
     const int64_t T = (int64_t)a.N * g.tiles_per_image;
     int64_t t0, t1;
     cta_range(T, gridDim.x, blockIdx.x, &t0, &t1);
@@ -524,7 +524,7 @@ __global__ void __launch_bounds__(128, 1) bwd_kernel_cc(StepArgs a)
     float *XS = RHt;  // the halo tile is dead before RHt is written
 
     const int tid = threadIdx.x;
-    const TileGeom g = make_geom(a.H, a.W);
+    const TileGeom g = make_geom(a.H, a.W, GROWING);
     const int64_t T = (int64_t)a.N * g.tiles_per_image;
     int64_t t0, t1;
     cta_range(T, gridDim.x, blockIdx.x, &t0, &t1);
@@ -695,7 +695,7 @@ __global__ void __launch_bounds__(128, 1) bwd_kernel_tc(StepArgs a)
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bar + 1);
 
     const int tid = threadIdx.x, warp = tid / 32;
-    const TileGeom g = make_geom(a.H, a.W);
+    const TileGeom g = make_geom(a.H, a.W, GROWING);
     const int64_t T = (int64_t)a.N * g.tiles_per_image;
     int64_t t0, t1;
     cta_range(T, gridDim.x, blockIdx.x, &t0, &t1);
