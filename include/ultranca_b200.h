@@ -48,7 +48,9 @@ int nca_forward(const float *x, const float *w1, const float *b1, const float *w
                 uint64_t seed, float update_rate, int fp32, int growing, int64_t image_offset, void *stream);
 
 /* `steps` forward steps from x into y without gradients; step i uses seed nca_step_seed(seed, i); x is not modified;
- * steps = 0 copies x. tmp: workspace like x when steps > 1 (ping-pong). Growing: alpha (N, H, W), alive (N, H, W).
+ * steps = 0 copies x. tmp: workspace like x when steps > 1 (ping-pong). Growing: alpha (N, H, W) and alive
+ * (2N, H, W): one alive map per ping-pong buffer, so that from the third step on only the cells that were alive in
+ * the destination two steps ago or that the forward wrote are visited by the alive pass (the others are 0 there).
  * Replaces nca_cuda.rollout (ncaops/nca_cuda.cu:166-188, bound at :341-344). */
 int nca_rollout(const float *x, const float *w1, const float *b1, const float *w2, float *y, float *tmp, float *alpha,
                 uint8_t *alive, int64_t N, int64_t C, int64_t H, int64_t W, int64_t K, int64_t hidden, uint32_t steps,

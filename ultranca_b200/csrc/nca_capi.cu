@@ -299,11 +299,14 @@ int bwd_rows_grid(const Shape &s)
 }
 
 // seed_dev != nullptr: the kernels read the rollout seed there and derive step `step`'s seed themselves.
+// reuse (growing rollouts from their third step): alive holds this destination's map of two steps ago; the forward
+// marks the cells it writes and the alive pass skips the others (already 0 in the destination).
 void launch_forward(const float *x, const float *w1, const float *b1, const float *w2, float *y, float *alpha,
                     uint8_t *alive, const Shape &s, uint64_t seed, float rate, bool fp32, bool growing, int64_t n_offset,
-                    cudaStream_t stream, const uint64_t *seed_dev = nullptr, int64_t step = 0)
+                    cudaStream_t stream, const uint64_t *seed_dev = nullptr, int64_t step = 0, bool reuse = false)
 {
     StepArgs a{};
+    a.written = reuse ? alive : nullptr;
     a.x = x; a.w1 = w1; a.b1 = b1; a.w2 = w2; a.y = y; a.alpha = alpha;
     a.N = (int)s.N; a.B = (int)s.B; a.H = (int)s.H; a.W = (int)s.W;
     a.seed = seed; a.rate = rate; a.n_offset = n_offset;
@@ -337,7 +340,8 @@ void launch_forward(const float *x, const float *w1, const float *b1, const floa
         CUDA_OK(cudaGetLastError());
         if (II::GROW) {
             const int64_t total = s.N * s.H * s.W;
-            alive_kernel<II::C><<<(unsigned)((total + 255) / 256), 256, 0, stream>>>(x, alpha, y, alive, (int)s.H, (int)s.W, total);
+            alive_kernel<II::C><<<(unsigned)((total + 255) / 256), 256, 0, stream>>>(x, alpha, y, alive, (int)s.H, (int)s.W, total,
+                                                                                    reuse);
             CUDA_OK(cudaGetLastError());
         }
     });
@@ -470,8 +474,10 @@ int nca_rollout(const float *x, const float *w1, const float *b1, const float *w
         const float *src = x;
         for (uint32_t i = 0; i < steps; ++i) {  // ping-pong so that the result ends in y (x is not modified)
             float *dst = (steps - i) % 2 ? y : tmp;
-            launch_forward(src, w1, b1, w2, dst, alpha, alive, s, nca_step_seed(seed, i), update_rate, fp32, growing,
-                           image_offset, st);
+            // growing: one alive map per destination buffer (steps of the same parity write the same buffer)
+            uint8_t *map = growing ? alive + (size_t)(i % 2) * (size_t)(N * H * W) : alive;
+            launch_forward(src, w1, b1, w2, dst, alpha, map, s, nca_step_seed(seed, i), update_rate, fp32, growing,
+                           image_offset, st, nullptr, 0, growing && i >= 2);
             src = dst;
         }
     });

@@ -68,6 +68,7 @@ struct StepArgs {
     const uint64_t *seed_dev;      // non-null: the step's seed is splitmix_step(*seed_dev, step), read at run time
     int64_t step;                  // (a launch recorded once in a CUDA graph and replayed with new rollout seeds)
     int band_s4, band_n4;          // row kernels: switch costs of the cost-balanced bands (Bands)
+    uint8_t *written;              // growing rollout after its first two steps: the forward sets 1 where it writes y
 };
 
 // The row bands of a row-kernel launch of `a` over `G` CTAs.
@@ -400,6 +401,8 @@ __global__ void __launch_bounds__(128, 1) fwd_kernel(StepArgs a)
             const float m = stoch ? update_mask_at(a.seed, a.rate, tc.n + a.n_offset, a.H, a.W, Y, X) : 1.f;
             const int SS = g.S + 2, per = (g.R + 2) * SS;
             float *yn = a.y + (size_t)tc.n * C * plane + (size_t)Y * a.W + X;
+            if (GROWING && a.written != nullptr)
+                a.written[(size_t)tc.n * plane + (size_t)Y * a.W + X] = 1;
 #pragma unroll
             for (int c = 0; c < C; ++c) {
                 const float xc = XS[c * per + (r + 1) * SS + s + 1];
@@ -427,10 +430,14 @@ __global__ void __launch_bounds__(128, 1) fwd_kernel(StepArgs a)
 // padding; y *= a (zeroing the whole cell); alive = a. One thread per pixel.
 template <int C>
 __global__ void alive_kernel(const float *__restrict__ x, const float *__restrict__ alpha, float *__restrict__ y,
-                             uint8_t *__restrict__ alive, int H, int W, int64_t total)
+                             uint8_t *__restrict__ alive, int H, int W, int64_t total, bool reuse)
 {
     const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
-    if (i >= total)
+    // reuse (a rollout's step i >= 2, alive = this destination's map of step i - 2, set to 1 where this step's forward
+    // wrote y): a cell marked 0 was dead in this destination two steps ago (its state there is 0) and was not written
+    // now (no living cell within two pixels before the step: it is dead now too), so there is nothing to do
+    // (the reference's rollout does the same, ncaops/nca_cuda.cu:166-188, nca_step.cuh:695-705)
+    if (i >= total || (reuse && !alive[i]))
         return;
     const int64_t plane = (int64_t)H * W, n = i / plane, pix = i - n * plane;
     const int Y = (int)(pix / W), X = (int)(pix - (int64_t)Y * W);

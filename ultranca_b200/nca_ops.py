@@ -161,7 +161,8 @@ def rollout(x, w1, b1, w2, update_rate, steps, growing=False, fp32=False, seed=N
     tmp = torch.empty(K * B if steps > 1 else 0, C, H, W, device=x.device)
     n = (K * B, H, W) if growing else (0, 0, 0)
     alpha = torch.empty(n, device=x.device)
-    alive = torch.empty(n, dtype=torch.uint8, device=x.device)
+    # growing: one alive map per ping-pong buffer (the reference's (2N, H, W), nca_cuda.cu:166-188)
+    alive = torch.empty((2 * K * B, H, W) if growing else (0, 0, 0), dtype=torch.uint8, device=x.device)
     with torch.cuda.device(x.device):
         check(lib.nca_rollout(ptr(x), ptr(w1), ptr(b1), ptr(w2), ptr(y), ptr(tmp) if steps > 1 else None,
                               ptr(alpha) if growing else None, ptr(alive) if growing else None, K * B, C, H, W, K, HID,
