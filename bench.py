@@ -327,10 +327,12 @@ def train_inputs(cfg, ctx, k0, Kr):
 
 
 def launches_per_iteration(cfg, steps, rows_path, growing):
-    """Kernels of one training iteration: control advance 1, pool sample 2 (draw, gather), per forward step 1 (+1 alive
-    pass when growing), loss 2, per backward step 1 (row kernel) or 2 (tile path: main + adjoint; column strips: main
-    + edge fix-up), fused reduce + Adam 1, iteration counter 1, pool write-back 1."""
-    fwd = 1 + (1 if growing else 0)
+    """Kernels of one training iteration: control advance 1, pool sample 2 (draw, gather), per forward step 1 (the
+    growing alive mask is computed in the forward's epilogue), loss 2, per backward step 1 (row kernel) or 2 (tile
+    path: main + adjoint; column strips: main + edge fix-up), fused reduce + Adam 1, iteration counter 1, pool
+    write-back 1."""
+    del growing
+    fwd = 1
     bwd = 1 if rows_path == 1 else 2
     return 1 + 2 + steps * fwd + 2 + steps * bwd + 1 + 1 + 1
 

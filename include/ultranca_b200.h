@@ -41,16 +41,17 @@ int nca_version(void);
 
 /* One NCA step x -> y.
  * Replaces nca_cuda.forward (ncaops/nca_cuda.cu:147-155, bound at :335-340).
- * x, y: (N, C, H, W); growing: alpha (N, H, W) fp32 workspace and alive (N, H, W) uint8 output (the alive mask the
- * backward needs); both may be NULL when growing = 0. update_rate >= 1: every cell updates. */
+ * x, y: (N, C, H, W); growing: alive (N, H, W) uint8 output (the alive mask the backward needs), computed in the step
+ * kernel's epilogue; alpha is unused (the reference's alpha workspace; may be NULL); alive may be NULL when
+ * growing = 0. update_rate >= 1: every cell updates. */
 int nca_forward(const float *x, const float *w1, const float *b1, const float *w2, float *y, float *alpha, uint8_t *alive,
                 int64_t N, int64_t C, int64_t H, int64_t W, int64_t K, int64_t hidden, uint32_t batch_per_nca,
                 uint64_t seed, float update_rate, int fp32, int growing, int64_t image_offset, void *stream);
 
 /* `steps` forward steps from x into y without gradients; step i uses seed nca_step_seed(seed, i); x is not modified;
- * steps = 0 copies x. tmp: workspace like x when steps > 1 (ping-pong). Growing: alpha (N, H, W) and alive
- * (2N, H, W): one alive map per ping-pong buffer, so that from the third step on only the cells that were alive in
- * the destination two steps ago or that the forward wrote are visited by the alive pass (the others are 0 there).
+ * steps = 0 copies x. tmp: workspace like x when steps > 1 (ping-pong). Growing: alive (2N, H, W): one alive map
+ * per ping-pong buffer, so that from the third step on a dead tile leaves the cells that were dead in the destination
+ * two steps ago untouched (they hold state 0 and alive 0 there); alpha is unused and may be NULL.
  * Replaces nca_cuda.rollout (ncaops/nca_cuda.cu:166-188, bound at :341-344). */
 int nca_rollout(const float *x, const float *w1, const float *b1, const float *w2, float *y, float *tmp, float *alpha,
                 uint8_t *alive, int64_t N, int64_t C, int64_t H, int64_t W, int64_t K, int64_t hidden, uint32_t steps,

@@ -50,7 +50,7 @@ def _forward(**over):
     (dict(C=8, hidden=64, N=4), 3, 'no kernel instantiated'),  # nca_cuda.cu:75
     (dict(growing=1, C=3, hidden=96), 2, 'at least 4 channels'),  # nca_cuda.cu:140-141
     (dict(x=None), 1, 'x must not be null'),
-    (dict(growing=1), 1, 'alpha must not be null'),
+    (dict(growing=1), 1, 'alive must not be null'),  # alpha is unused: the alive mask is computed in the step
     (dict(H=0), 2, 'positive'),
 ])
 def test_forward_validation_errors(over, code, text):

@@ -299,14 +299,16 @@ int bwd_rows_grid(const Shape &s)
 }
 
 // seed_dev != nullptr: the kernels read the rollout seed there and derive step `step`'s seed themselves.
-// reuse (growing rollouts from their third step): alive holds this destination's map of two steps ago; the forward
-// marks the cells it writes and the alive pass skips the others (already 0 in the destination).
+// Growing: the forward computes the alive mask in its epilogue and writes alive (alpha is not used). reuse (growing
+// rollouts from their third step): alive holds this destination's map of two steps ago, and dead tiles skip the cells
+// that were dead there (they already hold state 0 and alive 0).
 void launch_forward(const float *x, const float *w1, const float *b1, const float *w2, float *y, float *alpha,
                     uint8_t *alive, const Shape &s, uint64_t seed, float rate, bool fp32, bool growing, int64_t n_offset,
                     cudaStream_t stream, const uint64_t *seed_dev = nullptr, int64_t step = 0, bool reuse = false)
 {
     StepArgs a{};
-    a.written = reuse ? alive : nullptr;
+    a.alive_out = alive;
+    a.reuse = reuse ? 1 : 0;
     a.x = x; a.w1 = w1; a.b1 = b1; a.w2 = w2; a.y = y; a.alpha = alpha;
     a.N = (int)s.N; a.B = (int)s.B; a.H = (int)s.H; a.W = (int)s.W;
     a.seed = seed; a.rate = rate; a.n_offset = n_offset;
@@ -331,19 +333,13 @@ void launch_forward(const float *x, const float *w1, const float *b1, const floa
     dispatch(s.C, s.HID, fp32, growing, [&](auto I) {
         using II = decltype(I);
         using D = Dims<II::C, II::HID>;
-        const TileGeom g = make_geom((int)s.H, (int)s.W, II::GROW);
+        const TileGeom g = II::GROW ? make_grow_fwd_geom((int)s.H, (int)s.W) : make_geom((int)s.H, (int)s.W);
         const int G = grid_for(s.N * g.tiles_per_image, fwd_ctas_per_sm<II>());
         if (II::FP32)
             fwd_kernel<II::C, II::HID, false, II::GROW><<<G, 128, D::fwd_smem(), stream>>>(a);
         else
             fwd_kernel<II::C, II::HID, true, II::GROW><<<G, 128, D::fwd_smem(), stream>>>(a);
         CUDA_OK(cudaGetLastError());
-        if (II::GROW) {
-            const int64_t total = s.N * s.H * s.W;
-            alive_kernel<II::C><<<(unsigned)((total + 255) / 256), 256, 0, stream>>>(x, alpha, y, alive, (int)s.H, (int)s.W, total,
-                                                                                    reuse);
-            CUDA_OK(cudaGetLastError());
-        }
     });
 }
 
@@ -423,10 +419,8 @@ int nca_forward(const float *x, const float *w1, const float *b1, const float *w
         const Shape s{N, C, H, W, K, hidden, (int64_t)batch_per_nca};
         validate(s, growing);
         check_ptr(x, "x"); check_ptr(w1, "w1"); check_ptr(b1, "b1"); check_ptr(w2, "w2"); check_ptr(y, "y");
-        if (growing) {
-            check_ptr(alpha, "alpha");
-            check_ptr(alive, "alive");
-        }
+        if (growing)
+            check_ptr(alive, "alive");  // alpha: unused (the alive mask is computed in the step's epilogue)
         launch_forward(x, w1, b1, w2, y, alpha, alive, s, seed, update_rate, fp32, growing, image_offset,
                        static_cast<cudaStream_t>(stream));
     });
@@ -444,10 +438,8 @@ int nca_forward_dseed(const float *x, const float *w1, const float *b1, const fl
         check_ptr(seed_dev, "seed_dev");
         if (step < 0)
             fail(NCA_ERR_ARGUMENT, "step must be >= 0");
-        if (growing) {
-            check_ptr(alpha, "alpha");
-            check_ptr(alive, "alive");
-        }
+        if (growing)
+            check_ptr(alive, "alive");  // alpha: unused (the alive mask is computed in the step's epilogue)
         launch_forward(x, w1, b1, w2, y, alpha, alive, s, 0, update_rate, fp32, growing, image_offset,
                        static_cast<cudaStream_t>(stream), seed_dev, step);
     });
@@ -464,10 +456,8 @@ int nca_rollout(const float *x, const float *w1, const float *b1, const float *w
         check_ptr(x, "x"); check_ptr(w1, "w1"); check_ptr(b1, "b1"); check_ptr(w2, "w2"); check_ptr(y, "y");
         if (steps > 1)
             check_ptr(tmp, "tmp");
-        if (growing) {
-            check_ptr(alpha, "alpha");
-            check_ptr(alive, "alive");
-        }
+        if (growing)
+            check_ptr(alive, "alive");  // alpha: unused (the alive mask is computed in the step's epilogue)
         const auto st = static_cast<cudaStream_t>(stream);
         if (steps == 0)
             CUDA_OK(cudaMemcpyAsync(y, x, (size_t)(N * C * H * W) * sizeof(float), cudaMemcpyDeviceToDevice, st));
@@ -663,7 +653,7 @@ int nca_launch_info(int64_t C, int64_t hidden, int fp32, int growing, int64_t N,
         int fwd_grid = 0, fwd_per = 0;
         dispatch(C, hidden, fp32, growing, [&](auto I) {
             using II = decltype(I);
-            const TileGeom g = make_geom((int)H, (int)W, II::GROW);
+            const TileGeom g = II::GROW ? make_grow_fwd_geom((int)H, (int)W) : make_geom((int)H, (int)W);
             fwd_per = fwd_ctas_per_sm<II>();
             fwd_grid = grid_for(N * g.tiles_per_image, fwd_per);
         });

@@ -68,8 +68,28 @@ struct StepArgs {
     const uint64_t *seed_dev;      // non-null: the step's seed is splitmix_step(*seed_dev, step), read at run time
     int64_t step;                  // (a launch recorded once in a CUDA graph and replayed with new rollout seeds)
     int band_s4, band_n4;          // row kernels: switch costs of the cost-balanced bands (Bands)
-    uint8_t *written;              // growing rollout after its first two steps: the forward sets 1 where it writes y
+    uint8_t *alive_out;            // growing forward: the alive mask of the step (N, H, W)
+    int reuse;                     // growing rollout from its third step: alive_out holds this destination's map of two
+                                   // steps ago (cells 0 there hold state 0)
 };
+
+// Growing forward tiles (the alive mask fused into the step): an interior of GI_R x GI_S cells is written; the MLP runs
+// on the interior and its one-cell ring, an extended tile of (GI_R + 2) x (GI_S + 2) = 128 pixels (lane = extended
+// pixel), so that the unmasked new alpha of every cell the interior's 3 x 3 pooling reads is at hand.
+constexpr int GI_R = 6, GI_S = 14, GE_R = GI_R + 2, GE_S = GI_S + 2;
+static_assert(GE_R * GE_S == 128, "extended growing tile");
+
+// Extended-tile geometry of the fused growing forward (R, S: the extended tile; strips and tiles count interiors).
+__host__ __device__ inline TileGeom make_grow_fwd_geom(int H, int W)
+{
+    TileGeom g;
+    g.H = H; g.W = W;
+    g.S = GE_S;
+    g.R = GE_R;
+    g.strips = (W + GI_S - 1) / GI_S;
+    g.tiles_per_image = g.strips * ((H + GI_R - 1) / GI_R);
+    return g;
+}
 
 // The row bands of a row-kernel launch of `a` over `G` CTAs.
 __host__ __device__ inline Bands row_bands(const StepArgs &a, int G)
@@ -192,53 +212,46 @@ __device__ __forceinline__ TileCoord tile_coord(int64_t t, const TileGeom &g, in
 }
 
 // ================================================================ forward
-// One CTA per SM slot, tiles [T c / G, T (c+1) / G). Writes y (growing: the unmasked y and its alpha plane, the alive
-// kernel then masks it).
-// Growing NCAs, active tiles (block-wide, every thread calls it): whether some cell of the grid within two pixels of
-// the tile (no wrap: the alive pooling pads with zeros) has x_alpha > 0.1. If none has, every cell within one pixel of
-// the tile is dead before the step (3x3 max-pool of x_alpha <= 0.1), so the alive mask is 0 on the tile whatever the
-// update computes (the alive pass then writes y = 0 there), and the post-step alpha of the tile's cells only enters
-// the pooling of cells that are dead already: the tile's MLP can be skipped without changing any output.
-// The liveness of 32 consecutive tiles [t, t + 32) (tiles >= t1 count as dead) in one pass, one bit per tile: every
-// thread reads its share of each tile's (R + 4) x (S + 4) window of x_alpha (no wrap), all of them in flight together,
-// then a block-wide OR; every thread of the block calls it. Deciding one tile at a time cost a memory latency per tile,
-// which dominated growing steps where most tiles are dead.
+// One CTA per SM slot, tiles [T c / G, T (c+1) / G). Writes y (growing: masked by the alive mask, which the epilogue
+// computes and writes too).
+// Growing NCAs, active tiles: the liveness of 32 consecutive tiles [t, t + 32) (tiles >= t1 count as dead), one bit per
+// tile: whether some cell within two pixels of the tile's interior (no wrap: the alive pooling pads with zeros) has
+// x_alpha > 0.1. If none has, every cell within one pixel of the interior is dead before the step, so the alive mask
+// is 0 on the whole interior whatever the update computes: the tile writes zeros and runs no MLP. Every thread reads its
+// share of each tile's (GI_R + 4) x (GI_S + 4) window, 8 tiles' worth in flight per round, then a block-wide OR; every
+// thread of the block calls it.
 template <int C>
-__device__ __forceinline__ uint32_t tiles_live_before(const StepArgs &a, const TileGeom &g, int64_t t, int64_t t1,
-                                                      uint32_t *sw)
+__device__ __forceinline__ uint32_t grow_tiles_live(const StepArgs &a, const TileGeom &g, int64_t t, int64_t t1,
+                                                    uint32_t *sw)
 {
-    // window positions threadIdx.x + 128 q, q < 6 ((R + 4)(S + 4) <= 660 for R S <= 128): their offsets are the same
-    // for every tile, so they are computed once
-    const int RO = g.R + 4, SO = g.S + 4, WIN = RO * SO;
-    int dr[6], dc[6];
+    constexpr int SO = GI_S + 4, WIN = (GI_R + 4) * SO;  // 180 positions: threadIdx.x and threadIdx.x + 128
+    int dr[2], dc[2];
 #pragma unroll
-    for (int q = 0; q < 6; ++q) {
+    for (int q = 0; q < 2; ++q) {
         const int e = threadIdx.x + 128 * q;
         dr[q] = e < WIN ? e / SO - 2 : -1000000;
         dc[q] = e < WIN ? e % SO - 2 : 0;
     }
     uint32_t mine = 0;
-    for (int i0 = 0; i0 < 32; i0 += 8) {  // 8 tiles x 6 positions in flight per round
-        float v[8][6];
+    for (int i0 = 0; i0 < 32; i0 += 8) {
+        float v[8][2];
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
-            const bool tile_ok = t + i0 + i < t1;
-            const TileCoord tc = tile_coord(tile_ok ? t + i0 + i : t, g, a.B);
-            const float *xa = a.x + ((size_t)tc.n * C + 3) * (size_t)a.H * a.W;
+            const int64_t u = t + i0 + i;
+            const bool tile_ok = u < t1;
+            const int64_t n = (tile_ok ? u : t) / g.tiles_per_image;
+            const int ti = (int)((tile_ok ? u : t) - n * g.tiles_per_image);
+            const int iy0 = (ti / g.strips) * GI_R, ix0 = (ti % g.strips) * GI_S;
+            const float *xa = a.x + ((size_t)n * C + 3) * (size_t)a.H * a.W;
 #pragma unroll
-            for (int q = 0; q < 6; ++q) {
-                const int Y = tc.y0 + dr[q], X = tc.x0 + dc[q];
+            for (int q = 0; q < 2; ++q) {
+                const int Y = iy0 + dr[q], X = ix0 + dc[q];
                 v[i][q] = tile_ok && Y >= 0 && Y < a.H && X >= 0 && X < a.W ? __ldg(xa + (size_t)Y * a.W + X) : 0.f;
             }
         }
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            bool live = false;
-#pragma unroll
-            for (int q = 0; q < 6; ++q)
-                live |= v[i][q] > 0.1f;
-            mine |= live ? 1u << (i0 + i) : 0u;
-        }
+        for (int i = 0; i < 8; ++i)
+            mine |= v[i][0] > 0.1f || v[i][1] > 0.1f ? 1u << (i0 + i) : 0u;
     }
     return block_or_128(mine, sw);
 }
@@ -267,13 +280,14 @@ __global__ void __launch_bounds__(128, 1) fwd_kernel(StepArgs a)
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bar + 1);
 
     const int tid = threadIdx.x, warp = tid / 32;
-    const TileGeom g = make_geom(a.H, a.W, GROWING);
+    const TileGeom g = GROWING ? make_grow_fwd_geom(a.H, a.W) : make_geom(a.H, a.W);
     const int64_t T = (int64_t)a.N * g.tiles_per_image;
     int64_t t0, t1;
     cta_range(T, gridDim.x, blockIdx.x, &t0, &t1);
     const bool stoch = a.rate < 1.f;
     const size_t plane = (size_t)a.H * a.W;
     __shared__ uint32_t sw[4];
+    __shared__ float XA[GROWING ? 128 : 1], YA[GROWING ? 128 : 1];  // growing: x_alpha and unmasked new alpha per lane
     uint32_t live_bits = 0;  // growing: liveness of tiles [live_base, live_base + 32)
     int64_t live_base = t0 - 64;
 
@@ -296,17 +310,33 @@ __global__ void __launch_bounds__(128, 1) fwd_kernel(StepArgs a)
     int cur_k = -1;
     bool failed = false;
     for (int64_t t = t0; t < t1 && !failed; ++t) {
-        const TileCoord tc = tile_coord(t, g, a.B);
+        TileCoord tc = tile_coord(t, g, a.B);
+        if (GROWING) {  // the extended tile's origin: one cell above and left of the interior
+            const int ti = (int)(t - (int64_t)tc.n * g.tiles_per_image);
+            tc.y0 = (ti / g.strips) * GI_R - 1;
+            tc.x0 = (ti % g.strips) * GI_S - 1;
+        }
         const int r = tid / g.S, s = tid - r * g.S;
-        const bool valid = tid < g.R * g.S && tc.y0 + r < a.H && tc.x0 + s < a.W;
-        if (GROWING) {  // dead tile (block-uniform): no MLP, no halo copy; the alive pass zeroes y
+        const bool valid = GROWING ? tc.y0 + r >= 0 && tc.y0 + r < a.H && tc.x0 + s >= 0 && tc.x0 + s < a.W
+                                   : tid < g.R * g.S && tc.y0 + r < a.H && tc.x0 + s < a.W;
+        // growing: the lane's cell is in the interior (written by this tile)
+        const bool inner = GROWING && valid && r >= 1 && r <= GI_R && s >= 1 && s <= GI_S;
+        const size_t cell = (size_t)tc.n * plane + (size_t)(tc.y0 + r) * a.W + (tc.x0 + s);
+        if (GROWING) {  // dead tile (block-uniform): no MLP, no halo copy; its interior is dead after the step
             if (t >= live_base + 32) {
                 live_base = t;
-                live_bits = tiles_live_before<C>(a, g, t, t1, sw);
+                live_bits = grow_tiles_live<C>(a, g, t, t1, sw);
             }
             if (!((live_bits >> (t - live_base)) & 1u)) {
-                if (valid)
-                    a.alpha[(size_t)tc.n * plane + (size_t)(tc.y0 + r) * a.W + tc.x0 + s] = 0.f;
+                // y = 0 and alive = 0 on the interior; in a rollout's reuse steps a cell dead in this destination two
+                // steps ago already holds both
+                if (inner && (!a.reuse || a.alive_out[cell])) {
+                    float *yn = a.y + (size_t)tc.n * C * plane + (cell - (size_t)tc.n * plane);
+#pragma unroll
+                    for (int c = 0; c < C; ++c)
+                        yn[(size_t)c * plane] = 0.f;
+                    a.alive_out[cell] = 0;
+                }
                 continue;
             }
         }
@@ -396,20 +426,48 @@ __global__ void __launch_bounds__(128, 1) fwd_kernel(StepArgs a)
                 }
             }
         }
-        if (valid) {
+        if (!GROWING && valid) {
             const int Y = tc.y0 + r, X = tc.x0 + s;
             const float m = stoch ? update_mask_at(a.seed, a.rate, tc.n + a.n_offset, a.H, a.W, Y, X) : 1.f;
             const int SS = g.S + 2, per = (g.R + 2) * SS;
             float *yn = a.y + (size_t)tc.n * C * plane + (size_t)Y * a.W + X;
-            if (GROWING && a.written != nullptr)
-                a.written[(size_t)tc.n * plane + (size_t)Y * a.W + X] = 1;
 #pragma unroll
             for (int c = 0; c < C; ++c) {
                 const float xc = XS[c * per + (r + 1) * SS + s + 1];
-                const float v = m != 0.f ? xc + u[c] : xc;
-                yn[(size_t)c * plane] = v;
-                if (GROWING && c == 3)
-                    a.alpha[(size_t)tc.n * plane + (size_t)Y * a.W + X] = v;
+                yn[(size_t)c * plane] = m != 0.f ? xc + u[c] : xc;
+            }
+        }
+        if constexpr (GROWING) {
+            // the alive mask in the epilogue (ncaops/nca_step.cuh:693-727 semantics): a = (maxpool3(x_alpha) > 0.1) &
+            // (maxpool3(unmasked new alpha) > 0.1), cells outside the grid ignored; y = a ? unmasked y : 0
+            const int SS = g.S + 2, per = (g.R + 2) * SS;
+            float yv[C];
+            const float m = valid && stoch ? update_mask_at(a.seed, a.rate, tc.n + a.n_offset, a.H, a.W, tc.y0 + r,
+                                                            tc.x0 + s) : 1.f;
+#pragma unroll
+            for (int c = 0; c < C; ++c) {
+                const float xc = XS[c * per + (r + 1) * SS + s + 1];
+                yv[c] = m != 0.f ? xc + u[c] : xc;
+            }
+            XA[tid] = valid ? XS[3 * per + (r + 1) * SS + s + 1] : -1.f;
+            YA[tid] = valid ? yv[3] : -1.f;
+            __syncthreads();
+            if (inner) {
+                float mx = -1.f, my = -1.f;
+#pragma unroll
+                for (int dy = -1; dy <= 1; ++dy)
+#pragma unroll
+                    for (int dx = -1; dx <= 1; ++dx) {
+                        const int q = (r + dy) * GE_S + (s + dx);
+                        mx = fmaxf(mx, XA[q]);
+                        my = fmaxf(my, YA[q]);
+                    }
+                const bool live = mx > 0.1f && my > 0.1f;
+                float *yn = a.y + (size_t)tc.n * C * plane + (cell - (size_t)tc.n * plane);
+#pragma unroll
+                for (int c = 0; c < C; ++c)
+                    yn[(size_t)c * plane] = live ? yv[c] : 0.f;
+                a.alive_out[cell] = live ? 1 : 0;
             }
         }
         if constexpr (TC)
@@ -424,41 +482,6 @@ __global__ void __launch_bounds__(128, 1) fwd_kernel(StepArgs a)
         if (failed && tid == 0)
             set_device_error(1);
     }
-}
-
-// Growing NCA alive mask (ncaops/nca_step.cuh:693-727): a = (maxpool3(x_alpha) > 0.1) & (maxpool3(alpha) > 0.1), zero
-// padding; y *= a (zeroing the whole cell); alive = a. One thread per pixel.
-template <int C>
-__global__ void alive_kernel(const float *__restrict__ x, const float *__restrict__ alpha, float *__restrict__ y,
-                             uint8_t *__restrict__ alive, int H, int W, int64_t total, bool reuse)
-{
-    const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
-    // reuse (a rollout's step i >= 2, alive = this destination's map of step i - 2, set to 1 where this step's forward
-    // wrote y): a cell marked 0 was dead in this destination two steps ago (its state there is 0) and was not written
-    // now (no living cell within two pixels before the step: it is dead now too), so there is nothing to do
-    // (the reference's rollout does the same, ncaops/nca_cuda.cu:166-188, nca_step.cuh:695-705)
-    if (i >= total || (reuse && !alive[i]))
-        return;
-    const int64_t plane = (int64_t)H * W, n = i / plane, pix = i - n * plane;
-    const int Y = (int)(pix / W), X = (int)(pix - (int64_t)Y * W);
-    const float *xa = x + (n * C + 3) * plane, *ya = alpha + n * plane;
-    float mx = 0.f, my = 0.f;
-#pragma unroll
-    for (int dy = -1; dy <= 1; ++dy)
-#pragma unroll
-        for (int dx = -1; dx <= 1; ++dx) {
-            const int yy = Y + dy, xx = X + dx;
-            if (yy >= 0 && yy < H && xx >= 0 && xx < W) {
-                mx = fmaxf(mx, xa[(int64_t)yy * W + xx]);
-                my = fmaxf(my, ya[(int64_t)yy * W + xx]);
-            }
-        }
-    const bool live = mx > 0.1f && my > 0.1f;
-    alive[i] = live;
-    if (!live)
-#pragma unroll
-        for (int c = 0; c < C; ++c)
-            y[(n * C + c) * plane + pix] = 0.f;
 }
 
 // ================================================================ backward

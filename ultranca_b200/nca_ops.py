@@ -59,11 +59,9 @@ def _forward(x, w1, b1, w2, update_rate, seed, fp32, growing, image_offset=0):
     K, B, C, H, W, HID = _shapes(x, w1, b1, w2)
     y = torch.empty_like(x)
     n = (K * B, H, W) if growing else (0, 0, 0)
-    alpha = torch.empty(n, device=x.device)
     alive = torch.empty(n, dtype=torch.uint8, device=x.device)
     with torch.cuda.device(x.device):
-        check(lib.nca_forward(ptr(x), ptr(w1), ptr(b1), ptr(w2), ptr(y), ptr(alpha) if growing else None,
-                              ptr(alive) if growing else None, K * B, C, H, W, K, HID, B, seed & (2 ** 64 - 1),
+        check(lib.nca_forward(ptr(x), ptr(w1), ptr(b1), ptr(w2), ptr(y), None, ptr(alive) if growing else None, K * B, C, H, W, K, HID, B, seed & (2 ** 64 - 1),
                               float(update_rate), int(bool(fp32)), int(bool(growing)), int(image_offset),
                               _stream(x.device)))
     return y, alive
@@ -159,13 +157,11 @@ def rollout(x, w1, b1, w2, update_rate, steps, growing=False, fp32=False, seed=N
     K, B, C, H, W, HID = _shapes(x, w1, b1, w2)
     y = torch.empty_like(x)
     tmp = torch.empty(K * B if steps > 1 else 0, C, H, W, device=x.device)
-    n = (K * B, H, W) if growing else (0, 0, 0)
-    alpha = torch.empty(n, device=x.device)
     # growing: one alive map per ping-pong buffer (the reference's (2N, H, W), nca_cuda.cu:166-188)
     alive = torch.empty((2 * K * B, H, W) if growing else (0, 0, 0), dtype=torch.uint8, device=x.device)
     with torch.cuda.device(x.device):
         check(lib.nca_rollout(ptr(x), ptr(w1), ptr(b1), ptr(w2), ptr(y), ptr(tmp) if steps > 1 else None,
-                              ptr(alpha) if growing else None, ptr(alive) if growing else None, K * B, C, H, W, K, HID,
+                              None, ptr(alive) if growing else None, K * B, C, H, W, K, HID,
                               int(steps), B, seed & (2 ** 64 - 1), float(update_rate), int(bool(fp32)),
                               int(bool(growing)), int(image_offset), _stream(x.device)))
     return y

@@ -5,7 +5,7 @@ ncaops/testing/profile_one_step.py runs one fwd + bwd step at K = 24, B = 2, 128
     ncu --set full --clock-control none -k regex:bwd_kernel_tc -s 1 -c 1 -o prof python -m ultranca_b200.profile_step
 
 Default: BASELINE configuration 1's step (32 texture NCAs, batch 2, 128 x 128), whose state (50 MB) plus dp scratch
-(201 MB) exceed the L2, so DRAM counters are representative. Launches per step: forward (+ alive when growing),
+(201 MB) exceed the L2, so DRAM counters are representative. Launches per step: forward (growing: with the alive mask),
 backward main, adjoint, reduce; the warm-up step comes first (skip its launches with ncu -s).
 """
 import argparse

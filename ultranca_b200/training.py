@@ -107,7 +107,6 @@ class RolloutTrainer:
         self.loss_work = torch.empty(self.K * LOSS_CHUNKS * 2, device=dev)
         nmap = (steps, self.N, H, W) if growing else (0,)
         self.alive = torch.empty(nmap, dtype=torch.uint8, device=dev)
-        self.alpha = torch.empty((self.N, H, W) if growing else (0,), device=dev)
         self.dp_floats, self.partial_floats, _ = backward_workspace(self.C, self.HID, fp32, self.N, H, W, self.K,
                                                                     update_rate, growing, dev)
         self.dp = torch.empty(self.dp_floats, device=dev)
@@ -123,7 +122,7 @@ class RolloutTrainer:
         for i in range(self.steps if steps is None else steps):
             alive = ptr(self.alive[i]) if self.growing else None
             common = (ptr(s[i]), ptr(self.w1), ptr(self.b1), ptr(self.w2), ptr(s[i + 1]),
-                      ptr(self.alpha) if self.growing else None, alive, self.N, self.C, self.H, self.W, self.K,
+                      None, alive, self.N, self.C, self.H, self.W, self.K,
                       self.HID, self.B)
             tail = (self.rate, int(self.fp32), int(self.growing), self.image_offset, st)
             on = i % timer_stride == timer_stride // 2
