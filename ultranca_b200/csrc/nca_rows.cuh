@@ -372,6 +372,108 @@ __device__ __forceinline__ int nth_pixel(const uint32_t *m, int n)
     return 32 * w + nth_set_bit(m[w], n);
 }
 
+// Tile table of a CTA's row band [g0, g1), built by one warp (every lane calls it). Each segment of the band (the rows of
+// one image; each of its S column strips in turn) is a sequence of L rows: its owned rows and, when halo = 1, one halo
+// row on each side, whose 128-bit update masks MKX holds in sequence order. Writes CUM (per segment, the exclusive
+// prefix counts of the updating pixels of its rows), TILE (per tile: queue start; count | first row << 8 | last row <<
+// 20, rows segment-relative) and SEGT (per segment, the cumulative tile count).
+template <int SPAN>
+__device__ __forceinline__ void build_tile_table(const uint32_t *MKX, int *CUM, int2 *TILE, int *SEGT, int64_t g0,
+                                                 int64_t g1, int H, int S, int halo, int lane32)
+{
+    int64_t g = g0;
+    RowSeg sg;
+    int s = 0, nt = 0, u0 = 0;
+    while (next_segment(g, g1, H, sg))
+      for (int strip = 0; strip < S; ++strip) {
+        const int L = sg.r1 - sg.r0 + 2 * halo;
+        int run = 0;
+        for (int b = 0; b < L; b += 32) {
+            const int j = b + lane32;
+            int cnt = 0;
+            if (j < L) {
+                const uint32_t *m = MKX + (size_t)(u0 + j) * 4;
+                cnt = __popc(m[0]) + __popc(m[1]) + __popc(m[2]) + __popc(m[3]);
+            }
+            int inc = cnt;
+#pragma unroll
+            for (int d = 1; d < 32; d <<= 1) {
+                const int t = __shfl_up_sync(~0u, inc, d);
+                if (lane32 >= d)
+                    inc += t;
+            }
+            if (j < L)
+                CUM[u0 + j] = run + inc - cnt;
+            run += __shfl_sync(~0u, inc, 31);
+        }
+        __syncwarp();
+        const int Q = run;
+        // The tiles are the greedy cut of the queue: from q, up to 128 pixels, ending before the pixels of row
+        // j(q) + SPAN, where j(p) is the row holding queue position p (the last row whose prefix count is <= p).
+        // Usually no tile is cut short by the SPAN rule, and then the tiles are the fixed cut q = 128 t: every lane
+        // builds one fixed tile (binary searches in the prefix counts) and checks the rule; only a segment where
+        // some tile would be cut short takes the sequential greedy pass, which rewrites its entries.
+        auto row_bs = [&](int p) {
+            int lo = 0, hi = L - 1;
+            while (lo < hi) {
+                const int mid = (lo + hi + 1) >> 1;
+                if (CUM[u0 + mid] <= p)
+                    lo = mid;
+                else
+                    hi = mid - 1;
+            }
+            return lo;
+        };
+        const int TF = (Q + 127) / 128;
+        bool fixed = true;
+        for (int t0 = 0; t0 < TF; t0 += 32) {
+            const int t = t0 + lane32;
+            bool fits = true;
+            if (t < TF) {
+                const int q = 128 * t, end = min(q + 128, Q);
+                const int j = row_bs(q), jh = row_bs(end - 1);
+                const int lim = j + SPAN < L ? CUM[u0 + j + SPAN] : Q;
+                fits = lim >= end;
+                TILE[nt + t] = make_int2(q, (end - q) | (j << 8) | (jh << 20));
+            }
+            fixed &= __all_sync(~0u, fits);
+        }
+        if (fixed) {
+            nt += TF;
+        } else {
+            // greedy tiles, warp-parallel: lanes hold the prefix counts of a 64-row window [wb, wb + 64) (rows past
+            // the segment: Q)
+            auto cx = [&](int jj) { return jj < L ? CUM[u0 + jj] : Q; };
+            int wb = 0, cw0 = cx(lane32), cw1 = cx(32 + lane32);
+            auto row_of = [&](int p) {
+                const uint32_t b0 = __ballot_sync(~0u, cw0 <= p), b1 = __ballot_sync(~0u, cw1 <= p);
+                return wb + (b1 ? 63 - __clz(b1) : 31 - __clz(b0));
+            };
+            int q = 0;
+            while (q < Q) {
+                while (__shfl_sync(~0u, cw1, 0) <= q) {  // the tile's first row is past the window's first half
+                    wb += 32;
+                    cw0 = cw1;
+                    cw1 = cx(wb + 32 + lane32);
+                }
+                const int j = row_of(q);  // in [wb, wb + 32): the tile's rows stay inside the window
+                const int lim = __shfl_sync(~0u, j + SPAN - wb < 32 ? cw0 : cw1, (j + SPAN - wb) & 31);
+                const int end = min(q + 128, lim), jh = row_of(end - 1);
+                __syncwarp();
+                if (lane32 == 0)
+                    TILE[nt] = make_int2(q, (end - q) | (j << 8) | (jh << 20));
+                ++nt;
+                q = end;
+            }
+        }
+        if (lane32 == 0)
+            SEGT[s] = nt;
+        __syncwarp();
+        ++s;
+        u0 += L;
+    }
+}
+
 // Forward over the updating pixels only (the reference's forward also runs the MLP on the updating pixels alone,
 // ncaops/nca_step.cuh:344-349): the pixels with m = 1 of a segment of rows, in row-major order, are cut into tiles of
 // up to 128 (one MMA tile, lane = queue position) that span at most SPAN rows; the other pixels get y = x. Warps
@@ -492,98 +594,8 @@ __global__ void __launch_bounds__(128 * NPART + 96, 1) fwd_rows_kernel(StepArgs 
     }
     __syncthreads();
     int cur_k = -1;
-    if (warp == 0) {  // tile table: per segment (pass), the prefix counts of its rows, then tiles of <= 128 pixels,
-        int64_t g = g0;  // <= SPAN rows
-        RowSeg sg;
-        int s = 0, nt = 0, u0 = 0;
-        while (next_segment(g, g1, H, sg))
-          for (int strip = 0; strip < S; ++strip) {
-            const int L = sg.r1 - sg.r0;
-            int run = 0;
-            for (int b = 0; b < L; b += 32) {
-                const int j = b + lane32;
-                int cnt = 0;
-                if (j < L) {
-                    const uint32_t *m = MKX + (size_t)(u0 + j) * 4;
-                    cnt = __popc(m[0]) + __popc(m[1]) + __popc(m[2]) + __popc(m[3]);
-                }
-                int inc = cnt;
-#pragma unroll
-                for (int d = 1; d < 32; d <<= 1) {
-                    const int t = __shfl_up_sync(~0u, inc, d);
-                    if (lane32 >= d)
-                        inc += t;
-                }
-                if (j < L)
-                    CUM[u0 + j] = run + inc - cnt;
-                run += __shfl_sync(~0u, inc, 31);
-            }
-            __syncwarp();
-            const int Q = run;
-            // The tiles are the greedy cut of the queue: from q, up to 128 pixels, ending before the pixels of row
-            // j(q) + SPAN, where j(p) is the row holding queue position p (the last row whose prefix count is <= p).
-            // Usually no tile is cut short by the SPAN rule, and then the tiles are the fixed cut q = 128 t: every lane
-            // builds one fixed tile (binary searches in the prefix counts) and checks the rule; only a segment where
-            // some tile would be cut short takes the sequential greedy pass, which rewrites its entries.
-            auto row_bs = [&](int p) {
-                int lo = 0, hi = L - 1;
-                while (lo < hi) {
-                    const int mid = (lo + hi + 1) >> 1;
-                    if (CUM[u0 + mid] <= p)
-                        lo = mid;
-                    else
-                        hi = mid - 1;
-                }
-                return lo;
-            };
-            const int TF = (Q + 127) / 128;
-            bool fixed = true;
-            for (int t0 = 0; t0 < TF; t0 += 32) {
-                const int t = t0 + lane32;
-                bool fits = true;
-                if (t < TF) {
-                    const int q = 128 * t, end = min(q + 128, Q);
-                    const int j = row_bs(q), jh = row_bs(end - 1);
-                    const int lim = j + F::SPAN < L ? CUM[u0 + j + F::SPAN] : Q;
-                    fits = lim >= end;
-                    TILE[nt + t] = make_int2(q, (end - q) | (j << 8) | (jh << 20));
-                }
-                fixed &= __all_sync(~0u, fits);
-            }
-            if (fixed) {
-                nt += TF;
-            } else {
-                // greedy tiles, warp-parallel: lanes hold the prefix counts of a 64-row window [wb, wb + 64) (rows past
-                // the segment: Q)
-                auto cx = [&](int jj) { return jj < L ? CUM[u0 + jj] : Q; };
-                int wb = 0, cw0 = cx(lane32), cw1 = cx(32 + lane32);
-                auto row_of = [&](int p) {
-                    const uint32_t b0 = __ballot_sync(~0u, cw0 <= p), b1 = __ballot_sync(~0u, cw1 <= p);
-                    return wb + (b1 ? 63 - __clz(b1) : 31 - __clz(b0));
-                };
-                int q = 0;
-                while (q < Q) {
-                    while (__shfl_sync(~0u, cw1, 0) <= q) {  // the tile's first row is past the window's first half
-                        wb += 32;
-                        cw0 = cw1;
-                        cw1 = cx(wb + 32 + lane32);
-                    }
-                    const int j = row_of(q);  // in [wb, wb + 32): the tile's rows stay inside the window
-                    const int lim = __shfl_sync(~0u, j + F::SPAN - wb < 32 ? cw0 : cw1, (j + F::SPAN - wb) & 31);
-                    const int end = min(q + 128, lim), jh = row_of(end - 1);
-                    __syncwarp();
-                    if (lane32 == 0)
-                        TILE[nt] = make_int2(q, (end - q) | (j << 8) | (jh << 20));
-                    ++nt;
-                    q = end;
-                }
-            }
-            if (lane32 == 0)
-                SEGT[s] = nt;
-            __syncwarp();
-            ++s;
-            u0 += L;
-        }
+    if (warp == 0) {  // tile table: tiles of <= 128 updating pixels over <= SPAN rows
+        build_tile_table<F::SPAN>(MKX, CUM, TILE, SEGT, g0, g1, H, S, 0, lane32);
     } else if (nrows > 0) {  // the first segment's NCA: its weights, by warps 1..
         const int k = (int)(n0 / a.B);
         stage_rows_weights<D, false>(W1s, nullptr, W2s, a.w1 + (size_t)k * HID * D::PIN, a.b1 + (size_t)k * HID,
