@@ -224,7 +224,7 @@ int bwd_ctas_per_sm()
     using D = Dims<I::C, I::HID>;
     if (I::FP32)
         return ctas_per_sm(bwd_kernel_cc<I::C, I::HID, I::GROW>, D::bwd_smem_cc(), 0);
-    return ctas_per_sm(bwd_kernel_tc<I::C, I::HID, I::GROW>, D::bwd_smem_tc(), D::BWD_TMEM);
+    return ctas_per_sm(bwd_kernel_tc<I::C, I::HID, I::GROW>, D::bwd_smem_tc(), D::BWD_TMEM, 128 * BWD_TILE_PARTS);
 }
 
 // Row-streaming kernels (the benchmark's hot path): TF32 texture NCAs whose rows are whole 16-byte multiples that
@@ -582,7 +582,7 @@ int backward_stages_impl(const float *x, const float *gy, const uint8_t *alive, 
                     if (II::FP32)
                         bwd_kernel_cc<II::C, II::HID, II::GROW><<<w.grid, 128, D::bwd_smem_cc(), st>>>(a);
                     else
-                        bwd_kernel_tc<II::C, II::HID, II::GROW><<<w.grid, 128, D::bwd_smem_tc(), st>>>(a);
+                        bwd_kernel_tc<II::C, II::HID, II::GROW><<<w.grid, 128 * BWD_TILE_PARTS, D::bwd_smem_tc(), st>>>(a);
                     CUDA_OK(cudaGetLastError());
                 }
                 if (stages & NCA_STAGE_ADJOINT) {

@@ -53,6 +53,9 @@ struct Dims {
     static constexpr int PART = HID * PIN + HID + C * HID;  // weight-gradient partial: dW1, db1, dW2
 };
 
+// Parts of 128 threads of the TF32 tile backward (bwd_kernel_tc).
+constexpr int BWD_TILE_PARTS = 4;
+
 struct StepArgs {
     const float *x, *w1, *b1, *w2;
     float *y, *alpha;              // forward outputs (alpha: growing only)
@@ -133,18 +136,19 @@ __device__ __forceinline__ void cp_async4(float *dst, const float *src)
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 
 // State of image n around the tile at (y0, x0), with a one-pixel circular halo: XS[c][r][s], r < R+2, s < S+2, copied
-// asynchronously (cp.async; the caller waits with cp_async_wait_all + a barrier). Thread t copies the halo positions
-// t, t + 128, t + 256, t + 384 of every channel; index arithmetic is done once per tile, not per element.
-template <class D>
+// asynchronously (cp.async; the caller waits with cp_async_wait_all + a barrier). Thread t of the NT threads copies the
+// halo positions t, t + NT, .. (< 390) of every channel; index arithmetic is done once per tile, not per element.
+template <class D, int NT = 128>
 __device__ __forceinline__ void load_halo_async(float *XS, const float *x, int n, const TileGeom &g, int y0, int x0)
 {
+    constexpr int NI = (390 + NT - 1) / NT;
     const int SS = g.S + 2, per = (g.R + 2) * SS;
     const size_t plane = (size_t)g.H * g.W;
     const float *xn = x + (size_t)n * D::C * plane;
-    int goff[4], soff[4];
+    int goff[NI], soff[NI];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        const int e = threadIdx.x + 128 * i;
+    for (int i = 0; i < NI; ++i) {
+        const int e = threadIdx.x + NT * i;
         const int r = e / SS, s = e - r * SS;
         soff[i] = e < per ? e : -1;
         goff[i] = wrap_index(y0 - 1 + r, g.H) * g.W + wrap_index(x0 - 1 + s, g.W);
@@ -152,7 +156,7 @@ __device__ __forceinline__ void load_halo_async(float *XS, const float *x, int n
 #pragma unroll 4
     for (int c = 0; c < D::C; ++c)
 #pragma unroll
-        for (int i = 0; i < 4; ++i)
+        for (int i = 0; i < NI; ++i)
             if (soff[i] >= 0)
                 cp_async4(XS + c * per + soff[i], xn + c * plane + goff[i]);
 }
@@ -188,17 +192,22 @@ struct TileCoord {
     int n, k, y0, x0;
 };
 
-// Block-wide OR (blocks of 128 threads, every thread calls it) of a 32-bit word; sw: 4 words of shared memory.
-__device__ __forceinline__ uint32_t block_or_128(uint32_t v, uint32_t *sw)
+// Block-wide OR (blocks of NT threads, every thread calls it) of a 32-bit word; sw: NT / 32 words of shared memory.
+template <int NT>
+__device__ __forceinline__ uint32_t block_or(uint32_t v, uint32_t *sw)
 {
     v = __reduce_or_sync(~0u, v);
     if ((threadIdx.x & 31) == 0)
         sw[threadIdx.x >> 5] = v;
     __syncthreads();
-    const uint32_t r = sw[0] | sw[1] | sw[2] | sw[3];
+    uint32_t r = 0;
+#pragma unroll
+    for (int w = 0; w < NT / 32; ++w)
+        r |= sw[w];
     __syncthreads();  // sw is reused by the next call
     return r;
 }
+__device__ __forceinline__ uint32_t block_or_128(uint32_t v, uint32_t *sw) { return block_or<128>(v, sw); }
 
 __device__ __forceinline__ TileCoord tile_coord(int64_t t, const TileGeom &g, int B)
 {
@@ -258,15 +267,14 @@ __device__ __forceinline__ uint32_t grow_tiles_live(const StepArgs &a, const Til
 
 // Growing NCAs, backward: a tile with no pixel alive after its forward step has gm = gy m a = 0 throughout, so it adds
 // nothing to the weight gradients and its dp is 0; the backward skips it without writing its dp, and the adjoint
-// reads dp at alive cells only. This thread's pixel of tile t alive (false when the pixel is outside the image); the
-// backward loads it one tile ahead, so that the skip decision does not wait for memory.
-__device__ __forceinline__ bool pixel_alive(const StepArgs &a, const TileGeom &g, int64_t t)
+// reads dp at alive cells only. Tile pixel px of tile t alive (false when the pixel is outside the image).
+__device__ __forceinline__ bool pixel_alive(const StepArgs &a, const TileGeom &g, int64_t t, int px)
 {
     const int64_t n = t / g.tiles_per_image;
     const int ti = (int)(t - n * g.tiles_per_image);
-    const int r = threadIdx.x / g.S, s = threadIdx.x - r * g.S;
+    const int r = px / g.S, s = px - r * g.S;
     const int Y = (ti / g.strips) * g.R + r, X = (ti % g.strips) * g.S + s;
-    return threadIdx.x < g.R * g.S && Y < a.H && X < a.W && a.alive[((size_t)n * a.H + Y) * a.W + X] != 0;
+    return px < g.R * g.S && Y < a.H && X < a.W && a.alive[((size_t)n * a.H + Y) * a.W + X] != 0;
 }
 
 template <int C, int HID, bool TC, bool GROWING>
@@ -542,6 +550,28 @@ __device__ __forceinline__ bool load_gm(float (&gm)[16], const StepArgs &a, cons
     return live;
 }
 
+// load_gm for the NCH channels c0 .. c0 + NCH - 1 only.
+template <int C, int NCH, bool GROWING>
+__device__ __forceinline__ void load_gm_channels(float (&gm)[NCH], const StepArgs &a, const TileCoord &tc, int Y, int X,
+                                                 bool valid, bool stoch, int c0)
+{
+#pragma unroll
+    for (int c = 0; c < NCH; ++c)
+        gm[c] = 0.f;
+    if (!valid)
+        return;
+    const size_t plane = (size_t)a.H * a.W;
+    float m = stoch ? update_mask_at(a.seed, a.rate, tc.n + a.n_offset, a.H, a.W, Y, X) : 1.f;
+    if (GROWING && !a.alive[(size_t)tc.n * plane + (size_t)Y * a.W + X])
+        m = 0.f;
+    if (m == 0.f)
+        return;
+    const float *gyn = a.gy + ((size_t)tc.n * C + c0) * plane + (size_t)Y * a.W + X;
+#pragma unroll
+    for (int c = 0; c < NCH; ++c)
+        gm[c] = __ldg(gyn + (size_t)c * plane);
+}
+
 // fp32 mode: the MLP on CUDA cores in fp32, weight gradients accumulated by threads j < HID in registers.
 template <int C, int HID, bool GROWING>
 __global__ void __launch_bounds__(128, 1) bwd_kernel_cc(StepArgs a)
@@ -598,7 +628,7 @@ __global__ void __launch_bounds__(128, 1) bwd_kernel_cc(StepArgs a)
                 uint32_t mine = 0;
 #pragma unroll
                 for (int i = 0; i < 32; ++i)
-                    mine |= t + i < t1 && pixel_alive(a, g, t + i) ? 1u << i : 0u;
+                    mine |= t + i < t1 && pixel_alive(a, g, t + i, tid) ? 1u << i : 0u;
                 live_bits = block_or_128(mine, sw);
             }
             if (!((live_bits >> (t - live_base)) & 1u))
@@ -705,17 +735,25 @@ __device__ __forceinline__ void st_sw32x8(float *tile, int mn0, int k, int krows
     *reinterpret_cast<float4 *>(dst + 4) = make_float4(v[4], v[5], v[6], v[7]);
 }
 
-// TF32 mode. Per tile (thread = pixel = TMEM lane):
+// TF32 mode. One CTA of BWD_TILE_PARTS parts of 128 threads: thread lt of every part owns tile pixel lt (TMEM lane lt);
+// the CUDA-core work of each phase is split by part (part p: channels [CPP p, CPP (p+1)) of the halo, perception and
+// gm, hidden units [HPP p, HPP (p+1)) of the epilogues, dp features [4 CPP p, 4 CPP (p+1)) of the dp stores), so that
+// four warps of every SM sub-partition share each phase instead of one. Thread 0 issues the contractions. Per tile:
 //   1. halo tile (cp.async) and gm; p' and gm into TMEM (A operands) and into swizzled MN-major smem (weight grads);
 //   2. H = p' W1'^T and DHP = gm W2 (A from TMEM);
 //   3. relu(h) -> smem (swizzled), dh = DHP [h > 0] -> TMEM (A of dp);
 //   4. dW2^T += relu(h)^T gm and DP = dh W1 (A from TMEM);
 //   5. dh -> smem (swizzled, over relu(h)); dW1' += dh^T p' while dp is stored to the dp scratch.
+// The bias features of p' (1 at PIN and PIN + 1, zeros up to the operand widths) and gm's channels C..15 are constant:
+// written once.
 template <int C, int HID, bool GROWING>
-__global__ void __launch_bounds__(128, 1) bwd_kernel_tc(StepArgs a)
+__global__ void __launch_bounds__(128 * BWD_TILE_PARTS, 1) bwd_kernel_tc(StepArgs a)
 {
+    constexpr int NP = BWD_TILE_PARTS, NT = 128 * NP, CPP = C / NP, HPP = HID / NP, PPP = 4 * CPP;
+    static_assert(C % NP == 0 && HPP % 8 == 0, "tile backward parts");
     a.seed = step_seed_of(a);
     using D = Dims<C, HID>;
+    constexpr int KP16 = ((D::KP + 15) / 16) * 16;  // TMEM columns of p' (A of p -> h)
     extern __shared__ __align__(128) unsigned char smem_raw[];
     unsigned char *base = smem_raw + ((1024 - (umma::smem_u32(smem_raw) & 1023)) & 1023);
     float *W1s = reinterpret_cast<float *>(base), *W1T = W1s + D::W1S, *W2T = W1T + D::W1T;
@@ -724,7 +762,7 @@ __global__ void __launch_bounds__(128, 1) bwd_kernel_tc(StepArgs a)
     uint64_t *bar = reinterpret_cast<uint64_t *>(GSW + D::GSW);
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bar + 1);
 
-    const int tid = threadIdx.x, warp = tid / 32;
+    const int tid = threadIdx.x, warp = tid / 32, part = tid / 128, lt = tid % 128;
     const TileGeom g = make_geom(a.H, a.W, GROWING);
     const int64_t T = (int64_t)a.N * g.tiles_per_image;
     int64_t t0, t1;
@@ -732,9 +770,14 @@ __global__ void __launch_bounds__(128, 1) bwd_kernel_tc(StepArgs a)
     const bool stoch = a.rate < 1.f;
     const size_t plane = (size_t)a.H * a.W;
 
-    // the swizzled gm tile holds 16 channels in a 32-wide block: zero it once (its other 16 lanes are never written)
-    for (int e = tid; e < D::GSW; e += 128)
+    // the swizzled gm tile holds 16 channels in a 32-wide block: zero it once (its other lanes are never written);
+    // the constant features of the p' tile: 1 at PIN and PIN + 1, zeros up to NPW
+    for (int e = tid; e < D::GSW; e += NT)
         GSW[e] = 0.f;
+    for (int e = tid; e < 128 * (D::NPW - D::PIN); e += NT) {
+        const int q = e / (D::NPW - D::PIN), f = D::PIN + e % (D::NPW - D::PIN);
+        PSW[umma::sw32_offset(f, q, 128) / 4] = f < D::PIN + 2 ? 1.f : 0.f;
+    }
     if (tid == 0) {
         umma::mbar_init(bar, 1);
         umma::fence_mbar_init();
@@ -748,6 +791,20 @@ __global__ void __launch_bounds__(128, 1) bwd_kernel_tc(StepArgs a)
     umma::fence_after_sync();
     const uint32_t tmem = *tmem_slot;
     const uint32_t lane_base = umma::tmem_addr(tmem, warp, 0);
+    if (part == 0) {  // constant TMEM columns: gm channels C..15 (zeros), p' features PIN .. KP16 (1, 1, zeros)
+        float z[16], pb[KP16 - D::PIN];
+#pragma unroll
+        for (int e = 0; e < 16; ++e)
+            z[e] = 0.f;
+#pragma unroll
+        for (int e = 0; e < KP16 - D::PIN; ++e)
+            pb[e] = e < 2 ? 1.f : 0.f;
+        umma::tmem_st16(lane_base + D::T_G, z);
+#pragma unroll
+        for (int e = 0; e < KP16 - D::PIN; e += 8)
+            umma::tmem_st8(lane_base + D::T_P + D::PIN + e, pb + e);
+        umma::tmem_wait_st();
+    }
     const uint32_t sW1 = umma::smem_u32(W1s), sW1T = umma::smem_u32(W1T), sW2T = umma::smem_u32(W2T);
     const uint32_t sRH = umma::smem_u32(RHDH), sP = umma::smem_u32(PSW), sG = umma::smem_u32(GSW);
 
@@ -762,7 +819,9 @@ __global__ void __launch_bounds__(128, 1) bwd_kernel_tc(StepArgs a)
         umma::fence_after_sync();
         return !failed;
     };
-    auto flush = [&](int k) {  // this CTA's weight gradients of NCA k -> partial slot (blockIdx.x + k)
+    auto flush = [&](int k) {  // this CTA's weight gradients of NCA k -> partial slot (blockIdx.x + k), by part 0
+        if (part != 0)
+            return;
         float row[((D::PIN + 1 + 15) / 16) * 16], col[16];
 #pragma unroll
         for (int cc = 0; cc < (D::PIN + 1 + 15) / 16; ++cc) {
@@ -778,13 +837,13 @@ __global__ void __launch_bounds__(128, 1) bwd_kernel_tc(StepArgs a)
 #pragma unroll
         for (int e = 0; e < 16; ++e)
             col[e] = started ? col[e] : 0.f;
-        if (tid < HID)
-            write_partial_row<D>(a.partial + (size_t)(blockIdx.x + k) * D::PART, tid, row, row[D::PIN], col,
+        if (lt < HID)
+            write_partial_row<D>(a.partial + (size_t)(blockIdx.x + k) * D::PART, lt, row, row[D::PIN], col,
                                  a.partial_add != 0);
         umma::fence_before_sync();
     };
 
-    __shared__ uint32_t sw[4];
+    __shared__ uint32_t sw[NT / 32];
     uint32_t live_bits = 0;  // growing: whether tiles [live_base, live_base + 32) hold an alive pixel
     int64_t live_base = t0 - 64;
     bool staged = false;
@@ -799,13 +858,15 @@ __global__ void __launch_bounds__(128, 1) bwd_kernel_tc(StepArgs a)
             staged = false;
         }
         if (GROWING) {  // dead tile (block-uniform): nothing to add, its dp is not read
-            if (t >= live_base + 32) {  // the alive bytes of 32 tiles' pixels, all loads in flight together
+            if (t >= live_base + 32) {  // the alive bytes of 32 tiles' pixels (part 0), all loads in flight together
                 live_base = t;
                 uint32_t mine = 0;
+                if (part == 0) {
 #pragma unroll
-                for (int i = 0; i < 32; ++i)
-                    mine |= t + i < t1 && pixel_alive(a, g, t + i) ? 1u << i : 0u;
-                live_bits = block_or_128(mine, sw);
+                    for (int i = 0; i < 32; ++i)
+                        mine |= t + i < t1 && pixel_alive(a, g, t + i, lt) ? 1u << i : 0u;
+                }
+                live_bits = block_or<NT>(mine, sw);
             }
             if (!((live_bits >> (t - live_base)) & 1u))
                 continue;
@@ -816,25 +877,27 @@ __global__ void __launch_bounds__(128, 1) bwd_kernel_tc(StepArgs a)
             staged = true;
         }
         // ---- 1. inputs
-        load_halo_async<D>(XS, a.x, tc.n, g, tc.y0, tc.x0);
-        const int r = tid / g.S, s = tid - r * g.S;
-        const bool valid = tid < g.R * g.S && tc.y0 + r < a.H && tc.x0 + s < a.W;
+        load_halo_async<D, NT>(XS, a.x, tc.n, g, tc.y0, tc.x0);
+        const int r = lt / g.S, s = lt - r * g.S;
+        const bool valid = lt < g.R * g.S && tc.y0 + r < a.H && tc.x0 + s < a.W;
         const int Y = tc.y0 + r, X = tc.x0 + s;
-        float gm[16];
-        load_gm<C, GROWING>(gm, a, tc, Y, X, valid, stoch);
+        {  // gm of this part's channels -> TMEM G and the swizzled gm tile
+            float gm[CPP];
+            load_gm_channels<C, CPP, GROWING>(gm, a, tc, Y, X, valid, stoch, CPP * part);
 #pragma unroll
-        for (int c = 0; c < 16; ++c)
-            gm[c] = tf32_bias(gm[c]);
-        umma::tmem_st16(lane_base + D::T_G, gm);
-        st_sw32x8(GSW, 0, tid, 128, gm);
-        st_sw32x8(GSW, 8, tid, 128, gm + 8);
+            for (int cc = 0; cc < CPP; ++cc) {
+                gm[cc] = tf32_bias(gm[cc]);
+                umma::tmem_st1(lane_base + D::T_G + CPP * part + cc, gm[cc]);
+                GSW[umma::sw32_offset(CPP * part + cc, lt, 128) / 4] = gm[cc];
+            }
+        }
         cp_async_wait_all();
         __syncthreads();
-        {
+        {  // p' of this part's channels -> TMEM P and the swizzled p' tile
             const int SS = g.S + 2, per = (g.R + 2) * SS;
-            float pv[((D::KP + 15) / 16) * 16];
 #pragma unroll
-            for (int c = 0; c < C; ++c) {
+            for (int cc = 0; cc < CPP; ++cc) {
+                const int c = CPP * part + cc;
                 float4 p = make_float4(0.f, 0.f, 0.f, 0.f);
                 if (valid) {
                     float v[3][3];
@@ -846,22 +909,9 @@ __global__ void __launch_bounds__(128, 1) bwd_kernel_tc(StepArgs a)
                             v[dy][dx] = b[dy * SS + dx];
                     p = perceive3x3(v);
                 }
-                pv[4 * c] = tf32_bias(p.x); pv[4 * c + 1] = tf32_bias(p.y);
-                pv[4 * c + 2] = tf32_bias(p.z); pv[4 * c + 3] = tf32_bias(p.w);
-            }
-#pragma unroll
-            for (int f = D::PIN; f < ((D::KP + 15) / 16) * 16; ++f)
-                pv[f] = (valid && f < D::PIN + 2) ? 1.f : 0.f;  // bias-hi and bias-lo features
-#pragma unroll
-            for (int cc = 0; cc < ((D::KP + 15) / 16); ++cc)
-                umma::tmem_st16(lane_base + D::T_P + cc * 16, *reinterpret_cast<float(*)[16]>(pv + cc * 16));
-#pragma unroll
-            for (int f8 = 0; f8 < D::NPW / 8; ++f8) {
-                float z[8];
-#pragma unroll
-                for (int e = 0; e < 8; ++e)
-                    z[e] = f8 * 8 + e < ((D::KP + 15) / 16) * 16 ? pv[(f8 * 8 + e) % (((D::KP + 15) / 16) * 16)] : 0.f;
-                st_sw32x8(PSW, f8 * 8, tid, 128, z);
+                const float pv[4] = {tf32_bias(p.x), tf32_bias(p.y), tf32_bias(p.z), tf32_bias(p.w)};
+                umma::tmem_st4(lane_base + D::T_P + 4 * c, pv);
+                *reinterpret_cast<float4 *>(PSW + umma::sw32_offset(4 * c, lt, 128) / 4) = make_float4(pv[0], pv[1], pv[2], pv[3]);
             }
         }
         umma::tmem_wait_st();
@@ -883,21 +933,21 @@ __global__ void __launch_bounds__(128, 1) bwd_kernel_tc(StepArgs a)
         }
         if (!wait_mma())
             break;
-        // ---- 3. relu(h) -> smem (swizzled MN-major), dh -> TMEM
+        // ---- 3. relu(h) -> smem (swizzled MN-major), dh -> TMEM (this part's hidden units)
 #pragma unroll
-        for (int cc = 0; cc < HID / 16; ++cc) {
-            float h[16], d[16];
-            umma::tmem_ld16(lane_base + D::T_H + cc * 16, h);
-            umma::tmem_ld16(lane_base + D::T_DHP + cc * 16, d);
+        for (int q = 0; q < HPP / 8; ++q) {
+            const int j0 = HPP * part + 8 * q;
+            float h[8], d[8];
+            umma::tmem_ld8(lane_base + D::T_H + j0, h);
+            umma::tmem_ld8(lane_base + D::T_DHP + j0, d);
             umma::tmem_wait_ld();
 #pragma unroll
-            for (int e = 0; e < 16; ++e) {
+            for (int e = 0; e < 8; ++e) {
                 d[e] = h[e] > 0.f ? tf32_bias(d[e]) : 0.f;
                 h[e] = tf32_bias(fmaxf(h[e], 0.f));
             }
-            st_sw32x8(RHDH, cc * 16, tid, 128, h);
-            st_sw32x8(RHDH, cc * 16 + 8, tid, 128, h + 8);
-            umma::tmem_st16(lane_base + D::T_H + cc * 16, d);
+            st_sw32x8(RHDH, j0, lt, 128, h);
+            umma::tmem_st8(lane_base + D::T_H + j0, d);
         }
         umma::tmem_wait_st();
         umma::fence_proxy_async();
@@ -921,12 +971,12 @@ __global__ void __launch_bounds__(128, 1) bwd_kernel_tc(StepArgs a)
             break;
         // ---- 5. dh -> smem (swizzled, over relu(h)); dW1' += dh^T p'; dp -> dp scratch
 #pragma unroll
-        for (int cc = 0; cc < HID / 16; ++cc) {
-            float d[16];
-            umma::tmem_ld16(lane_base + D::T_H + cc * 16, d);
+        for (int q = 0; q < HPP / 8; ++q) {
+            const int j0 = HPP * part + 8 * q;
+            float d[8];
+            umma::tmem_ld8(lane_base + D::T_H + j0, d);
             umma::tmem_wait_ld();
-            st_sw32x8(RHDH, cc * 16, tid, 128, d);
-            st_sw32x8(RHDH, cc * 16 + 8, tid, 128, d + 8);
+            st_sw32x8(RHDH, j0, lt, 128, d);
         }
         umma::fence_proxy_async();
         umma::fence_before_sync();
@@ -941,18 +991,17 @@ __global__ void __launch_bounds__(128, 1) bwd_kernel_tc(StepArgs a)
             umma::commit(bar);
         }
         started = true;
-        {
+        {  // this part's dp features
             float *dpn = a.dp + (size_t)tc.n * D::PIN * plane + (size_t)Y * a.W + X;
+            float v[PPP];
 #pragma unroll
-            for (int cc = 0; cc < D::PIN / 16; ++cc) {
-                float v[16];
-                umma::tmem_ld16(lane_base + D::T_P + cc * 16, v);
-                umma::tmem_wait_ld();
-                if (valid)
+            for (int q = 0; q < PPP / 4; ++q)
+                umma::tmem_ld4(lane_base + D::T_P + PPP * part + 4 * q, v + 4 * q);
+            umma::tmem_wait_ld();
+            if (valid)
 #pragma unroll
-                    for (int e = 0; e < 16; ++e)
-                        dpn[(size_t)(cc * 16 + e) * plane] = v[e];
-            }
+                for (int e = 0; e < PPP; ++e)
+                    dpn[(size_t)(PPP * part + e) * plane] = v[e];
         }
         umma::fence_before_sync();
         if (!wait_mma())  // dW1' done: RHDH / PSW / TMEM are free for the next tile
@@ -990,7 +1039,7 @@ __global__ void __launch_bounds__(256) adjoint_kernel(const float *__restrict__ 
         bool some = false, all = true;  // of this thread's halo cells
         for (int e = threadIdx.x; e < HH_ * HW_; e += blockDim.x) {
             const int r = e / HW_, s = e - r * HW_;
-            const uint8_t v = alive[n * plane + (int64_t)wrap_index(y0 - 1 + r, H) * W + wrap_index(x0 - 1 + s, W)];
+            const uint8_t v = alive[n * plane + (int64_t)wrap_near(y0 - 1 + r, H) * W + wrap_near(x0 - 1 + s, W)];
             sal[e] = v;
             some |= v != 0;
             all &= v != 0;
@@ -1005,18 +1054,15 @@ __global__ void __launch_bounds__(256) adjoint_kernel(const float *__restrict__ 
         }
         gate = !all_alive;
     }
-    if (gate) {
-        for (int e = threadIdx.x; e < PIN * HH_ * HW_; e += blockDim.x) {
-            const int f = e / (HH_ * HW_), rem = e - f * HH_ * HW_, r = rem / HW_, s = rem - r * HW_;
-            const int Y = wrap_index(y0 - 1 + r, H), X = wrap_index(x0 - 1 + s, W);
-            sdp[e] = sal[GROWING ? rem : 0] ? dpn[(int64_t)f * plane + (int64_t)Y * W + X] : 0.f;
-        }
-    } else {
-        for (int e = threadIdx.x; e < PIN * HH_ * HW_; e += blockDim.x) {
-            const int f = e / (HH_ * HW_), rem = e - f * HH_ * HW_, r = rem / HW_, s = rem - r * HW_;
-            const int Y = wrap_index(y0 - 1 + r, H), X = wrap_index(x0 - 1 + s, W);
-            sdp[e] = dpn[(int64_t)f * plane + (int64_t)Y * W + X];
-        }
+    // thread t takes halo positions t, t + blockDim.x, ..: its address is computed once per position, then every
+    // feature plane is read at it (consecutive threads, consecutive columns)
+    for (int pos = threadIdx.x; pos < HH_ * HW_; pos += blockDim.x) {
+        const int r = pos / HW_, s = pos - r * HW_;
+        const float *src = dpn + (int64_t)wrap_near(y0 - 1 + r, H) * W + wrap_near(x0 - 1 + s, W);
+        const bool ld = !gate || sal[GROWING ? pos : 0];
+#pragma unroll 16
+        for (int f = 0; f < PIN; ++f)
+            sdp[f * HH_ * HW_ + pos] = ld ? __ldg(src + (int64_t)f * plane) : 0.f;
     }
     __syncthreads();
     const int r = threadIdx.x / ADJ_TW, s = threadIdx.x % ADJ_TW, Y = y0 + r, X = x0 + s;
