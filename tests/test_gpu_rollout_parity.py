@@ -164,3 +164,32 @@ def test_backward_step_at_the_benchmark_shape(x_stable):
         e = O.rel(a.cpu(), b)
         print(f'x_stable={x_stable} {name}: rel err {e:.1e}')
         assert e < TOL, (name, e)
+
+
+def test_growing_backward_at_config2_scale():
+    """64 growing NCAs x 8 images of 72 x 72 with a disc of living cells over ~20% of each image (the config-2 launch
+    size, cost-balanced tiles across many NCAs, dead tiles skipped): the gradients of selected NCAs against the TF32
+    oracle with the perception summed as the kernels sum it (perceive_grouped). With conv2d's summation order one NCA
+    of this input moves a pre-activation 1.4e-5 (relative to its terms) from zero across the ReLU; the grouped oracle
+    removes that rounding difference, so the bound can be tight."""
+    from ultranca_b200 import nca_ops
+    K, B, C, HID, H, W = 64, 8, 16, 128, 72, 72
+    x, w1, b1, w2 = O.make(K, B, C, HID, H, W, seed=4, growing=True)
+    r = (0.20 * H * W / 3.14159) ** 0.5
+    yy, xx = torch.meshgrid(torch.arange(H), torch.arange(W), indexing='ij')
+    inside = ((yy - H / 2) ** 2 + (xx - W / 2) ** 2 <= r * r).float()
+    x = x * inside
+    x[:, :, 3] = (x[:, :, 3].abs() + 0.2) * inside
+    gy = torch.randn(x.shape, generator=torch.Generator().manual_seed(11)) * 1e-3
+    xd, w1d, b1d, w2d, gyd = (t.cuda().contiguous() for t in (x, w1, b1, w2, gy))
+    y, alive = nca_ops._forward(xd, w1d, b1d, w2d, 0.5, 7, False, True)
+    got = nca_ops._backward(xd, gyd, alive, w1d, b1d, w2d, 0.5, 7, False, True)
+    torch.cuda.synchronize()
+    mask = O.mask_for(K, B, H, W, 7, 0.5)
+    for k in (0, 21, 56, 63):
+        sl, im = slice(k, k + 1), slice(k * B, (k + 1) * B)
+        am = alive[im].cpu().view(1, B, 1, H, W)
+        ref = O.step_backward(x[sl], w1[sl], b1[sl], w2[sl], mask[sl], gy[sl], True, tf32=True, alive_mask=am,
+                              grouped=True)
+        for a, b, name in zip(got, ref, ('gx', 'dw1', 'db1', 'dw2')):
+            assert O.rel(a[sl].cpu(), b) < 1e-4, (k, name, O.rel(a[sl].cpu(), b))

@@ -131,3 +131,12 @@ def test_synthetic_loss_gradient():
     expect += 10.0 * torch.sign(xd) * (xd.abs() > 1)
     assert torch.allclose(gx, expect, atol=1e-6)
     assert per.shape == (K,)
+
+
+def test_grouped_perception_matches_conv2d():
+    """The kernels' summation grouping of the perception (nca_step.cuh:317-320) equals the conv2d perception of
+    test_nca.py up to fp32 rounding, for every filter and circular edge."""
+    x = torch.randn(2, 3, 12, 9, 13, generator=torch.Generator().manual_seed(5))
+    a, b = O.perceive(x), O.perceive_grouped(x)
+    assert a.shape == b.shape
+    assert float((a - b).abs().max()) <= 4e-6 * float(a.abs().max())

@@ -179,6 +179,13 @@ void dispatch(int64_t C, int64_t HID, bool fp32, bool growing, F &&f)
     }
 }
 
+// The tile kernels index a launch's tiles in 32 bits.
+void check_tiles(int64_t tiles)
+{
+    if (tiles >= ((int64_t)1 << 31))
+        fail(NCA_ERR_SHAPE, "too many tiles in one launch (%lld)", (long long)tiles);
+}
+
 void check_ptr(const void *p, const char *name)
 {
     if (!p)
@@ -334,6 +341,7 @@ void launch_forward(const float *x, const float *w1, const float *b1, const floa
         using II = decltype(I);
         using D = Dims<II::C, II::HID>;
         const TileGeom g = II::GROW ? make_grow_fwd_geom((int)s.H, (int)s.W) : make_geom((int)s.H, (int)s.W);
+        check_tiles(s.N * g.tiles_per_image);
         const int G = grid_for(s.N * g.tiles_per_image, fwd_ctas_per_sm<II>());
         if (II::FP32)
             fwd_kernel<II::C, II::HID, false, II::GROW><<<G, 128, D::fwd_smem(), stream>>>(a);
@@ -356,6 +364,7 @@ BwdWork backward_work(const Shape &s, bool fp32, bool growing)
         using II = decltype(I);
         using D = Dims<II::C, II::HID>;
         const TileGeom g = make_geom((int)s.H, (int)s.W, II::GROW);
+        check_tiles(s.N * g.tiles_per_image);
         w.grid = grid_for(s.N * g.tiles_per_image, bwd_ctas_per_sm<II>());
         w.dp_floats = s.N * D::PIN * s.H * s.W;
         int slots = w.grid;
@@ -588,8 +597,12 @@ int backward_stages_impl(const float *x, const float *gy, const uint8_t *alive, 
                 if (stages & NCA_STAGE_ADJOINT) {
                     const size_t adj_smem = (size_t)D::PIN * (ADJ_TH + 2) * (ADJ_TW + 2) * sizeof(float);
                     set_smem_once(adjoint_kernel<II::C, II::GROW>, adj_smem);
-                    const dim3 agrid((unsigned)(((W + ADJ_TW - 1) / ADJ_TW) * ((H + ADJ_TH - 1) / ADJ_TH)), (unsigned)N);
-                    adjoint_kernel<II::C, II::GROW><<<agrid, ADJ_TW * ADJ_TH, adj_smem, st>>>(dp, gy, alive, gx, (int)H, (int)W);
+                    // persistent: the resident blocks loop over the 8 x 32 blocks of all images
+                    const int64_t blocks = N * (int64_t)(((W + ADJ_TW - 1) / ADJ_TW) * ((H + ADJ_TH - 1) / ADJ_TH));
+                    const int per = ctas_per_sm(adjoint_kernel<II::C, II::GROW>, adj_smem, 0, 256);
+                    const int agrid = (int)std::min<int64_t>(blocks, (int64_t)device_info().sms * per);
+                    adjoint_kernel<II::C, II::GROW><<<agrid, ADJ_TW * ADJ_TH, adj_smem, st>>>(dp, gy, alive, gx, (int)N, (int)H,
+                                                                                           (int)W);
                     CUDA_OK(cudaGetLastError());
                 }
             }

@@ -133,6 +133,12 @@ __device__ __forceinline__ void cp_async4(float *dst, const float *src)
 {
     asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(umma::smem_u32(dst)), "l"(src) : "memory");
 }
+// The same, with the destination zero-filled instead when !ld (nothing is read from src then).
+__device__ __forceinline__ void cp_async4_zfill(float *dst, const float *src, bool ld)
+{
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(umma::smem_u32(dst)), "l"(src), "r"(ld ? 4 : 0)
+                 : "memory");
+}
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 
 // State of image n around the tile at (y0, x0), with a one-pixel circular halo: XS[c][r][s], r < R+2, s < S+2, copied
@@ -189,7 +195,7 @@ __device__ __forceinline__ void perceive_tile(float *P, const float *XS, const T
 }
 
 struct TileCoord {
-    int n, k, y0, x0;
+    int n, k, y0, x0, ty, tx;  // image, NCA, first row and column, tile row and column (strip) in the image
 };
 
 // Block-wide OR (blocks of NT threads, every thread calls it) of a 32-bit word; sw: NT / 32 words of shared memory.
@@ -209,14 +215,18 @@ __device__ __forceinline__ uint32_t block_or(uint32_t v, uint32_t *sw)
 }
 __device__ __forceinline__ uint32_t block_or_128(uint32_t v, uint32_t *sw) { return block_or<128>(v, sw); }
 
+// Tile t of a launch (32-bit arithmetic: the host keeps a launch's tile count below 2^31).
 __device__ __forceinline__ TileCoord tile_coord(int64_t t, const TileGeom &g, int B)
 {
     TileCoord tc;
-    tc.n = (int)(t / g.tiles_per_image);
-    const int ti = (int)(t - (int64_t)tc.n * g.tiles_per_image);
-    tc.k = tc.n / B;
-    tc.y0 = (ti / g.strips) * g.R;
-    tc.x0 = (ti % g.strips) * g.S;
+    const uint32_t u = (uint32_t)t, tpi = (uint32_t)g.tiles_per_image, strips = (uint32_t)g.strips;
+    const uint32_t n = u / tpi, ti = u - n * tpi, ty = ti / strips;
+    tc.n = (int)n;
+    tc.k = (int)(n / (uint32_t)B);
+    tc.ty = (int)ty;
+    tc.tx = (int)(ti - ty * strips);
+    tc.y0 = tc.ty * g.R;
+    tc.x0 = tc.tx * g.S;
     return tc;
 }
 
@@ -248,10 +258,9 @@ __device__ __forceinline__ uint32_t grow_tiles_live(const StepArgs &a, const Til
         for (int i = 0; i < 8; ++i) {
             const int64_t u = t + i0 + i;
             const bool tile_ok = u < t1;
-            const int64_t n = (tile_ok ? u : t) / g.tiles_per_image;
-            const int ti = (int)((tile_ok ? u : t) - n * g.tiles_per_image);
-            const int iy0 = (ti / g.strips) * GI_R, ix0 = (ti % g.strips) * GI_S;
-            const float *xa = a.x + ((size_t)n * C + 3) * (size_t)a.H * a.W;
+            const TileCoord tc = tile_coord(tile_ok ? u : t, g, a.B);
+            const int iy0 = tc.ty * GI_R, ix0 = tc.tx * GI_S;
+            const float *xa = a.x + ((size_t)tc.n * C + 3) * (size_t)a.H * a.W;
 #pragma unroll
             for (int q = 0; q < 2; ++q) {
                 const int Y = iy0 + dr[q], X = ix0 + dc[q];
@@ -270,11 +279,10 @@ __device__ __forceinline__ uint32_t grow_tiles_live(const StepArgs &a, const Til
 // reads dp at alive cells only. Tile pixel px of tile t alive (false when the pixel is outside the image).
 __device__ __forceinline__ bool pixel_alive(const StepArgs &a, const TileGeom &g, int64_t t, int px)
 {
-    const int64_t n = t / g.tiles_per_image;
-    const int ti = (int)(t - n * g.tiles_per_image);
+    const TileCoord tc = tile_coord(t, g, a.B);
     const int r = px / g.S, s = px - r * g.S;
-    const int Y = (ti / g.strips) * g.R + r, X = (ti % g.strips) * g.S + s;
-    return px < g.R * g.S && Y < a.H && X < a.W && a.alive[((size_t)n * a.H + Y) * a.W + X] != 0;
+    const int Y = tc.y0 + r, X = tc.x0 + s;
+    return px < g.R * g.S && Y < a.H && X < a.W && a.alive[((size_t)tc.n * a.H + Y) * a.W + X] != 0;
 }
 
 template <int C, int HID, bool TC, bool GROWING>
@@ -320,9 +328,8 @@ __global__ void __launch_bounds__(128, 1) fwd_kernel(StepArgs a)
     for (int64_t t = t0; t < t1 && !failed; ++t) {
         TileCoord tc = tile_coord(t, g, a.B);
         if (GROWING) {  // the extended tile's origin: one cell above and left of the interior
-            const int ti = (int)(t - (int64_t)tc.n * g.tiles_per_image);
-            tc.y0 = (ti / g.strips) * GI_R - 1;
-            tc.x0 = (ti % g.strips) * GI_S - 1;
+            tc.y0 = tc.ty * GI_R - 1;
+            tc.x0 = tc.tx * GI_S - 1;
         }
         const int r = tid / g.S, s = tid - r * g.S;
         const bool valid = GROWING ? tc.y0 + r >= 0 && tc.y0 + r < a.H && tc.x0 + s >= 0 && tc.x0 + s < a.W
@@ -819,7 +826,9 @@ __global__ void __launch_bounds__(128 * BWD_TILE_PARTS, 1) bwd_kernel_tc(StepArg
         umma::fence_after_sync();
         return !failed;
     };
-    auto flush = [&](int k) {  // this CTA's weight gradients of NCA k -> partial slot (blockIdx.x + k), by part 0
+    // this CTA's weight gradients of NCA k -> partial slot (blockIdx.x + k), by part 0; zeros when no tile of NCA k ran
+    // here (growing: all dead)
+    auto flush = [&](int k, bool have) {
         if (part != 0)
             return;
         float row[((D::PIN + 1 + 15) / 16) * 16], col[16];
@@ -830,13 +839,13 @@ __global__ void __launch_bounds__(128 * BWD_TILE_PARTS, 1) bwd_kernel_tc(StepArg
             umma::tmem_wait_ld();
 #pragma unroll
             for (int e = 0; e < 16; ++e)
-                row[cc * 16 + e] = started ? v[e] : 0.f;  // no tile of NCA k ran an MMA (growing: all dead)
+                row[cc * 16 + e] = have ? v[e] : 0.f;
         }
         umma::tmem_ld16(lane_base + D::T_ACC2, col);
         umma::tmem_wait_ld();
 #pragma unroll
         for (int e = 0; e < 16; ++e)
-            col[e] = started ? col[e] : 0.f;
+            col[e] = have ? col[e] : 0.f;
         if (lt < HID)
             write_partial_row<D>(a.partial + (size_t)(blockIdx.x + k) * D::PART, lt, row, row[D::PIN], col,
                                  a.partial_add != 0);
@@ -847,29 +856,42 @@ __global__ void __launch_bounds__(128 * BWD_TILE_PARTS, 1) bwd_kernel_tc(StepArg
     uint32_t live_bits = 0;  // growing: whether tiles [live_base, live_base + 32) hold an alive pixel
     int64_t live_base = t0 - 64;
     bool staged = false;
-    for (int64_t t = t0; t < t1; ++t) {
+    // every NCA this CTA's tile range overlaps gets its partial slot written (the reduction reads them all)
+    const int k_last = t1 > t0 ? tile_coord(t1 - 1, g, a.B).k : -1;
+    if (t1 > t0)
+        cur_k = tile_coord(t0, g, a.B).k;
+    for (int64_t t = t0;; ++t) {
+        if (GROWING) {  // on to the next tile with an alive pixel (a dead tile adds nothing and its dp is not read)
+            while (t < t1) {
+                if (t >= live_base + 32) {  // the alive bytes of 32 tiles' pixels (part 0), all loads in flight together
+                    live_base = t;
+                    uint32_t mine = 0;
+                    if (part == 0) {
+#pragma unroll
+                        for (int i = 0; i < 32; ++i)
+                            mine |= t + i < t1 && pixel_alive(a, g, t + i, lt) ? 1u << i : 0u;
+                    }
+                    live_bits = block_or<NT>(mine, sw);
+                }
+                const uint32_t rest = live_bits >> (t - live_base);
+                if (rest != 0) {
+                    t += __ffs(rest) - 1;
+                    break;
+                }
+                t = live_base + 32;
+            }
+        }
+        if (t >= t1)
+            break;
         const TileCoord tc = tile_coord(t, g, a.B);
         if (tc.k != cur_k) {
-            if (cur_k >= 0)
-                flush(cur_k);
+            flush(cur_k, started);
+            for (int kk = cur_k + 1; kk < tc.k; ++kk)  // NCAs whose tiles here are all dead
+                flush(kk, false);
             __syncthreads();
             cur_k = tc.k;
             started = false;
             staged = false;
-        }
-        if (GROWING) {  // dead tile (block-uniform): nothing to add, its dp is not read
-            if (t >= live_base + 32) {  // the alive bytes of 32 tiles' pixels (part 0), all loads in flight together
-                live_base = t;
-                uint32_t mine = 0;
-                if (part == 0) {
-#pragma unroll
-                    for (int i = 0; i < 32; ++i)
-                        mine |= t + i < t1 && pixel_alive(a, g, t + i, lt) ? 1u << i : 0u;
-                }
-                live_bits = block_or<NT>(mine, sw);
-            }
-            if (!((live_bits >> (t - live_base)) & 1u))
-                continue;
         }
         if (!staged) {  // the NCA's weights, at its first live tile (the flush above needs none)
             stage_bwd_weights<D>(W1s, W1T, W2T, a.w1 + (size_t)tc.k * HID * D::PIN, a.b1 + (size_t)tc.k * HID,
@@ -1007,8 +1029,11 @@ __global__ void __launch_bounds__(128 * BWD_TILE_PARTS, 1) bwd_kernel_tc(StepArg
         if (!wait_mma())  // dW1' done: RHDH / PSW / TMEM are free for the next tile
             break;
     }
-    if (cur_k >= 0 && !failed)
-        flush(cur_k);
+    if (cur_k >= 0 && !failed) {
+        flush(cur_k, started);
+        for (int kk = cur_k + 1; kk <= k_last; ++kk)
+            flush(kk, false);
+    }
     umma::fence_before_sync();
     __syncthreads();
     umma::fence_after_sync();
@@ -1023,69 +1048,100 @@ __global__ void __launch_bounds__(128 * BWD_TILE_PARTS, 1) bwd_kernel_tc(StepArg
 constexpr int ADJ_TW = 32, ADJ_TH = 8;
 template <int C, bool GROWING>
 __global__ void __launch_bounds__(256) adjoint_kernel(const float *__restrict__ dp, const float *__restrict__ gy,
-                                                      const uint8_t *__restrict__ alive, float *__restrict__ gx, int H, int W)
+                                                      const uint8_t *__restrict__ alive, float *__restrict__ gx, int N,
+                                                      int H, int W)
 {
-    constexpr int PIN = 4 * C, HW_ = ADJ_TW + 2, HH_ = ADJ_TH + 2;
+    constexpr int PIN = 4 * C, HW_ = ADJ_TW + 2, HH_ = ADJ_TH + 2, NPOS = HH_ * HW_;
+    constexpr int NQ = (NPOS + 255) / 256;  // halo positions per thread
     extern __shared__ __align__(16) float sdp[];  // [PIN][HH_][HW_]
-    __shared__ uint8_t sal[GROWING ? HH_ * HW_ : 1];  // growing: the alive mask of the halo
-    const int tiles_x = (W + ADJ_TW - 1) / ADJ_TW;
-    const int x0 = (blockIdx.x % tiles_x) * ADJ_TW, y0 = (blockIdx.x / tiles_x) * ADJ_TH;
-    const int64_t n = blockIdx.y, plane = (int64_t)H * W;
-    const float *dpn = dp + n * PIN * plane;
-    bool gate = false;  // growing, block with dead cells in its halo: read dp at alive cells only
-    if (GROWING) {
-        // dp is 0 wherever the cell is dead (gm = 0 there); the backward skips all-dead tiles without writing their
-        // dp, so dp is read at alive cells only, and a block with no alive cell in its halo has gx = 0
-        bool some = false, all = true;  // of this thread's halo cells
-        for (int e = threadIdx.x; e < HH_ * HW_; e += blockDim.x) {
-            const int r = e / HW_, s = e - r * HW_;
-            const uint8_t v = alive[n * plane + (int64_t)wrap_near(y0 - 1 + r, H) * W + wrap_near(x0 - 1 + s, W)];
-            sal[e] = v;
-            some |= v != 0;
-            all &= v != 0;
+    __shared__ uint8_t sal[GROWING ? NPOS : 1];   // growing: the alive mask of the halo
+    const int tiles_x = (W + ADJ_TW - 1) / ADJ_TW, per_image = tiles_x * ((H + ADJ_TH - 1) / ADJ_TH);
+    const int64_t plane = (int64_t)H * W, total = (int64_t)N * per_image;
+    // persistent over the blocks b = blockIdx.x, blockIdx.x + gridDim.x, .. (block b: image b / per_image, tile
+    // b % per_image); growing: this thread's alive bytes of the next block's halo are loaded one block ahead
+    auto halo_alive = [&](int64_t b, uint8_t (&v)[NQ]) {
+        const int64_t n = b / per_image;
+        const int tb = (int)(b - n * per_image), x0 = (tb % tiles_x) * ADJ_TW, y0 = (tb / tiles_x) * ADJ_TH;
+#pragma unroll
+        for (int q = 0; q < NQ; ++q) {
+            const int e = threadIdx.x + 256 * q, r = e / HW_, s = e - r * HW_;
+            v[q] = e < NPOS ? alive[n * plane + (int64_t)wrap_near(y0 - 1 + r, H) * W + wrap_near(x0 - 1 + s, W)] : 0;
         }
-        const bool any_alive = __syncthreads_or(some), all_alive = __syncthreads_and(all);
-        if (!any_alive) {
-            const int r = threadIdx.x / ADJ_TW, s = threadIdx.x % ADJ_TW, Y = y0 + r, X = x0 + s;
-            if (Y < H && X < W)
-                for (int c = 0; c < C; ++c)
-                    gx[(n * C + c) * plane + (int64_t)Y * W + X] = 0.f;
-            return;
-        }
-        gate = !all_alive;
-    }
-    // thread t takes halo positions t, t + blockDim.x, ..: its address is computed once per position, then every
-    // feature plane is read at it (consecutive threads, consecutive columns)
-    for (int pos = threadIdx.x; pos < HH_ * HW_; pos += blockDim.x) {
-        const int r = pos / HW_, s = pos - r * HW_;
-        const float *src = dpn + (int64_t)wrap_near(y0 - 1 + r, H) * W + wrap_near(x0 - 1 + s, W);
-        const bool ld = !gate || sal[GROWING ? pos : 0];
-#pragma unroll 16
-        for (int f = 0; f < PIN; ++f)
-            sdp[f * HH_ * HW_ + pos] = ld ? __ldg(src + (int64_t)f * plane) : 0.f;
-    }
-    __syncthreads();
-    const int r = threadIdx.x / ADJ_TW, s = threadIdx.x % ADJ_TW, Y = y0 + r, X = x0 + s;
-    if (Y >= H || X >= W)
-        return;
-    const int64_t pix = (int64_t)Y * W + X;
-    const bool live = !GROWING || alive[n * plane + pix];
-#pragma unroll 1
-    for (int c = 0; c < C; ++c) {
-        float acc = 0.f;
+    };
+    uint8_t nxt[NQ];
+    if (GROWING && blockIdx.x < total)
+        halo_alive(blockIdx.x, nxt);
+    for (int64_t b = blockIdx.x; b < total; b += gridDim.x) {
+        const int64_t n = b / per_image;
+        const int tb = (int)(b - n * per_image), x0 = (tb % tiles_x) * ADJ_TW, y0 = (tb / tiles_x) * ADJ_TH;
+        const float *dpn = dp + n * PIN * plane;
+        const int r = threadIdx.x / ADJ_TW, s = threadIdx.x % ADJ_TW, Y = y0 + r, X = x0 + s;
+        bool gate = false;  // growing, block with dead cells in its halo: read dp at alive cells only
+        if (GROWING) {
+            // dp is 0 wherever the cell is dead (gm = 0 there); the backward skips all-dead tiles without writing their
+            // dp, so dp is read at alive cells only, and a block with no alive cell in its halo has gx = 0
+            uint8_t cur[NQ];
+            bool some = false, all = true;  // of this thread's halo cells
 #pragma unroll
-        for (int f = 0; f < 4; ++f)
-#pragma unroll
-            for (int i = 0; i < 3; ++i)
-#pragma unroll
-                for (int j = 0; j < 3; ++j) {
-                    // output (Y, X) receives tap (i, j) of the pixel (Y - (i - 1), X - (j - 1))
-                    const float k = filter_tap(f, i, j);
-                    if (k != 0.f)
-                        acc = fmaf(k, sdp[((4 * c + f) * HH_ + (r + 1 - (i - 1))) * HW_ + (s + 1 - (j - 1))], acc);
+            for (int q = 0; q < NQ; ++q) {
+                const int e = threadIdx.x + 256 * q;
+                cur[q] = nxt[q];
+                if (e < NPOS) {
+                    sal[e] = cur[q];
+                    some |= cur[q] != 0;
+                    all &= cur[q] != 0;
                 }
-        const int64_t o = (n * C + c) * plane + pix;
-        gx[o] = (live ? gy[o] : 0.f) + acc;
+            }
+            if (b + gridDim.x < total)
+                halo_alive(b + gridDim.x, nxt);
+            const bool any_alive = __syncthreads_or(some), all_alive = __syncthreads_and(all);
+            if (!any_alive) {
+                if (Y < H && X < W)
+#pragma unroll 4
+                    for (int c = 0; c < C; ++c)
+                        gx[(n * C + c) * plane + (int64_t)Y * W + X] = 0.f;
+                continue;
+            }
+            gate = !all_alive;
+        }
+        // dp halo -> sdp: thread t takes halo positions t, t + 256: its address is computed once per position, then
+        // every feature plane is copied from it asynchronously (zeros where a growing halo cell is dead)
+#pragma unroll
+        for (int q = 0; q < NQ; ++q) {
+            const int pos = threadIdx.x + 256 * q;
+            if (pos < NPOS) {
+                const int hr = pos / HW_, hs = pos - hr * HW_;
+                const float *src = dpn + (int64_t)wrap_near(y0 - 1 + hr, H) * W + wrap_near(x0 - 1 + hs, W);
+                const bool ld = !gate || sal[GROWING ? pos : 0];
+#pragma unroll 16
+                for (int f = 0; f < PIN; ++f)
+                    cp_async4_zfill(sdp + f * NPOS + pos, src + (int64_t)f * plane, ld);
+            }
+        }
+        cp_async_wait_all();
+        __syncthreads();
+        if (Y < H && X < W) {
+            const int64_t pix = (int64_t)Y * W + X;
+            const bool live = !GROWING || alive[n * plane + pix];
+#pragma unroll 1
+            for (int c = 0; c < C; ++c) {
+                float acc = 0.f;
+#pragma unroll
+                for (int f = 0; f < 4; ++f)
+#pragma unroll
+                    for (int i = 0; i < 3; ++i)
+#pragma unroll
+                        for (int j = 0; j < 3; ++j) {
+                            // output (Y, X) receives tap (i, j) of the pixel (Y - (i - 1), X - (j - 1))
+                            const float k = filter_tap(f, i, j);
+                            if (k != 0.f)
+                                acc = fmaf(k, sdp[((4 * c + f) * HH_ + (r + 1 - (i - 1))) * HW_ + (s + 1 - (j - 1))], acc);
+                        }
+                const int64_t o = (n * C + c) * plane + pix;
+                gx[o] = (live ? gy[o] : 0.f) + acc;
+            }
+        }
+        __syncthreads();  // sdp and sal are rewritten for the next block
     }
 }
 
