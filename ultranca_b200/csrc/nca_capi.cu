@@ -231,7 +231,7 @@ int bwd_ctas_per_sm()
     using D = Dims<I::C, I::HID>;
     if (I::FP32)
         return ctas_per_sm(bwd_kernel_cc<I::C, I::HID, I::GROW>, D::bwd_smem_cc(), 0);
-    return ctas_per_sm(bwd_kernel_tc<I::C, I::HID, I::GROW>, D::bwd_smem_tc(), D::BWD_TMEM, 128 * BWD_TILE_PARTS);
+    return ctas_per_sm(bwd_kernel_tc<I::C, I::HID, I::GROW>, D::bwd_smem_tc(I::GROW), D::BWD_TMEM, 128 * BWD_TILE_PARTS);
 }
 
 // Row-streaming kernels (the benchmark's hot path): TF32 texture NCAs whose rows are whole 16-byte multiples that
@@ -591,14 +591,15 @@ int backward_stages_impl(const float *x, const float *gy, const uint8_t *alive, 
                     if (II::FP32)
                         bwd_kernel_cc<II::C, II::HID, II::GROW><<<w.grid, 128, D::bwd_smem_cc(), st>>>(a);
                     else
-                        bwd_kernel_tc<II::C, II::HID, II::GROW><<<w.grid, 128 * BWD_TILE_PARTS, D::bwd_smem_tc(), st>>>(a);
+                        bwd_kernel_tc<II::C, II::HID, II::GROW><<<w.grid, 128 * BWD_TILE_PARTS, D::bwd_smem_tc(II::GROW), st>>>(a);
                     CUDA_OK(cudaGetLastError());
                 }
                 if (stages & NCA_STAGE_ADJOINT) {
-                    const size_t adj_smem = (size_t)D::PIN * (ADJ_TH + 2) * (ADJ_TW + 2) * sizeof(float);
+                    const size_t adj_smem = (size_t)(D::PIN / ADJ_HALVES) * (ADJ_TH + 2) * (ADJ_TW + 2) * sizeof(float);
                     set_smem_once(adjoint_kernel<II::C, II::GROW>, adj_smem);
                     // persistent: the resident blocks loop over the 8 x 32 blocks of all images
                     const int64_t blocks = N * (int64_t)(((W + ADJ_TW - 1) / ADJ_TW) * ((H + ADJ_TH - 1) / ADJ_TH));
+                    check_tiles(blocks);
                     const int per = ctas_per_sm(adjoint_kernel<II::C, II::GROW>, adj_smem, 0, 256);
                     const int agrid = (int)std::min<int64_t>(blocks, (int64_t)device_info().sms * per);
                     adjoint_kernel<II::C, II::GROW><<<agrid, ADJ_TW * ADJ_TH, adj_smem, st>>>(dp, gy, alive, gx, (int)N, (int)H,

@@ -48,7 +48,14 @@ struct Dims {
     static constexpr size_t fwd_smem() { return (size_t)(W1S + W2S + P + XS_FLOATS) * 4 + 16; }
     // TF32 backward: [W1S | W1T | W2T | pad to 1 KB] [RHDH (XS aliases it) | PSW | GSW] + barrier
     static constexpr int BWD_W = ((W1S + W1T + W2T) * 4 + 1023) / 1024 * 1024;
-    static constexpr size_t bwd_smem_tc() { return 1024 + (size_t)BWD_W + (size_t)(RHDH + PSW + GSW) * 4 + 16; }
+    // + the halo buffer of the next tile (prefetched during the current tile's contractions), positions: growing
+    // (compact 8 x 16 tiles) 180, otherwise up to 390 (R S <= 128), or as many as fit in 227 KB
+    static constexpr size_t BWD_BASE = 1024 + (size_t)BWD_W + (size_t)(RHDH + PSW + GSW) * 4 + 16;
+    static constexpr int xs_pos(bool growing)
+    {
+        return growing ? 180 : (BWD_BASE + (size_t)C * 390 * 4 <= 232448 ? 390 : (int)((232448 - BWD_BASE) / (4 * C)));
+    }
+    static constexpr size_t bwd_smem_tc(bool growing) { return BWD_BASE + (size_t)C * xs_pos(growing) * 4; }
     static constexpr size_t bwd_smem_cc() { return (size_t)(W1S + W2S + P + G + 2 * HID * HT) * 4 + 16; }
     static constexpr int PART = HID * PIN + HID + C * HID;  // weight-gradient partial: dW1, db1, dW2
 };
@@ -765,8 +772,8 @@ __global__ void __launch_bounds__(128 * BWD_TILE_PARTS, 1) bwd_kernel_tc(StepArg
     unsigned char *base = smem_raw + ((1024 - (umma::smem_u32(smem_raw) & 1023)) & 1023);
     float *W1s = reinterpret_cast<float *>(base), *W1T = W1s + D::W1S, *W2T = W1T + D::W1T;
     float *RHDH = reinterpret_cast<float *>(base + D::BWD_W), *PSW = RHDH + D::RHDH, *GSW = PSW + D::PSW;
-    float *XS = RHDH;
-    uint64_t *bar = reinterpret_cast<uint64_t *>(GSW + D::GSW);
+    float *XSP = GSW + D::GSW;  // the prefetched halo
+    uint64_t *bar = reinterpret_cast<uint64_t *>(XSP + C * D::xs_pos(GROWING));
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bar + 1);
 
     const int tid = threadIdx.x, warp = tid / 32, part = tid / 128, lt = tid % 128;
@@ -860,8 +867,9 @@ __global__ void __launch_bounds__(128 * BWD_TILE_PARTS, 1) bwd_kernel_tc(StepArg
     const int k_last = t1 > t0 ? tile_coord(t1 - 1, g, a.B).k : -1;
     if (t1 > t0)
         cur_k = tile_coord(t0, g, a.B).k;
-    for (int64_t t = t0;; ++t) {
-        if (GROWING) {  // on to the next tile with an alive pixel (a dead tile adds nothing and its dp is not read)
+    // the next tile with an alive pixel from t on (growing; a dead tile adds nothing and its dp is not read), or t1
+    auto next_live = [&](int64_t t) {
+        if (GROWING) {
             while (t < t1) {
                 if (t >= live_base + 32) {  // the alive bytes of 32 tiles' pixels (part 0), all loads in flight together
                     live_base = t;
@@ -874,15 +882,30 @@ __global__ void __launch_bounds__(128 * BWD_TILE_PARTS, 1) bwd_kernel_tc(StepArg
                     live_bits = block_or<NT>(mine, sw);
                 }
                 const uint32_t rest = live_bits >> (t - live_base);
-                if (rest != 0) {
-                    t += __ffs(rest) - 1;
-                    break;
-                }
+                if (rest != 0)
+                    return t + __ffs(rest) - 1;
                 t = live_base + 32;
             }
         }
-        if (t >= t1)
-            break;
+        return t < t1 ? t : t1;
+    };
+    // a tile's inputs: its halo (cp.async into XS) and this part's gm channels (registers). With the dedicated buffer
+    // (the tile's halo fits it) the next tile's inputs are requested right after the current tile's perception, so
+    // that they arrive during its contractions; otherwise the halo goes to RHDH at the start of its own tile.
+    const bool prefetch = (g.R + 2) * (g.S + 2) <= D::xs_pos(GROWING);
+    float *XS = prefetch ? XSP : RHDH;
+    float gmn[CPP];
+    auto request = [&](int64_t tn) {
+        const TileCoord tq = tile_coord(tn, g, a.B);
+        load_halo_async<D, NT>(XS, a.x, tq.n, g, tq.y0, tq.x0);
+        const int rq = lt / g.S, sq = lt - rq * g.S;
+        const bool vq = lt < g.R * g.S && tq.y0 + rq < a.H && tq.x0 + sq < a.W;
+        load_gm_channels<C, CPP, GROWING>(gmn, a, tq, tq.y0 + rq, tq.x0 + sq, vq, stoch, CPP * part);
+    };
+    int64_t t = next_live(t0);
+    if (prefetch && t < t1)
+        request(t);
+    while (t < t1) {
         const TileCoord tc = tile_coord(t, g, a.B);
         if (tc.k != cur_k) {
             flush(cur_k, started);
@@ -898,20 +921,17 @@ __global__ void __launch_bounds__(128 * BWD_TILE_PARTS, 1) bwd_kernel_tc(StepArg
                                  a.w2 + (size_t)tc.k * C * HID);
             staged = true;
         }
-        // ---- 1. inputs
-        load_halo_async<D, NT>(XS, a.x, tc.n, g, tc.y0, tc.x0);
+        // ---- 1. inputs (requested one tile ahead when prefetching)
+        if (!prefetch)
+            request(t);
         const int r = lt / g.S, s = lt - r * g.S;
         const bool valid = lt < g.R * g.S && tc.y0 + r < a.H && tc.x0 + s < a.W;
         const int Y = tc.y0 + r, X = tc.x0 + s;
-        {  // gm of this part's channels -> TMEM G and the swizzled gm tile
-            float gm[CPP];
-            load_gm_channels<C, CPP, GROWING>(gm, a, tc, Y, X, valid, stoch, CPP * part);
 #pragma unroll
-            for (int cc = 0; cc < CPP; ++cc) {
-                gm[cc] = tf32_bias(gm[cc]);
-                umma::tmem_st1(lane_base + D::T_G + CPP * part + cc, gm[cc]);
-                GSW[umma::sw32_offset(CPP * part + cc, lt, 128) / 4] = gm[cc];
-            }
+        for (int cc = 0; cc < CPP; ++cc) {  // gm of this part's channels -> TMEM G and the swizzled gm tile
+            const float gv = tf32_bias(gmn[cc]);
+            umma::tmem_st1(lane_base + D::T_G + CPP * part + cc, gv);
+            GSW[umma::sw32_offset(CPP * part + cc, lt, 128) / 4] = gv;
         }
         cp_async_wait_all();
         __syncthreads();
@@ -940,6 +960,10 @@ __global__ void __launch_bounds__(128 * BWD_TILE_PARTS, 1) bwd_kernel_tc(StepArg
         umma::fence_proxy_async();
         umma::fence_before_sync();
         __syncthreads();
+        // the halo is consumed: the next live tile's inputs may land in it during this tile's contractions
+        const int64_t t_next = next_live(t + 1);
+        if (prefetch && t_next < t1)
+            request(t_next);
         // ---- 2. H = p' W1'^T, DHP = gm W2 (A from TMEM)
         if (tid == 0) {
             umma::fence_after_sync();
@@ -1028,12 +1052,14 @@ __global__ void __launch_bounds__(128 * BWD_TILE_PARTS, 1) bwd_kernel_tc(StepArg
         umma::fence_before_sync();
         if (!wait_mma())  // dW1' done: RHDH / PSW / TMEM are free for the next tile
             break;
+        t = t_next;
     }
     if (cur_k >= 0 && !failed) {
         flush(cur_k, started);
         for (int kk = cur_k + 1; kk <= k_last; ++kk)
             flush(kk, false);
     }
+    cp_async_wait_all();  // a prefetch issued before a failed wait lands before the block ends
     umma::fence_before_sync();
     __syncthreads();
     umma::fence_after_sync();
@@ -1045,103 +1071,119 @@ __global__ void __launch_bounds__(128 * BWD_TILE_PARTS, 1) bwd_kernel_tc(StepArg
 
 // gx = gy a + sum_f P_f^T dp_f: the transpose of the circular perception (ncaops/nca_step.cuh:1195-1263), fp32, fixed
 // tap order. Block: 32 x 8 output pixels of one image, all channels; dp halo staged in shared memory.
-constexpr int ADJ_TW = 32, ADJ_TH = 8;
+constexpr int ADJ_TW = 32, ADJ_TH = 8, ADJ_HALVES = 2;
 template <int C, bool GROWING>
 __global__ void __launch_bounds__(256) adjoint_kernel(const float *__restrict__ dp, const float *__restrict__ gy,
                                                       const uint8_t *__restrict__ alive, float *__restrict__ gx, int N,
                                                       int H, int W)
 {
-    constexpr int PIN = 4 * C, HW_ = ADJ_TW + 2, HH_ = ADJ_TH + 2, NPOS = HH_ * HW_;
+    // the dp halo is staged in ADJ_HALVES passes of PIN / ADJ_HALVES features (channels [c0, c0 + C / ADJ_HALVES)), so
+    // that several blocks of 256 threads fit an SM (dead blocks, the common case of a growing grid, are latency-bound)
+    constexpr int PIN = 4 * C, HW_ = ADJ_TW + 2, HH_ = ADJ_TH + 2, NPOS = HH_ * HW_, FH = PIN / ADJ_HALVES;
     constexpr int NQ = (NPOS + 255) / 256;  // halo positions per thread
-    extern __shared__ __align__(16) float sdp[];  // [PIN][HH_][HW_]
+    static_assert(C % ADJ_HALVES == 0, "adjoint feature passes");
+    extern __shared__ __align__(16) float sdp[];  // [FH][HH_][HW_]
     __shared__ uint8_t sal[GROWING ? NPOS : 1];   // growing: the alive mask of the halo
-    const int tiles_x = (W + ADJ_TW - 1) / ADJ_TW, per_image = tiles_x * ((H + ADJ_TH - 1) / ADJ_TH);
-    const int64_t plane = (int64_t)H * W, total = (int64_t)N * per_image;
+    const uint32_t tiles_x = (W + ADJ_TW - 1) / ADJ_TW, per_image = tiles_x * ((H + ADJ_TH - 1) / ADJ_TH);
+    const int64_t plane = (int64_t)H * W;
+    const uint32_t total = (uint32_t)N * per_image;  // < 2^31 (the host checks)
     // persistent over the blocks b = blockIdx.x, blockIdx.x + gridDim.x, .. (block b: image b / per_image, tile
     // b % per_image); growing: this thread's alive bytes of the next block's halo are loaded one block ahead
-    auto halo_alive = [&](int64_t b, uint8_t (&v)[NQ]) {
-        const int64_t n = b / per_image;
-        const int tb = (int)(b - n * per_image), x0 = (tb % tiles_x) * ADJ_TW, y0 = (tb / tiles_x) * ADJ_TH;
+    auto origin = [&](uint32_t b, int &n, int &y0, int &x0) {
+        const uint32_t nn = b / per_image, tb = b - nn * per_image, ty = tb / tiles_x;
+        n = (int)nn;
+        y0 = (int)ty * ADJ_TH;
+        x0 = (int)(tb - ty * tiles_x) * ADJ_TW;
+    };
+    auto halo_alive = [&](uint32_t b, uint8_t (&v)[NQ]) {
+        int n, y0, x0;
+        origin(b, n, y0, x0);
+        const uint8_t *an = alive + (int64_t)n * plane;
 #pragma unroll
         for (int q = 0; q < NQ; ++q) {
             const int e = threadIdx.x + 256 * q, r = e / HW_, s = e - r * HW_;
-            v[q] = e < NPOS ? alive[n * plane + (int64_t)wrap_near(y0 - 1 + r, H) * W + wrap_near(x0 - 1 + s, W)] : 0;
+            v[q] = e < NPOS ? an[(int64_t)wrap_near(y0 - 1 + r, H) * W + wrap_near(x0 - 1 + s, W)] : 0;
         }
     };
     uint8_t nxt[NQ];
     if (GROWING && blockIdx.x < total)
         halo_alive(blockIdx.x, nxt);
-    for (int64_t b = blockIdx.x; b < total; b += gridDim.x) {
-        const int64_t n = b / per_image;
-        const int tb = (int)(b - n * per_image), x0 = (tb % tiles_x) * ADJ_TW, y0 = (tb / tiles_x) * ADJ_TH;
-        const float *dpn = dp + n * PIN * plane;
+    for (uint32_t b = blockIdx.x; b < total; b += gridDim.x) {
+        int n, y0, x0;
+        origin(b, n, y0, x0);
         const int r = threadIdx.x / ADJ_TW, s = threadIdx.x % ADJ_TW, Y = y0 + r, X = x0 + s;
+        const bool out = Y < H && X < W;
         bool gate = false;  // growing, block with dead cells in its halo: read dp at alive cells only
         if (GROWING) {
             // dp is 0 wherever the cell is dead (gm = 0 there); the backward skips all-dead tiles without writing their
             // dp, so dp is read at alive cells only, and a block with no alive cell in its halo has gx = 0
-            uint8_t cur[NQ];
             bool some = false, all = true;  // of this thread's halo cells
 #pragma unroll
             for (int q = 0; q < NQ; ++q) {
                 const int e = threadIdx.x + 256 * q;
-                cur[q] = nxt[q];
                 if (e < NPOS) {
-                    sal[e] = cur[q];
-                    some |= cur[q] != 0;
-                    all &= cur[q] != 0;
+                    sal[e] = nxt[q];
+                    some |= nxt[q] != 0;
+                    all &= nxt[q] != 0;
                 }
             }
             if (b + gridDim.x < total)
                 halo_alive(b + gridDim.x, nxt);
             const bool any_alive = __syncthreads_or(some), all_alive = __syncthreads_and(all);
             if (!any_alive) {
-                if (Y < H && X < W)
-#pragma unroll 4
+                if (out) {
+                    float *g = gx + (int64_t)n * C * plane + (int64_t)Y * W + X;
+#pragma unroll
                     for (int c = 0; c < C; ++c)
-                        gx[(n * C + c) * plane + (int64_t)Y * W + X] = 0.f;
+                        g[(int64_t)c * plane] = 0.f;
+                }
                 continue;
             }
             gate = !all_alive;
         }
-        // dp halo -> sdp: thread t takes halo positions t, t + 256: its address is computed once per position, then
-        // every feature plane is copied from it asynchronously (zeros where a growing halo cell is dead)
-#pragma unroll
-        for (int q = 0; q < NQ; ++q) {
-            const int pos = threadIdx.x + 256 * q;
-            if (pos < NPOS) {
-                const int hr = pos / HW_, hs = pos - hr * HW_;
-                const float *src = dpn + (int64_t)wrap_near(y0 - 1 + hr, H) * W + wrap_near(x0 - 1 + hs, W);
-                const bool ld = !gate || sal[GROWING ? pos : 0];
-#pragma unroll 16
-                for (int f = 0; f < PIN; ++f)
-                    cp_async4_zfill(sdp + f * NPOS + pos, src + (int64_t)f * plane, ld);
-            }
-        }
-        cp_async_wait_all();
-        __syncthreads();
-        if (Y < H && X < W) {
-            const int64_t pix = (int64_t)Y * W + X;
-            const bool live = !GROWING || alive[n * plane + pix];
+        const bool live = out && (!GROWING || alive[(int64_t)n * plane + (int64_t)Y * W + X]);
 #pragma unroll 1
-            for (int c = 0; c < C; ++c) {
-                float acc = 0.f;
+        for (int hf = 0; hf < ADJ_HALVES; ++hf) {
+            // dp halo of features [hf FH, (hf + 1) FH) -> sdp: thread t takes halo positions t, t + 256; its address is
+            // computed once per position, then each feature plane is copied from it asynchronously (zeros where a
+            // growing halo cell is dead)
+            const float *dpn = dp + ((int64_t)n * PIN + hf * FH) * plane;
 #pragma unroll
-                for (int f = 0; f < 4; ++f)
-#pragma unroll
-                    for (int i = 0; i < 3; ++i)
-#pragma unroll
-                        for (int j = 0; j < 3; ++j) {
-                            // output (Y, X) receives tap (i, j) of the pixel (Y - (i - 1), X - (j - 1))
-                            const float k = filter_tap(f, i, j);
-                            if (k != 0.f)
-                                acc = fmaf(k, sdp[((4 * c + f) * HH_ + (r + 1 - (i - 1))) * HW_ + (s + 1 - (j - 1))], acc);
-                        }
-                const int64_t o = (n * C + c) * plane + pix;
-                gx[o] = (live ? gy[o] : 0.f) + acc;
+            for (int q = 0; q < NQ; ++q) {
+                const int pos = threadIdx.x + 256 * q;
+                if (pos < NPOS) {
+                    const int hr = pos / HW_, hs = pos - hr * HW_;
+                    const float *src = dpn + (int64_t)wrap_near(y0 - 1 + hr, H) * W + wrap_near(x0 - 1 + hs, W);
+                    const bool ld = !gate || sal[GROWING ? pos : 0];
+#pragma unroll 16
+                    for (int f = 0; f < FH; ++f)
+                        cp_async4_zfill(sdp + f * NPOS + pos, src + (int64_t)f * plane, ld);
+                }
             }
+            cp_async_wait_all();
+            __syncthreads();
+            if (out) {
+                const int64_t pix = (int64_t)Y * W + X;
+#pragma unroll 1
+                for (int cl = 0; cl < C / ADJ_HALVES; ++cl) {
+                    float acc = 0.f;
+#pragma unroll
+                    for (int f = 0; f < 4; ++f)
+#pragma unroll
+                        for (int i = 0; i < 3; ++i)
+#pragma unroll
+                            for (int j = 0; j < 3; ++j) {
+                                // output (Y, X) receives tap (i, j) of the pixel (Y - (i - 1), X - (j - 1))
+                                const float k = filter_tap(f, i, j);
+                                if (k != 0.f)
+                                    acc = fmaf(k, sdp[((4 * cl + f) * HH_ + (r + 1 - (i - 1))) * HW_ + (s + 1 - (j - 1))], acc);
+                            }
+                    const int64_t o = ((int64_t)n * C + hf * (C / ADJ_HALVES) + cl) * plane + pix;
+                    gx[o] = (live ? gy[o] : 0.f) + acc;
+                }
+            }
+            __syncthreads();  // sdp (and sal) are rewritten by the next pass or block
         }
-        __syncthreads();  // sdp and sal are rewritten for the next block
     }
 }
 
