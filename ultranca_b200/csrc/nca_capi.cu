@@ -222,7 +222,7 @@ int fwd_ctas_per_sm()
 {
     using D = Dims<I::C, I::HID>;
     auto kernel = I::FP32 ? fwd_kernel<I::C, I::HID, false, I::GROW> : fwd_kernel<I::C, I::HID, true, I::GROW>;
-    return ctas_per_sm(kernel, D::fwd_smem(), I::FP32 ? 0 : D::FWD_TMEM);
+    return ctas_per_sm(kernel, D::fwd_smem(), I::FP32 ? 0 : D::FWD_TMEM, I::FP32 ? 128 : 128 * FWD_TILE_PARTS);
 }
 
 template <class I>
@@ -346,7 +346,7 @@ void launch_forward(const float *x, const float *w1, const float *b1, const floa
         if (II::FP32)
             fwd_kernel<II::C, II::HID, false, II::GROW><<<G, 128, D::fwd_smem(), stream>>>(a);
         else
-            fwd_kernel<II::C, II::HID, true, II::GROW><<<G, 128, D::fwd_smem(), stream>>>(a);
+            fwd_kernel<II::C, II::HID, true, II::GROW><<<G, 128 * FWD_TILE_PARTS, D::fwd_smem(), stream>>>(a);
         CUDA_OK(cudaGetLastError());
     });
 }

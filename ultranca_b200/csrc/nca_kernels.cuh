@@ -177,11 +177,12 @@ __device__ __forceinline__ void load_halo_async(float *XS, const float *x, int n
 // Perception of tile pixel i into P (chunk-planar, plane c = the four filters of channel c, then the bias plane
 // {1, 1, 0, 0} and a zero plane). Invalid pixels get an all-zero row.
 template <class D, bool TC>
-__device__ __forceinline__ void perceive_tile(float *P, const float *XS, const TileGeom &g, int i, bool valid)
+__device__ __forceinline__ void perceive_tile(float *P, const float *XS, const TileGeom &g, int i, bool valid, int c0 = 0,
+                                              int nc = D::C, bool bias = true)
 {
     const int r = i / g.S, s = i - r * g.S, SS = g.S + 2, per = (g.R + 2) * SS;
 #pragma unroll 4
-    for (int c = 0; c < D::C; ++c) {
+    for (int c = c0; c < c0 + nc; ++c) {
         float4 p = make_float4(0.f, 0.f, 0.f, 0.f);
         if (valid) {
             float v[3][3];
@@ -197,6 +198,8 @@ __device__ __forceinline__ void perceive_tile(float *P, const float *XS, const T
         }
         *reinterpret_cast<float4 *>(P + c * D::PLANE + i * 4) = p;
     }
+    if (!bias)
+        return;
     *reinterpret_cast<float4 *>(P + (D::PIN / 4) * D::PLANE + i * 4) = valid ? make_float4(1.f, 1.f, 0.f, 0.f) : make_float4(0.f, 0.f, 0.f, 0.f);
     *reinterpret_cast<float4 *>(P + (D::PIN / 4 + 1) * D::PLANE + i * 4) = make_float4(0.f, 0.f, 0.f, 0.f);
 }
@@ -246,21 +249,22 @@ __device__ __forceinline__ TileCoord tile_coord(int64_t t, const TileGeom &g, in
 // is 0 on the whole interior whatever the update computes: the tile writes zeros and runs no MLP. Every thread reads its
 // share of each tile's (GI_R + 4) x (GI_S + 4) window, 8 tiles' worth in flight per round, then a block-wide OR; every
 // thread of the block calls it.
-template <int C>
+template <int C, int NT = 128>
 __device__ __forceinline__ uint32_t grow_tiles_live(const StepArgs &a, const TileGeom &g, int64_t t, int64_t t1,
                                                     uint32_t *sw)
 {
-    constexpr int SO = GI_S + 4, WIN = (GI_R + 4) * SO;  // 180 positions: threadIdx.x and threadIdx.x + 128
-    int dr[2], dc[2];
+    constexpr int SO = GI_S + 4, WIN = (GI_R + 4) * SO;  // 180 positions: threadIdx.x, threadIdx.x + NT, ..
+    constexpr int NQ = (WIN + NT - 1) / NT;
+    int dr[NQ], dc[NQ];
 #pragma unroll
-    for (int q = 0; q < 2; ++q) {
-        const int e = threadIdx.x + 128 * q;
+    for (int q = 0; q < NQ; ++q) {
+        const int e = threadIdx.x + NT * q;
         dr[q] = e < WIN ? e / SO - 2 : -1000000;
         dc[q] = e < WIN ? e % SO - 2 : 0;
     }
     uint32_t mine = 0;
     for (int i0 = 0; i0 < 32; i0 += 8) {
-        float v[8][2];
+        float v[8][NQ];
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
             const int64_t u = t + i0 + i;
@@ -269,16 +273,21 @@ __device__ __forceinline__ uint32_t grow_tiles_live(const StepArgs &a, const Til
             const int iy0 = tc.ty * GI_R, ix0 = tc.tx * GI_S;
             const float *xa = a.x + ((size_t)tc.n * C + 3) * (size_t)a.H * a.W;
 #pragma unroll
-            for (int q = 0; q < 2; ++q) {
+            for (int q = 0; q < NQ; ++q) {
                 const int Y = iy0 + dr[q], X = ix0 + dc[q];
                 v[i][q] = tile_ok && Y >= 0 && Y < a.H && X >= 0 && X < a.W ? __ldg(xa + (size_t)Y * a.W + X) : 0.f;
             }
         }
 #pragma unroll
-        for (int i = 0; i < 8; ++i)
-            mine |= v[i][0] > 0.1f || v[i][1] > 0.1f ? 1u << (i0 + i) : 0u;
+        for (int i = 0; i < 8; ++i) {
+            bool lv = false;
+#pragma unroll
+            for (int q = 0; q < NQ; ++q)
+                lv |= v[i][q] > 0.1f;
+            mine |= lv ? 1u << (i0 + i) : 0u;
+        }
     }
-    return block_or_128(mine, sw);
+    return block_or<NT>(mine, sw);
 }
 
 // Growing NCAs, backward: a tile with no pixel alive after its forward step has gm = gy m a = 0 throughout, so it adds
@@ -292,9 +301,16 @@ __device__ __forceinline__ bool pixel_alive(const StepArgs &a, const TileGeom &g
     return px < g.R * g.S && Y < a.H && X < a.W && a.alive[((size_t)tc.n * a.H + Y) * a.W + X] != 0;
 }
 
+// Parts of 128 threads of the TF32 tile forward (fwd_kernel<.., true, ..>): part p runs channels [C p / NP, ..) of the
+// halo perception and the epilogue and hidden units [HID p / NP, ..) of the relu pass, for its lane's pixel; two CTAs
+// per SM (registers capped for it).
+constexpr int FWD_TILE_PARTS = 2;
+
 template <int C, int HID, bool TC, bool GROWING>
-__global__ void __launch_bounds__(128, 1) fwd_kernel(StepArgs a)
+__global__ void __launch_bounds__(128 * (TC ? FWD_TILE_PARTS : 1), TC ? 2 : 1) fwd_kernel(StepArgs a)
 {
+    constexpr int NP = TC ? FWD_TILE_PARTS : 1, NT = 128 * NP, CPP = C / NP, HPP = HID / NP;
+    static_assert(C % NP == 0 && HPP % 16 == 0, "forward tile parts");
     a.seed = step_seed_of(a);
     using D = Dims<C, HID>;
     extern __shared__ __align__(128) float smem[];
@@ -302,14 +318,14 @@ __global__ void __launch_bounds__(128, 1) fwd_kernel(StepArgs a)
     uint64_t *bar = reinterpret_cast<uint64_t *>(XS + D::XS_FLOATS);
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bar + 1);
 
-    const int tid = threadIdx.x, warp = tid / 32;
+    const int tid = threadIdx.x, warp = tid / 32, part = tid / 128, lt = tid % 128;
     const TileGeom g = GROWING ? make_grow_fwd_geom(a.H, a.W) : make_geom(a.H, a.W);
     const int64_t T = (int64_t)a.N * g.tiles_per_image;
     int64_t t0, t1;
     cta_range(T, gridDim.x, blockIdx.x, &t0, &t1);
     const bool stoch = a.rate < 1.f;
     const size_t plane = (size_t)a.H * a.W;
-    __shared__ uint32_t sw[4];
+    __shared__ uint32_t sw[NT / 32];
     __shared__ float XA[GROWING ? 128 : 1], YA[GROWING ? 128 : 1];  // growing: x_alpha and unmasked new alpha per lane
     uint32_t live_bits = 0;  // growing: liveness of tiles [live_base, live_base + 32)
     int64_t live_base = t0 - 64;
@@ -338,21 +354,21 @@ __global__ void __launch_bounds__(128, 1) fwd_kernel(StepArgs a)
             tc.y0 = tc.ty * GI_R - 1;
             tc.x0 = tc.tx * GI_S - 1;
         }
-        const int r = tid / g.S, s = tid - r * g.S;
+        const int r = lt / g.S, s = lt - r * g.S;
         const bool valid = GROWING ? tc.y0 + r >= 0 && tc.y0 + r < a.H && tc.x0 + s >= 0 && tc.x0 + s < a.W
-                                   : tid < g.R * g.S && tc.y0 + r < a.H && tc.x0 + s < a.W;
+                                   : lt < g.R * g.S && tc.y0 + r < a.H && tc.x0 + s < a.W;
         // growing: the lane's cell is in the interior (written by this tile)
         const bool inner = GROWING && valid && r >= 1 && r <= GI_R && s >= 1 && s <= GI_S;
         const size_t cell = (size_t)tc.n * plane + (size_t)(tc.y0 + r) * a.W + (tc.x0 + s);
         if (GROWING) {  // dead tile (block-uniform): no MLP, no halo copy; its interior is dead after the step
             if (t >= live_base + 32) {
                 live_base = t;
-                live_bits = grow_tiles_live<C>(a, g, t, t1, sw);
+                live_bits = grow_tiles_live<C, NT>(a, g, t, t1, sw);
             }
             if (!((live_bits >> (t - live_base)) & 1u)) {
-                // y = 0 and alive = 0 on the interior; in a rollout's reuse steps a cell dead in this destination two
-                // steps ago already holds both
-                if (inner && (!a.reuse || a.alive_out[cell])) {
+                // y = 0 and alive = 0 on the interior, by part 0 (its reuse check reads the alive byte it writes); in a
+                // rollout's reuse steps a cell dead in this destination two steps ago already holds both
+                if (part == 0 && inner && (!a.reuse || a.alive_out[cell])) {
                     float *yn = a.y + (size_t)tc.n * C * plane + (cell - (size_t)tc.n * plane);
 #pragma unroll
                     for (int c = 0; c < C; ++c)
@@ -367,11 +383,11 @@ __global__ void __launch_bounds__(128, 1) fwd_kernel(StepArgs a)
                                  a.w2 + (size_t)tc.k * C * HID);
             cur_k = tc.k;
         }
-        load_halo_async<D>(XS, a.x, tc.n, g, tc.y0, tc.x0);
+        load_halo_async<D, NT>(XS, a.x, tc.n, g, tc.y0, tc.x0);
         cp_async_wait_all();
         __syncthreads();
-        perceive_tile<D, TC>(P, XS, g, tid, valid);
-        float u[16];
+        perceive_tile<D, TC>(P, XS, g, lt, valid, CPP * part, CPP, part == 0);
+        float u[CPP];  // this part's channels of the update
         if constexpr (TC) {
             umma::fence_proxy_async();
             __syncthreads();
@@ -392,11 +408,11 @@ __global__ void __launch_bounds__(128, 1) fwd_kernel(StepArgs a)
                 break;
             }
             umma::fence_after_sync();
-            // relu(h) back into the same TMEM columns (TF32-rounded): the A operand of h -> u
+            // relu(h) back into the same TMEM columns (TF32-rounded): the A operand of h -> u (this part's columns)
 #pragma unroll
-            for (int cc = 0; cc < HID / 16; ++cc) {
+            for (int cc = 0; cc < HPP / 16; ++cc) {
                 float v[16];
-                const uint32_t ad = umma::tmem_addr(tmem, warp, cc * 16);
+                const uint32_t ad = umma::tmem_addr(tmem, warp, HPP * part + cc * 16);
                 umma::tmem_ld16(ad, v);
                 umma::tmem_wait_ld();
 #pragma unroll
@@ -423,17 +439,19 @@ __global__ void __launch_bounds__(128, 1) fwd_kernel(StepArgs a)
                 break;
             }
             umma::fence_after_sync();
-            umma::tmem_ld16(umma::tmem_addr(tmem, warp, HID), u);
-            umma::tmem_wait_ld();
+#pragma unroll
+            for (int cc = 0; cc < CPP; ++cc)
+                u[cc] = umma::tmem_ld1(umma::tmem_addr(tmem, warp, HID + CPP * part + cc));
+            umma::tmem_wait_ld();  // the loaded registers are defined only after this wait
         } else {
 #pragma unroll
-            for (int c = 0; c < 16; ++c)
+            for (int c = 0; c < CPP; ++c)
                 u[c] = 0.f;
             if (valid) {
                 float p[D::PIN];
 #pragma unroll
                 for (int f = 0; f < D::PIN; ++f)
-                    p[f] = P[(f / 4) * D::PLANE + tid * 4 + (f % 4)];
+                    p[f] = P[(f / 4) * D::PLANE + lt * 4 + (f % 4)];
                 for (int j = 0; j < HID; ++j) {
                     const float *wrow = W1s + j * 4;
                     float h = wrow[(D::PIN / 4) * HID * 4];
@@ -443,7 +461,7 @@ __global__ void __launch_bounds__(128, 1) fwd_kernel(StepArgs a)
                     h = fmaxf(h, 0.f);
                     const float *w2c = W2s + (j / 4) * D::CP * 4 + (j % 4);
 #pragma unroll
-                    for (int c = 0; c < C; ++c)
+                    for (int c = 0; c < CPP; ++c)
                         u[c] = fmaf(w2c[c * 4], h, u[c]);
                 }
             }
@@ -454,25 +472,29 @@ __global__ void __launch_bounds__(128, 1) fwd_kernel(StepArgs a)
             const int SS = g.S + 2, per = (g.R + 2) * SS;
             float *yn = a.y + (size_t)tc.n * C * plane + (size_t)Y * a.W + X;
 #pragma unroll
-            for (int c = 0; c < C; ++c) {
+            for (int cc = 0; cc < CPP; ++cc) {
+                const int c = CPP * part + cc;
                 const float xc = XS[c * per + (r + 1) * SS + s + 1];
-                yn[(size_t)c * plane] = m != 0.f ? xc + u[c] : xc;
+                yn[(size_t)c * plane] = m != 0.f ? xc + u[cc] : xc;
             }
         }
         if constexpr (GROWING) {
             // the alive mask in the epilogue (ncaops/nca_step.cuh:693-727 semantics): a = (maxpool3(x_alpha) > 0.1) &
             // (maxpool3(unmasked new alpha) > 0.1), cells outside the grid ignored; y = a ? unmasked y : 0
+            static_assert(!GROWING || CPP > 3, "the alpha channel belongs to part 0");
             const int SS = g.S + 2, per = (g.R + 2) * SS;
-            float yv[C];
+            float yv[CPP];
             const float m = valid && stoch ? update_mask_at(a.seed, a.rate, tc.n + a.n_offset, a.H, a.W, tc.y0 + r,
                                                             tc.x0 + s) : 1.f;
 #pragma unroll
-            for (int c = 0; c < C; ++c) {
-                const float xc = XS[c * per + (r + 1) * SS + s + 1];
-                yv[c] = m != 0.f ? xc + u[c] : xc;
+            for (int cc = 0; cc < CPP; ++cc) {
+                const float xc = XS[(CPP * part + cc) * per + (r + 1) * SS + s + 1];
+                yv[cc] = m != 0.f ? xc + u[cc] : xc;
             }
-            XA[tid] = valid ? XS[3 * per + (r + 1) * SS + s + 1] : -1.f;
-            YA[tid] = valid ? yv[3] : -1.f;
+            if (part == 0) {
+                XA[lt] = valid ? XS[3 * per + (r + 1) * SS + s + 1] : -1.f;
+                YA[lt] = valid ? yv[3] : -1.f;
+            }
             __syncthreads();
             if (inner) {
                 float mx = -1.f, my = -1.f;
@@ -485,11 +507,12 @@ __global__ void __launch_bounds__(128, 1) fwd_kernel(StepArgs a)
                         my = fmaxf(my, YA[q]);
                     }
                 const bool live = mx > 0.1f && my > 0.1f;
-                float *yn = a.y + (size_t)tc.n * C * plane + (cell - (size_t)tc.n * plane);
+                float *yn = a.y + ((size_t)tc.n * C + CPP * part) * plane + (cell - (size_t)tc.n * plane);
 #pragma unroll
-                for (int c = 0; c < C; ++c)
-                    yn[(size_t)c * plane] = live ? yv[c] : 0.f;
-                a.alive_out[cell] = live ? 1 : 0;
+                for (int cc = 0; cc < CPP; ++cc)
+                    yn[(size_t)cc * plane] = live ? yv[cc] : 0.f;
+                if (part == 0)
+                    a.alive_out[cell] = live ? 1 : 0;
             }
         }
         if constexpr (TC)
