@@ -13,6 +13,7 @@
 #include <cstring>
 #include <map>
 #include <mutex>
+#include <numeric>
 #include <stdexcept>
 #include <utility>
 #include <string>
@@ -179,6 +180,22 @@ void dispatch(int64_t C, int64_t HID, bool fp32, bool growing, F &&f)
     }
 }
 
+// Visiting order of an NCA's M tiles in the growing tile kernels: u -> u P mod M with P coprime to M near M times the
+// golden ratio, so that consecutive tiles (a living region) land far apart and the CTAs sharing an NCA get similar
+// numbers of live tiles. Only where a CTA's share of the launch is under half an image (tiles per CTA < tiles per image
+// / 2): there one CTA may hold most of an image's living region while its neighbours idle. With larger shares every
+// CTA already spans whole images, and the natural order keeps the locality of consecutive tiles (measured: 72 x 72
+// grids at 3.5 images per CTA ran 25% slower scattered, 128 x 128 ones at 0.4 images per CTA 13% faster). 0: in order.
+uint32_t tile_perm_for(int64_t M, int64_t tiles, int64_t grid, int64_t tiles_per_image)
+{
+    if (M <= 2 || tiles >= grid * (tiles_per_image / 2))
+        return 0;
+    int64_t P = std::max<int64_t>(1, (int64_t)((double)M * 0.6180339887498949));
+    while (std::gcd(P, M) != 1)
+        ++P;
+    return (uint32_t)P;
+}
+
 // The tile kernels index a launch's tiles in 32 bits.
 void check_tiles(int64_t tiles)
 {
@@ -343,6 +360,22 @@ void launch_forward(const float *x, const float *w1, const float *b1, const floa
         const TileGeom g = II::GROW ? make_grow_fwd_geom((int)s.H, (int)s.W) : make_geom((int)s.H, (int)s.W);
         check_tiles(s.N * g.tiles_per_image);
         const int G = grid_for(s.N * g.tiles_per_image, fwd_ctas_per_sm<II>());
+        a.tile_perm = II::GROW ? tile_perm_for(s.B * g.tiles_per_image, s.N * g.tiles_per_image, G, g.tiles_per_image) : 0;
+        // (the scattered tile order is a kernel instance of its own; growing NCAs only)
+        auto go = [&](auto kern, int threads) {
+            set_smem_once(kern, D::fwd_smem());
+            kern<<<G, threads, D::fwd_smem(), stream>>>(a);
+        };
+        if constexpr (II::GROW) {
+            if (a.tile_perm != 0) {
+                if (II::FP32)
+                    go(fwd_kernel<II::C, II::HID, false, true, true>, 128);
+                else
+                    go(fwd_kernel<II::C, II::HID, true, true, true>, 128 * FWD_TILE_PARTS);
+                CUDA_OK(cudaGetLastError());
+                return;
+            }
+        }
         if (II::FP32)
             fwd_kernel<II::C, II::HID, false, II::GROW><<<G, 128, D::fwd_smem(), stream>>>(a);
         else
@@ -540,6 +573,9 @@ int backward_stages_impl(const float *x, const float *gy, const uint8_t *alive, 
             a.seed_dev = seed_dev; a.step = step;
             a.partial_add = (stages & NCA_STAGE_PARTIAL_ADD) ? 1 : 0;
             const TileGeom g = make_geom((int)H, (int)W, II::GROW);
+            a.tile_perm = II::GROW ? tile_perm_for((int64_t)batch_per_nca * g.tiles_per_image, N * g.tiles_per_image, w.grid,
+                                                   g.tiles_per_image)
+                                   : 0;
             const bool strip = strip_path(s, fp32, growing) && aligned16(x) && aligned16(gy) && aligned16(gx) &&
                                aligned16(dp);
             const bool rows = strip || (rows_path(s, fp32, growing) && aligned16(x) && aligned16(gy) && aligned16(gx));
@@ -587,7 +623,18 @@ int backward_stages_impl(const float *x, const float *gy, const uint8_t *alive, 
                     CUDA_OK(cudaGetLastError());
                 }
             } else {
-                if (stages & NCA_STAGE_MAIN) {
+                if ((stages & NCA_STAGE_MAIN) && II::GROW && a.tile_perm != 0) {  // the scattered tile order
+                    if constexpr (II::GROW) {
+                        if (II::FP32) {
+                            set_smem_once(bwd_kernel_cc<II::C, II::HID, true, true>, D::bwd_smem_cc());
+                            bwd_kernel_cc<II::C, II::HID, true, true><<<w.grid, 128, D::bwd_smem_cc(), st>>>(a);
+                        } else {
+                            set_smem_once(bwd_kernel_tc<II::C, II::HID, true, true>, D::bwd_smem_tc(true));
+                            bwd_kernel_tc<II::C, II::HID, true, true><<<w.grid, 128 * BWD_TILE_PARTS, D::bwd_smem_tc(true), st>>>(a);
+                        }
+                    }
+                    CUDA_OK(cudaGetLastError());
+                } else if (stages & NCA_STAGE_MAIN) {
                     if (II::FP32)
                         bwd_kernel_cc<II::C, II::HID, II::GROW><<<w.grid, 128, D::bwd_smem_cc(), st>>>(a);
                     else

@@ -78,6 +78,9 @@ struct StepArgs {
     const uint64_t *seed_dev;      // non-null: the step's seed is splitmix_step(*seed_dev, step), read at run time
     int64_t step;                  // (a launch recorded once in a CUDA graph and replayed with new rollout seeds)
     int band_s4, band_n4;          // row kernels: switch costs of the cost-balanced bands (Bands)
+    uint32_t tile_perm;            // growing tile kernels: an NCA's M tiles are visited in the order u -> u tile_perm mod
+                                   // M (coprime to M; 0: in order), so that the tiles of a living region, which are
+                                   // consecutive, spread over the CTAs that share the NCA
     uint8_t *alive_out;            // growing forward: the alive mask of the step (N, H, W)
     int reuse;                     // growing rollout from its third step: alive_out holds this destination's map of two
                                    // steps ago (cells 0 there hold state 0)
@@ -225,11 +228,18 @@ __device__ __forceinline__ uint32_t block_or(uint32_t v, uint32_t *sw)
 }
 __device__ __forceinline__ uint32_t block_or_128(uint32_t v, uint32_t *sw) { return block_or<128>(v, sw); }
 
-// Tile t of a launch (32-bit arithmetic: the host keeps a launch's tile count below 2^31).
-__device__ __forceinline__ TileCoord tile_coord(int64_t t, const TileGeom &g, int B)
+// Tile t of a launch (32-bit arithmetic: the host keeps a launch's tile count below 2^31); PERM: visited in the order
+// of a.tile_perm within its NCA (a separate kernel instance, so that the in-order kernels carry none of it).
+template <bool PERM = false>
+__device__ __forceinline__ TileCoord tile_coord(int64_t t, const TileGeom &g, const StepArgs &a)
 {
     TileCoord tc;
-    const uint32_t u = (uint32_t)t, tpi = (uint32_t)g.tiles_per_image, strips = (uint32_t)g.strips;
+    const uint32_t tpi = (uint32_t)g.tiles_per_image, strips = (uint32_t)g.strips, B = (uint32_t)a.B;
+    uint32_t u = (uint32_t)t;
+    if (PERM) {
+        const uint32_t M = B * tpi, k = u / M, v = u - k * M;
+        u = k * M + (uint32_t)(((uint64_t)v * a.tile_perm) % M);
+    }
     const uint32_t n = u / tpi, ti = u - n * tpi, ty = ti / strips;
     tc.n = (int)n;
     tc.k = (int)(n / (uint32_t)B);
@@ -249,7 +259,7 @@ __device__ __forceinline__ TileCoord tile_coord(int64_t t, const TileGeom &g, in
 // is 0 on the whole interior whatever the update computes: the tile writes zeros and runs no MLP. Every thread reads its
 // share of each tile's (GI_R + 4) x (GI_S + 4) window, 8 tiles' worth in flight per round, then a block-wide OR; every
 // thread of the block calls it.
-template <int C, int NT = 128>
+template <int C, int NT = 128, bool PERM = false>
 __device__ __forceinline__ uint32_t grow_tiles_live(const StepArgs &a, const TileGeom &g, int64_t t, int64_t t1,
                                                     uint32_t *sw)
 {
@@ -269,7 +279,7 @@ __device__ __forceinline__ uint32_t grow_tiles_live(const StepArgs &a, const Til
         for (int i = 0; i < 8; ++i) {
             const int64_t u = t + i0 + i;
             const bool tile_ok = u < t1;
-            const TileCoord tc = tile_coord(tile_ok ? u : t, g, a.B);
+            const TileCoord tc = tile_coord<PERM>(tile_ok ? u : t, g, a);
             const int iy0 = tc.ty * GI_R, ix0 = tc.tx * GI_S;
             const float *xa = a.x + ((size_t)tc.n * C + 3) * (size_t)a.H * a.W;
 #pragma unroll
@@ -293,9 +303,10 @@ __device__ __forceinline__ uint32_t grow_tiles_live(const StepArgs &a, const Til
 // Growing NCAs, backward: a tile with no pixel alive after its forward step has gm = gy m a = 0 throughout, so it adds
 // nothing to the weight gradients and its dp is 0; the backward skips it without writing its dp, and the adjoint
 // reads dp at alive cells only. Tile pixel px of tile t alive (false when the pixel is outside the image).
+template <bool PERM = false>
 __device__ __forceinline__ bool pixel_alive(const StepArgs &a, const TileGeom &g, int64_t t, int px)
 {
-    const TileCoord tc = tile_coord(t, g, a.B);
+    const TileCoord tc = tile_coord<PERM>(t, g, a);
     const int r = px / g.S, s = px - r * g.S;
     const int Y = tc.y0 + r, X = tc.x0 + s;
     return px < g.R * g.S && Y < a.H && X < a.W && a.alive[((size_t)tc.n * a.H + Y) * a.W + X] != 0;
@@ -306,7 +317,7 @@ __device__ __forceinline__ bool pixel_alive(const StepArgs &a, const TileGeom &g
 // per SM (registers capped for it).
 constexpr int FWD_TILE_PARTS = 2;
 
-template <int C, int HID, bool TC, bool GROWING>
+template <int C, int HID, bool TC, bool GROWING, bool PERM = false>
 __global__ void __launch_bounds__(128 * (TC ? FWD_TILE_PARTS : 1), TC ? 2 : 1) fwd_kernel(StepArgs a)
 {
     constexpr int NP = TC ? FWD_TILE_PARTS : 1, NT = 128 * NP, CPP = C / NP, HPP = HID / NP;
@@ -349,7 +360,7 @@ __global__ void __launch_bounds__(128 * (TC ? FWD_TILE_PARTS : 1), TC ? 2 : 1) f
     int cur_k = -1;
     bool failed = false;
     for (int64_t t = t0; t < t1 && !failed; ++t) {
-        TileCoord tc = tile_coord(t, g, a.B);
+        TileCoord tc = tile_coord<PERM>(t, g, a);
         if (GROWING) {  // the extended tile's origin: one cell above and left of the interior
             tc.y0 = tc.ty * GI_R - 1;
             tc.x0 = tc.tx * GI_S - 1;
@@ -363,7 +374,7 @@ __global__ void __launch_bounds__(128 * (TC ? FWD_TILE_PARTS : 1), TC ? 2 : 1) f
         if (GROWING) {  // dead tile (block-uniform): no MLP, no halo copy; its interior is dead after the step
             if (t >= live_base + 32) {
                 live_base = t;
-                live_bits = grow_tiles_live<C, NT>(a, g, t, t1, sw);
+                live_bits = grow_tiles_live<C, NT, PERM>(a, g, t, t1, sw);
             }
             if (!((live_bits >> (t - live_base)) & 1u)) {
                 // y = 0 and alive = 0 on the interior, by part 0 (its reuse check reads the alive byte it writes); in a
@@ -610,7 +621,7 @@ __device__ __forceinline__ void load_gm_channels(float (&gm)[NCH], const StepArg
 }
 
 // fp32 mode: the MLP on CUDA cores in fp32, weight gradients accumulated by threads j < HID in registers.
-template <int C, int HID, bool GROWING>
+template <int C, int HID, bool GROWING, bool PERM = false>
 __global__ void __launch_bounds__(128, 1) bwd_kernel_cc(StepArgs a)
 {
     a.seed = step_seed_of(a);
@@ -651,7 +662,7 @@ __global__ void __launch_bounds__(128, 1) bwd_kernel_cc(StepArgs a)
     int64_t live_base = t0 - 64;
     bool staged = false;
     for (int64_t t = t0; t < t1; ++t) {
-        const TileCoord tc = tile_coord(t, g, a.B);
+        const TileCoord tc = tile_coord<PERM>(t, g, a);
         if (tc.k != cur_k) {
             if (cur_k >= 0)
                 flush(cur_k);
@@ -665,7 +676,7 @@ __global__ void __launch_bounds__(128, 1) bwd_kernel_cc(StepArgs a)
                 uint32_t mine = 0;
 #pragma unroll
                 for (int i = 0; i < 32; ++i)
-                    mine |= t + i < t1 && pixel_alive(a, g, t + i, tid) ? 1u << i : 0u;
+                    mine |= t + i < t1 && pixel_alive<PERM>(a, g, t + i, tid) ? 1u << i : 0u;
                 live_bits = block_or_128(mine, sw);
             }
             if (!((live_bits >> (t - live_base)) & 1u))
@@ -783,7 +794,7 @@ __device__ __forceinline__ void st_sw32x8(float *tile, int mn0, int k, int krows
 //   5. dh -> smem (swizzled, over relu(h)); dW1' += dh^T p' while dp is stored to the dp scratch.
 // The bias features of p' (1 at PIN and PIN + 1, zeros up to the operand widths) and gm's channels C..15 are constant:
 // written once.
-template <int C, int HID, bool GROWING>
+template <int C, int HID, bool GROWING, bool PERM = false>
 __global__ void __launch_bounds__(128 * BWD_TILE_PARTS, 1) bwd_kernel_tc(StepArgs a)
 {
     constexpr int NP = BWD_TILE_PARTS, NT = 128 * NP, CPP = C / NP, HPP = HID / NP, PPP = 4 * CPP;
@@ -887,9 +898,9 @@ __global__ void __launch_bounds__(128 * BWD_TILE_PARTS, 1) bwd_kernel_tc(StepArg
     int64_t live_base = t0 - 64;
     bool staged = false;
     // every NCA this CTA's tile range overlaps gets its partial slot written (the reduction reads them all)
-    const int k_last = t1 > t0 ? tile_coord(t1 - 1, g, a.B).k : -1;
+    const int k_last = t1 > t0 ? tile_coord<PERM>(t1 - 1, g, a).k : -1;
     if (t1 > t0)
-        cur_k = tile_coord(t0, g, a.B).k;
+        cur_k = tile_coord<PERM>(t0, g, a).k;
     // the next tile with an alive pixel from t on (growing; a dead tile adds nothing and its dp is not read), or t1
     auto next_live = [&](int64_t t) {
         if (GROWING) {
@@ -900,7 +911,7 @@ __global__ void __launch_bounds__(128 * BWD_TILE_PARTS, 1) bwd_kernel_tc(StepArg
                     if (part == 0) {
 #pragma unroll
                         for (int i = 0; i < 32; ++i)
-                            mine |= t + i < t1 && pixel_alive(a, g, t + i, lt) ? 1u << i : 0u;
+                            mine |= t + i < t1 && pixel_alive<PERM>(a, g, t + i, lt) ? 1u << i : 0u;
                     }
                     live_bits = block_or<NT>(mine, sw);
                 }
@@ -919,7 +930,7 @@ __global__ void __launch_bounds__(128 * BWD_TILE_PARTS, 1) bwd_kernel_tc(StepArg
     float *XS = prefetch ? XSP : RHDH;
     float gmn[CPP];
     auto request = [&](int64_t tn) {
-        const TileCoord tq = tile_coord(tn, g, a.B);
+        const TileCoord tq = tile_coord<PERM>(tn, g, a);
         load_halo_async<D, NT>(XS, a.x, tq.n, g, tq.y0, tq.x0);
         const int rq = lt / g.S, sq = lt - rq * g.S;
         const bool vq = lt < g.R * g.S && tq.y0 + rq < a.H && tq.x0 + sq < a.W;
@@ -929,7 +940,7 @@ __global__ void __launch_bounds__(128 * BWD_TILE_PARTS, 1) bwd_kernel_tc(StepArg
     if (prefetch && t < t1)
         request(t);
     while (t < t1) {
-        const TileCoord tc = tile_coord(t, g, a.B);
+        const TileCoord tc = tile_coord<PERM>(t, g, a);
         if (tc.k != cur_k) {
             flush(cur_k, started);
             for (int kk = cur_k + 1; kk < tc.k; ++kk)  // NCAs whose tiles here are all dead
