@@ -598,26 +598,28 @@ __device__ __forceinline__ bool load_gm(float (&gm)[16], const StepArgs &a, cons
     return live;
 }
 
-// load_gm for the NCH channels c0 .. c0 + NCH - 1 only.
+// load_gm for the NCH channels c0 .. c0 + NCH - 1 only. Returns whether the pixel is valid and (growing) alive.
 template <int C, int NCH, bool GROWING>
-__device__ __forceinline__ void load_gm_channels(float (&gm)[NCH], const StepArgs &a, const TileCoord &tc, int Y, int X,
+__device__ __forceinline__ bool load_gm_channels(float (&gm)[NCH], const StepArgs &a, const TileCoord &tc, int Y, int X,
                                                  bool valid, bool stoch, int c0)
 {
 #pragma unroll
     for (int c = 0; c < NCH; ++c)
         gm[c] = 0.f;
     if (!valid)
-        return;
+        return false;
     const size_t plane = (size_t)a.H * a.W;
     float m = stoch ? update_mask_at(a.seed, a.rate, tc.n + a.n_offset, a.H, a.W, Y, X) : 1.f;
-    if (GROWING && !a.alive[(size_t)tc.n * plane + (size_t)Y * a.W + X])
+    const bool live = !GROWING || a.alive[(size_t)tc.n * plane + (size_t)Y * a.W + X];
+    if (!live)
         m = 0.f;
     if (m == 0.f)
-        return;
+        return live;
     const float *gyn = a.gy + ((size_t)tc.n * C + c0) * plane + (size_t)Y * a.W + X;
 #pragma unroll
     for (int c = 0; c < NCH; ++c)
         gm[c] = __ldg(gyn + (size_t)c * plane);
+    return true;
 }
 
 // fp32 mode: the MLP on CUDA cores in fp32, weight gradients accumulated by threads j < HID in registers.
@@ -929,12 +931,13 @@ __global__ void __launch_bounds__(128 * BWD_TILE_PARTS, 1) bwd_kernel_tc(StepArg
     const bool prefetch = (g.R + 2) * (g.S + 2) <= D::xs_pos(GROWING);
     float *XS = prefetch ? XSP : RHDH;
     float gmn[CPP];
+    bool livn = false;  // the requested tile's pixel is valid and (growing) alive
     auto request = [&](int64_t tn) {
         const TileCoord tq = tile_coord<PERM>(tn, g, a);
         load_halo_async<D, NT>(XS, a.x, tq.n, g, tq.y0, tq.x0);
         const int rq = lt / g.S, sq = lt - rq * g.S;
         const bool vq = lt < g.R * g.S && tq.y0 + rq < a.H && tq.x0 + sq < a.W;
-        load_gm_channels<C, CPP, GROWING>(gmn, a, tq, tq.y0 + rq, tq.x0 + sq, vq, stoch, CPP * part);
+        livn = load_gm_channels<C, CPP, GROWING>(gmn, a, tq, tq.y0 + rq, tq.x0 + sq, vq, stoch, CPP * part);
     };
     int64_t t = next_live(t0);
     if (prefetch && t < t1)
@@ -961,6 +964,8 @@ __global__ void __launch_bounds__(128 * BWD_TILE_PARTS, 1) bwd_kernel_tc(StepArg
         const int r = lt / g.S, s = lt - r * g.S;
         const bool valid = lt < g.R * g.S && tc.y0 + r < a.H && tc.x0 + s < a.W;
         const int Y = tc.y0 + r, X = tc.x0 + s;
+        // the pixel's dp is stored where the adjoint reads it: valid pixels, growing: alive ones (dp = 0 elsewhere)
+        const bool store_dp = livn;
 #pragma unroll
         for (int cc = 0; cc < CPP; ++cc) {  // gm of this part's channels -> TMEM G and the swizzled gm tile
             const float gv = tf32_bias(gmn[cc]);
@@ -1078,7 +1083,7 @@ __global__ void __launch_bounds__(128 * BWD_TILE_PARTS, 1) bwd_kernel_tc(StepArg
             for (int q = 0; q < PPP / 4; ++q)
                 umma::tmem_ld4(lane_base + D::T_P + PPP * part + 4 * q, v + 4 * q);
             umma::tmem_wait_ld();
-            if (valid)
+            if (store_dp)
 #pragma unroll
                 for (int e = 0; e < PPP; ++e)
                     dpn[(size_t)(PPP * part + e) * plane] = v[e];
