@@ -598,30 +598,6 @@ __device__ __forceinline__ bool load_gm(float (&gm)[16], const StepArgs &a, cons
     return live;
 }
 
-// load_gm for the NCH channels c0 .. c0 + NCH - 1 only. Returns whether the pixel is valid and (growing) alive.
-template <int C, int NCH, bool GROWING>
-__device__ __forceinline__ bool load_gm_channels(float (&gm)[NCH], const StepArgs &a, const TileCoord &tc, int Y, int X,
-                                                 bool valid, bool stoch, int c0)
-{
-#pragma unroll
-    for (int c = 0; c < NCH; ++c)
-        gm[c] = 0.f;
-    if (!valid)
-        return false;
-    const size_t plane = (size_t)a.H * a.W;
-    float m = stoch ? update_mask_at(a.seed, a.rate, tc.n + a.n_offset, a.H, a.W, Y, X) : 1.f;
-    const bool live = !GROWING || a.alive[(size_t)tc.n * plane + (size_t)Y * a.W + X];
-    if (!live)
-        m = 0.f;
-    if (m == 0.f)
-        return live;
-    const float *gyn = a.gy + ((size_t)tc.n * C + c0) * plane + (size_t)Y * a.W + X;
-#pragma unroll
-    for (int c = 0; c < NCH; ++c)
-        gm[c] = __ldg(gyn + (size_t)c * plane);
-    return true;
-}
-
 // fp32 mode: the MLP on CUDA cores in fp32, weight gradients accumulated by threads j < HID in registers.
 template <int C, int HID, bool GROWING, bool PERM = false>
 __global__ void __launch_bounds__(128, 1) bwd_kernel_cc(StepArgs a)
@@ -903,17 +879,25 @@ __global__ void __launch_bounds__(128 * BWD_TILE_PARTS, 1) bwd_kernel_tc(StepArg
     const int k_last = t1 > t0 ? tile_coord<PERM>(t1 - 1, g, a).k : -1;
     if (t1 > t0)
         cur_k = tile_coord<PERM>(t0, g, a).k;
+    // the lane's pixel within a tile (row, column), and whether it exists
+    const int lr = lt / g.S, ls = lt - lr * g.S;
+    const bool lin = lt < g.R * g.S;
     // the next tile with an alive pixel from t on (growing; a dead tile adds nothing and its dp is not read), or t1
     auto next_live = [&](int64_t t) {
         if (GROWING) {
             while (t < t1) {
-                if (t >= live_base + 32) {  // the alive bytes of 32 tiles' pixels (part 0), all loads in flight together
-                    live_base = t;
+                if (t >= live_base + 32) {  // the alive bytes of 32 tiles' pixels, part p the tiles p, p + NP, .., all
+                    live_base = t;          // loads in flight together
                     uint32_t mine = 0;
-                    if (part == 0) {
 #pragma unroll
-                        for (int i = 0; i < 32; ++i)
-                            mine |= t + i < t1 && pixel_alive<PERM>(a, g, t + i, lt) ? 1u << i : 0u;
+                    for (int i = part; i < 32; i += NP) {
+                        bool al = false;
+                        if (lin && t + i < t1) {
+                            const TileCoord tq = tile_coord<PERM>(t + i, g, a);
+                            const int Yq = tq.y0 + lr, Xq = tq.x0 + ls;
+                            al = Yq < a.H && Xq < a.W && a.alive[((size_t)tq.n * a.H + Yq) * a.W + Xq] != 0;
+                        }
+                        mine |= al ? 1u << i : 0u;
                     }
                     live_bits = block_or<NT>(mine, sw);
                 }
@@ -930,18 +914,38 @@ __global__ void __launch_bounds__(128 * BWD_TILE_PARTS, 1) bwd_kernel_tc(StepArg
     // that they arrive during its contractions; otherwise the halo goes to RHDH at the start of its own tile.
     const bool prefetch = (g.R + 2) * (g.S + 2) <= D::xs_pos(GROWING);
     float *XS = prefetch ? XSP : RHDH;
+    // The request is in two steps, so that no thread waits on memory in it: request() copies the halo, loads the
+    // pixel's alive byte (growing) and draws its update mask; request_gm(), some phases later, reads that byte and
+    // loads gy of this part's channels where gm = gy m a is not 0.
     float gmn[CPP];
-    bool livn = false;  // the requested tile's pixel is valid and (growing) alive
+    bool livn = false;     // the requested tile's pixel is valid and (growing) alive
+    size_t gq = 0;         // ... its offset in a channel plane of gy (image base included)
+    bool vq = false;       // ... is valid
+    uint8_t aq = 1;        // ... alive byte (growing)
+    float mq = 1.f;        // ... update mask
     auto request = [&](int64_t tn) {
         const TileCoord tq = tile_coord<PERM>(tn, g, a);
         load_halo_async<D, NT>(XS, a.x, tq.n, g, tq.y0, tq.x0);
-        const int rq = lt / g.S, sq = lt - rq * g.S;
-        const bool vq = lt < g.R * g.S && tq.y0 + rq < a.H && tq.x0 + sq < a.W;
-        livn = load_gm_channels<C, CPP, GROWING>(gmn, a, tq, tq.y0 + rq, tq.x0 + sq, vq, stoch, CPP * part);
+        const int Yq = tq.y0 + lr, Xq = tq.x0 + ls;
+        vq = lin && Yq < a.H && Xq < a.W;
+        gq = (size_t)tq.n * C * plane + (size_t)Yq * a.W + Xq;
+        if (GROWING)
+            aq = vq ? a.alive[(size_t)tq.n * plane + (size_t)Yq * a.W + Xq] : 0;
+        mq = vq && stoch ? update_mask_at(a.seed, a.rate, tq.n + a.n_offset, a.H, a.W, Yq, Xq) : 1.f;
+    };
+    auto request_gm = [&]() {
+        livn = vq && (!GROWING || aq != 0);
+        const bool act = livn && mq != 0.f;
+        const float *gyq = a.gy + gq + (size_t)(CPP * part) * plane;
+#pragma unroll
+        for (int cc = 0; cc < CPP; ++cc)
+            gmn[cc] = act ? __ldg(gyq + (size_t)cc * plane) : 0.f;
     };
     int64_t t = next_live(t0);
-    if (prefetch && t < t1)
+    if (prefetch && t < t1) {
         request(t);
+        request_gm();
+    }
     while (t < t1) {
         const TileCoord tc = tile_coord<PERM>(t, g, a);
         if (tc.k != cur_k) {
@@ -959,8 +963,10 @@ __global__ void __launch_bounds__(128 * BWD_TILE_PARTS, 1) bwd_kernel_tc(StepArg
             staged = true;
         }
         // ---- 1. inputs (requested one tile ahead when prefetching)
-        if (!prefetch)
+        if (!prefetch) {
             request(t);
+            request_gm();
+        }
         const int r = lt / g.S, s = lt - r * g.S;
         const bool valid = lt < g.R * g.S && tc.y0 + r < a.H && tc.x0 + s < a.W;
         const int Y = tc.y0 + r, X = tc.x0 + s;
@@ -1038,6 +1044,8 @@ __global__ void __launch_bounds__(128 * BWD_TILE_PARTS, 1) bwd_kernel_tc(StepArg
         umma::fence_proxy_async();
         umma::fence_before_sync();
         __syncthreads();
+        if (prefetch && t_next < t1)  // the next tile's alive byte has arrived by now: its gy loads
+            request_gm();
         // ---- 4. dW2^T += relu(h)^T gm (K = pixels, MN-major), DP = dh W1 (A from TMEM)
         if (tid == 0) {
             umma::fence_after_sync();
