@@ -50,7 +50,7 @@ struct Dims {
     static constexpr int BWD_W = ((W1S + W1T + W2T) * 4 + 1023) / 1024 * 1024;
     // + the halo buffer of the next tile (prefetched during the current tile's contractions), positions: growing
     // (compact 8 x 16 tiles) 180, otherwise up to 390 (R S <= 128), or as many as fit in 227 KB
-    static constexpr size_t BWD_BASE = 1024 + (size_t)BWD_W + (size_t)(RHDH + PSW + GSW) * 4 + 16;
+    static constexpr size_t BWD_BASE = 1024 + (size_t)BWD_W + (size_t)(RHDH + PSW + GSW) * 4 + 24;
     static constexpr int xs_pos(bool growing)
     {
         return growing ? 180 : (BWD_BASE + (size_t)C * 390 * 4 <= 232448 ? 390 : (int)((232448 - BWD_BASE) / (4 * C)));
@@ -785,8 +785,10 @@ __global__ void __launch_bounds__(128 * BWD_TILE_PARTS, 1) bwd_kernel_tc(StepArg
     float *W1s = reinterpret_cast<float *>(base), *W1T = W1s + D::W1S, *W2T = W1T + D::W1T;
     float *RHDH = reinterpret_cast<float *>(base + D::BWD_W), *PSW = RHDH + D::RHDH, *GSW = PSW + D::PSW;
     float *XSP = GSW + D::GSW;  // the prefetched halo
-    uint64_t *bar = reinterpret_cast<uint64_t *>(XSP + C * D::xs_pos(GROWING));
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bar + 1);
+    // bar: the contractions issued by thread 0; bar2: the dW2 chain, issued by thread 32 (another SM sub-partition)
+    // beside thread 0's dp chain
+    uint64_t *bar = reinterpret_cast<uint64_t *>(XSP + C * D::xs_pos(GROWING)), *bar2 = bar + 1;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bar + 2);
 
     const int tid = threadIdx.x, warp = tid / 32, part = tid / 128, lt = tid % 128;
     const TileGeom g = make_geom(a.H, a.W, GROWING);
@@ -806,6 +808,7 @@ __global__ void __launch_bounds__(128 * BWD_TILE_PARTS, 1) bwd_kernel_tc(StepArg
     }
     if (tid == 0) {
         umma::mbar_init(bar, 1);
+        umma::mbar_init(bar2, 1);
         umma::fence_mbar_init();
     }
     if (warp == 0) {
@@ -834,12 +837,16 @@ __global__ void __launch_bounds__(128 * BWD_TILE_PARTS, 1) bwd_kernel_tc(StepArg
     const uint32_t sW1 = umma::smem_u32(W1s), sW1T = umma::smem_u32(W1T), sW2T = umma::smem_u32(W2T);
     const uint32_t sRH = umma::smem_u32(RHDH), sP = umma::smem_u32(PSW), sG = umma::smem_u32(GSW);
 
-    uint32_t phase = 0;
+    uint32_t phase = 0, phase2 = 0;
     int cur_k = -1;
     bool started = false, failed = false;
-    auto wait_mma = [&]() {
-        const bool ok = umma::mbar_wait(bar, phase);
+    auto wait_mma = [&](bool both = false) {  // both: the dW2 chain (bar2) too
+        bool ok = umma::mbar_wait(bar, phase);
         phase ^= 1;
+        if (both) {
+            ok &= umma::mbar_wait(bar2, phase2);
+            phase2 ^= 1;
+        }
         if (!__syncthreads_and(ok))
             failed = true;
         umma::fence_after_sync();
@@ -1046,21 +1053,25 @@ __global__ void __launch_bounds__(128 * BWD_TILE_PARTS, 1) bwd_kernel_tc(StepArg
         __syncthreads();
         if (prefetch && t_next < t1)  // the next tile's alive byte has arrived by now: its gy loads
             request_gm();
-        // ---- 4. dW2^T += relu(h)^T gm (K = pixels, MN-major), DP = dh W1 (A from TMEM)
-        if (tid == 0) {
+        // ---- 4. dW2^T += relu(h)^T gm (K = pixels, MN-major; thread 32), DP = dh W1 (A from TMEM; thread 0)
+        if (tid == 32) {
             umma::fence_after_sync();
 #pragma unroll
             for (int ks = 0; ks < 16; ++ks)
                 umma::mma_ss(tmem + D::T_ACC2, umma::smem_desc(sRH + ks * 1024, 128 * 128, 512, umma::LAYOUT_SW128_32B),
                              umma::smem_desc(sG + ks * 1024, 128 * 128, 512, umma::LAYOUT_SW128_32B),
                              umma::idesc_tf32(128, 16, true, true), started || ks > 0);
+            umma::commit(bar2);
+        }
+        if (tid == 0) {
+            umma::fence_after_sync();
 #pragma unroll
             for (int ks = 0; ks < HID / 8; ++ks)
                 umma::mma_ts(tmem + D::T_P, tmem + D::T_H + ks * 8, umma::smem_desc(sW1T + ks * 2 * D::PIN * 16, D::PIN * 16, 128),
                              umma::idesc_tf32(128, D::PIN, false, false), ks > 0);
             umma::commit(bar);
         }
-        if (!wait_mma())
+        if (!wait_mma(true))
             break;
         // ---- 5. dh -> smem (swizzled, over relu(h)); dW1' += dh^T p'; dp -> dp scratch
 #pragma unroll
