@@ -1093,35 +1093,53 @@ __global__ void __launch_bounds__(128 * NPART + 96, 1) bwd_rows_kernel(StepArgs 
             if (lane32 == 0)
                 mbar_arrive(bar);
         };
-        auto flush = [&](int kk) {  // WG accumulator -> partial slot (blockIdx.x + kk); TMEM lanes 0..63 are read by
-            if (!compute || wq >= 2)  // the warps of lane quadrants 0 and 1, part p taking column chunks p, p + NPART, ..
+        // WG accumulator -> partial slot (blockIdx.x + kk). TMEM lane f is the accumulator row f: dW1[.][f] (f < PIN) and
+        // db1 (f = PIN) in columns HID.., dW2[f - GM0][.] (GM0 <= f < GM0 + C) in columns 0..HID-1. Only the warps of lane
+        // quadrants 0 and 1 can read lanes 0..63; each reads the column groups its rows need, in chunks of 8 columns,
+        // chunk i of a group going to part i % NPART. Every old value a lane adds to is in flight before the first store
+        // (one memory latency per flush, not one per chunk).
+        auto flush = [&](int kk) {
+            if (!compute || wq >= 2)
                 return;
             const int f = x;
             float *out = a.partial + (size_t)(blockIdx.x + kk) * D::PART;
             const bool add = a.partial_add != 0;
-#pragma unroll 1
-            for (int cc = part; cc < F::NACC / 16; cc += NPART) {
-                float v[16], old[16];
-                umma::tmem_ld16(lane + F::T_ACC + cc * 16, v);
-                // this thread's slot element for column j = cc 16 + e, or null: dw2[c][j] (rows GM0.., j < HID),
-                // dw1[j - HID][f] (rows < PIN) and db1[j - HID] (row PIN)
-                auto dst = [&](int e) -> float * {
-                    const int j = cc * 16 + e;
-                    if (j < HID)
-                        return f >= F::GM0 && f < F::GM0 + C ? out + HID * (D::PIN + 1) + (f - F::GM0) * HID + j : nullptr;
-                    return f < D::PIN ? out + (j - HID) * D::PIN + f : f == D::PIN ? out + HID * D::PIN + (j - HID) : nullptr;
-                };
+            constexpr int NCH = HID / 8, MY = (NCH + NPART - 1) / NPART;  // chunks per group, per part
+            const int q0 = 32 * wq;                                      // the warp's rows q0 .. q0 + 31
+            const bool need2 = q0 < F::GM0 + C && q0 + 32 > F::GM0, need1 = q0 <= D::PIN;  // warp-uniform
+            const bool row2 = f >= F::GM0 && f < F::GM0 + C;
+            auto dst = [&](int m, int e) -> float * {  // the slot element of column 8 (part + m NPART) + e, or null
+                const int j = (part + m * NPART) * 8 + e;
+                if (row2)
+                    return out + HID * (D::PIN + 1) + (f - F::GM0) * HID + j;
+                if (f < D::PIN)
+                    return out + j * D::PIN + f;
+                return f == D::PIN ? out + HID * D::PIN + j : nullptr;
+            };
+            float old[MY][8];
 #pragma unroll
-                for (int e = 0; e < 16; ++e) {  // every old value in flight before the first store
-                    float *o = dst(e);
-                    old[e] = add && o != nullptr ? *o : 0.f;
+            for (int m = 0; m < MY; ++m)
+#pragma unroll
+                for (int e = 0; e < 8; ++e) {
+                    float *o = dst(m, e);
+                    old[m][e] = add && o != nullptr && part + m * NPART < NCH ? *o : 0.f;
                 }
+#pragma unroll
+            for (int m = 0; m < MY; ++m) {
+                const int i = part + m * NPART;
+                if (i >= NCH)
+                    break;
+                float v2[8] = {}, v1[8] = {};
+                if (need2)
+                    umma::tmem_ld8(lane + F::T_ACC + i * 8, v2);
+                if (need1)
+                    umma::tmem_ld8(lane + F::T_ACC + HID + i * 8, v1);
                 umma::tmem_wait_ld();
 #pragma unroll
-                for (int e = 0; e < 16; ++e) {
-                    float *o = dst(e);
+                for (int e = 0; e < 8; ++e) {
+                    float *o = dst(m, e);
                     if (o != nullptr)
-                        *o = old[e] + v[e];
+                        *o = old[m][e] + (row2 ? v2[e] : v1[e]);
                 }
             }
         };
