@@ -545,8 +545,10 @@ __global__ void __launch_bounds__(128 * NPART + 96, 1) fwd_rows_kernel(StepArgs 
     const int RS = STRIP ? F::XS : W;   // ring row stride
     const size_t plane = (size_t)H * W;
     __shared__ int64_t band[2];  // this CTA's rows [g0, g1), found by thread 0
+    __shared__ uint64_t seed_sh; // the step's mask seed (a device read when the seed lives on the device)
 
     if (tid == 0) {
+        const uint64_t sd = step_seed_of(a);  // in flight while the band is found and the mbarriers initialised
         band_range(row_bands(a, gridDim.x), blockIdx.x, &band[0], &band[1]);
         for (int i = 0; i < 2 * F::XRING; ++i)
             umma::mbar_init(&xfull[i], i < F::XRING ? 1 : F::W_M1);  // full: the copy bytes; empty: every compute warp
@@ -558,6 +560,7 @@ __global__ void __launch_bounds__(128 * NPART + 96, 1) fwd_rows_kernel(StepArgs 
         umma::mbar_init(epi_done, F::W_M1);
         *abort = 0;
         umma::fence_mbar_init();
+        seed_sh = sd;
     }
     __syncthreads();
     const int64_t g0 = band[0], g1 = band[1];
@@ -577,7 +580,7 @@ __global__ void __launch_bounds__(128 * NPART + 96, 1) fwd_rows_kernel(StepArgs 
         umma::tmem_alloc(tslot, F::TMEM);
         umma::tmem_relinquish();
     } else {
-        const uint64_t seed = step_seed_of(a);
+        const uint64_t seed = seed_sh;
         for (int rel = warp - 1; rel < nrows; rel += nw - 1) {
             const int yy = r0 + rel, dn = yy / H, Y = yy - dn * H;
             if (!STRIP) {
@@ -936,13 +939,13 @@ struct BwdRows {
     static constexpr size_t OFF_BAR = OFF_MK + 2 * 128;
     // x ring, mask buffers, g1, dp, wg (tensor-core completions), wg_go, ea_done, fe_done (one arrival per warp)
     static constexpr int NBAR = XRING + 8;
-    // then the TMEM slot and abort words (8 bytes) and this CTA's row band (two int64)
+    // then the TMEM slot and abort words (8 bytes), this CTA's row band and the step's mask seed (three int64)
     static constexpr size_t OFF_BAND = OFF_BAR + 8 * NBAR + 8;
     // The swizzled operands need a 1024-byte aligned base. The strip layout leaves no room for alignment slack: its
     // kernel requires the dynamic shared memory to start 1024-aligned (it does when the kernel has no static shared
     // memory) and reports a device error otherwise.
     static constexpr size_t ALIGN_SLACK = STRIP ? 0 : 1024;
-    static constexpr size_t smem() { return ALIGN_SLACK + OFF_BAND + 16; }
+    static constexpr size_t smem() { return ALIGN_SLACK + OFF_BAND + 24; }
     static_assert(OFF_BAR % 8 == 0, "mbarrier alignment");
     static_assert(smem() <= 232448, "227 KB of shared memory per CTA");
 };
@@ -986,9 +989,9 @@ __global__ void __launch_bounds__(128 * NPART + 96, 1) bwd_rows_kernel(StepArgs 
               ir = STRIP ? x + 5 : xc + 1 >= W ? 0 : xc + 1;
     const int RS = STRIP ? F::XS : W;  // ring row stride
     const size_t plane = (size_t)H * W;
-    // this CTA's rows [g0, g1), found by thread 0 (STRIP: in the dynamic shared memory, so that the kernel has no static
-    // shared memory and its dynamic shared memory starts 1024-aligned)
-    __shared__ int64_t band_static[2];
+    // this CTA's rows [g0, g1) and the step's mask seed, found by thread 0 (STRIP: in the dynamic shared memory, so that
+    // the kernel has no static shared memory and its dynamic shared memory starts 1024-aligned)
+    __shared__ int64_t band_static[3];
     int64_t *band = STRIP ? reinterpret_cast<int64_t *>(base + F::OFF_BAND) : band_static;
 
     // constant PSW features of both buffers: 1 at PIN and PIN + 1, 0 at GM0 + C .. 63
@@ -999,6 +1002,7 @@ __global__ void __launch_bounds__(128 * NPART + 96, 1) bwd_rows_kernel(StepArgs 
         PSW[b * D::PSW + umma::sw32_offset(f, q, 128) / 4] = f < F::GM0 ? 1.f : 0.f;
     }
     if (tid == 0) {
+        const uint64_t sd = step_seed_of(a);  // in flight while the band is found and the mbarriers initialised
         band_range(row_bands(a, gridDim.x), blockIdx.x, &band[0], &band[1]);
         for (int i = 0; i < F::XRING; ++i)
             umma::mbar_init(&xfull[i], 1);
@@ -1012,6 +1016,7 @@ __global__ void __launch_bounds__(128 * NPART + 96, 1) bwd_rows_kernel(StepArgs 
         umma::mbar_init(fe_done, F::W_MMA);
         *abort = 0;
         umma::fence_mbar_init();
+        band[2] = (int64_t)sd;
     }
     if (warp == 0) {
         umma::tmem_alloc(tslot, F::TMEM);
@@ -1214,14 +1219,14 @@ __global__ void __launch_bounds__(128 * NPART + 96, 1) bwd_rows_kernel(StepArgs 
                     umma::bulk_prefetch_l2(gyn + ((size_t)c * H + rowY(e - 1)) * W + c0, bytes);
             };
             // producer warp: update mask of sequence row j (the strip's columns) -> MK[j % 2], then mkfull[j % 2]
-            auto draw_mask = [&](int j) {
+            auto draw_mask = [&](int j, uint64_t sd) {
                 ok = __shfl_sync(~0u, ok, 0);
                 if (ok) {
                     if (STRIP)
-                        row_mask_strip_warp(MK + (j & 1) * 128, step_seed_of(a), a.rate, n + a.n_offset, H, W, rowY(j),
+                        row_mask_strip_warp(MK + (j & 1) * 128, sd, a.rate, n + a.n_offset, H, W, rowY(j),
                                             lane32, c0);
                     else
-                        row_mask_warp(MK + (j & 1) * 128, step_seed_of(a), a.rate, n + a.n_offset, H, W, rowY(j), lane32);
+                        row_mask_warp(MK + (j & 1) * 128, sd, a.rate, n + a.n_offset, H, W, rowY(j), lane32);
                     __syncwarp();
                     if (lane32 == 0)
                         mbar_arrive(&mkfull[j & 1]);
@@ -1260,9 +1265,10 @@ __global__ void __launch_bounds__(128 * NPART + 96, 1) bwd_rows_kernel(StepArgs 
             if (prod) {
                 // ======== producer: entries 0..2 (issued above) and masks 0, 1; after every warp's FE(j): entry j + 3,
                 // mask j + 2
-                draw_mask(0);
+                const uint64_t sd = (uint64_t)band[2];
+                draw_mask(0, sd);
                 if (L > 1)
-                    draw_mask(1);
+                    draw_mask(1, sd);
                 for (int j = 0; j < L; ++j) {
                     if (lane32 == 0)
                         ok &= wait_bar(fe_done, feph, abort);
@@ -1272,7 +1278,7 @@ __global__ void __launch_bounds__(128 * NPART + 96, 1) bwd_rows_kernel(StepArgs 
                         issue_x(j + 3);
                     prefetch_rows(j + 2 * F::XRING);
                     if (j + 2 < L)
-                        draw_mask(j + 2);
+                        draw_mask(j + 2, sd);
                     // the partial slot this NCA's accumulator is added to when the segment ends: into L2 a few rows
                     // ahead, so that the flush's reads of the old values hit
                     if (a.partial_add && lane32 == 0 && j == (L > 4 ? L - 4 : 0))
