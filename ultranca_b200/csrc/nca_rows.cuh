@@ -1121,50 +1121,41 @@ __global__ void __launch_bounds__(128 * NPART + 96, 1) bwd_rows_kernel(StepArgs 
         // WG accumulator -> partial slot (blockIdx.x + kk). TMEM lane f is the accumulator row f: dW1[.][f] (f < PIN) and
         // db1 (f = PIN) in columns HID.., dW2[f - GM0][.] (GM0 <= f < GM0 + C) in columns 0..HID-1. Only the warps of lane
         // quadrants 0 and 1 can read lanes 0..63; each reads the column groups its rows need, in chunks of 8 columns,
-        // chunk i of a group going to part i % NPART. Every old value a lane adds to is in flight before the first store
-        // (one memory latency per flush, not one per chunk).
+        // chunk i of a group going to part i % NPART. partial_add: the slot already holds this rollout's later steps and
+        // the chunk is added by reductions at L2 (red.global.add: no old value travels to the SM; this CTA is the slot's
+        // only writer in the launch, so each element is old + v rounded once, as a load-add-store would give, except
+        // that a subnormal sum flushes to zero); otherwise the chunk is stored.
         auto flush = [&](int kk) {
             if (!compute || wq >= 2)
                 return;
             const int f = x;
             float *out = a.partial + (size_t)(blockIdx.x + kk) * D::PART;
             const bool add = a.partial_add != 0;
-            constexpr int NCH = HID / 8, MY = (NCH + NPART - 1) / NPART;  // chunks per group, per part
-            const int q0 = 32 * wq;                                      // the warp's rows q0 .. q0 + 31
+            constexpr int NCH = HID / 8;  // chunks per group
+            const int q0 = 32 * wq;       // the warp's rows q0 .. q0 + 31
             const bool need2 = q0 < F::GM0 + C && q0 + 32 > F::GM0, need1 = q0 <= D::PIN;  // warp-uniform
             const bool row2 = f >= F::GM0 && f < F::GM0 + C;
-            auto dst = [&](int m, int e) -> float * {  // the slot element of column 8 (part + m NPART) + e, or null
-                const int j = (part + m * NPART) * 8 + e;
-                if (row2)
-                    return out + HID * (D::PIN + 1) + (f - F::GM0) * HID + j;
-                if (f < D::PIN)
-                    return out + j * D::PIN + f;
-                return f == D::PIN ? out + HID * D::PIN + j : nullptr;
-            };
-            float old[MY][8];
-#pragma unroll
-            for (int m = 0; m < MY; ++m)
-#pragma unroll
-                for (int e = 0; e < 8; ++e) {
-                    float *o = dst(m, e);
-                    old[m][e] = add && o != nullptr && part + m * NPART < NCH ? *o : 0.f;
-                }
-#pragma unroll
-            for (int m = 0; m < MY; ++m) {
-                const int i = part + m * NPART;
-                if (i >= NCH)
-                    break;
+            float *row = row2 ? out + HID * (D::PIN + 1) + (f - F::GM0) * HID : f < D::PIN ? out + f : out + HID * D::PIN;
+            const int js = row2 || f == D::PIN ? 1 : D::PIN;  // element stride along the columns j
+            const bool mine = row2 || f <= D::PIN;
+#pragma unroll 1
+            for (int i = part; i < NCH; i += NPART) {
                 float v2[8] = {}, v1[8] = {};
                 if (need2)
                     umma::tmem_ld8(lane + F::T_ACC + i * 8, v2);
                 if (need1)
                     umma::tmem_ld8(lane + F::T_ACC + HID + i * 8, v1);
                 umma::tmem_wait_ld();
+                if (mine) {
+                    float *o = row + (size_t)(i * 8) * js;
 #pragma unroll
-                for (int e = 0; e < 8; ++e) {
-                    float *o = dst(m, e);
-                    if (o != nullptr)
-                        *o = old[m][e] + (row2 ? v2[e] : v1[e]);
+                    for (int e = 0; e < 8; ++e) {
+                        const float v = row2 ? v2[e] : v1[e];
+                        if (add)
+                            atomicAdd(o + e * js, v);
+                        else
+                            o[e * js] = v;
+                    }
                 }
             }
         };
