@@ -102,6 +102,10 @@ __device__ __forceinline__ void bar_sync(int id, int count)
 {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
 }
+__device__ __forceinline__ void bar_arrive(int id, int count)
+{
+    asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
 __device__ __forceinline__ bool bar_and(int id, int count, bool pred)
 {
     uint32_t r;
@@ -959,13 +963,13 @@ struct BwdRows {
     static constexpr size_t OFF_BAR = OFF_MK + 2 * 128;
     // x ring, mask buffers, g1, dp, wg (tensor-core completions), wg_go, ea_done, fe_done (one arrival per warp)
     static constexpr int NBAR = XRING + 8;
-    // then the TMEM slot and abort words (8 bytes), this CTA's row band and the step's mask seed (three int64)
-    static constexpr size_t OFF_BAND = OFF_BAR + 8 * NBAR + 8;
+    // then the TMEM slot and abort words (8 bytes) and the step's mask seed (8 bytes)
+    static constexpr size_t OFF_SEED = OFF_BAR + 8 * NBAR + 8;
     // The swizzled operands need a 1024-byte aligned base. The strip layout leaves no room for alignment slack: its
     // kernel requires the dynamic shared memory to start 1024-aligned (it does when the kernel has no static shared
     // memory) and reports a device error otherwise.
     static constexpr size_t ALIGN_SLACK = STRIP ? 0 : 1024;
-    static constexpr size_t smem() { return ALIGN_SLACK + OFF_BAND + 24; }
+    static constexpr size_t smem() { return ALIGN_SLACK + OFF_SEED + 8; }
     static_assert(OFF_BAR % 8 == 0, "mbarrier alignment");
     static_assert(smem() <= 232448, "227 KB of shared memory per CTA");
 };
@@ -1009,10 +1013,18 @@ __global__ void __launch_bounds__(128 * NPART + 96, 1) bwd_rows_kernel(StepArgs 
               ir = STRIP ? x + 5 : xc + 1 >= W ? 0 : xc + 1;
     const int RS = STRIP ? F::XS : W;  // ring row stride
     const size_t plane = (size_t)H * W;
-    // this CTA's rows [g0, g1) and the step's mask seed, found by thread 0 (STRIP: in the dynamic shared memory, so that
-    // the kernel has no static shared memory and its dynamic shared memory starts 1024-aligned)
-    __shared__ int64_t band_static[3];
-    int64_t *band = STRIP ? reinterpret_cast<int64_t *>(base + F::OFF_BAND) : band_static;
+    // this CTA's rows [g0, g1), found by every thread (no thread waits for another to find them), and the step's mask
+    // seed, read once by thread 0 (STRIP: in the dynamic shared memory, so that the kernel has no static shared memory
+    // and its dynamic shared memory starts 1024-aligned)
+    __shared__ uint64_t seed_static;
+    uint64_t *seed_sh = STRIP ? reinterpret_cast<uint64_t *>(base + F::OFF_SEED) : &seed_static;
+    int64_t g0, g1;
+    band_range(row_bands(a, gridDim.x), blockIdx.x, &g0, &g1);
+    const int k_first = g1 > g0 ? (int)(g0 / ((int64_t)a.B * H)) : -1;  // the NCA of the band's first row
+    // X_STABLE (x not written by the previous kernel) and one tile per row: the producer copies the first segment's
+    // first x rows, and prefetches the next ones into L2, as soon as the mbarriers exist, while the weights are staged
+    constexpr bool EARLY_X = X_STABLE && !STRIP;
+    const bool early_x = EARLY_X && k_first >= 0;
 
     // constant PSW features of both buffers: 1 at PIN and PIN + 1, 0 at GM0 + C .. 63
     constexpr int NCONST = 64 - C - D::PIN;  // features PIN .. 63 other than gm
@@ -1021,31 +1033,65 @@ __global__ void __launch_bounds__(128 * NPART + 96, 1) bwd_rows_kernel(StepArgs 
         const int f = i < F::GM0 - D::PIN ? D::PIN + i : F::GM0 + C + (i - (F::GM0 - D::PIN));
         PSW[b * D::PSW + umma::sw32_offset(f, q, 128) / 4] = f < F::GM0 ? 1.f : 0.f;
     }
-    if (tid == 0) {
-        const uint64_t sd = step_seed_of(a);  // in flight while the band is found and the mbarriers initialised
-        band_range(row_bands(a, gridDim.x), blockIdx.x, &band[0], &band[1]);
-        for (int i = 0; i < F::XRING; ++i)
-            umma::mbar_init(&xfull[i], 1);
-        umma::mbar_init(&mkfull[0], 1);
-        umma::mbar_init(&mkfull[1], 1);
-        umma::mbar_init(g1bar, 1);
-        umma::mbar_init(dpbar, 1);
-        umma::mbar_init(wgbar, 1);
-        umma::mbar_init(wggo, 1);
-        umma::mbar_init(ea_done, F::W_MMA);
-        umma::mbar_init(fe_done, F::W_MMA);
-        *abort = 0;
-        umma::fence_mbar_init();
-        band[2] = (int64_t)sd;
-    }
+    // Set-up: warp 0 initialises the mbarriers (then the producer may copy) and allocates the Tensor Memory; the
+    // producer copies / prefetches the first rows (early_x); warps 1 .. W_PROD - 1 stage the first NCA's weights, the
+    // set-up's longest part, from the kernel's entry on.
     if (warp == 0) {
+        if (lane32 == 0) {
+            const uint64_t sd = step_seed_of(a);  // in flight while the mbarriers are initialised
+            for (int i = 0; i < F::XRING; ++i)
+                umma::mbar_init(&xfull[i], 1);
+            umma::mbar_init(&mkfull[0], 1);
+            umma::mbar_init(&mkfull[1], 1);
+            umma::mbar_init(g1bar, 1);
+            umma::mbar_init(dpbar, 1);
+            umma::mbar_init(wgbar, 1);
+            umma::mbar_init(wggo, 1);
+            umma::mbar_init(ea_done, F::W_MMA);
+            umma::mbar_init(fe_done, F::W_MMA);
+            *abort = 0;
+            umma::fence_mbar_init();
+            *seed_sh = sd;
+        }
+        __syncwarp();
+        if (early_x)
+            bar_arrive(2, 64);
         umma::tmem_alloc(tslot, F::TMEM);
         umma::tmem_relinquish();
+    } else if (prod) {
+        if (early_x) {
+            bar_sync(2, 64);  // warp 0 initialised the mbarriers
+            int64_t gg = g0;
+            RowSeg sg0;
+            next_segment(gg, g1, H, sg0);
+            const int L0 = sg0.r1 - sg0.r0 + 2;
+            const float *xn0 = a.x + (size_t)sg0.n * C * plane, *gyn0 = a.gy + (size_t)sg0.n * C * plane;
+            for (int e = 0; e < F::XRING; ++e) {  // entries 0 .. XRING - 1 (the segment's prologue skips them)
+                if (lane32 == 0)
+                    umma::mbar_arrive_expect_tx(&xfull[e], (uint32_t)(C * W * 4));
+                __syncwarp();
+                if (lane32 < C)
+                    umma::bulk_g2s(XR + ((size_t)e * C + lane32) * W,
+                                   xn0 + ((size_t)lane32 * H + wrap_index(sg0.r0 - 2 + e, H)) * W, (uint32_t)(W * 4),
+                                   &xfull[e]);
+            }
+            for (int e = F::XRING; e < 2 * F::XRING && e <= L0 + 1; ++e) {  // the prologue's L2 prefetches, early
+                const int Y = wrap_index(sg0.r0 - 2 + e, H), c = lane32 - 16;
+                if (lane32 < C)
+                    umma::bulk_prefetch_l2(xn0 + ((size_t)lane32 * H + Y) * W, (uint32_t)(W * 4));
+                if (c >= 0 && c < C && e - 1 < L0)
+                    umma::bulk_prefetch_l2(gyn0 + ((size_t)c * H + Y) * W, (uint32_t)(W * 4));
+            }
+        }
+    } else if (warp < F::W_PROD && k_first >= 0) {
+        const int k = k_first;
+        stage_rows_weights<D, true>(W1s, W1T, W2T, a.w1 + (size_t)k * HID * D::PIN, a.b1 + (size_t)k * HID,
+                                    a.w2 + (size_t)k * C * HID, tid - 32, 32 * (F::W_PROD - 1), F::GM0 - D::PIN);
+        umma::fence_proxy_async();
     }
     umma::fence_before_sync();
     __syncthreads();
     umma::fence_after_sync();
-    const int64_t g0 = band[0], g1 = band[1];
     const uint32_t tmem = *tslot, lane = umma::tmem_addr(tmem, warp, 0);
     if (compute && part == 0) {  // constant P columns of both buffers: 1, 1 at PIN, PIN + 1; 0 up to 63
         const float v[8] = {1.f, 1.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f}, z[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
@@ -1105,7 +1151,13 @@ __global__ void __launch_bounds__(128 * NPART + 96, 1) bwd_rows_kernel(StepArgs 
         const uint64_t dW2T = umma::smem_desc(umma::smem_u32(W2T), HID * 16, 128);
         constexpr uint32_t I1 = umma::idesc_tf32(128, HID, false, false), IP = umma::idesc_tf32(128, D::PIN, false, false);
         uint32_t xpar = 0, mkpar = 0, g1ph = 0, dpph = 0, wgph = 0, eaph = 0, feph = 0;
-        int cur_k = -1, g1_issued = 0, dp_issued = 0, x_issued[F::XRING] = {0, 0, 0};
+        // k_first's weights were staged above; early_x: the first segment's entries 0 .. XRING - 1 were issued and its
+        // prologue's prefetches made above
+        int cur_k = k_first, g1_issued = 0, dp_issued = 0, x_issued[F::XRING] = {0, 0, 0};
+        bool x_pre = early_x && prod;
+        if (x_pre)
+            for (int e = 0; e < F::XRING; ++e)
+                x_issued[e] = 1;
         bool dep_waited = false;
         auto group_sync = [&]() {
             umma::fence_before_sync();
@@ -1252,12 +1304,13 @@ __global__ void __launch_bounds__(128 * NPART + 96, 1) bwd_rows_kernel(StepArgs 
                 asm volatile("griddepcontrol.wait;" ::: "memory");
                 dep_waited = true;
             }
-            if (prod) {
+            if (prod && !x_pre) {
                 for (int e = 0; e < F::XRING; ++e)
                     issue_x(e);
                 for (int e = F::XRING; e < 2 * F::XRING; ++e)
                     prefetch_rows(e);
             }
+            x_pre = false;
             // a new NCA needs its weights (and the old accumulator flushed)
             if (k != cur_k) {
                 group_sync();  // every warp finished the previous segment; its tensor-core work completed
@@ -1276,7 +1329,7 @@ __global__ void __launch_bounds__(128 * NPART + 96, 1) bwd_rows_kernel(StepArgs 
             if (prod) {
                 // ======== producer: entries 0..2 (issued above) and masks 0, 1; after every warp's FE(j): entry j + 3,
                 // mask j + 2
-                const uint64_t sd = (uint64_t)band[2];
+                const uint64_t sd = *seed_sh;
                 draw_mask(0, sd);
                 if (L > 1)
                     draw_mask(1, sd);
