@@ -544,7 +544,7 @@ struct FwdRows {
 };
 
 template <int C, int HID, int NPART, bool STRIP = false>
-__global__ void __launch_bounds__(128 * NPART + 96, 1) fwd_rows_kernel(StepArgs a)
+__global__ void __maxnreg__(128) fwd_rows_kernel(StepArgs a)
 {
     using F = FwdRows<C, HID, NPART, STRIP>;
     using D = typename F::D;
@@ -600,12 +600,43 @@ __global__ void __launch_bounds__(128 * NPART + 96, 1) fwd_rows_kernel(StepArgs 
     const int nrows = (int)(g1 - g0);  // <= MAXROWS / S (the host sizes the grid so)
     const int64_t n0 = g0 / H;         // the band's first image and row
     const int r0 = (int)(g0 - n0 * H), nw = blockDim.x / 32;
-    if (warp == 0) {
+    // EARLY_X (one tile per row): the producer takes no part in the set-up; it waits for the previous kernel at once and
+    // copies the first segment's first ring entries, which land while the others build the tables and stage the
+    // weights (on the SMs the previous step frees last, that wait is already over). The set-up's barriers are then
+    // named barrier 1 over the other warps.
+    constexpr bool EARLY_X = !STRIP;
+    const int nset = EARLY_X ? nw - 1 : nw;  // warps of the set-up
+    auto setup_sync = [&]() {
+        if (EARLY_X)
+            bar_sync(1, 32 * nset);
+        else
+            __syncthreads();
+    };
+    int x_pre = 0;  // producer: ring entries of the first segment copied during the set-up
+    if (EARLY_X && prod) {
+        if (nrows > 0) {
+            asm volatile("griddepcontrol.wait;" ::: "memory");
+            int64_t gg = g0;
+            RowSeg sg0;
+            next_segment(gg, g1, H, sg0);
+            const float *xn0 = a.x + (size_t)sg0.n * C * plane;
+            x_pre = min(F::XRING, sg0.r1 - sg0.r0 + 2);
+            for (int e = 0; e < x_pre; ++e) {
+                if (lane32 == 0)
+                    umma::mbar_arrive_expect_tx(&xfull[e], (uint32_t)(C * W * 4));
+                __syncwarp();
+                if (lane32 < C)
+                    umma::bulk_g2s(XR + ((size_t)e * C + lane32) * W,
+                                   xn0 + ((size_t)lane32 * H + wrap_near(sg0.r0 - 1 + e, H)) * W, (uint32_t)(W * 4),
+                                   &xfull[e]);
+            }
+        }
+    } else if (warp == 0) {
         umma::tmem_alloc(tslot, F::TMEM);
         umma::tmem_relinquish();
     } else {
         const uint64_t seed = seed_sh;
-        for (int rel = warp - 1; rel < nrows; rel += nw - 1) {
+        for (int rel = warp - 1; rel < nrows; rel += nset - 1) {
             const int yy = r0 + rel, dn = yy / H, Y = yy - dn * H;
             if (!STRIP) {
                 row_mask_xorder_warp(MKX + (size_t)rel * 4, seed, a.rate, n0 + dn + a.n_offset, H, W, Y, lane32);
@@ -619,28 +650,36 @@ __global__ void __launch_bounds__(128 * NPART + 96, 1) fwd_rows_kernel(StepArgs 
             }
         }
     }
-    __syncthreads();
+    if (!(EARLY_X && prod))
+        setup_sync();
     int cur_k = -1;
-    if (warp == 0) {  // tile table: tiles of <= 128 updating pixels over <= SPAN rows
+    if (EARLY_X && prod) {
+    } else if (warp == 0) {  // tile table: tiles of <= 128 updating pixels over <= SPAN rows
         build_tile_table<F::SPAN>(MKX, CUM, TILE, SEGT, g0, g1, H, S, 0, lane32);
-    } else if (nrows > 0) {  // the first segment's NCA: its weights, by warps 1..
+    } else if (nrows > 0) {  // the first segment's NCA: its weights, by warps 1 .. nset - 1
         const int k = (int)(n0 / a.B);
         stage_rows_weights<D, false>(W1s, nullptr, W2s, a.w1 + (size_t)k * HID * D::PIN, a.b1 + (size_t)k * HID,
-                                     a.w2 + (size_t)k * C * HID, tid - 32, blockDim.x - 32, 0);
+                                     a.w2 + (size_t)k * C * HID, tid - 32, 32 * (nset - 1), 0);
         umma::fence_proxy_async();
     }
     if (nrows > 0)
         cur_k = (int)(n0 / a.B);
-    const uint32_t tmem = *tslot, lane = umma::tmem_addr(tmem, warp, 0);
+    uint32_t tmem = 0, lane = 0;  // (the producer uses no Tensor Memory)
+    if (!(EARLY_X && prod)) {
+        tmem = *tslot;
+        lane = umma::tmem_addr(tmem, warp, 0);
+    }
     if (compute && part == 0) {  // p' columns past the channel features: bias-hi, bias-lo = 1, zeros (never overwritten)
         const float v[8] = {1.f, 1.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
         umma::tmem_st8(lane + F::T_P0 + D::PIN, v);
         umma::tmem_st8(lane + F::T_P1 + D::PIN, v);
         umma::tmem_wait_st();
     }
-    umma::fence_before_sync();
-    __syncthreads();
-    umma::fence_after_sync();
+    if (!(EARLY_X && prod)) {
+        umma::fence_before_sync();
+        setup_sync();
+        umma::fence_after_sync();
+    }
 
     const uint64_t dW1 = umma::smem_desc(umma::smem_u32(W1s), HID * 16, 128);
     const uint64_t dW2 = umma::smem_desc(umma::smem_u32(W2s), D::CP * 16, 128);
@@ -649,6 +688,8 @@ __global__ void __launch_bounds__(128 * NPART + 96, 1) fwd_rows_kernel(StepArgs 
     bool ok = true;
     uint32_t epar = 0, g1par = 0, g2par = 0, eph = 0, fepar = 0;  // *par: one parity bit per buffer / ring slot
     int x_uses[F::XRING] = {0, 0, 0, 0, 0, 0, 0, 0};
+    for (int e = 0; e < x_pre; ++e)  // producer: the entries copied during the set-up
+        x_uses[e] = 1;
     uint64_t *last_bar = nullptr;
     uint32_t last_par = 0;
     auto wait_par = [&](uint64_t *bars, uint32_t &par, int bj) {  // the next phase of bars[bj]
@@ -690,7 +731,7 @@ __global__ void __launch_bounds__(128 * NPART + 96, 1) fwd_rows_kernel(StepArgs 
         if (prod) {
             // ======== producer: x row wrap(r0 - 1 + e) -> slot (ebase + e) % XRING, e = 0 .. L + 1; lane c copies
             // channel c (a starved single lane issuing all of them falls behind the compute warps)
-            for (int e = 0; e < L + 2; ++e) {
+            for (int e = seg == 0 && s == 0 ? x_pre : 0; e < L + 2; ++e) {
                 const int slot = (ebase + e) & (F::XRING - 1);
                 if (lane32 == 0 && x_uses[slot] > 0)  // every compute warp released the slot's previous row
                     ok &= wait_bar(&xempty[slot], (uint32_t)((x_uses[slot] - 1) & 1), abort);
