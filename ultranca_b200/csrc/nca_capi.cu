@@ -292,9 +292,9 @@ void launch_pdl(Kern kern, int grid, int threads, size_t smem, cudaStream_t st, 
 
 // Switch costs (quarter rows) of the cost-balanced row bands, measured per CTA on the B200 (config 1, per-CTA clock
 // stamps against band composition): a band that crosses into another image costs the forward ~2.6 rows and the
-// backward ~2.7 rows more (halo rows, pipeline drain and refill), one that crosses into another NCA ~8.9 and ~6.8
-// rows in all (weights restaged; the backward also flushes its weight-gradient accumulator).
-constexpr int FWD_BAND_S4 = 10, FWD_BAND_N4 = 25, BWD_BAND_S4 = 11, BWD_BAND_N4 = 16;
+// backward ~2.7 rows more (halo rows, pipeline drain and refill), one that crosses into another NCA ~8.9 and ~4.0
+// rows in all (weights restaged; the backward also flushes its weight-gradient accumulator, by L2 reductions).
+constexpr int FWD_BAND_S4 = 10, FWD_BAND_N4 = 25, BWD_BAND_S4 = 11, BWD_BAND_N4 = 5;
 
 Bands fwd_bands(const Shape &s, int G) { return Bands{s.N * s.H, s.H, s.B * s.H, G, FWD_BAND_S4, FWD_BAND_N4}; }
 Bands bwd_bands(const Shape &s, int G) { return Bands{s.N * s.H, s.H, s.B * s.H, G, BWD_BAND_S4, BWD_BAND_N4}; }
